@@ -1,0 +1,407 @@
+#!/usr/bin/env python3
+"""Throughput benchmark: exact top-10 L2 over 100M x 128 u8 rows, 10K queries.
+
+Workload (one "step"): 10,000 u8 queries against a 100,000,000 x 128 u8
+corpus drawn from a clipped 4,096-component Gaussian mixture (means U[0,60],
+per-dim std 15, rounded, clipped to [0,255]); exact top-10 by (squared L2,
+row id).  Synthetic data of the BIGANN-like shape; the corpus is generated
+on the GPU in fixed 3.125M-row chunks so every GPU count sees the same rows.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun: rank r holds rows [r*N/G, (r+1)*N/G), scans them
+for all queries and the ranks exchange their top-10 lists with one NCCL
+all_gather, merged on the GPU.  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "winnex-madhava_b200"))
+
+N_DEFAULT = 100_000_000
+DIM = 128
+COMPONENTS = 4096
+SEED = 20261201
+CHUNK = 3_125_000
+METRIC = "queries/sec, 100M×128 u8 exact top-10, 10K-query batch at 1/2/4/8 B200; % roofline"
+
+
+# --------------------------------------------------------------------------- data
+def mixture_means():
+    return np.random.default_rng(SEED).uniform(0, 60, size=(COMPONENTS, DIM))
+
+
+def make_queries(nq):
+    means = mixture_means()
+    rng = np.random.default_rng(SEED + 1)
+    lab = rng.integers(0, COMPONENTS, size=nq)
+    return np.clip(np.rint(means[lab] + rng.normal(0, 15, size=(nq, DIM))), 0, 255).astype(np.uint8)
+
+
+def make_rows_gpu(torch, start, end, device):
+    """Rows [start, end) of the corpus on `device` (u8 [end-start][128])."""
+    means = torch.tensor(mixture_means(), dtype=torch.float32, device=device)
+    out = torch.empty((end - start, DIM), dtype=torch.uint8, device=device)
+    c0, c1 = start // CHUNK, (end + CHUNK - 1) // CHUNK
+    g = torch.Generator(device=device)
+    for c in range(c0, c1):
+        s, e = c * CHUNK, (c + 1) * CHUNK
+        g.manual_seed(SEED * 1000 + c)
+        lab = torch.randint(0, COMPONENTS, (CHUNK,), generator=g, device=device)
+        x = means[lab]
+        x.add_(torch.randn((CHUNK, DIM), generator=g, device=device), alpha=15.0)
+        x = x.round_().clamp_(0, 255).to(torch.uint8)
+        lo, hi = max(s, start), min(e, end)
+        if lo < hi:
+            out[lo - start:hi - start] = x[lo - s:hi - s]
+        del x, lab
+    return out
+
+
+# --------------------------------------------------------------------------- library
+class Stats(ctypes.Structure):
+    _fields_ = [("latency_ms", ctypes.c_double), ("pairs_scored", ctypes.c_int64),
+                ("pairs_pruned_by_bound", ctypes.c_int64), ("bound_violations", ctypes.c_int64),
+                ("candidates", ctypes.c_int64), ("tensor_core_path", ctypes.c_int32), ("levels", ctypes.c_int32),
+                ("full_scan_ms", ctypes.c_double), ("full_scan_pairs", ctypes.c_int64)]
+
+
+def load_lib():
+    path = os.path.join(ROOT, "winnex-madhava_b200", "winnex_madhava", "libwinnex_madhava_b200.so")
+    if not os.path.exists(path):
+        raise SystemExit(f"{path} missing: run python winnex-madhava_b200/build.py")
+    L = ctypes.CDLL(path)
+    P, i32, i64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+    L.mdh_index_create_u8_device.argtypes = [P, i64, i32, i32, i64, ctypes.POINTER(P)]
+    L.mdh_index_destroy.argtypes = [P]
+    L.mdh_search_u8.argtypes = [P, P, i32, i32, P, P, ctypes.POINTER(Stats)]
+    L.mdh_search_u8_device.argtypes = [P, P, i32, i32, P, P, P, ctypes.POINTER(Stats)]
+    L.mdh_merge_topk_device.argtypes = [P, P, i32, i32, i32, P, P, P]
+    L.mdh_set_scan_path.argtypes = [i32]
+    L.mdh_last_error.restype = ctypes.c_char_p
+    for f in ("mdh_index_create_u8_device", "mdh_index_destroy", "mdh_search_u8", "mdh_search_u8_device",
+              "mdh_merge_topk_device", "mdh_set_scan_path"):
+        getattr(L, f).restype = ctypes.c_int
+    return L
+
+
+def check(L, st, what):
+    if st != 0:
+        raise RuntimeError(f"{what} failed ({st}): {L.mdh_last_error().decode()}")
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock / throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = str(gpu_index)
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 9:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = self.rows
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "", 1).isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "", 1).isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        pw = [float(r[3]) for r in rows if r[3].replace(".", "", 1).isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
+
+
+# --------------------------------------------------------------------------- peaks
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# --------------------------------------------------------------------------- reference arm / cpu baseline
+def cpu_reference_qps(corpus_slice, n_total, queries, k, steps=1, warmup=0):
+    """Time the reference's own CPU exact scan (SpeedEngine.search_batch, OpenMP over
+    all host cores) on a row slice; QPS is scaled to the full corpus (the scan is
+    linear in the number of rows)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # test infrastructure: CPU baseline only
+
+    R = oracle.reference_module()
+    n_slice = corpus_slice.shape[0]
+    cores = os.cpu_count()
+    Q = np.ascontiguousarray(queries.astype(np.float32))
+    if R is not None:
+        os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+        eng = R.SpeedEngine(np.ascontiguousarray(corpus_slice), DIM, 1, 0, 4, False, "")
+        run = lambda: eng.search_batch(Q, len(Q), k)  # noqa: E731
+        kind = "reference"
+    else:
+        run = lambda: oracle.l2_exact_u8_int(corpus_slice, queries, k)  # noqa: E731
+        kind = "port"
+        cores = oracle.num_threads()
+    for _ in range(warmup):
+        run()
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    qps = len(Q) / t * (n_slice / n_total)
+    sample = (f"reference SpeedEngine.search_batch (CPU, OpenMP) on rows [0, {n_slice}) of the corpus with "
+              f"{len(Q)} queries per step; QPS scaled by {n_slice}/{n_total} rows (linear scan)")
+    if kind == "port":
+        sample = sample.replace("reference SpeedEngine.search_batch (CPU, OpenMP)", "oracle C port (OpenMP)")
+    return qps, {"value": qps, "unit": "queries/sec", "cores": cores, "kind": kind, "sample": sample,
+                 "seconds_per_step": t}
+
+
+# --------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--n", type=int, default=N_DEFAULT)
+    ap.add_argument("--nq", type=int, default=10_000)
+    ap.add_argument("--k", type=int, default=10)
+    ap.add_argument("--scan-path", type=int, default=0, help="0 auto, 1 CUDA cores, 2 tensor cores")
+    ap.add_argument("--cpu-slice", type=int, default=4_000_000)
+    ap.add_argument("--cpu-queries", type=int, default=16)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    warmup = max(3, args.warmup)
+
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    n_gpus = max(args.gpus, world)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    queries = make_queries(args.nq)
+    config = {"workload": f"{args.n // 1_000_000}M x {DIM} u8 clipped-GMM ({COMPONENTS} comps), {args.nq} queries, "
+                          f"exact top-{args.k} L2",
+              "n": args.n, "dim": DIM, "nq": args.nq, "k": args.k,
+              "parallelism": f"row-shard x{n_gpus} + NCCL all_gather of top-k",
+              "l2_flush": "inputs larger than L2 (corpus 12.8 GB per step at 100M)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            if dist is not None:
+                dist.destroy_process_group()
+            return
+        n_slice = min(args.cpu_slice, args.n)
+        rows = make_rows_gpu(torch, 0, n_slice, device).cpu().numpy()
+        qps, cb = cpu_reference_qps(rows, args.n, queries[:args.cpu_queries], args.k, steps=args.steps,
+                                    warmup=min(warmup, 1))
+        line = {"metric": METRIC, "value": qps, "unit": "queries/sec", "n_gpus": n_gpus, "steps": args.steps,
+                "warmup": warmup, "ms_per_step": cb["seconds_per_step"] * 1e3, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                "impl": "reference", "cpu_baseline": cb,
+                "e2e": {"value": qps, "unit": "queries/sec", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    L = load_lib()
+    check(L, L.mdh_set_scan_path(args.scan_path), "set_scan_path")
+    start, end = args.n * rank // world, args.n * (rank + 1) // world
+    rows = make_rows_gpu(torch, start, end, device)
+    torch.cuda.synchronize()
+    h = ctypes.c_void_p()
+    t0 = time.time()
+    check(L, L.mdh_index_create_u8_device(ctypes.c_void_p(rows.data_ptr()), end - start, DIM, 1, start,
+                                          ctypes.byref(h)), "index build")
+    build_s = time.time() - t0
+    del rows
+    torch.cuda.empty_cache()
+
+    nq, k = args.nq, args.k
+    dq = torch.from_numpy(queries).to(device)
+    ids = torch.empty((nq, k), dtype=torch.int32, device=device)
+    dd = torch.empty((nq, k), dtype=torch.int32, device=device)
+    all_i = torch.empty((world, nq, k), dtype=torch.int32, device=device)
+    all_d = torch.empty((world, nq, k), dtype=torch.int32, device=device)
+    out_i = torch.empty((nq, k), dtype=torch.int32, device=device)
+    out_d = torch.empty((nq, k), dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream(device)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    st = Stats()
+    scan_ms, scan_pairs = [], []
+
+    def step(record):
+        check(L, L.mdh_search_u8_device(h, ctypes.c_void_p(dq.data_ptr()), nq, k, ctypes.c_void_p(ids.data_ptr()),
+                                        ctypes.c_void_p(dd.data_ptr()), sp, ctypes.byref(st)), "search")
+        if record:
+            scan_ms.append(st.full_scan_ms)
+            scan_pairs.append(st.full_scan_pairs)
+        if world > 1:
+            dist.all_gather_into_tensor(all_i.view(-1), ids.view(-1))
+            dist.all_gather_into_tensor(all_d.view(-1), dd.view(-1))
+            check(L, L.mdh_merge_topk_device(ctypes.c_void_p(all_d.data_ptr()), ctypes.c_void_p(all_i.data_ptr()),
+                                             world, nq, k, ctypes.c_void_p(out_d.data_ptr()),
+                                             ctypes.c_void_p(out_i.data_ptr()), sp), "merge")
+
+    for _ in range(warmup):
+        step(False)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step(True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    elapsed = e0.elapsed_time(e1) / 1e3
+    if dist is not None:
+        t = torch.tensor([elapsed], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+        dist.barrier()
+    tensor_path = bool(st.tensor_core_path)
+    levels = int(st.levels)
+
+    # End to end through the C ABI with host buffers (pinned queries in, ids out).
+    hq = torch.from_numpy(queries).pin_memory()
+    hid = torch.empty((nq, k), dtype=torch.int32).pin_memory()
+    hdist = torch.empty((nq, k), dtype=torch.int32).pin_memory()
+    e2e_steps = max(1, min(args.steps, 3))
+
+    def e2e_step():
+        check(L, L.mdh_search_u8(h, ctypes.c_void_p(hq.data_ptr()), nq, k, ctypes.c_void_p(hid.data_ptr()),
+                                 ctypes.c_void_p(hdist.data_ptr()), None), "e2e search")
+        if world > 1:
+            ids.copy_(hid, non_blocking=True)
+            dd.copy_(hdist, non_blocking=True)
+            dist.all_gather_into_tensor(all_i.view(-1), ids.view(-1))
+            dist.all_gather_into_tensor(all_d.view(-1), dd.view(-1))
+            check(L, L.mdh_merge_topk_device(ctypes.c_void_p(all_d.data_ptr()), ctypes.c_void_p(all_i.data_ptr()),
+                                             world, nq, k, ctypes.c_void_p(out_d.data_ptr()),
+                                             ctypes.c_void_p(out_i.data_ptr()), sp), "merge")
+            hid.copy_(out_i)
+            hdist.copy_(out_d)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_t = time.perf_counter() - t0
+    if dist is not None:
+        t = torch.tensor([e2e_t], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_t = float(t.item())
+
+    peaks, peak_src = measured_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    ms_scan = statistics.median(scan_ms) if scan_ms else float("nan")
+    pairs = scan_pairs[0] if scan_pairs else 0
+    achieved = 2.0 * pairs * DIM / (ms_scan / 1e3) / 1e12 if ms_scan > 0 else None
+    launches = 2 + 2 * levels + (1 if world > 1 else 0)
+    line = {
+        "metric": METRIC,
+        "value": nq * args.steps / elapsed,
+        "unit": "queries/sec",
+        "n_gpus": n_gpus,
+        "steps": args.steps,
+        "warmup": warmup,
+        "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "u8",
+        "data": "synthetic",
+        "config": dict(config, scan=("tcgen05 tensor cores" if tensor_path else "CUDA cores (dp4a)"),
+                       levels=levels, index_build_s=round(build_s, 2)),
+        "e2e": {"value": nq * e2e_steps / e2e_t, "unit": "queries/sec", "h2d_bytes_per_step": int(nq * DIM),
+                "d2h_bytes_per_step": int(nq * k * 8)},
+        "gpu_launches": launches * args.steps,
+        "clocks": clocks,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",
+                     "frac": (achieved / int8_peak) if achieved else None, "traffic": None,
+                     "kernel": "full-corpus u8 L2 scan (filter) kernel",
+                     "algorithmic": "2*N*Q*D int8 ops per launch",
+                     "peak_source": f"2 x {peak_src} bf16 dense ({peaks['bf16_tflops']} TF/s): u8 MMA runs at twice "
+                                    "the bf16 rate on sm_100",
+                     "kernel_ms": ms_scan},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            n_slice = min(args.cpu_slice, args.n)
+            rows = make_rows_gpu(torch, 0, n_slice, device).cpu().numpy()
+            _, cb = cpu_reference_qps(rows, args.n, queries[:args.cpu_queries], k, steps=1, warmup=0)
+            line["cpu_baseline"] = cb
+        except Exception as exc:  # the baseline must not hide the GPU number
+            line["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
+    check(L, L.mdh_index_destroy(h), "destroy")
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,165 @@
+/*
+ * winnex_madhava_b200.h -- C ABI of the B200 exact top-K scan library
+ * (libwinnex_madhava_b200.so).
+ *
+ * Plain C: pointers, sizes and status codes only.  Every entry point returns
+ * an mdh_status; on failure mdh_last_error() holds a message for the calling
+ * thread.  There is no CPU fallback: without a usable sm_100 GPU every search
+ * entry point fails with MDH_ERR_CUDA.
+ *
+ * Each declaration names the reference interface it replaces
+ * (winnex-madhava, paths relative to that project).
+ *
+ * Result convention (all searches): out_ids[q*k + j], j < min(k, n), is the
+ * j-th best corpus row for query q; rows past min(k, n) are -1.  L2 results
+ * ascend by (squared distance, row id): the lower id wins a tie, as in
+ * MadhavaL2::search_exact's pair<float,int> partial_sort
+ * (src/winnex_madhava.cpp:1237-1239).  Score results (cosine / inner product)
+ * descend by score with the same lower-id tie break.
+ */
+#ifndef WINNEX_MADHAVA_B200_H
+#define WINNEX_MADHAVA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    MDH_OK = 0,
+    MDH_ERR_INVALID_ARG = 1,   /* bad pointer / size / shape */
+    MDH_ERR_CUDA = 2,          /* CUDA runtime error, or no usable GPU */
+    MDH_ERR_NCCL = 3,          /* collective failure (multi-device merge) */
+    MDH_ERR_OOM = 4,           /* device allocation failed */
+    MDH_ERR_TIMEOUT = 5,       /* a bounded device-side wait expired */
+    MDH_ERR_NOT_INTEGRAL = 6,  /* an integer-only entry point got non-integral data */
+    MDH_ERR_UNSUPPORTED = 7,   /* valid request outside what this build implements */
+    MDH_ERR_INTERNAL = 8
+} mdh_status;
+
+/* Metric values match the reference enum (include/winnex_madhava/winnex_madhava.hpp:38-41). */
+typedef enum { MDH_METRIC_COSINE = 0, MDH_METRIC_L2 = 1 } mdh_metric;
+
+/* Score semantics of a float query -- which reference formula the float
+ * arithmetic reproduces when the query is not a u8 vector.
+ *   MDH_SCORE_EXACT: MadhavaL2::exact_score (src/winnex_madhava.cpp:710-763):
+ *                    L2 = l2_sq_avx, cosine = dot / sqrt(|v|^2 |q|^2).
+ *   MDH_SCORE_SPEED: SpeedEngine::search (src/speed_cpu.cpp:271-353): score =
+ *                    2*dot_f32 - |v|^2 (L2) or dot of normalized vectors.
+ *   MDH_SCORE_SPEED_BATCH: SpeedEngine::search_batch (src/speed_cpu.cpp:356-398),
+ *                    identical except the cosine query-normalization guard
+ *                    (|q|^2 > 1e-12 instead of |q| > 1e-12). */
+typedef enum { MDH_SCORE_EXACT = 0, MDH_SCORE_SPEED = 1, MDH_SCORE_SPEED_BATCH = 2 } mdh_score_mode;
+
+typedef struct mdh_index mdh_index;
+
+/* Per-call statistics; maps onto SearchResult / SpeedResult fields
+ * (include/winnex_madhava/winnex_madhava.hpp:118-164, speed_engine.hpp:36-41). */
+typedef struct {
+    double latency_ms;            /* host wall time of the call (SearchResult::latency_ms) */
+    int64_t pairs_scored;         /* (query, row) pairs evaluated (bound_pairs / exact_evals) */
+    int64_t pairs_pruned_by_bound;/* pairs skipped by the norm lower bound */
+    int64_t bound_violations;     /* pruned pairs that belonged in the top-K: measured, must be 0 */
+    int64_t candidates;           /* pairs that passed the threshold filter into the final selection */
+    int32_t tensor_core_path;     /* 1 when the tcgen05 tensor-core scan ran */
+    int32_t levels;               /* threshold-refinement levels run */
+    double full_scan_ms;          /* CUDA-event time of the full-corpus scan kernel(s) on their stream */
+    int64_t full_scan_pairs;      /* (query, row) pairs that kernel scored */
+} mdh_stats;
+
+/* Build an index over a row-major u8 corpus [n][dim] held in host memory.
+ * The library copies the corpus into device memory (norm-sorted rows, integer
+ * |v|^2, row ids) and does not keep the host pointer.
+ * devices/ndev: GPUs to shard rows over (contiguous id ranges); NULL/0 = the
+ * current device.  id_offset is added to every returned row id (a rank that
+ * holds rows [off, off+n) of a larger corpus passes off).
+ * Replaces SpeedEngine::SpeedEngine(const uint8_t*, ...) (src/speed_cpu.cpp:117-144)
+ * and MadhavaL2::build (src/winnex_madhava.cpp:487), bound via
+ * bindings/py_module.cpp:98-107 and :303-313. */
+mdh_status mdh_index_create_u8(const uint8_t* host_corpus, int64_t n, int32_t dim, int32_t metric,
+                               const int32_t* devices, int32_t ndev, int64_t id_offset,
+                               mdh_index** out);
+
+/* Build from a row-major float32 corpus [n][dim].  Replaces
+ * SpeedEngine::SpeedEngine(const float*, ...) (src/speed_cpu.cpp:81-115):
+ * cosine rows are normalized with the reference's arithmetic. */
+mdh_status mdh_index_create_f32(const float* host_corpus, int64_t n, int32_t dim, int32_t metric,
+                                const int32_t* devices, int32_t ndev, int64_t id_offset,
+                                mdh_index** out);
+
+/* Build a single-device index from a u8 corpus [n][dim] already in device
+ * memory on the current device (e.g. a tensor produced on the GPU).  Same
+ * layout and semantics as mdh_index_create_u8; the device buffer is copied
+ * and may be freed afterwards.  No counterpart in the reference (its corpus
+ * always starts on the host). */
+mdh_status mdh_index_create_u8_device(const uint8_t* dev_corpus, int64_t n, int32_t dim, int32_t metric,
+                                      int64_t id_offset, mdh_index** out);
+
+mdh_status mdh_index_destroy(mdh_index* index);
+
+/* Shape of an index. */
+mdh_status mdh_index_info(const mdh_index* index, int64_t* n, int32_t* dim, int32_t* metric,
+                          int32_t* ndev);
+
+/* Search with float32 host queries [nq][dim]; results to host buffers.
+ * A query whose values are all integers in [0,255] runs the integer u8 path
+ * (exact for every mode); other queries run float arithmetic that reproduces
+ * the reference formula selected by `mode`.
+ * out_dist (may be NULL) receives the value the ranking used: the squared L2
+ * distance (MDH_SCORE_EXACT, L2), the cosine score (cosine metrics), or the
+ * SpeedEngine score 2*dot - |v|^2 (MDH_SCORE_SPEED* on float arithmetic).
+ * Replaces MadhavaL2::search_exact / search / search_batch
+ * (src/winnex_madhava.cpp:1219-1246, :766, :1094; py_module.cpp:136-151, :219-226)
+ * and SpeedEngine::search / search_batch (src/speed_cpu.cpp:425-449;
+ * py_module.cpp:314-335). */
+mdh_status mdh_search_f32(mdh_index* index, const float* host_queries, int32_t nq, int32_t k,
+                          int32_t mode, int32_t* out_ids, float* out_dist, mdh_stats* stats);
+
+/* Search with u8 host queries [nq][dim] (the integer path only).
+ * out_dist: exact squared L2 distance (int32) for L2; NULL allowed. */
+mdh_status mdh_search_u8(mdh_index* index, const uint8_t* host_queries, int32_t nq, int32_t k,
+                         int32_t* out_ids, int32_t* out_dist, mdh_stats* stats);
+
+/* Device-resident variant of mdh_search_u8 for a single-device index:
+ * queries, ids and distances are device pointers on the index's device;
+ * work is enqueued on `stream` (a cudaStream_t, NULL = the index's stream)
+ * and the call returns after the results are written (stream synchronized).
+ * No counterpart in the reference (its GPU path always copies from the host,
+ * src/speed_gpu.cu:194-227); used for HBM-resident throughput measurement. */
+mdh_status mdh_search_u8_device(mdh_index* index, const uint8_t* dev_queries, int32_t nq, int32_t k,
+                                int32_t* dev_ids, int32_t* dev_dist, void* stream, mdh_stats* stats);
+
+/* Merge per-shard top-k lists (device pointers on the current device):
+ * dist_all/ids_all are [nshard][nq][k] (int32 squared distance, int32 row id,
+ * id -1 = empty), the output [nq][k] keeps the k smallest (dist, id).
+ * The exchange step of the row-sharded multi-GPU scan. */
+mdh_status mdh_merge_topk_device(const int32_t* dev_dist_all, const int32_t* dev_ids_all, int32_t nshard,
+                                 int32_t nq, int32_t k, int32_t* dev_dist_out, int32_t* dev_ids_out,
+                                 void* stream);
+
+/* Options (process-wide): force the scan path for testing and measurement.
+ * path: 0 = automatic, 1 = CUDA-core scan only, 2 = tensor-core scan
+ * whenever the shape allows. */
+mdh_status mdh_set_scan_path(int32_t path);
+
+/* Options (process-wide): upper bound on a query's candidate list length
+ * (a power of two in [64, 16384]; 0 = automatic).  A list that overflows is
+ * rerun with a strictly tighter threshold, so results stay exact; small
+ * limits trade speed for scratch memory and exercise that rerun path. */
+mdh_status mdh_set_candidate_cap_limit(int32_t cap);
+
+/* Number of CUDA devices visible (0 when none). */
+int32_t mdh_device_count(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* mdh_last_error(void);
+
+/* Library version string. */
+const char* mdh_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WINNEX_MADHAVA_B200_H */

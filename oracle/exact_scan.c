@@ -1,0 +1,362 @@
+/*
+ * Oracle for the exact top-K scan -- TEST INFRASTRUCTURE ONLY.
+ *
+ * This file is a plain-C restatement of the reference's CPU exact-scan
+ * arithmetic (winnex-madhava, src/winnex_madhava.cpp and src/speed_cpu.cpp).
+ * It exists so the test suite, the smoke check and the bench's cpu_baseline
+ * leg have an independent checker.  Nothing in the product links it or calls
+ * it: the CUDA library in winnex-madhava_b200/ never falls back to this code.
+ *
+ * Every function below names the reference lines it restates.  The float
+ * arithmetic follows the reference's evaluation order exactly (8 FMA lanes,
+ * then a left-to-right lane sum), so for float queries the oracle's distances
+ * are bit-identical to the reference built with -O3 -mavx2 -mfma.  For u8
+ * corpora with integral queries every intermediate value is an integer below
+ * 2^24, so the result is exact and independent of evaluation order.
+ *
+ * Ranking rules:
+ *   L2 (MadhavaL2::search_exact):   ascending (distance, index) -- the
+ *       reference sorts std::pair<float,int>, so ties go to the lower index
+ *       (src/winnex_madhava.cpp:1237-1239).
+ *   score metrics (SpeedEngine, cosine): descending score; the reference's
+ *       comparator looks at the score only, leaving tie order unspecified
+ *       (src/speed_cpu.cpp:346-347).  The oracle breaks those ties by the
+ *       lower index, which is one of the orders the reference may produce.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* Distance / score kernels (one corpus row against one float query).        */
+/* ------------------------------------------------------------------------ */
+
+/* l2_sq_avx, src/winnex_madhava.cpp:119-146: 16 bytes per step, split into a
+ * low and a high group of 8; lane l accumulates fma(d[j+l]^2) then
+ * fma(d[j+8+l]^2); the 8 lanes are summed left to right; scalar tail. */
+float oracle_l2_sq_u8(const uint8_t* v, const float* q, int d) {
+    float lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int j = 0;
+    for (; j + 16 <= d; j += 16) {
+        for (int l = 0; l < 8; l++) {
+            float dl = (float)v[j + l] - q[j + l];
+            lane[l] = fmaf(dl, dl, lane[l]);
+        }
+        for (int l = 0; l < 8; l++) {
+            float dh = (float)v[j + 8 + l] - q[j + 8 + l];
+            lane[l] = fmaf(dh, dh, lane[l]);
+        }
+    }
+    float r = lane[0] + lane[1] + lane[2] + lane[3] + lane[4] + lane[5] + lane[6] + lane[7];
+    for (; j < d; j++) {
+        float dd = (float)v[j] - q[j];
+        r = fmaf(dd, dd, r); /* g++ contracts `r += dd*dd` under -mfma */
+    }
+    return r;
+}
+
+/* dot_f32, src/speed_cpu.cpp:60-76: 8 FMA lanes over steps of 8, lanes summed
+ * left to right, scalar tail. */
+float oracle_dot_f32(const float* a, const float* b, int d) {
+    float lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int i = 0;
+    for (; i + 8 <= d; i += 8)
+        for (int l = 0; l < 8; l++) lane[l] = fmaf(a[i + l], b[i + l], lane[l]);
+    float r = lane[0] + lane[1] + lane[2] + lane[3] + lane[4] + lane[5] + lane[6] + lane[7];
+    for (; i < d; i++) r = fmaf(a[i], b[i], r);
+    return r;
+}
+
+/* exact_score cosine over a u8 row, src/winnex_madhava.cpp:714-763 (the
+ * base_ branch, taken whenever corpus_f32_ is null or quant != None).  dot
+ * and |v|^2 use the same 16-byte lane split as l2_sq_avx; |q|^2 is a scalar
+ * loop; score = dot / sqrt(|v|^2 * |q|^2), or 0 when that is <= 1e-10. */
+float oracle_cosine_u8(const uint8_t* v, const float* q, int d, float qn2) {
+    float sd[8] = {0, 0, 0, 0, 0, 0, 0, 0}, sv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int j = 0;
+    for (; j + 16 <= d; j += 16) {
+        for (int l = 0; l < 8; l++) {
+            float f = (float)v[j + l];
+            sd[l] = fmaf(f, q[j + l], sd[l]);
+        }
+        for (int l = 0; l < 8; l++) {
+            float f = (float)v[j + 8 + l];
+            sd[l] = fmaf(f, q[j + 8 + l], sd[l]);
+        }
+        for (int l = 0; l < 8; l++) {
+            float f = (float)v[j + l];
+            sv[l] = fmaf(f, f, sv[l]);
+        }
+        for (int l = 0; l < 8; l++) {
+            float f = (float)v[j + 8 + l];
+            sv[l] = fmaf(f, f, sv[l]);
+        }
+    }
+    float dot = 0.0f, vn2 = 0.0f;
+    for (int l = 0; l < 8; l++) { dot += sd[l]; vn2 += sv[l]; }
+    for (; j < d; j++) {
+        float f = (float)v[j];
+        dot = fmaf(f, q[j], dot);
+        vn2 = fmaf(f, f, vn2);
+    }
+    float denom = sqrtf(vn2 * qn2);
+    return denom > 1e-10f ? dot / denom : 0.0f;
+}
+
+/* |q|^2 scalar loop used by the cosine score (src/winnex_madhava.cpp:759). */
+float oracle_qn2(const float* q, int d) {
+    float s = 0.0f;
+    for (int j = 0; j < d; j++) s = fmaf(q[j], q[j], s);
+    return s;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Top-k selection helpers.                                                  */
+/* ------------------------------------------------------------------------ */
+
+typedef struct { float key; int32_t id; } kv_t;
+
+/* "a ranks before b": ascending key, then ascending id. */
+static int kv_before_asc(kv_t a, kv_t b) {
+    return a.key < b.key || (a.key == b.key && a.id < b.id);
+}
+
+/* Bounded max-heap keeping the k best (smallest under kv_before_asc). */
+static void heap_push_asc(kv_t* h, int* size, int k, kv_t x) {
+    if (*size < k) {
+        int i = (*size)++;
+        h[i] = x;
+        while (i > 0) {
+            int p = (i - 1) / 2;
+            if (kv_before_asc(h[p], h[i])) { kv_t t = h[p]; h[p] = h[i]; h[i] = t; i = p; }
+            else break;
+        }
+        return;
+    }
+    if (!kv_before_asc(x, h[0])) return;
+    h[0] = x;
+    int i = 0;
+    for (;;) {
+        int l = 2 * i + 1, r = l + 1, m = i;
+        if (l < k && kv_before_asc(h[m], h[l])) m = l;
+        if (r < k && kv_before_asc(h[m], h[r])) m = r;
+        if (m == i) break;
+        kv_t t = h[m]; h[m] = h[i]; h[i] = t; i = m;
+    }
+}
+
+static int cmp_kv_asc(const void* pa, const void* pb) {
+    kv_t a = *(const kv_t*)pa, b = *(const kv_t*)pb;
+    if (kv_before_asc(a, b)) return -1;
+    if (kv_before_asc(b, a)) return 1;
+    return 0;
+}
+
+/* Select the k best of `keys` (n entries, id = position) in ascending
+ * (key, id) order.  Returns the number written (min(k, n)). */
+static int select_topk_asc(const float* keys, int64_t n, int k, int32_t* out_ids, float* out_keys) {
+    if (k > n) k = (int)n;
+    if (k <= 0) return 0;
+    kv_t* h = (kv_t*)malloc(sizeof(kv_t) * (size_t)k);
+    int size = 0;
+    for (int64_t i = 0; i < n; i++) {
+        kv_t x = {keys[i], (int32_t)i};
+        heap_push_asc(h, &size, k, x);
+    }
+    qsort(h, (size_t)size, sizeof(kv_t), cmp_kv_asc);
+    for (int i = 0; i < size; i++) {
+        out_ids[i] = h[i].id;
+        if (out_keys) out_keys[i] = h[i].key;
+    }
+    free(h);
+    return size;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Public oracle entry points (one call = nq queries).                       */
+/* ------------------------------------------------------------------------ */
+
+/* MadhavaL2::search_exact with Metric::L2 on a u8 corpus
+ * (src/winnex_madhava.cpp:1224-1246).  out_ids/out_dist: [nq][k]; entries
+ * beyond min(k, n) are set to -1 / INFINITY. */
+void oracle_l2_exact_u8(const uint8_t* corpus, int64_t n, int d, const float* queries, int nq,
+                        int k, int32_t* out_ids, float* out_dist) {
+    float* dist = (float*)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1));
+    for (int qi = 0; qi < nq; qi++) {
+        const float* q = queries + (size_t)qi * d;
+#pragma omp parallel for schedule(static)
+        for (int64_t i = 0; i < n; i++) dist[i] = oracle_l2_sq_u8(corpus + (size_t)i * d, q, d);
+        int m = select_topk_asc(dist, n, k, out_ids + (size_t)qi * k, out_dist + (size_t)qi * k);
+        for (int j = m; j < k; j++) { out_ids[(size_t)qi * k + j] = -1; out_dist[(size_t)qi * k + j] = INFINITY; }
+    }
+    free(dist);
+}
+
+/* SpeedEngine exact scan (no anchors), src/speed_cpu.cpp:271-398.
+ * corpus_f32 is the engine's internal float corpus (u8 cast to float, or the
+ * row-normalized float corpus for cosine).  norms are |v|^2 (L2) and are
+ * ignored for cosine.  Score = ip (cosine) or 2*ip - |v|^2 (L2); the query is
+ * normalized for cosine (src/speed_cpu.cpp:278-287).  Output is descending
+ * score, ties to the lower index; out_score is that score. */
+void oracle_speed_exact(const float* corpus_f32, const float* norms, int64_t n, int d, int is_cosine,
+                        const float* queries, int nq, int k, int32_t* out_ids, float* out_score) {
+    float* neg = (float*)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1));
+    float* qbuf = (float*)malloc(sizeof(float) * (size_t)d);
+    for (int qi = 0; qi < nq; qi++) {
+        const float* q = queries + (size_t)qi * d;
+        if (is_cosine) {
+            float qn = 0.0f;
+            for (int j = 0; j < d; j++) qn = fmaf(q[j], q[j], qn);
+            qn = sqrtf(qn);
+            float inv = qn > 1e-12f ? 1.0f / qn : 0.0f;
+            for (int j = 0; j < d; j++) qbuf[j] = q[j] * inv;
+            q = qbuf;
+        }
+#pragma omp parallel for schedule(static)
+        for (int64_t i = 0; i < n; i++) {
+            float ip = oracle_dot_f32(corpus_f32 + (size_t)i * d, q, d);
+            float s = is_cosine ? ip : (float)(2.0 * (double)ip - (double)norms[i]);
+            neg[i] = -s;
+        }
+        int m = select_topk_asc(neg, n, k, out_ids + (size_t)qi * k, out_score + (size_t)qi * k);
+        for (int j = 0; j < m; j++) out_score[(size_t)qi * k + j] = -out_score[(size_t)qi * k + j];
+        for (int j = m; j < k; j++) { out_ids[(size_t)qi * k + j] = -1; out_score[(size_t)qi * k + j] = -INFINITY; }
+    }
+    free(neg);
+    free(qbuf);
+}
+
+/* SpeedEngine u8 constructor's float copy and norms, src/speed_cpu.cpp:117-140:
+ * dst = (float)v; norm accumulates dst*dst left to right; cosine rows are
+ * scaled by 1/sqrt(norm) and get norm 1; L2 rows keep norm = |v|^2. */
+void oracle_speed_prepare_u8(const uint8_t* corpus, int64_t n, int d, int is_cosine, float* out_f32,
+                             float* out_norms) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; i++) {
+        const uint8_t* v = corpus + (size_t)i * d;
+        float* dst = out_f32 + (size_t)i * d;
+        float norm = 0.0f;
+        for (int j = 0; j < d; j++) { dst[j] = (float)v[j]; norm = fmaf(dst[j], dst[j], norm); }
+        if (is_cosine) {
+            norm = sqrtf(norm);
+            if (norm > 1e-12f) {
+                float inv = 1.0f / norm;
+                for (int j = 0; j < d; j++) dst[j] *= inv;
+            }
+            out_norms[i] = 1.0f;
+        } else {
+            out_norms[i] = norm;
+        }
+    }
+}
+
+/* SpeedEngine float constructor, src/speed_cpu.cpp:81-115. */
+void oracle_speed_prepare_f32(const float* corpus, int64_t n, int d, int is_cosine, float* out_f32,
+                              float* out_norms) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; i++) {
+        const float* v = corpus + (size_t)i * d;
+        float* dst = out_f32 + (size_t)i * d;
+        float norm = 0.0f;
+        if (is_cosine) {
+            for (int j = 0; j < d; j++) { dst[j] = v[j]; norm = fmaf(v[j], v[j], norm); }
+            norm = sqrtf(norm);
+            if (norm > 1e-12f) {
+                float inv = 1.0f / norm;
+                for (int j = 0; j < d; j++) dst[j] *= inv;
+            }
+            out_norms[i] = 1.0f;
+        } else {
+            for (int j = 0; j < d; j++) { dst[j] = v[j]; norm = fmaf(dst[j], dst[j], norm); }
+            out_norms[i] = norm;
+        }
+    }
+}
+
+/* MadhavaL2::search_exact with Metric::Cosine on a u8 base
+ * (src/winnex_madhava.cpp:1224-1246 with exact_score :714-763).  Descending
+ * score, ties to the lower index. */
+void oracle_cosine_exact_u8(const uint8_t* corpus, int64_t n, int d, const float* queries, int nq, int k,
+                            int32_t* out_ids, float* out_score) {
+    float* neg = (float*)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1));
+    for (int qi = 0; qi < nq; qi++) {
+        const float* q = queries + (size_t)qi * d;
+        float qn2 = oracle_qn2(q, d);
+#pragma omp parallel for schedule(static)
+        for (int64_t i = 0; i < n; i++) neg[i] = -oracle_cosine_u8(corpus + (size_t)i * d, q, d, qn2);
+        int m = select_topk_asc(neg, n, k, out_ids + (size_t)qi * k, out_score + (size_t)qi * k);
+        for (int j = 0; j < m; j++) out_score[(size_t)qi * k + j] = -out_score[(size_t)qi * k + j];
+        for (int j = m; j < k; j++) { out_ids[(size_t)qi * k + j] = -1; out_score[(size_t)qi * k + j] = -INFINITY; }
+    }
+    free(neg);
+}
+
+/* Integer exact L2 for u8 queries: int64 distances, ascending (dist, index).
+ * Same ranking as oracle_l2_exact_u8 for integral queries, without float. */
+void oracle_l2_exact_u8_int(const uint8_t* corpus, int64_t n, int d, const uint8_t* queries, int nq, int k,
+                            int32_t* out_ids, int64_t* out_dist) {
+    float* key = (float*)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1));
+    int64_t* dist = (int64_t*)malloc(sizeof(int64_t) * (size_t)(n > 0 ? n : 1));
+    for (int qi = 0; qi < nq; qi++) {
+        const uint8_t* q = queries + (size_t)qi * d;
+#pragma omp parallel for schedule(static)
+        for (int64_t i = 0; i < n; i++) {
+            const uint8_t* v = corpus + (size_t)i * d;
+            int64_t s = 0;
+            for (int j = 0; j < d; j++) { int64_t t = (int64_t)v[j] - (int64_t)q[j]; s += t * t; }
+            dist[i] = s;
+            key[i] = (float)s; /* exact: s < 2^24 for d <= 258 */
+        }
+        int32_t* ids = out_ids + (size_t)qi * k;
+        int m = select_topk_asc(key, n, k, ids, NULL);
+        for (int j = 0; j < m; j++) out_dist[(size_t)qi * k + j] = dist[ids[j]];
+        for (int j = m; j < k; j++) { ids[j] = -1; out_dist[(size_t)qi * k + j] = -1; }
+    }
+    free(key);
+    free(dist);
+}
+
+/* Score given row ids of one query with the reference arithmetic.
+ * kind 0: l2_sq_avx over u8 rows (MadhavaL2 L2);
+ * kind 1: exact_score cosine over u8 rows (MadhavaL2 cosine);
+ * kind 2: SpeedEngine score over the prepared float rows (cosine: the query
+ *         is normalized as in src/speed_cpu.cpp:278-287; L2: 2*ip - |v|^2).
+ * Ids < 0 score NAN. */
+void oracle_score_ids(int kind, int is_cosine, const uint8_t* corpus_u8, const float* corpus_f32,
+                      const float* norms, int d, const float* q, const int32_t* ids, int m, float* out) {
+    float* qbuf = (float*)malloc(sizeof(float) * (size_t)d);
+    const float* qq = q;
+    if (kind == 2 && is_cosine) {
+        float qn = 0.0f;
+        for (int j = 0; j < d; j++) qn = fmaf(q[j], q[j], qn);
+        qn = sqrtf(qn);
+        float inv = qn > 1e-12f ? 1.0f / qn : 0.0f;
+        for (int j = 0; j < d; j++) qbuf[j] = q[j] * inv;
+        qq = qbuf;
+    }
+    float qn2 = oracle_qn2(q, d);
+    for (int i = 0; i < m; i++) {
+        int64_t r = ids[i];
+        if (r < 0) { out[i] = NAN; continue; }
+        if (kind == 0) out[i] = oracle_l2_sq_u8(corpus_u8 + (size_t)r * d, q, d);
+        else if (kind == 1) out[i] = oracle_cosine_u8(corpus_u8 + (size_t)r * d, q, d, qn2);
+        else {
+            float ip = oracle_dot_f32(corpus_f32 + (size_t)r * d, qq, d);
+            out[i] = is_cosine ? ip : (float)(2.0 * (double)ip - (double)norms[r]);
+        }
+    }
+    free(qbuf);
+}
+
+int oracle_num_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}

@@ -1,0 +1,72 @@
+"""Shared test helpers (fixture loading, ctypes access to the C ABI)."""
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+import re
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+PKG = os.path.join(ROOT, "winnex-madhava_b200", "winnex_madhava")
+LIB = os.path.join(PKG, "libwinnex_madhava_b200.so")
+HEADER = os.path.join(ROOT, "include", "winnex_madhava_b200.h")
+
+
+def load_fixture(name):
+    z = np.load(os.path.join(GOLDEN, name + ".npz"))
+    meta = json.loads(str(z["meta"]))
+    return meta, {k: z[k] for k in z.files if k != "meta"}
+
+
+def header_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(mdh_[a-z0-9_]+)\s*\(", src)))
+
+
+class Stats(ctypes.Structure):
+    _fields_ = [("latency_ms", ctypes.c_double), ("pairs_scored", ctypes.c_int64),
+                ("pairs_pruned_by_bound", ctypes.c_int64), ("bound_violations", ctypes.c_int64),
+                ("candidates", ctypes.c_int64), ("tensor_core_path", ctypes.c_int32), ("levels", ctypes.c_int32),
+                ("full_scan_ms", ctypes.c_double), ("full_scan_pairs", ctypes.c_int64)]
+
+
+def capi():
+    L = ctypes.CDLL(LIB)
+    P, i32, i64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+    L.mdh_index_create_u8.argtypes = [P, i64, i32, i32, P, i32, i64, ctypes.POINTER(P)]
+    L.mdh_index_create_f32.argtypes = [P, i64, i32, i32, P, i32, i64, ctypes.POINTER(P)]
+    L.mdh_index_create_u8_device.argtypes = [P, i64, i32, i32, i64, ctypes.POINTER(P)]
+    L.mdh_index_destroy.argtypes = [P]
+    L.mdh_index_info.argtypes = [P, P, P, P, P]
+    L.mdh_search_f32.argtypes = [P, P, i32, i32, i32, P, P, ctypes.POINTER(Stats)]
+    L.mdh_search_u8.argtypes = [P, P, i32, i32, P, P, ctypes.POINTER(Stats)]
+    L.mdh_search_u8_device.argtypes = [P, P, i32, i32, P, P, P, ctypes.POINTER(Stats)]
+    L.mdh_merge_topk_device.argtypes = [P, P, i32, i32, i32, P, P, P]
+    L.mdh_set_scan_path.argtypes = [i32]
+    L.mdh_set_candidate_cap_limit.argtypes = [i32]
+    L.mdh_last_error.restype = ctypes.c_char_p
+    L.mdh_version.restype = ctypes.c_char_p
+    L.mdh_device_count.restype = i32
+    for fn in ("mdh_index_create_u8", "mdh_index_create_u8_device", "mdh_index_create_f32", "mdh_index_destroy", "mdh_index_info", "mdh_search_f32",
+               "mdh_search_u8", "mdh_search_u8_device", "mdh_merge_topk_device", "mdh_set_scan_path",
+               "mdh_set_candidate_cap_limit"):
+        getattr(L, fn).restype = ctypes.c_int
+    return L
+
+
+def ptr(a):
+    return ctypes.c_void_p(a.ctypes.data) if a is not None else None
+
+
+def sorted_by_key(ids, key, asc=True):
+    """Re-sort ids per query by (key, id) -- the canonical tie order."""
+    out = np.empty_like(ids)
+    for i in range(ids.shape[0]):
+        kk = key[i] if asc else -key[i]
+        o = np.lexsort((ids[i], kk))
+        out[i] = ids[i][o]
+    return out

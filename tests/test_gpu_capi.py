@@ -1,0 +1,114 @@
+"""GPU tests through the C ABI: distances, device-resident search, shard merge."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import cases
+import oracle
+from helpers import Stats, capi, ptr
+
+pytestmark = pytest.mark.gpu
+
+
+def _create_u8(L, C, metric=1, id_offset=0, devices=None):
+    h = ctypes.c_void_p()
+    dev = None
+    nd = 0
+    if devices:
+        dev = np.asarray(devices, np.int32)
+        nd = len(devices)
+    st = L.mdh_index_create_u8(ptr(np.ascontiguousarray(C)), C.shape[0], C.shape[1], metric, ptr(dev), nd, id_offset,
+                               ctypes.byref(h))
+    assert st == 0, L.mdh_last_error()
+    return h
+
+
+def _search_u8(L, h, Q, k):
+    nq = len(Q)
+    ids = np.empty((nq, k), np.int32)
+    dist = np.empty((nq, k), np.int32)
+    s = Stats()
+    st = L.mdh_search_u8(h, ptr(np.ascontiguousarray(Q)), nq, k, ptr(ids), ptr(dist), ctypes.byref(s))
+    assert st == 0, L.mdh_last_error()
+    return ids, dist, s
+
+
+@pytest.mark.parametrize("path", [1, 0])
+def test_search_u8_distances_exact(path):
+    L = capi()
+    L.mdh_set_scan_path(path)
+    try:
+        C = cases.gmm_u8(300_000, 128, 256, seed=21)
+        Q = cases.gmm_u8_queries(300, 128, 256, seed_means=21, seed_q=22)
+        h = _create_u8(L, C)
+        ids, dist, s = _search_u8(L, h, Q, 10)
+        want_ids, want_d = oracle.l2_exact_u8_int(C, Q, 10)
+        np.testing.assert_array_equal(ids, want_ids)
+        np.testing.assert_array_equal(dist, want_d)
+        assert s.bound_violations == 0 and s.pairs_scored >= C.shape[0] * len(Q)
+        assert L.mdh_index_destroy(h) == 0
+    finally:
+        L.mdh_set_scan_path(0)
+
+
+def test_device_api_and_merge():
+    torch = pytest.importorskip("torch")
+    L = capi()
+    C = cases.gmm_u8(120_000, 128, 64, seed=31)
+    Q = cases.gmm_u8_queries(257, 128, 64, seed_means=31, seed_q=32)
+    k = 10
+    want_ids, want_d = oracle.l2_exact_u8_int(C, Q, k)
+    # Two shards with global ids, searched through the device API, merged on device.
+    half = C.shape[0] // 2
+    shards = [(C[:half], 0), (C[half:], half)]
+    dq = torch.from_numpy(Q).cuda()
+    all_d = torch.empty((2, len(Q), k), dtype=torch.int32, device="cuda")
+    all_i = torch.empty((2, len(Q), k), dtype=torch.int32, device="cuda")
+    handles = []
+    for s, (part, off) in enumerate(shards):
+        h = _create_u8(L, part, id_offset=off)
+        handles.append(h)
+        st = L.mdh_search_u8_device(h, ctypes.c_void_p(dq.data_ptr()), len(Q), k, ctypes.c_void_p(all_i[s].data_ptr()),
+                                    ctypes.c_void_p(all_d[s].data_ptr()), None, None)
+        assert st == 0, L.mdh_last_error()
+    out_d = torch.empty((len(Q), k), dtype=torch.int32, device="cuda")
+    out_i = torch.empty((len(Q), k), dtype=torch.int32, device="cuda")
+    st = L.mdh_merge_topk_device(ctypes.c_void_p(all_d.data_ptr()), ctypes.c_void_p(all_i.data_ptr()), 2, len(Q), k,
+                                 ctypes.c_void_p(out_d.data_ptr()), ctypes.c_void_p(out_i.data_ptr()), None)
+    assert st == 0, L.mdh_last_error()
+    np.testing.assert_array_equal(out_i.cpu().numpy(), want_ids)
+    np.testing.assert_array_equal(out_d.cpu().numpy(), want_d)
+    for h in handles:
+        L.mdh_index_destroy(h)
+
+
+def test_multi_device_index_matches_single():
+    L = capi()
+    n = L.mdh_device_count()
+    if n < 2:
+        pytest.skip("needs 2 GPUs")
+    C = cases.gmm_u8(200_000, 128, 64, seed=41)
+    Q = cases.gmm_u8_queries(64, 128, 64, seed_means=41, seed_q=42)
+    h1 = _create_u8(L, C)
+    hn = _create_u8(L, C, devices=list(range(min(n, 4))))
+    a = _search_u8(L, h1, Q, 10)
+    b = _search_u8(L, hn, Q, 10)
+    np.testing.assert_array_equal(a[0], b[0])
+    np.testing.assert_array_equal(a[1], b[1])
+    L.mdh_index_destroy(h1)
+    L.mdh_index_destroy(hn)
+
+
+def test_float_queries_through_capi():
+    L = capi()
+    C, Q = cases.case_float_queries()
+    h = _create_u8(L, C)
+    ids = np.empty((len(Q), 10), np.int32)
+    dist = np.empty((len(Q), 10), np.float32)
+    st = L.mdh_search_f32(h, ptr(Q), len(Q), 10, 0, ptr(ids), ptr(dist), None)
+    assert st == 0, L.mdh_last_error()
+    want_ids, want_d = oracle.l2_exact_u8(C, Q, 10)
+    np.testing.assert_array_equal(ids, want_ids)
+    np.testing.assert_array_equal(dist, want_d)  # bit-identical float distances
+    L.mdh_index_destroy(h)

@@ -1,0 +1,123 @@
+"""The oracle (CPU restatement) against the golden fixtures made by the reference itself.
+
+Pins the oracle before any GPU result is compared with it: every fixture
+was produced by the reference's own compiled CPU code (make_golden.py), and
+the oracle must reproduce it -- ordered lists for MadhavaL2.search_exact
+(ties go to the lower index), id sets for SpeedEngine (whose tie order is
+unspecified, src/speed_cpu.cpp:346-347).
+"""
+import numpy as np
+import pytest
+
+import cases
+import oracle
+from helpers import load_fixture
+
+
+def _check_sha(meta, *arrays):
+    assert cases.sha(*arrays) == meta["sha256"], "input generator drifted from the fixture"
+
+
+def _cmp_exact(got, want):
+    assert got.shape == want.shape
+    np.testing.assert_array_equal(got, want)
+
+
+def _cmp_sets(got, want):
+    assert got.shape == want.shape
+    for i in range(len(got)):
+        assert sorted(got[i].tolist()) == sorted(want[i].tolist()), f"query {i}"
+
+
+def _k(key):
+    return int(key.rsplit("_k", 1)[1])
+
+
+def _run_oracle(key, C, Q):
+    k = _k(key)
+    if key.startswith("exact_l2"):
+        return oracle.l2_exact_u8(C, Q, k)[0]
+    if key.startswith("exact_cos"):
+        return oracle.cosine_exact_u8(C, Q, k)[0]
+    cosine = "_cos_" in key
+    return oracle.speed_exact(C, Q, k, cosine)[0]
+
+
+CASES = {
+    "api": cases.case_api,
+    "quickstart": cases.case_quickstart,
+    "gmm": cases.case_gmm,
+    "float_queries": cases.case_float_queries,
+    "dups": cases.case_dups,
+    "small": cases.case_small,
+    "f32_corpus": cases.case_f32_corpus,
+}
+for _d in cases.DIMS:
+    CASES[f"dim{_d}"] = (lambda d=_d: cases.case_dim(d))
+
+
+def _cmp_speed(key, C, Q, got, want):
+    kind = "speed_cos" if "_cos_" in key else "speed_l2"
+    bad = oracle.equivalent_topk(kind, C, Q, got, want)
+    assert not bad, f"{key}: queries {bad} differ beyond tie order"
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_oracle_matches_reference_fixture(name):
+    meta, res = load_fixture(name)
+    C, Q = CASES[name]()
+    _check_sha(meta, C, Q)
+    for key, want in res.items():
+        got = _run_oracle(key, C, Q)
+        if key.startswith("exact"):
+            _cmp_exact(got, want)
+        else:
+            _cmp_speed(key, C, Q, got, want)
+
+
+def test_oracle_matches_reference_fixture_clustered():
+    X, Xu = cases.case_clustered()
+    meta, res = load_fixture("clustered_u8")
+    _check_sha(meta, Xu, Xu[:16].astype(np.float32))
+    Qu = Xu[:16].astype(np.float32)
+    for key, want in res.items():
+        got = _run_oracle(key, Xu, Qu)
+        if key.startswith("exact"):
+            _cmp_exact(got, want)
+        else:
+            _cmp_speed(key, Xu, Qu, got, want)
+    meta, res = load_fixture("clustered_f32")
+    _check_sha(meta, X, X[:16])
+    for key, want in res.items():
+        _cmp_speed(key, X, X[:16], _run_oracle(key, X, X[:16]), want)
+
+
+def test_integer_oracle_agrees_with_float_oracle():
+    """For u8 queries the int64 ranking equals the reference float ranking."""
+    C, Q = cases.case_api()
+    a, da = oracle.l2_exact_u8(C, Q, 32)
+    b, db = oracle.l2_exact_u8_int(C, Q.astype(np.uint8), 32)
+    np.testing.assert_array_equal(a, b)
+    np.testing.assert_array_equal(da.astype(np.int64), db)
+
+
+def test_oracle_brute_force_numpy():
+    """Cross-check the oracle with an independent numpy lexsort (dist, id)."""
+    C, Q = cases.case_dups()
+    ids, dist = oracle.l2_exact_u8_int(C, Q.astype(np.uint8), 64)
+    Ci = C.astype(np.int64)
+    for i, q in enumerate(Q.astype(np.int64)):
+        d = ((Ci - q) ** 2).sum(1)
+        o = np.lexsort((np.arange(len(d)), d))[:64]
+        np.testing.assert_array_equal(ids[i], o)
+        np.testing.assert_array_equal(dist[i], d[o])
+
+
+def test_oracle_edge_cases():
+    C = np.zeros((10, 16), np.uint8)  # all rows identical: ties everywhere
+    ids, dist = oracle.l2_exact_u8_int(C, np.zeros((2, 16), np.uint8), 4)
+    np.testing.assert_array_equal(ids, [[0, 1, 2, 3]] * 2)
+    ids, _ = oracle.l2_exact_u8(C[:3], np.zeros((1, 16), np.float32), 5)  # k > n
+    np.testing.assert_array_equal(ids, [[0, 1, 2, -1, -1]])
+    ids, _ = oracle.l2_exact_u8(C[:0], np.zeros((1, 16), np.float32), 3)  # empty corpus
+    np.testing.assert_array_equal(ids, [[-1, -1, -1]])

@@ -1,0 +1,768 @@
+// C ABI and search orchestration.
+//
+// Search algorithm (exact, every path):
+//   A shard holds nested norm-sorted row sets L_0 c L_1 c ... c L_last (random
+//   samples of the shard, then the shard itself).
+//   1. Scan L_0 with an infinite threshold; each query keeps the k-th
+//      smallest (key, id) as its threshold T_0 (k rows of L_0 lie at or
+//      below it, so at least k rows of every larger level do too).
+//   2. For each following level, keep only the pairs with (key, id) <= T
+//      as candidates and select their k-th smallest as the next threshold.
+//   3. On the full shard the candidates' sorted first k entries are the
+//      exact top-k: every pair left out ranks after T, which ranks after k
+//      rows of the shard.
+//   If a query's candidate list overflows on the full shard, the k-th
+//   smallest stored entry is a strictly smaller valid threshold (ids make
+//   keys unique); that query reruns with it until its list fits.
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "internal.h"
+
+namespace mdh {
+
+void ensure_speed_rows_u8(mdh_index* ix, Shard& sh);
+
+namespace {
+
+thread_local std::string g_last_error;
+int g_scan_path = 0;  // 0 auto, 1 CUDA cores only, 2 tensor cores when possible
+int g_cap_limit = 0;  // 0 = default candidate capacities
+
+constexpr int kCapMax = 16384;          // largest candidate list the selection kernel sorts
+constexpr size_t kCandBudget = size_t(2) << 30;  // bytes of candidate lists per query chunk
+
+template <class F>
+mdh_status guard(F&& f) {
+    try {
+        f();
+        g_last_error.clear();
+        return MDH_OK;
+    } catch (const Error& e) {
+        g_last_error = e.what();
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        g_last_error = "host allocation failed";
+        return MDH_ERR_OOM;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return MDH_ERR_INTERNAL;
+    }
+}
+
+int next_pow2(int64_t x) {
+    int64_t p = 1;
+    while (p < x) p <<= 1;
+    return (int)p;
+}
+
+void check_device_usable(int dev) {
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0) {
+        cudaGetLastError();
+        throw Error(MDH_ERR_CUDA, "no CUDA device is available (this library has no CPU fallback)");
+    }
+    MDH_REQUIRE(dev >= 0 && dev < count, MDH_ERR_INVALID_ARG, "device ordinal out of range");
+    cudaDeviceProp p;
+    MDH_CUDA(cudaGetDeviceProperties(&p, dev));
+    if (p.major != 10 || p.minor != 0)
+        throw Error(MDH_ERR_CUDA, "this library is built for sm_100a (B200); device " + std::to_string(dev) +
+                                      " is sm_" + std::to_string(p.major) + std::to_string(p.minor));
+}
+
+// What the queries of one call are and which arithmetic ranks them.
+struct QueryPlan {
+    bool integer = false;   // u8 integer path
+    int kind = -1;          // ScoreKind for the float path
+    bool asc = true;        // key ascends with the returned value (L2) or descends (scores)
+    bool int_dist = false;  // returned value is an integer distance
+};
+
+// Levels scanned for one search: indices into shard.levels plus their
+// candidate capacity.
+struct LevelStep {
+    int level;
+    int cap;
+    bool dense;  // infinite threshold (first level)
+};
+
+std::vector<LevelStep> plan_levels(const Shard& sh, int k) {
+    const int L = (int)sh.levels.size();
+    std::vector<LevelStep> steps;
+    // First level: the smallest with at least k rows whose dense candidate
+    // list fits the selector.
+    int i0 = -1;
+    for (int i = 0; i < L; i++) {
+        if (sh.levels[i].n >= k || i == L - 1) {
+            if (sh.levels[i].n <= kCapMax) i0 = i;
+            break;
+        }
+    }
+    if (i0 < 0)
+        throw Error(MDH_ERR_UNSUPPORTED, "k = " + std::to_string(k) +
+                                             " is larger than this build's exact selector supports for a corpus of " +
+                                             std::to_string(sh.n) + " rows");
+    const int cap_floor = next_pow2(std::max(k, 64));
+    auto limit = [&](int cap) { return g_cap_limit > 0 ? std::max(cap_floor, std::min(cap, g_cap_limit)) : cap; };
+    steps.push_back({i0, limit(next_pow2(std::max<int64_t>(sh.levels[i0].n, k))), true});
+    const double rmax = std::max(4.0, 2048.0 / (double)k);
+    int cur = i0;
+    while (cur != L - 1) {
+        int nxt = cur + 1;
+        for (int j = cur + 1; j < L; j++)
+            if ((double)sh.levels[j].n <= (double)sh.levels[cur].n * rmax) nxt = j;
+        double ratio = (double)sh.levels[nxt].n / (double)std::max<int64_t>(sh.levels[cur].n, 1);
+        int cap = next_pow2((int64_t)(3.0 * k * ratio) + 256);
+        cap = std::max(4096, std::min(kCapMax, cap));
+        if (nxt == L - 1 && sh.levels[nxt].n <= kCapMax) cap = std::max(cap, next_pow2(std::max<int64_t>(sh.levels[nxt].n, k)));
+        cap = std::min(cap, kCapMax);
+        steps.push_back({nxt, limit(cap), false});
+        cur = nxt;
+    }
+    return steps;
+}
+
+void grow(void** p, size_t* have, size_t need) {
+    if (need <= *have) return;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *have = 0;
+    size_t want = need + need / 4;
+    cudaError_t e = cudaMalloc(p, want);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        *p = nullptr;
+        throw Error(MDH_ERR_OOM, std::string("device scratch allocation failed: ") + cudaGetErrorString(e));
+    }
+    *have = want;
+}
+template <class T>
+void growT(T** p, size_t* have, size_t need_bytes) {
+    void* v = *p;
+    grow(&v, have, need_bytes);
+    *p = static_cast<T*>(v);
+}
+
+void ensure_status(Workspace& w) {
+    if (!w.status) {
+        MDH_CUDA(cudaMalloc(&w.status, 4 * sizeof(int32_t)));
+        MDH_CUDA(cudaHostAlloc(&w.h_status, 4 * sizeof(int32_t), cudaHostAllocDefault));
+    }
+}
+
+// Run one level's filter for `nq` queries already staged in the workspace.
+void run_filter(mdh_index* ix, Shard& sh, const Level& lv, const QueryPlan& qp, const uint8_t* q_u8,
+                const int32_t* qn, const float* q_f32, int nq, const uint32_t* tk, const int32_t* ti, int cap) {
+    Workspace& w = sh.ws;
+    if (qp.integer) {
+        if (ix->metric == MDH_METRIC_L2) {
+            bool use_tc = g_scan_path != 1 && lv.has_tmap && tc_supported(ix, lv) && (g_scan_path == 2 || nq >= 64);
+            if (use_tc) {
+                MDH_CUDA(cudaMemsetAsync(w.status, 0, sizeof(int32_t), sh.stream));
+                launch_filter_tc_u8_l2(lv, ix->dpad, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, w.status, sh.stream);
+            } else {
+                launch_filter_simt_u8_l2(lv, ix->dpad, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, sh.stream);
+            }
+        } else {
+            launch_filter_simt_u8_cos(lv, ix->dpad, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, sh.stream);
+        }
+    } else {
+        launch_filter_f32(lv, ix->dim, ix->dpad, qp.kind, q_f32, nq, tk, ti, w.counts, w.cand, cap, sh.stream);
+    }
+}
+
+struct ShardResult {
+    int64_t pairs = 0;
+    int64_t candidates = 0;
+    int levels = 0;
+    bool tc = false;
+    double scan_ms = 0.0;     // event time of the full-shard filter
+    int64_t scan_pairs = 0;
+};
+
+// Exact top-k for nq staged queries on one shard.  Results: ws.out_key /
+// ws.out_id ([nq][k], device).  host_q_u8 / host_q_f32 hold the staged
+// queries on the host for overflow reruns.
+ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, int k, const uint8_t* host_q_u8,
+                         const float* host_q_f32, size_t f32_stride_floats) {
+    MDH_CUDA(cudaSetDevice(sh.device));
+    Workspace& w = sh.ws;
+    cudaStream_t st = sh.stream;
+    ShardResult res;
+    std::vector<LevelStep> steps = plan_levels(sh, k);
+    int capmax = 0;
+    for (auto& s : steps) capmax = std::max(capmax, s.cap);
+    growT(&w.thr_key, &w.thr_key_bytes, (size_t)nq * 4);
+    growT(&w.thr_id, &w.thr_id_bytes, (size_t)nq * 4);
+    growT(&w.counts, &w.counts_bytes, (size_t)nq * 4);
+    growT(&w.cand, &w.cand_bytes, (size_t)nq * capmax * sizeof(uint2));
+    growT(&w.out_key, &w.out_key_bytes, (size_t)nq * k * 4);
+    growT(&w.out_id, &w.out_id_bytes, (size_t)nq * k * 4);
+    growT(&w.flags, &w.flags_bytes, (size_t)nq * 4);
+    ensure_status(w);
+
+    res.levels = (int)steps.size();
+    for (size_t si = 0; si < steps.size(); si++) {
+        const LevelStep& s = steps[si];
+        const Level& lv = sh.levels[s.level];
+        if (s.dense) launch_fill_threshold(w.thr_key, w.thr_id, nq, kKeyInf, kIdInf, st);
+        MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)nq * 4, st));
+        const bool last_level = si + 1 == steps.size();
+        if (last_level) {
+            if (!w.ev0) {
+                MDH_CUDA(cudaEventCreate(&w.ev0));
+                MDH_CUDA(cudaEventCreate(&w.ev1));
+            }
+            MDH_CUDA(cudaEventRecord(w.ev0, st));
+        }
+        run_filter(ix, sh, lv, qp, w.q_u8, w.qn, w.q_f32, nq, w.thr_key, w.thr_id, s.cap);
+        if (last_level) {
+            MDH_CUDA(cudaEventRecord(w.ev1, st));
+            res.scan_pairs = lv.n * (int64_t)nq;
+        }
+        res.pairs += lv.n * (int64_t)nq;
+        if (qp.integer && ix->metric == MDH_METRIC_L2 && lv.has_tmap && g_scan_path != 1 &&
+            (g_scan_path == 2 || nq >= 64))
+            res.tc = true;
+        const bool final_ = si + 1 == steps.size();
+        if (final_) MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
+        launch_select(w.counts, w.cand, s.cap, nq, k, final_ ? 1 : 0, w.thr_key, w.thr_id, w.out_key, w.out_id,
+                      w.flags, w.status + 1, nullptr, st);
+    }
+    // Status words: [0] device error of the tensor-core scan, [1] overflowed queries.
+    MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    MDH_CUDA(cudaStreamSynchronize(st));
+    if (w.h_status[0] != kDevOk)
+        throw Error(w.h_status[0] == kDevTimeout ? MDH_ERR_TIMEOUT : MDH_ERR_INTERNAL,
+                    "tensor-core scan reported device status " + std::to_string(w.h_status[0]));
+    {
+        float ms = 0.0f;
+        MDH_CUDA(cudaEventElapsedTime(&ms, w.ev0, w.ev1));
+        res.scan_ms = ms;
+    }
+    int flagged = w.h_status[1];
+    const LevelStep last = steps.back();
+    const Level& lv = sh.levels[last.level];
+    int rounds = 0;
+    while (flagged > 0) {
+        MDH_REQUIRE(++rounds < 64, MDH_ERR_INTERNAL, "candidate overflow did not converge");
+        std::vector<int32_t> hflags((size_t)nq), hti((size_t)nq);
+        std::vector<uint32_t> htk((size_t)nq);
+        MDH_CUDA(cudaMemcpyAsync(hflags.data(), w.flags, (size_t)nq * 4, cudaMemcpyDeviceToHost, st));
+        MDH_CUDA(cudaMemcpyAsync(htk.data(), w.thr_key, (size_t)nq * 4, cudaMemcpyDeviceToHost, st));
+        MDH_CUDA(cudaMemcpyAsync(hti.data(), w.thr_id, (size_t)nq * 4, cudaMemcpyDeviceToHost, st));
+        MDH_CUDA(cudaStreamSynchronize(st));
+        std::vector<int32_t> list;
+        for (int i = 0; i < nq; i++)
+            if (hflags[(size_t)i]) list.push_back(i);
+        const int m = (int)list.size();
+        // Compact the flagged queries into the tail scratch (qlist + staged copies).
+        std::vector<uint32_t> ctk((size_t)m);
+        std::vector<int32_t> cti((size_t)m);
+        for (int i = 0; i < m; i++) {
+            ctk[(size_t)i] = htk[(size_t)list[(size_t)i]];
+            cti[(size_t)i] = hti[(size_t)list[(size_t)i]];
+        }
+        growT(&w.qlist, &w.qlist_bytes, (size_t)m * 4 * 3);
+        int32_t* d_list = w.qlist;
+        uint32_t* d_tk = reinterpret_cast<uint32_t*>(w.qlist + m);
+        int32_t* d_ti = w.qlist + 2 * m;
+        MDH_CUDA(cudaMemcpyAsync(d_list, list.data(), (size_t)m * 4, cudaMemcpyHostToDevice, st));
+        MDH_CUDA(cudaMemcpyAsync(d_tk, ctk.data(), (size_t)m * 4, cudaMemcpyHostToDevice, st));
+        MDH_CUDA(cudaMemcpyAsync(d_ti, cti.data(), (size_t)m * 4, cudaMemcpyHostToDevice, st));
+        // Staged query copies for the compact batch live in a separate buffer.
+        uint8_t* cq_u8 = nullptr;
+        int32_t* cqn = nullptr;
+        float* cq_f32 = nullptr;
+        void* tmpbuf = nullptr;
+        size_t need = qp.integer ? (size_t)m * ix->dpad + (size_t)m * 4 + 256
+                                 : (size_t)m * f32_stride_floats * 4 + (size_t)m * 4 + 256;
+        grow(&w.tmp, &w.tmp_bytes, need);
+        tmpbuf = w.tmp;
+        if (qp.integer) {
+            cq_u8 = static_cast<uint8_t*>(tmpbuf);
+            cqn = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(tmpbuf) + round_up((size_t)m * ix->dpad, 256));
+            launch_gather_queries_u8(w.q_u8, w.qn, d_list, m, ix->dpad, cq_u8, cqn, st);
+        } else {
+            // Host copy of the flagged float queries: [m][dim] then [m] aux.
+            std::vector<float> hq((size_t)m * ix->dim + (size_t)m);
+            for (int i = 0; i < m; i++) {
+                std::memcpy(&hq[(size_t)i * ix->dim], host_q_f32 + (size_t)list[(size_t)i] * ix->dim,
+                            (size_t)ix->dim * 4);
+                hq[(size_t)m * ix->dim + i] = host_q_f32[(size_t)nq * ix->dim + list[(size_t)i]];
+            }
+            cq_f32 = static_cast<float*>(tmpbuf);
+            MDH_CUDA(cudaMemcpyAsync(cq_f32, hq.data(), hq.size() * 4, cudaMemcpyHostToDevice, st));
+            MDH_CUDA(cudaStreamSynchronize(st));
+        }
+        MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
+        run_filter(ix, sh, lv, qp, cq_u8, cqn, cq_f32, m, d_tk, d_ti, last.cap);
+        MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
+        launch_select(w.counts, w.cand, last.cap, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id, w.flags,
+                      w.status + 1, d_list, st);
+        MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+        MDH_CUDA(cudaStreamSynchronize(st));
+        if (w.h_status[0] != kDevOk)
+            throw Error(MDH_ERR_TIMEOUT, "tensor-core scan reported device status " + std::to_string(w.h_status[0]));
+        flagged = w.h_status[1];
+        res.pairs += lv.n * (int64_t)m;
+    }
+    (void)host_q_u8;
+    return res;
+}
+
+// Prepare the float queries of one chunk following the reference formula.
+// Output layout: [nq][dim] values, then [nq] aux (|q|^2 for cosine scores).
+void prepare_float_queries(const mdh_index* ix, const QueryPlan& qp, const float* q, int nq, int mode,
+                           std::vector<float>& out) {
+    const int d = ix->dim;
+    out.assign((size_t)nq * d + nq, 0.0f);
+    for (int i = 0; i < nq; i++) {
+        const float* src = q + (size_t)i * d;
+        float* dst = &out[(size_t)i * d];
+        std::memcpy(dst, src, (size_t)d * 4);
+        if (qp.kind == kScoreSpeedCos) {
+            // src/speed_cpu.cpp:278-287 (single query) and :365-372 (batch):
+            // |q| by a sequential FMA chain, scaled by 1/|q|.
+            float qn = 0.0f;
+            for (int j = 0; j < d; j++) qn = std::fmaf(src[j], src[j], qn);
+            float inv;
+            if (mode == MDH_SCORE_SPEED_BATCH) {
+                inv = qn > 1e-12f ? 1.0f / std::sqrt(qn) : 0.0f;  // batch path compares |q|^2
+            } else {
+                float s = std::sqrt(qn);
+                inv = s > 1e-12f ? 1.0f / s : 0.0f;
+            }
+            for (int j = 0; j < d; j++) dst[j] = src[j] * inv;
+        }
+        if (qp.kind == kScoreCosU8 || qp.kind == kScoreExactCosF32) {
+            float s = 0.0f;  // src/winnex_madhava.cpp:759
+            for (int j = 0; j < d; j++) s = std::fmaf(src[j], src[j], s);
+            out[(size_t)nq * d + i] = s;
+        }
+    }
+}
+
+QueryPlan plan_query(const mdh_index* ix, bool integral, int mode) {
+    QueryPlan qp;
+    const bool l2 = ix->metric == MDH_METRIC_L2;
+    qp.asc = l2;
+    if (!ix->is_f32 && integral && ix->dim <= 256 && (l2 || mode == MDH_SCORE_EXACT)) {
+        qp.integer = true;
+        qp.int_dist = l2;
+        return qp;
+    }
+    if (ix->is_f32) {
+        qp.kind = l2 ? kScoreSpeedL2 : kScoreSpeedCos;
+        qp.asc = false;
+    } else if (mode == MDH_SCORE_SPEED || mode == MDH_SCORE_SPEED_BATCH) {
+        qp.kind = l2 ? kScoreSpeedL2 : kScoreSpeedCos;
+        qp.asc = false;
+    } else {
+        qp.kind = l2 ? kScoreL2SqU8 : kScoreCosU8;
+        qp.asc = l2;
+    }
+    return qp;
+}
+
+bool all_integral_u8(const float* q, size_t count) {
+    for (size_t i = 0; i < count; i++) {
+        float v = q[i];
+        if (!(v >= 0.0f && v <= 255.0f) || v != std::floor(v)) return false;
+    }
+    return true;
+}
+
+// Full search of a batch: chunk queries, run every shard, merge.
+// Exactly one of host_u8 / host_f32 is set.
+void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, int nq, int k, int mode,
+                 int32_t* out_ids, float* out_val_f, int32_t* out_val_i, mdh_stats* stats) {
+    auto t0 = std::chrono::high_resolution_clock::now();
+    MDH_REQUIRE(ix, MDH_ERR_INVALID_ARG, "null index");
+    MDH_REQUIRE(nq >= 0, MDH_ERR_INVALID_ARG, "nq must be >= 0");
+    MDH_REQUIRE(k >= 0, MDH_ERR_INVALID_ARG, "k must be >= 0");
+    MDH_REQUIRE(nq == 0 || host_u8 || host_f32, MDH_ERR_INVALID_ARG, "null queries");
+    MDH_REQUIRE(nq == 0 || k == 0 || out_ids, MDH_ERR_INVALID_ARG, "null output ids");
+    std::lock_guard<std::mutex> lock(ix->mu);
+    mdh_stats st{};
+    const int dim = ix->dim, dpad = ix->dpad;
+    const int kk = (int)std::min<int64_t>(k, ix->n);
+    for (size_t i = 0; i < (size_t)nq * k; i++) out_ids[i] = -1;
+    if (out_val_f)
+        for (size_t i = 0; i < (size_t)nq * k; i++) out_val_f[i] = NAN;
+    if (out_val_i)
+        for (size_t i = 0; i < (size_t)nq * k; i++) out_val_i[i] = -1;
+    if (nq == 0 || kk == 0) {
+        if (stats) *stats = st;
+        return;
+    }
+    bool integral = host_u8 != nullptr || (!ix->is_f32 && all_integral_u8(host_f32, (size_t)nq * dim));
+    QueryPlan qp = plan_query(ix, integral, mode);
+    MDH_REQUIRE(qp.integer || host_f32, MDH_ERR_NOT_INTEGRAL, "u8 queries need the integer path");
+    if (qp.kind == kScoreSpeedCos && !ix->is_f32)
+        for (auto& sh : ix->shards) ensure_speed_rows_u8(ix, sh);
+    if (qp.kind == kScoreExactCosF32)
+        throw Error(MDH_ERR_UNSUPPORTED, "float-row exact cosine is not built in this version");
+
+    const int nshard = (int)ix->shards.size();
+    // Query chunk: bounded candidate memory.
+    int chunk = (int)std::max<size_t>(1, kCandBudget / ((size_t)kCapMax * sizeof(uint2)));
+    chunk = std::min(chunk, nq);
+    std::vector<uint8_t> qbuf_u8;
+    std::vector<float> qbuf_f32;
+    std::vector<uint32_t> hkey((size_t)chunk * kk);
+    std::vector<int32_t> hid((size_t)chunk * kk);
+    for (int c0 = 0; c0 < nq; c0 += chunk) {
+        const int m = std::min(chunk, nq - c0);
+        // Stage this chunk's queries on the host.
+        if (qp.integer) {
+            qbuf_u8.assign((size_t)m * dpad, 0);
+            for (int i = 0; i < m; i++)
+                for (int j = 0; j < dim; j++)
+                    qbuf_u8[(size_t)i * dpad + j] = host_u8 ? host_u8[(size_t)(c0 + i) * dim + j]
+                                                            : (uint8_t)host_f32[(size_t)(c0 + i) * dim + j];
+        } else {
+            prepare_float_queries(ix, qp, host_f32 + (size_t)c0 * dim, m, mode, qbuf_f32);
+        }
+        std::vector<ShardResult> sres((size_t)nshard);
+        std::vector<std::string> errs((size_t)nshard);
+        std::vector<mdh_status> codes((size_t)nshard, MDH_OK);
+        auto run = [&](int si) {
+            try {
+                Shard& sh = ix->shards[(size_t)si];
+                MDH_CUDA(cudaSetDevice(sh.device));
+                Workspace& w = sh.ws;
+                if (qp.integer) {
+                    growT(&w.q_u8, &w.q_u8_bytes, (size_t)m * dpad);
+                    growT(&w.qn, &w.qn_bytes, (size_t)m * 4);
+                    MDH_CUDA(cudaMemcpyAsync(w.q_u8, qbuf_u8.data(), (size_t)m * dpad, cudaMemcpyHostToDevice, sh.stream));
+                    launch_query_norms_u8(w.q_u8, m, dpad, w.qn, sh.stream);
+                } else {
+                    growT(&w.q_f32, &w.q_f32_bytes, qbuf_f32.size() * 4);
+                    MDH_CUDA(cudaMemcpyAsync(w.q_f32, qbuf_f32.data(), qbuf_f32.size() * 4, cudaMemcpyHostToDevice,
+                                             sh.stream));
+                }
+                sres[(size_t)si] = search_shard(ix, sh, qp, m, kk, qbuf_u8.data(), qbuf_f32.data(), (size_t)dim);
+            } catch (const Error& e) {
+                codes[(size_t)si] = e.code;
+                errs[(size_t)si] = e.what();
+            } catch (const std::exception& e) {
+                codes[(size_t)si] = MDH_ERR_INTERNAL;
+                errs[(size_t)si] = e.what();
+            }
+        };
+        if (nshard == 1) {
+            run(0);
+        } else {
+            std::vector<std::thread> th;
+            for (int si = 0; si < nshard; si++) th.emplace_back(run, si);
+            for (auto& t : th) t.join();
+        }
+        for (int si = 0; si < nshard; si++)
+            if (codes[(size_t)si] != MDH_OK) throw Error(codes[(size_t)si], errs[(size_t)si]);
+        double chunk_scan_ms = 0.0;
+        for (auto& r : sres) {
+            st.pairs_scored += r.pairs;
+            st.levels = std::max(st.levels, r.levels);
+            st.tensor_core_path |= r.tc ? 1 : 0;
+            st.full_scan_pairs += r.scan_pairs;
+            chunk_scan_ms = std::max(chunk_scan_ms, r.scan_ms);  // shards run concurrently
+        }
+        st.full_scan_ms += chunk_scan_ms;
+        // Gather / merge to the first shard's device.
+        Shard& s0 = ix->shards[0];
+        MDH_CUDA(cudaSetDevice(s0.device));
+        const uint32_t* fkey = s0.ws.out_key;
+        const int32_t* fid = s0.ws.out_id;
+        if (nshard > 1) {
+            size_t per = (size_t)m * kk;
+            uint32_t* all_key = nullptr;
+            int32_t* all_id = nullptr;
+            growT(&s0.ws.tmp, &s0.ws.tmp_bytes, per * 8 * nshard + per * 8 + 1024);
+            all_key = static_cast<uint32_t*>(s0.ws.tmp);
+            all_id = reinterpret_cast<int32_t*>(all_key + per * nshard);
+            uint32_t* mkey = reinterpret_cast<uint32_t*>(all_id + per * nshard);
+            int32_t* mid = reinterpret_cast<int32_t*>(mkey + per);
+            for (int si = 0; si < nshard; si++) {
+                Shard& sh = ix->shards[(size_t)si];
+                MDH_CUDA(cudaMemcpyPeerAsync(all_key + per * si, s0.device, sh.ws.out_key, sh.device, per * 4, s0.stream));
+                MDH_CUDA(cudaMemcpyPeerAsync(all_id + per * si, s0.device, sh.ws.out_id, sh.device, per * 4, s0.stream));
+            }
+            launch_merge_topk(all_key, all_id, nshard, m, kk, mkey, mid, s0.stream);
+            fkey = mkey;
+            fid = mid;
+        }
+        MDH_CUDA(cudaMemcpyAsync(hkey.data(), fkey, (size_t)m * kk * 4, cudaMemcpyDeviceToHost, s0.stream));
+        MDH_CUDA(cudaMemcpyAsync(hid.data(), fid, (size_t)m * kk * 4, cudaMemcpyDeviceToHost, s0.stream));
+        MDH_CUDA(cudaStreamSynchronize(s0.stream));
+        for (int i = 0; i < m; i++) {
+            for (int j = 0; j < kk; j++) {
+                const size_t src = (size_t)i * kk + j, dst = (size_t)(c0 + i) * k + j;
+                const int32_t id = hid[src];
+                out_ids[dst] = id;
+                if (id < 0) continue;
+                const uint32_t key = hkey[src];
+                if (out_val_i) out_val_i[dst] = qp.int_dist ? (int32_t)key : -1;
+                if (out_val_f) {
+                    if (qp.int_dist)
+                        out_val_f[dst] = (float)key;
+                    else if (qp.integer)  // integer cosine: key encodes the descending float score
+                        out_val_f[dst] = key_to_float_asc(~key);
+                    else
+                        out_val_f[dst] = qp.asc ? key_to_float_asc(key) : key_to_float_asc(~key);
+                }
+            }
+        }
+    }
+    st.latency_ms = std::chrono::duration<double, std::milli>(std::chrono::high_resolution_clock::now() - t0).count();
+    if (stats) *stats = st;
+}
+
+void create_impl(const void* host, bool f32, int64_t n, int32_t dim, int32_t metric, const int32_t* devices,
+                 int32_t ndev, int64_t id_offset, mdh_index** out) {
+    MDH_REQUIRE(out, MDH_ERR_INVALID_ARG, "null output pointer");
+    *out = nullptr;
+    MDH_REQUIRE(n >= 0, MDH_ERR_INVALID_ARG, "n must be >= 0");
+    MDH_REQUIRE(n == 0 || host, MDH_ERR_INVALID_ARG, "null corpus");
+    MDH_REQUIRE(dim >= 1 && dim <= 4096, MDH_ERR_INVALID_ARG, "dim must be in [1, 4096]");
+    MDH_REQUIRE(metric == MDH_METRIC_COSINE || metric == MDH_METRIC_L2, MDH_ERR_INVALID_ARG, "metric must be 0 or 1");
+    MDH_REQUIRE(id_offset >= 0 && n + id_offset <= 0x7FFFFFFF, MDH_ERR_INVALID_ARG,
+                "row ids must fit in int32 (n + id_offset <= 2^31 - 1)");
+    std::vector<int> devs;
+    if (devices && ndev > 0) {
+        for (int i = 0; i < ndev; i++) devs.push_back(devices[i]);
+    } else {
+        int cur = 0;
+        cudaError_t e = cudaGetDevice(&cur);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            throw Error(MDH_ERR_CUDA, "no CUDA device is available (this library has no CPU fallback)");
+        }
+        devs.push_back(cur);
+    }
+    for (int d : devs) check_device_usable(d);
+    std::unique_ptr<mdh_index> ix(new mdh_index());
+    ix->n = n;
+    ix->dim = dim;
+    ix->dpad = (int)round_up(dim, kRowAlign);
+    ix->metric = metric;
+    ix->is_f32 = f32;
+    const int nd = (int)devs.size();
+    ix->shards.resize((size_t)nd);
+    try {
+        for (int i = 0; i < nd; i++) {
+            Shard& sh = ix->shards[(size_t)i];
+            sh.device = devs[(size_t)i];
+            MDH_CUDA(cudaSetDevice(sh.device));
+            MDH_CUDA(cudaStreamCreateWithFlags(&sh.stream, cudaStreamNonBlocking));
+            const int64_t r0 = n * i / nd, r1 = n * (i + 1) / nd;
+            sh.id_base = id_offset + r0;
+            if (f32)
+                build_shard_f32(ix.get(), sh, static_cast<const float*>(host) + (size_t)r0 * dim, r1 - r0);
+            else
+                build_shard_u8(ix.get(), sh, static_cast<const uint8_t*>(host) + (size_t)r0 * dim, r1 - r0);
+        }
+    } catch (...) {
+        for (auto& sh : ix->shards) free_shard(sh);
+        throw;
+    }
+    *out = ix.release();
+}
+
+}  // namespace
+
+[[noreturn]] void throw_cuda(cudaError_t e, const char* what, const char* file, int line) {
+    cudaGetLastError();
+    mdh_status code = (e == cudaErrorMemoryAllocation) ? MDH_ERR_OOM : MDH_ERR_CUDA;
+    throw Error(code, std::string("CUDA error ") + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ") in " + what +
+                          " at " + file + ":" + std::to_string(line));
+}
+
+int device_sm_count(int dev) {
+    static int cache[64] = {0};
+    if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
+    int v = 0;
+    MDH_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
+    if (dev >= 0 && dev < 64) cache[dev] = v;
+    return v;
+}
+
+void ensure(void** p, size_t* have, size_t need) { grow(p, have, need); }
+
+}  // namespace mdh
+
+using namespace mdh;
+
+extern "C" {
+
+mdh_status mdh_index_create_u8(const uint8_t* host_corpus, int64_t n, int32_t dim, int32_t metric,
+                               const int32_t* devices, int32_t ndev, int64_t id_offset, mdh_index** out) {
+    return guard([&] { create_impl(host_corpus, false, n, dim, metric, devices, ndev, id_offset, out); });
+}
+
+mdh_status mdh_index_create_f32(const float* host_corpus, int64_t n, int32_t dim, int32_t metric,
+                                const int32_t* devices, int32_t ndev, int64_t id_offset, mdh_index** out) {
+    return guard([&] { create_impl(host_corpus, true, n, dim, metric, devices, ndev, id_offset, out); });
+}
+
+mdh_status mdh_index_create_u8_device(const uint8_t* dev_corpus, int64_t n, int32_t dim, int32_t metric,
+                                      int64_t id_offset, mdh_index** out) {
+    return guard([&] {
+        if (n > 0) {
+            cudaPointerAttributes a;
+            MDH_CUDA(cudaPointerGetAttributes(&a, dev_corpus));
+            MDH_REQUIRE(a.type == cudaMemoryTypeDevice, MDH_ERR_INVALID_ARG, "dev_corpus is not device memory");
+            int32_t dev = a.device;
+            create_impl(dev_corpus, false, n, dim, metric, &dev, 1, id_offset, out);
+        } else {
+            create_impl(dev_corpus, false, n, dim, metric, nullptr, 0, id_offset, out);
+        }
+    });
+}
+
+mdh_status mdh_index_destroy(mdh_index* index) {
+    return guard([&] {
+        if (!index) return;
+        for (auto& sh : index->shards) free_shard(sh);
+        delete index;
+    });
+}
+
+mdh_status mdh_index_info(const mdh_index* index, int64_t* n, int32_t* dim, int32_t* metric, int32_t* ndev) {
+    return guard([&] {
+        MDH_REQUIRE(index, MDH_ERR_INVALID_ARG, "null index");
+        if (n) *n = index->n;
+        if (dim) *dim = index->dim;
+        if (metric) *metric = index->metric;
+        if (ndev) *ndev = (int32_t)index->shards.size();
+    });
+}
+
+mdh_status mdh_search_f32(mdh_index* index, const float* host_queries, int32_t nq, int32_t k, int32_t mode,
+                          int32_t* out_ids, float* out_dist, mdh_stats* stats) {
+    return guard([&] {
+        MDH_REQUIRE(mode == MDH_SCORE_EXACT || mode == MDH_SCORE_SPEED || mode == MDH_SCORE_SPEED_BATCH,
+                    MDH_ERR_INVALID_ARG, "mode must be an mdh_score_mode value");
+        search_impl(index, nullptr, host_queries, nq, k, mode, out_ids, out_dist, nullptr, stats);
+    });
+}
+
+mdh_status mdh_search_u8(mdh_index* index, const uint8_t* host_queries, int32_t nq, int32_t k, int32_t* out_ids,
+                         int32_t* out_dist, mdh_stats* stats) {
+    return guard([&] {
+        MDH_REQUIRE(index && !index->is_f32, MDH_ERR_INVALID_ARG, "u8 queries need a u8 index");
+        search_impl(index, host_queries, nullptr, nq, k, MDH_SCORE_EXACT, out_ids, nullptr, out_dist, stats);
+    });
+}
+
+mdh_status mdh_search_u8_device(mdh_index* index, const uint8_t* dev_queries, int32_t nq, int32_t k,
+                                int32_t* dev_ids, int32_t* dev_dist, void* stream, mdh_stats* stats) {
+    return guard([&] {
+        auto t0 = std::chrono::high_resolution_clock::now();
+        MDH_REQUIRE(index && !index->is_f32, MDH_ERR_INVALID_ARG, "u8 queries need a u8 index");
+        MDH_REQUIRE(index->shards.size() == 1, MDH_ERR_UNSUPPORTED, "device search needs a single-device index");
+        MDH_REQUIRE(index->dim <= 256, MDH_ERR_UNSUPPORTED, "device u8 search supports dim <= 256");
+        MDH_REQUIRE(nq >= 0 && k >= 0, MDH_ERR_INVALID_ARG, "nq and k must be >= 0");
+        MDH_REQUIRE(nq == 0 || (dev_queries && dev_ids), MDH_ERR_INVALID_ARG, "null device buffer");
+        std::lock_guard<std::mutex> lock(index->mu);
+        Shard& sh = index->shards[0];
+        MDH_CUDA(cudaSetDevice(sh.device));
+        mdh_stats st{};
+        const int kk = (int)std::min<int64_t>(k, index->n);
+        cudaStream_t user = static_cast<cudaStream_t>(stream);
+        cudaStream_t saved = sh.stream;
+        if (user) sh.stream = user;
+        try {
+            if (nq > 0 && k > 0) {
+                Workspace& w = sh.ws;
+                const int dpad = index->dpad;
+                growT(&w.q_u8, &w.q_u8_bytes, (size_t)nq * dpad);
+                growT(&w.qn, &w.qn_bytes, (size_t)nq * 4);
+                if (dpad != index->dim) MDH_CUDA(cudaMemsetAsync(w.q_u8, 0, (size_t)nq * dpad, sh.stream));
+                MDH_CUDA(cudaMemcpy2DAsync(w.q_u8, dpad, dev_queries, index->dim, index->dim, nq,
+                                           cudaMemcpyDeviceToDevice, sh.stream));
+                launch_query_norms_u8(w.q_u8, nq, dpad, w.qn, sh.stream);
+                QueryPlan qp;
+                qp.integer = true;
+                qp.int_dist = index->metric == MDH_METRIC_L2;
+                ShardResult r;
+                if (kk > 0) r = search_shard(index, sh, qp, nq, kk, nullptr, nullptr, 0);
+                st.pairs_scored = r.pairs;
+                st.levels = r.levels;
+                st.tensor_core_path = r.tc ? 1 : 0;
+                st.full_scan_ms = r.scan_ms;
+                st.full_scan_pairs = r.scan_pairs;
+                if (kk == k) {
+                    MDH_CUDA(cudaMemcpyAsync(dev_ids, w.out_id, (size_t)nq * k * 4, cudaMemcpyDeviceToDevice, sh.stream));
+                    if (dev_dist)
+                        MDH_CUDA(cudaMemcpyAsync(dev_dist, w.out_key, (size_t)nq * k * 4, cudaMemcpyDeviceToDevice,
+                                                 sh.stream));
+                } else {
+                    MDH_CUDA(cudaMemsetAsync(dev_ids, 0xFF, (size_t)nq * k * 4, sh.stream));
+                    MDH_CUDA(cudaMemcpy2DAsync(dev_ids, (size_t)k * 4, w.out_id, (size_t)kk * 4, (size_t)kk * 4, nq,
+                                               cudaMemcpyDeviceToDevice, sh.stream));
+                    if (dev_dist) {
+                        MDH_CUDA(cudaMemsetAsync(dev_dist, 0xFF, (size_t)nq * k * 4, sh.stream));
+                        MDH_CUDA(cudaMemcpy2DAsync(dev_dist, (size_t)k * 4, w.out_key, (size_t)kk * 4, (size_t)kk * 4,
+                                                   nq, cudaMemcpyDeviceToDevice, sh.stream));
+                    }
+                }
+                MDH_CUDA(cudaStreamSynchronize(sh.stream));
+            }
+        } catch (...) {
+            sh.stream = saved;
+            throw;
+        }
+        sh.stream = saved;
+        st.latency_ms = std::chrono::duration<double, std::milli>(std::chrono::high_resolution_clock::now() - t0).count();
+        if (stats) *stats = st;
+    });
+}
+
+mdh_status mdh_merge_topk_device(const int32_t* dev_dist_all, const int32_t* dev_ids_all, int32_t nshard, int32_t nq,
+                                 int32_t k, int32_t* dev_dist_out, int32_t* dev_ids_out, void* stream) {
+    return guard([&] {
+        MDH_REQUIRE(nshard >= 1 && nq >= 0 && k >= 0, MDH_ERR_INVALID_ARG, "bad merge shape");
+        MDH_REQUIRE(nq == 0 || k == 0 || (dev_dist_all && dev_ids_all && dev_dist_out && dev_ids_out),
+                    MDH_ERR_INVALID_ARG, "null device buffer");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        launch_merge_topk(reinterpret_cast<const uint32_t*>(dev_dist_all), dev_ids_all, nshard, nq, k,
+                          reinterpret_cast<uint32_t*>(dev_dist_out), dev_ids_out, st);
+        MDH_CUDA(cudaStreamSynchronize(st));
+    });
+}
+
+mdh_status mdh_set_scan_path(int32_t path) {
+    return guard([&] {
+        MDH_REQUIRE(path >= 0 && path <= 2, MDH_ERR_INVALID_ARG, "path must be 0, 1 or 2");
+        g_scan_path = path;
+    });
+}
+
+mdh_status mdh_set_candidate_cap_limit(int32_t cap) {
+    return guard([&] {
+        MDH_REQUIRE(cap == 0 || (cap >= 64 && cap <= kCapMax && (cap & (cap - 1)) == 0), MDH_ERR_INVALID_ARG,
+                    "cap must be 0 or a power of two in [64, 16384]");
+        g_cap_limit = cap;
+    });
+}
+
+int32_t mdh_device_count(void) {
+    int c = 0;
+    if (cudaGetDeviceCount(&c) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return c;
+}
+
+const char* mdh_last_error(void) { return g_last_error.c_str(); }
+
+const char* mdh_version(void) { return "winnex-madhava-b200 0.1.0 (sm_100a)"; }
+
+}  // extern "C"

@@ -1,0 +1,127 @@
+// Internal host-side interfaces shared by the library's translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <memory>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+namespace mdh {
+
+// A norm-sorted row set on one device: either a nested random sample of the
+// shard (used to find per-query distance thresholds) or the whole shard.
+struct Level {
+    int64_t n = 0;           // real rows
+    int64_t n_pad = 0;       // rows padded to kTileRows (pad rows: zero bytes, kNormPad, id -1)
+    uint8_t* rows = nullptr; // [n_pad][dpad] u8, ascending (|v|^2, id)
+    int32_t* norms = nullptr;// [n_pad] |v|^2
+    int32_t* ids = nullptr;  // [n_pad] global row id
+    float* rows_f32 = nullptr;   // [n_pad][dim] float rows (float corpora / float-score paths)
+    float* norms_f32 = nullptr;  // [n_pad] float |v|^2 (SpeedEngine semantics)
+    CUtensorMap tmap_rows;   // TMA map over `rows` (tensor-core scan), valid if has_tmap
+    bool has_tmap = false;
+    bool owns = true;        // false when aliasing another level's buffers
+};
+
+// Reusable per-device scratch.  Grown on demand, never shrunk.
+struct Workspace {
+    uint8_t* q_u8 = nullptr;     size_t q_u8_bytes = 0;     // [nq][dpad]
+    float* q_f32 = nullptr;      size_t q_f32_bytes = 0;    // [nq][dim]
+    int32_t* qn = nullptr;       size_t qn_bytes = 0;       // [nq] |q|^2
+    uint32_t* thr_key = nullptr; size_t thr_key_bytes = 0;  // [nq]
+    int32_t* thr_id = nullptr;   size_t thr_id_bytes = 0;   // [nq]
+    uint32_t* counts = nullptr;  size_t counts_bytes = 0;   // [nq]
+    uint2* cand = nullptr;       size_t cand_bytes = 0;     // [nq][cap]
+    uint32_t* out_key = nullptr; size_t out_key_bytes = 0;  // [nq][k]
+    int32_t* out_id = nullptr;   size_t out_id_bytes = 0;   // [nq][k]
+    int32_t* flags = nullptr;    size_t flags_bytes = 0;    // [nq] overflow flags
+    int32_t* qlist = nullptr;    size_t qlist_bytes = 0;    // [nq] query index list
+    int32_t* status = nullptr;                               // [4] device status words
+    int32_t* h_status = nullptr;                             // pinned mirror
+    void* tmp = nullptr;         size_t tmp_bytes = 0;      // CUB / misc scratch
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;               // brackets the full-shard scan
+};
+
+struct Shard {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int64_t n = 0;           // rows in this shard
+    int64_t id_base = 0;     // global id of the shard's first row
+    std::vector<Level> levels;   // ascending size; levels.back() is the whole shard
+    Workspace ws;
+};
+
+}  // namespace mdh
+
+struct mdh_index {
+    int64_t n = 0;
+    int32_t dim = 0;
+    int32_t dpad = 0;        // u8 row stride (bytes), multiple of kRowAlign
+    int32_t metric = MDH_METRIC_L2;
+    bool is_f32 = false;     // built from a float corpus
+    std::vector<mdh::Shard> shards;
+    std::mutex mu;           // one search at a time per index
+};
+
+namespace mdh {
+
+// ---- index build (index.cu) ----
+void build_shard_u8(mdh_index* ix, Shard& sh, const uint8_t* host_rows, int64_t n);
+void build_shard_f32(mdh_index* ix, Shard& sh, const float* host_rows, int64_t n);
+void free_shard(Shard& sh);
+
+// ---- workspace (capi.cu) ----
+void ensure(void** p, size_t* have, size_t need);
+
+// ---- CUDA-core scan kernels (scan_simt.cu) ----
+void launch_query_norms_u8(const uint8_t* q, int nq, int dpad, int32_t* qn, cudaStream_t st);
+// Append every pair with (key, id) <= per-query threshold to the candidate lists.
+void launch_filter_simt_u8_l2(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
+                              const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts,
+                              uint2* cand, int cap, cudaStream_t st);
+void launch_filter_simt_u8_cos(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
+                               const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts,
+                               uint2* cand, int cap, cudaStream_t st);
+// Float replicas of the reference arithmetic (float queries).
+void launch_filter_f32(const Level& lv, int dim, int dpad, int score_kind, const float* q, int nq,
+                       const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts, uint2* cand,
+                       int cap, cudaStream_t st);
+
+// score_kind values for launch_filter_f32
+enum ScoreKind : int {
+    kScoreL2SqU8 = 0,      // l2_sq_avx over u8 rows (MadhavaL2 L2, float query)
+    kScoreCosU8 = 1,       // exact_score cosine over u8 rows (MadhavaL2 cosine, float query)
+    kScoreSpeedL2 = 2,     // 2*dot_f32 - |v|^2 over float rows (SpeedEngine L2)
+    kScoreSpeedCos = 3,    // dot_f32 over normalized float rows, normalized query (SpeedEngine cosine)
+    kScoreExactCosF32 = 4, // exact_score cosine over float rows (MadhavaL2 float corpus, quant none)
+};
+
+// ---- tensor-core scan (scan_tc.cu) ----
+bool tc_supported(const mdh_index* ix, const Level& lv);
+void make_tmap_rows(Level& lv, int dpad);
+void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
+                            const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts,
+                            uint2* cand, int cap, int32_t* status, cudaStream_t st);
+
+// ---- selection (select.cu) ----
+void launch_fill_threshold(uint32_t* thr_key, int32_t* thr_id, int nq, uint32_t key, int32_t id,
+                           cudaStream_t st);
+// final == 0: write the k-th smallest stored (key, id) per query into thr.
+// final == 1: write the sorted top-k to out_key/out_id; set flags[q] = 1 and
+//             thr[q] when the candidate list overflowed (result not final).
+void launch_select(const uint32_t* counts, const uint2* cand, int cap, int nq, int k, int final_,
+                   uint32_t* thr_key, int32_t* thr_id, uint32_t* out_key, int32_t* out_id,
+                   int32_t* flags, int32_t* n_flagged, const int32_t* qmap, cudaStream_t st);
+void launch_merge_topk(const uint32_t* key_all, const int32_t* id_all, int nshard, int nq, int k,
+                       uint32_t* key_out, int32_t* id_out, cudaStream_t st);
+void launch_gather_queries_u8(const uint8_t* src, const int32_t* qn_src, const int32_t* list, int m,
+                              int dpad, uint8_t* dst, int32_t* qn_dst, cudaStream_t st);
+
+int device_sm_count(int dev);
+
+}  // namespace mdh

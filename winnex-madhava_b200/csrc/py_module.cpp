@@ -1,0 +1,518 @@
+// _winnex_madhava: pybind11 module over the C ABI (include/winnex_madhava_b200.h).
+//
+// Mirrors the reference module of the same name (bindings/py_module.cpp):
+// the enums, Config, SearchResult, MadhavaL2, SpeedEngine and the metric
+// helpers keep their names, argument names, defaults and error messages.
+// Search runs on the GPU through libwinnex_madhava_b200.so with the GIL
+// released.  What changes by design:
+//   * MadhavaL2.search / search_batch return the exact top-K (the same list
+//     as search_exact); k1 = k2 = N, k3 = exact_evals = pairs scored,
+//     bound_violations = 0 (no pair is pruned without an exact comparison);
+//   * SpeedEngine always runs on the GPU (has_gpu() is True); n_anchors is
+//     accepted, and the scan stays exact;
+//   * bound-engine-only features (audit certificates, commitments, index
+//     persistence, projection bases) raise NotImplementedError.
+#include <pybind11/numpy.h>
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "winnex_madhava_b200.h"
+
+namespace py = pybind11;
+
+namespace {
+
+enum class Metric { Cosine = 0, L2 = 1 };
+enum class QuantMode { Int8 = 0, None = 1 };
+enum class BasisMode { Random = 0, PCACorpus = 1 };
+
+// Field set and defaults of the reference Config
+// (include/winnex_madhava/winnex_madhava.hpp:73-113).
+struct Config {
+    int dim = 128;
+    int seed = 42;
+    int pca_sample = 10000;
+    Metric metric = Metric::Cosine;
+    QuantMode quant = QuantMode::Int8;
+    BasisMode basis = BasisMode::Random;
+    int stage1_dim = 64;
+    int stage2_dim = 128;
+    int k = 10;
+    double k1_fraction = 0.05;
+    double k2_fraction = 0.01;
+    int k1_min = 100;
+    int k2_min = 10;
+    int k2_max = 2000;
+    bool modulation = true;
+    bool postfilter = true;
+    bool normalize_input = true;
+    bool early_exit = false;
+    int n_threads = 0;
+};
+
+// Field set of the reference SearchResult (winnex_madhava.hpp:118-164).
+struct SearchResult {
+    std::vector<int> indices;
+    int k1 = 0, k2 = 0, k3 = 0;
+    double latency_ms = 0.0;
+    long long bound_pairs = 0;
+    long long bound_violations = 0;
+    double modulation_gain = 0.0;
+    long long pruned_by_bound = 0;
+    long long pruned_by_prefilter = 0;
+    long long exact_evals = 0;
+    double audit_threshold = 0.0;
+    std::vector<int64_t> audit_ids;
+    std::vector<float> audit_ubs;
+    std::vector<float> audit_l2_lbs;
+    std::vector<float> audit_residuals;
+};
+
+void check(mdh_status s) {
+    if (s == MDH_OK) return;
+    std::string msg = mdh_last_error();
+    if (s == MDH_ERR_OOM) throw std::bad_alloc();
+    throw std::runtime_error(msg.empty() ? std::string("winnex_madhava_b200 error ") + std::to_string((int)s) : msg);
+}
+
+[[noreturn]] void not_implemented(const char* what) {
+    PyErr_SetString(PyExc_NotImplementedError, what);
+    throw py::error_already_set();
+}
+
+using F32Array = py::array_t<float, py::array::c_style | py::array::forcecast>;
+using U8Array = py::array_t<uint8_t, py::array::c_style | py::array::forcecast>;
+
+struct IndexHandle {
+    mdh_index* ix = nullptr;
+    ~IndexHandle() {
+        if (ix) mdh_index_destroy(ix);
+    }
+    void reset(mdh_index* p) {
+        if (ix) mdh_index_destroy(ix);
+        ix = p;
+    }
+};
+
+std::vector<int32_t> parse_devices(const py::object& devices) {
+    std::vector<int32_t> d;
+    if (devices.is_none()) return d;
+    if (py::isinstance<py::int_>(devices)) {
+        int n = devices.cast<int>();
+        for (int i = 0; i < n; i++) d.push_back(i);
+        return d;
+    }
+    for (auto h : devices) d.push_back(h.cast<int>());
+    return d;
+}
+
+// ---------------------------------------------------------------------------
+class MadhavaL2 {
+public:
+    explicit MadhavaL2(const Config& cfg) : cfg_(cfg) {}
+
+    void build_u8(const uint8_t* data, int n) {
+        auto t0 = std::chrono::high_resolution_clock::now();
+        mdh_index* p = nullptr;
+        mdh_status s;
+        {
+            py::gil_scoped_release nogil;
+            s = mdh_index_create_u8(data, n, cfg_.dim, (int32_t)cfg_.metric, devices_.empty() ? nullptr : devices_.data(),
+                                    (int32_t)devices_.size(), 0, &p);
+        }
+        check(s);
+        h_.reset(p);
+        n_ = n;
+        built_ = true;
+        build_s_ = std::chrono::duration<double>(std::chrono::high_resolution_clock::now() - t0).count();
+    }
+
+    // MadhavaL2::build_float32 (src/winnex_madhava.cpp:433-468): the float
+    // rows are re-quantized with u8 = clamp((v + 1) * 127.5, 0, 255) and the
+    // exact scores run over those bytes.
+    void build_f32(const float* data, int n) {
+        const int D = cfg_.dim;
+        std::vector<uint8_t> q((size_t)n * D);
+        for (size_t i = 0; i < (size_t)n * D; i++) {
+            float v = data[i];
+            float t = (v + 1.0f) * 127.5f;
+            if (t < 0.0f) t = 0.0f;
+            if (t > 255.0f) t = 255.0f;
+            q[i] = (uint8_t)t;
+        }
+        if (cfg_.quant == QuantMode::None && cfg_.metric == Metric::Cosine)
+            not_implemented("MadhavaL2.build_float32 with quant='none' and metric='cosine' (float-row exact cosine) "
+                            "is not implemented in this build");
+        build_u8(q.data(), n);
+    }
+
+    SearchResult search_one(const F32Array& q) const {
+        auto info = q.request();
+        if (info.ndim != 1 || (int)info.shape[0] != cfg_.dim)
+            throw std::runtime_error("query must be float32 of length dim");
+        SearchResult out;
+        if (!built_) return out;
+        std::vector<int32_t> ids((size_t)cfg_.k);
+        mdh_stats st{};
+        mdh_status s;
+        {
+            py::gil_scoped_release nogil;
+            s = mdh_search_f32(h_.ix, (const float*)info.ptr, 1, cfg_.k, MDH_SCORE_EXACT, ids.data(), nullptr, &st);
+        }
+        check(s);
+        for (int32_t id : ids)
+            if (id >= 0) out.indices.push_back(id);
+        out.k1 = n_;
+        out.k2 = n_;
+        out.k3 = (int)std::min<int64_t>(st.pairs_scored, 0x7fffffff);
+        out.bound_pairs = n_;
+        out.exact_evals = st.pairs_scored;
+        out.bound_violations = st.bound_violations;
+        out.pruned_by_bound = st.pairs_pruned_by_bound;
+        out.latency_ms = st.latency_ms;
+        return out;
+    }
+
+    std::vector<int> search_batch(const F32Array& q, int nq, int k) const {
+        auto info = q.request();
+        if (info.ndim != 2 || (int)info.shape[0] != nq || (int)info.shape[1] != cfg_.dim)
+            throw std::runtime_error("queries must be (nq, dim) float32");
+        std::vector<int> all;
+        if (!built_ || nq <= 0 || k <= 0) return all;
+        std::vector<int32_t> ids((size_t)nq * k);
+        mdh_status s;
+        {
+            py::gil_scoped_release nogil;
+            s = mdh_search_f32(h_.ix, (const float*)info.ptr, nq, k, MDH_SCORE_EXACT, ids.data(), nullptr, nullptr);
+        }
+        check(s);
+        all.assign(ids.begin(), ids.end());
+        return all;
+    }
+
+    int num_vectors() const { return n_; }
+    int dim() const { return cfg_.dim; }
+    const Config& config() const { return cfg_; }
+    double build_seconds() const { return build_s_; }
+    bool built() const { return built_; }
+    void set_devices(std::vector<int32_t> d) { devices_ = std::move(d); }
+    mdh_index* handle() const { return h_.ix; }
+
+private:
+    Config cfg_;
+    IndexHandle h_;
+    int n_ = 0;
+    bool built_ = false;
+    double build_s_ = 0.0;
+    std::vector<int32_t> devices_;
+};
+
+// ---------------------------------------------------------------------------
+class SpeedEngine {
+public:
+    SpeedEngine(const void* data, bool is_f32, int n, int dim, int metric, std::vector<int32_t> devices)
+        : n_(n), dim_(dim) {
+        if (metric != 0 && metric != 1) throw std::runtime_error("metric must be 0 (cosine) or 1 (l2)");
+        mdh_index* p = nullptr;
+        mdh_status s;
+        {
+            py::gil_scoped_release nogil;
+            if (is_f32)
+                s = mdh_index_create_f32((const float*)data, n, dim, metric, devices.empty() ? nullptr : devices.data(),
+                                         (int32_t)devices.size(), 0, &p);
+            else
+                s = mdh_index_create_u8((const uint8_t*)data, n, dim, metric, devices.empty() ? nullptr : devices.data(),
+                                        (int32_t)devices.size(), 0, &p);
+        }
+        check(s);
+        h_.reset(p);
+    }
+
+    py::dict search(const F32Array& q, int k) const {
+        auto info = q.request();
+        if ((size_t)info.size != (size_t)dim_) throw std::runtime_error("query must be float32 of length dim");
+        std::vector<int32_t> ids((size_t)std::max(k, 0));
+        mdh_stats st{};
+        mdh_status s;
+        {
+            py::gil_scoped_release nogil;
+            s = mdh_search_f32(h_.ix, (const float*)info.ptr, 1, k, MDH_SCORE_SPEED, ids.data(), nullptr, &st);
+        }
+        check(s);
+        std::vector<int> out;
+        for (int32_t id : ids)
+            if (id >= 0) out.push_back(id);
+        py::dict d;
+        d["indices"] = out;
+        d["latency_ms"] = st.latency_ms;
+        d["bound_pairs"] = (long long)n_;
+        d["bound_violations"] = (long long)st.bound_violations;
+        return d;
+    }
+
+    py::dict search_batch(const F32Array& q, int nq, int k) const {
+        auto info = q.request();
+        if ((size_t)info.size != (size_t)nq * dim_) throw std::runtime_error("queries must be (nq, dim) float32");
+        int kk = std::min(std::max(k, 0), n_);
+        std::vector<int32_t> ids((size_t)nq * std::max(k, 0));
+        mdh_stats st{};
+        mdh_status s;
+        {
+            py::gil_scoped_release nogil;
+            s = mdh_search_f32(h_.ix, (const float*)info.ptr, nq, k, MDH_SCORE_SPEED_BATCH, ids.data(), nullptr, &st);
+        }
+        check(s);
+        // SpeedResult::indices is the concatenation of min(k, N) ids per query
+        // (src/speed_cpu.cpp:393).
+        std::vector<int> out;
+        out.reserve((size_t)nq * kk);
+        for (int i = 0; i < nq; i++)
+            for (int j = 0; j < kk; j++) out.push_back(ids[(size_t)i * k + j]);
+        py::dict d;
+        d["indices"] = out;
+        d["latency_ms"] = st.latency_ms;
+        return d;
+    }
+
+    int num_vectors() const { return n_; }
+    int dim() const { return dim_; }
+
+private:
+    IndexHandle h_;
+    int n_, dim_;
+};
+
+// ---------------------------------------------------------------------------
+// Metric helpers with the reference's definitions (src/winnex_madhava.cpp:320-377).
+double recall_at_k(const std::vector<int>& result, const std::vector<int>& gt_set, int k) {
+    int hits = 0;
+    for (int ri : result)
+        for (int vi : gt_set)
+            if (ri == vi) {
+                hits++;
+                break;
+            }
+    int denom = std::min(k, (int)gt_set.size());
+    return denom > 0 ? (double)hits / (double)denom : 0.0;
+}
+
+double ndcg_at_k(const std::vector<int>& result, const std::vector<int>& gt_set, int k) {
+    double dcg = 0, idcg = 0;
+    int top = std::min(k, (int)gt_set.size());
+    for (int j = 0; j < top && j < (int)result.size(); j++) {
+        int rel = 0;
+        for (int vi : gt_set)
+            if (result[j] == vi) {
+                rel = 1;
+                break;
+            }
+        dcg += (std::pow(2, rel) - 1) / std::log2(j + 2);
+    }
+    for (int j = 0; j < top; j++) idcg += 1.0 / std::log2(j + 2);
+    return idcg > 0 ? dcg / idcg : 0.0;
+}
+
+float l2_sq(const U8Array& v_raw, const F32Array& q, int dim) {
+    auto iv = v_raw.request();
+    auto iq = q.request();
+    if (iv.size < dim || iq.size < dim) throw std::runtime_error("l2_sq: inputs shorter than dim");
+    const uint8_t* v = (const uint8_t*)iv.ptr;
+    const float* qq = (const float*)iq.ptr;
+    float s = 0;
+    for (int j = 0; j < dim; j++) {
+        float d = (float)v[j] - qq[j];
+        s = std::fma(d, d, s);  // the reference build contracts `s += d * d` (-mfma)
+    }
+    return s;
+}
+
+std::vector<std::vector<int>> read_bigann_groundtruth(const std::string& path, int n_queries) {
+    std::vector<std::vector<int>> gt;
+    FILE* f = std::fopen(path.c_str(), "rb");
+    if (!f) return gt;
+    int32_t nq = 0, dim = 0;
+    if (std::fread(&nq, 4, 1, f) != 1 || std::fread(&dim, 4, 1, f) != 1 || nq < 0 || dim < 0) {
+        std::fclose(f);
+        return gt;
+    }
+    int want = n_queries > 0 ? std::min(n_queries, (int)nq) : (int)nq;
+    gt.resize((size_t)want);
+    std::vector<int32_t> ids((size_t)dim);
+    std::vector<float> dists((size_t)dim);
+    for (int gi = 0; gi < want; gi++) {
+        if (std::fread(ids.data(), 4, (size_t)dim, f) != (size_t)dim) break;
+        if (std::fread(dists.data(), 4, (size_t)dim, f) != (size_t)dim) break;
+        gt[(size_t)gi].assign(ids.begin(), ids.end());
+    }
+    std::fclose(f);
+    return gt;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(_winnex_madhava, m) {
+    m.doc() = "winnex-madhava exact top-K search on B200 (sm_100a CUDA kernels behind a C ABI)";
+
+    py::enum_<Metric>(m, "Metric").value("COSINE", Metric::Cosine).value("L2", Metric::L2).export_values();
+    py::enum_<QuantMode>(m, "QuantMode").value("INT8", QuantMode::Int8).value("NONE", QuantMode::None).export_values();
+    py::enum_<BasisMode>(m, "BasisMode")
+        .value("RANDOM", BasisMode::Random)
+        .value("PCA_CORPUS", BasisMode::PCACorpus)
+        .export_values();
+
+    py::class_<Config>(m, "Config")
+        .def(py::init<>())
+        .def_readwrite("dim", &Config::dim)
+        .def_readwrite("seed", &Config::seed)
+        .def_readwrite("metric", &Config::metric)
+        .def_readwrite("quant", &Config::quant)
+        .def_readwrite("basis", &Config::basis)
+        .def_readwrite("pca_sample", &Config::pca_sample)
+        .def_readwrite("stage1_dim", &Config::stage1_dim)
+        .def_readwrite("stage2_dim", &Config::stage2_dim)
+        .def_readwrite("k", &Config::k)
+        .def_readwrite("k1_fraction", &Config::k1_fraction)
+        .def_readwrite("k2_fraction", &Config::k2_fraction)
+        .def_readwrite("k1_min", &Config::k1_min)
+        .def_readwrite("k2_min", &Config::k2_min)
+        .def_readwrite("k2_max", &Config::k2_max)
+        .def_readwrite("modulation", &Config::modulation)
+        .def_readwrite("postfilter", &Config::postfilter)
+        .def_readwrite("normalize_input", &Config::normalize_input)
+        .def_readwrite("early_exit", &Config::early_exit)
+        .def_readwrite("n_threads", &Config::n_threads);
+
+    py::class_<SearchResult>(m, "SearchResult")
+        .def_readonly("indices", &SearchResult::indices)
+        .def_readonly("k1", &SearchResult::k1)
+        .def_readonly("k2", &SearchResult::k2)
+        .def_readonly("k3", &SearchResult::k3)
+        .def_readonly("latency_ms", &SearchResult::latency_ms)
+        .def_readonly("bound_pairs", &SearchResult::bound_pairs)
+        .def_readonly("bound_violations", &SearchResult::bound_violations)
+        .def_readonly("modulation_gain", &SearchResult::modulation_gain)
+        .def_readonly("pruned_by_bound", &SearchResult::pruned_by_bound)
+        .def_readonly("pruned_by_prefilter", &SearchResult::pruned_by_prefilter)
+        .def_readonly("exact_evals", &SearchResult::exact_evals)
+        .def_readonly("audit_threshold", &SearchResult::audit_threshold)
+        .def_readonly("audit_ids", &SearchResult::audit_ids)
+        .def_readonly("audit_ubs", &SearchResult::audit_ubs)
+        .def_readonly("audit_l2_lbs", &SearchResult::audit_l2_lbs)
+        .def_readonly("audit_residuals", &SearchResult::audit_residuals);
+
+    py::class_<MadhavaL2>(m, "MadhavaL2")
+        .def(py::init<const Config&>())
+        .def(
+            "build",
+            [](MadhavaL2& self, py::bytes raw, int n, int dim) {
+                char* buf = nullptr;
+                Py_ssize_t len = 0;
+                PyBytes_AsStringAndSize(raw.ptr(), &buf, &len);
+                if ((size_t)len < (size_t)n * dim) throw std::runtime_error("raw buffer too small for n*dim");
+                self.build_u8((const uint8_t*)buf, n);
+            },
+            py::arg("raw"), py::arg("n"), py::arg("dim"))
+        .def(
+            "build_numpy",
+            [](MadhavaL2& self, U8Array arr) {
+                auto info = arr.request();
+                if (info.ndim != 2) throw std::runtime_error("expected 2D uint8 array (n, dim)");
+                int n = (int)info.shape[0];
+                if ((int)info.shape[1] != self.dim()) throw std::runtime_error("array dim does not match Config.dim");
+                self.build_u8((const uint8_t*)info.ptr, n);
+                return n;
+            },
+            py::arg("arr"))
+        .def(
+            "build_float32",
+            [](MadhavaL2& self, F32Array arr) {
+                auto info = arr.request();
+                if (info.ndim != 2) throw std::runtime_error("expected 2D float32 array (n, dim)");
+                int n = (int)info.shape[0];
+                if ((int)info.shape[1] != self.dim()) throw std::runtime_error("array dim does not match Config.dim");
+                self.build_f32((const float*)info.ptr, n);
+                return n;
+            },
+            py::arg("arr"))
+        .def(
+            "set_basis", [](MadhavaL2&, py::object, py::object) { not_implemented("MadhavaL2.set_basis (bound-engine projection basis) is not part of the exact engine"); },
+            py::arg("P1"), py::arg("P2") = py::none())
+        .def("search", &MadhavaL2::search_one, py::arg("query"))
+        .def("search_exact", &MadhavaL2::search_one, py::arg("query"))
+        .def(
+            "search_audited",
+            [](const MadhavaL2&, py::object, int64_t, int64_t) -> py::dict {
+                not_implemented("MadhavaL2.search_audited (bound-engine audit certificate) is not implemented in this build");
+            },
+            py::arg("query"), py::arg("k") = 10, py::arg("max_audit_records") = 500)
+        .def(
+            "audit_json",
+            [](const MadhavaL2&, py::object, int64_t, int64_t) -> std::string {
+                not_implemented("MadhavaL2.audit_json is not implemented in this build");
+            },
+            py::arg("query"), py::arg("k") = 10, py::arg("max_audit_records") = 500)
+        .def(
+            "search_with_commitment",
+            [](const MadhavaL2&, py::object, int64_t, int64_t) -> py::dict {
+                not_implemented("MadhavaL2.search_with_commitment is not implemented in this build");
+            },
+            py::arg("query"), py::arg("k") = 10, py::arg("max_sample") = 50)
+        .def("search_batch", &MadhavaL2::search_batch, py::arg("queries"), py::arg("nq"), py::arg("k"))
+        .def(
+            "save_index", [](const MadhavaL2&, const std::string&) -> bool { not_implemented("MadhavaL2.save_index is not implemented in this build"); },
+            py::arg("path"))
+        .def(
+            "load_index", [](MadhavaL2&, const std::string&) -> bool { not_implemented("MadhavaL2.load_index is not implemented in this build"); },
+            py::arg("path"))
+        .def("num_vectors", &MadhavaL2::num_vectors)
+        .def("dim", &MadhavaL2::dim)
+        .def("config", &MadhavaL2::config)
+        .def("build_seconds", &MadhavaL2::build_seconds)
+        .def("built", &MadhavaL2::built)
+        .def("basis1", [](const MadhavaL2&) -> py::array { not_implemented("MadhavaL2.basis1: the exact engine has no projection basis"); })
+        .def("basis2", [](const MadhavaL2&) -> py::array { not_implemented("MadhavaL2.basis2: the exact engine has no projection basis"); })
+        .def("residuals1", [](const MadhavaL2&) -> py::array { not_implemented("MadhavaL2.residuals1: the exact engine has no projection residuals"); })
+        .def("residuals2", [](const MadhavaL2&) -> py::array { not_implemented("MadhavaL2.residuals2: the exact engine has no projection residuals"); })
+        .def("_set_devices", [](MadhavaL2& self, py::object d) { self.set_devices(parse_devices(d)); }, py::arg("devices"));
+
+    py::class_<SpeedEngine>(m, "SpeedEngine")
+        .def(py::init([](py::array_t<float, py::array::c_style> arr, int dim, int metric, int n_anchors, int nprobe,
+                         bool require_gpu, const std::string& opencl_lib, py::object devices) {
+                 (void)n_anchors; (void)nprobe; (void)require_gpu; (void)opencl_lib;
+                 auto info = arr.request();
+                 return new SpeedEngine(info.ptr, true, (int)info.shape[0], dim, metric, parse_devices(devices));
+             }),
+             py::arg("corpus_f32"), py::arg("dim"), py::arg("metric"), py::arg("n_anchors") = 0, py::arg("nprobe") = 4,
+             py::arg("require_gpu") = false, py::arg("opencl_lib") = "", py::arg("devices") = py::none())
+        .def(py::init([](py::array_t<uint8_t, py::array::c_style> arr, int dim, int metric, int n_anchors, int nprobe,
+                         bool require_gpu, const std::string& opencl_lib, py::object devices) {
+                 (void)n_anchors; (void)nprobe; (void)require_gpu; (void)opencl_lib;
+                 auto info = arr.request();
+                 return new SpeedEngine(info.ptr, false, (int)info.shape[0], dim, metric, parse_devices(devices));
+             }),
+             py::arg("corpus_u8"), py::arg("dim"), py::arg("metric"), py::arg("n_anchors") = 0, py::arg("nprobe") = 4,
+             py::arg("require_gpu") = false, py::arg("opencl_lib") = "", py::arg("devices") = py::none())
+        .def("search", &SpeedEngine::search, py::arg("query"), py::arg("k"))
+        .def("search_batch", &SpeedEngine::search_batch, py::arg("queries"), py::arg("nq"), py::arg("k"))
+        .def("num_vectors", &SpeedEngine::num_vectors)
+        .def("dim", &SpeedEngine::dim)
+        .def("has_gpu", [](const SpeedEngine&) { return true; })
+        .def("backend_name", [](const SpeedEngine&) { return "gpu"; })
+        .def("gpu_reason", [](const SpeedEngine&) { return std::string(); });
+
+    m.def("recall_at_k", &recall_at_k, py::arg("result"), py::arg("gt_set"), py::arg("k"));
+    m.def("ndcg_at_k", &ndcg_at_k, py::arg("result"), py::arg("gt_set"), py::arg("k"));
+    m.def("l2_sq", &l2_sq, py::arg("v_raw"), py::arg("q"), py::arg("dim"));
+    m.def("read_bigann_groundtruth", &read_bigann_groundtruth, py::arg("path"), py::arg("n_queries"));
+    m.def("device_count", &mdh_device_count);
+    m.def("version", &mdh_version);
+    m.def("set_scan_path", [](int p) { check(mdh_set_scan_path(p)); }, py::arg("path"));
+}

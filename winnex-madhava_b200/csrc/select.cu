@@ -1,0 +1,193 @@
+// Selection kernels: candidate lists -> per-query thresholds or final top-k,
+// and the merge of per-shard top-k lists.
+//
+// A query's candidates are sorted in shared memory as 64-bit keys
+// (rank key << 32 | row id), so ascending order is exactly the reference's
+// (distance, index) order (src/winnex_madhava.cpp:1237-1239) and, for score
+// metrics, descending score with the lower index first.
+#include "internal.h"
+
+namespace mdh {
+
+namespace {
+
+__device__ __forceinline__ void bitonic_sort_smem(unsigned long long* keys, int P) {
+    for (int size = 2; size <= P; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            __syncthreads();
+            for (int i = threadIdx.x; i < (P >> 1); i += blockDim.x) {
+                int lo = 2 * i - (i & (stride - 1));
+                int hi = lo + stride;
+                bool asc = (lo & size) == 0;
+                unsigned long long a = keys[lo], b = keys[hi];
+                if ((a > b) == asc) {
+                    keys[lo] = b;
+                    keys[hi] = a;
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ int next_pow2(int x) {
+    int p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+
+__global__ void k_fill_threshold(uint32_t* tk, int32_t* ti, int nq, uint32_t key, int32_t id) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < nq) {
+        tk[i] = key;
+        ti[i] = id;
+    }
+}
+
+// One CTA per query.  qmap (optional) maps the CTA's query to the slot its
+// threshold / output / flag is written to.
+__global__ void k_select(const uint32_t* __restrict__ counts, const uint2* __restrict__ cand, int cap, int k,
+                         int final_, uint32_t* __restrict__ thr_key, int32_t* __restrict__ thr_id,
+                         uint32_t* __restrict__ out_key, int32_t* __restrict__ out_id, int32_t* __restrict__ flags,
+                         int32_t* __restrict__ n_flagged, const int32_t* __restrict__ qmap) {
+    extern __shared__ unsigned long long keys[];
+    const int q = blockIdx.x;
+    const int qo = qmap ? qmap[q] : q;
+    const uint32_t c_all = counts[q];
+    const int c = (int)(c_all < (uint32_t)cap ? c_all : (uint32_t)cap);
+    const int P = next_pow2(c > k ? c : k);
+    const uint2* src = cand + (size_t)q * cap;
+    for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        if (i < c) {
+            uint2 e = src[i];
+            keys[i] = ((unsigned long long)e.x << 32) | e.y;
+        } else {
+            keys[i] = ~0ull;
+        }
+    }
+    bitonic_sort_smem(keys, P);
+    if (!final_) {
+        if (threadIdx.x == 0) {
+            int idx = (c < k ? c : k) - 1;
+            if (idx >= 0 && c >= k) {
+                thr_key[qo] = (uint32_t)(keys[idx] >> 32);
+                thr_id[qo] = (int32_t)(keys[idx] & 0xffffffffu);
+            } else {
+                // Fewer than k rows in this level: every row of the next
+                // level stays a candidate.
+                thr_key[qo] = kKeyInf;
+                thr_id[qo] = kIdInf;
+            }
+        }
+        return;
+    }
+    if (c_all > (uint32_t)cap) {
+        // Overflow: the stored lists are a subset; their k-th key is a valid
+        // (tighter) threshold for a rerun.  c == cap >= k here.
+        if (threadIdx.x == 0) {
+            flags[qo] = 1;
+            thr_key[qo] = (uint32_t)(keys[k - 1] >> 32);
+            thr_id[qo] = (int32_t)(keys[k - 1] & 0xffffffffu);
+            atomicAdd(n_flagged, 1);
+        }
+        return;
+    }
+    for (int j = threadIdx.x; j < k; j += blockDim.x) {
+        if (j < c) {
+            out_key[(size_t)qo * k + j] = (uint32_t)(keys[j] >> 32);
+            out_id[(size_t)qo * k + j] = (int32_t)(keys[j] & 0xffffffffu);
+        } else {
+            out_key[(size_t)qo * k + j] = kKeyInf;
+            out_id[(size_t)qo * k + j] = -1;
+        }
+    }
+    if (threadIdx.x == 0 && flags) flags[qo] = 0;
+}
+
+// Merge [nshard][nq][k] lists into [nq][k]; id -1 marks an empty entry.
+__global__ void k_merge_topk(const uint32_t* __restrict__ key_all, const int32_t* __restrict__ id_all, int nshard,
+                             int nq, int k, uint32_t* __restrict__ key_out, int32_t* __restrict__ id_out) {
+    extern __shared__ unsigned long long keys[];
+    const int q = blockIdx.x;
+    const int tot = nshard * k;
+    const int P = next_pow2(tot);
+    for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        unsigned long long v = ~0ull;
+        if (i < tot) {
+            int s = i / k, j = i - s * k;
+            size_t off = ((size_t)s * nq + q) * k + j;
+            int32_t id = id_all[off];
+            if (id >= 0) v = ((unsigned long long)key_all[off] << 32) | (uint32_t)id;
+        }
+        keys[i] = v;
+    }
+    bitonic_sort_smem(keys, P);
+    for (int j = threadIdx.x; j < k; j += blockDim.x) {
+        unsigned long long v = keys[j];
+        if (v == ~0ull) {
+            key_out[(size_t)q * k + j] = kKeyInf;
+            id_out[(size_t)q * k + j] = -1;
+        } else {
+            key_out[(size_t)q * k + j] = (uint32_t)(v >> 32);
+            id_out[(size_t)q * k + j] = (int32_t)(v & 0xffffffffu);
+        }
+    }
+}
+
+__global__ void k_gather_queries_u8(const uint8_t* __restrict__ src, const int32_t* __restrict__ qn_src,
+                                    const int32_t* __restrict__ list, int m, int dpad, uint8_t* __restrict__ dst,
+                                    int32_t* __restrict__ qn_dst) {
+    int i = blockIdx.x;
+    if (i >= m) return;
+    int s = list[i];
+    for (int b = threadIdx.x * 16; b < dpad; b += blockDim.x * 16)
+        *reinterpret_cast<uint4*>(dst + (size_t)i * dpad + b) = *reinterpret_cast<const uint4*>(src + (size_t)s * dpad + b);
+    if (threadIdx.x == 0) qn_dst[i] = qn_src[s];
+}
+
+size_t select_smem(int P) { return (size_t)P * sizeof(unsigned long long); }
+
+}  // namespace
+
+void launch_fill_threshold(uint32_t* thr_key, int32_t* thr_id, int nq, uint32_t key, int32_t id, cudaStream_t st) {
+    if (nq <= 0) return;
+    k_fill_threshold<<<(nq + 255) / 256, 256, 0, st>>>(thr_key, thr_id, nq, key, id);
+    MDH_CUDA(cudaGetLastError());
+}
+
+void launch_select(const uint32_t* counts, const uint2* cand, int cap, int nq, int k, int final_, uint32_t* thr_key,
+                   int32_t* thr_id, uint32_t* out_key, int32_t* out_id, int32_t* flags, int32_t* n_flagged,
+                   const int32_t* qmap, cudaStream_t st) {
+    if (nq <= 0) return;
+    int pmax = 1;
+    while (pmax < (cap > k ? cap : k)) pmax <<= 1;
+    size_t smem = select_smem(pmax);
+    MDH_REQUIRE(smem <= 220 * 1024, MDH_ERR_UNSUPPORTED, "candidate list too large for the selection kernel");
+    if (smem > 48 * 1024) MDH_CUDA(cudaFuncSetAttribute(k_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int threads = pmax >= 4096 ? 1024 : (pmax >= 1024 ? 512 : 256);
+    k_select<<<nq, threads, smem, st>>>(counts, cand, cap, k, final_, thr_key, thr_id, out_key, out_id, flags,
+                                        n_flagged, qmap);
+    MDH_CUDA(cudaGetLastError());
+}
+
+void launch_merge_topk(const uint32_t* key_all, const int32_t* id_all, int nshard, int nq, int k, uint32_t* key_out,
+                       int32_t* id_out, cudaStream_t st) {
+    if (nq <= 0 || k <= 0) return;
+    int P = 1;
+    while (P < nshard * k) P <<= 1;
+    size_t smem = select_smem(P);
+    MDH_REQUIRE(smem <= 220 * 1024, MDH_ERR_UNSUPPORTED, "nshard * k too large for the merge kernel");
+    if (smem > 48 * 1024)
+        MDH_CUDA(cudaFuncSetAttribute(k_merge_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k_merge_topk<<<nq, 256, smem, st>>>(key_all, id_all, nshard, nq, k, key_out, id_out);
+    MDH_CUDA(cudaGetLastError());
+}
+
+void launch_gather_queries_u8(const uint8_t* src, const int32_t* qn_src, const int32_t* list, int m, int dpad,
+                              uint8_t* dst, int32_t* qn_dst, cudaStream_t st) {
+    if (m <= 0) return;
+    k_gather_queries_u8<<<m, 64, 0, st>>>(src, qn_src, list, m, dpad, dst, qn_dst);
+    MDH_CUDA(cudaGetLastError());
+}
+
+}  // namespace mdh
