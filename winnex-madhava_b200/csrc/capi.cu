@@ -107,7 +107,10 @@ std::vector<LevelStep> plan_levels(const Shard& sh, int k) {
         throw Error(MDH_ERR_UNSUPPORTED, "k = " + std::to_string(k) +
                                              " is larger than this build's exact selector supports for a corpus of " +
                                              std::to_string(sh.n) + " rows");
-    const int cap_floor = next_pow2(std::max(k, 64));
+    // A list must hold more than k entries: the rerun threshold (k-th
+    // smallest stored key) is then strictly below the largest stored key,
+    // so every overflow round makes progress even when distances tie.
+    const int cap_floor = next_pow2(std::max(k + 1, 64));
     auto limit = [&](int cap) { return g_cap_limit > 0 ? std::max(cap_floor, std::min(cap, g_cap_limit)) : cap; };
     steps.push_back({i0, limit(next_pow2(std::max<int64_t>(sh.levels[i0].n, k))), true});
     const double rmax = std::max(4.0, 2048.0 / (double)k);
@@ -205,6 +208,7 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
     growT(&w.out_id, &w.out_id_bytes, (size_t)nq * k * 4);
     growT(&w.flags, &w.flags_bytes, (size_t)nq * 4);
     ensure_status(w);
+    MDH_CUDA(cudaMemsetAsync(w.status, 0, 2 * sizeof(int32_t), st));
 
     res.levels = (int)steps.size();
     for (size_t si = 0; si < steps.size(); si++) {
