@@ -62,7 +62,7 @@ typedef struct {
     int64_t pairs_pruned_by_bound;/* pairs skipped by the norm lower bound */
     int64_t bound_violations;     /* pruned pairs that belonged in the top-K: measured, must be 0 */
     int64_t candidates;           /* pairs that passed the threshold filter into the final selection */
-    int32_t tensor_core_path;     /* 1 when the tcgen05 tensor-core scan ran */
+    int32_t tensor_core_path;     /* full-corpus scan: 0 CUDA cores, 1 tcgen05 per SM, 2 tcgen05 on SM pairs */
     int32_t levels;               /* threshold-refinement levels run */
     double full_scan_ms;          /* CUDA-event time of the full-corpus scan kernel(s) on their stream */
     int64_t full_scan_pairs;      /* (query, row) pairs that kernel scored */
@@ -139,8 +139,9 @@ mdh_status mdh_merge_topk_device(const int32_t* dev_dist_all, const int32_t* dev
                                  void* stream);
 
 /* Options (process-wide): force the scan path for testing and measurement.
- * path: 0 = automatic, 1 = CUDA-core scan only, 2 = tensor-core scan
- * whenever the shape allows. */
+ * path: 0 = automatic, 1 = CUDA-core scan only, 2 = tensor-core scan on
+ * single SMs, 3 = tensor-core scan on SM pairs (each whenever the shape
+ * allows; otherwise the CUDA-core scan). */
 mdh_status mdh_set_scan_path(int32_t path);
 
 /* Options (process-wide): upper bound on a query's candidate list length

@@ -34,19 +34,20 @@ def _search_u8(L, h, Q, k):
     return ids, dist, s
 
 
-@pytest.mark.parametrize("path", [1, 0])
+@pytest.mark.parametrize("path", [1, 2, 3, 0])
 def test_search_u8_distances_exact(path):
     L = capi()
     L.mdh_set_scan_path(path)
     try:
         C = cases.gmm_u8(300_000, 128, 256, seed=21)
-        Q = cases.gmm_u8_queries(300, 128, 256, seed_means=21, seed_q=22)
+        Q = cases.gmm_u8_queries(1300, 128, 256, seed_means=21, seed_q=22)
         h = _create_u8(L, C)
         ids, dist, s = _search_u8(L, h, Q, 10)
         want_ids, want_d = oracle.l2_exact_u8_int(C, Q, 10)
         np.testing.assert_array_equal(ids, want_ids)
         np.testing.assert_array_equal(dist, want_d)
         assert s.bound_violations == 0 and s.pairs_scored >= C.shape[0] * len(Q)
+        assert s.tensor_core_path == {1: 0, 2: 1, 3: 2, 0: 2}[path]
         assert L.mdh_index_destroy(h) == 0
     finally:
         L.mdh_set_scan_path(0)

@@ -106,9 +106,9 @@ def test_fixture_parity_clustered():
     _check_case(X, X[:16], res)
 
 
-@pytest.mark.parametrize("path", [1, 2])
+@pytest.mark.parametrize("path", [1, 2, 3])
 def test_scan_paths_agree(path):
-    """CUDA-core and tensor-core scans give identical lists (and distances)."""
+    """CUDA-core, single-SM and SM-pair tensor-core scans give identical lists."""
     C, Q = cases.case_gmm()
     wm._native.set_scan_path(path)
     got = _run_exact(C, Q, 10, wm.Metric.L2)

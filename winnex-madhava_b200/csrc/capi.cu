@@ -159,24 +159,44 @@ void ensure_status(Workspace& w) {
 }
 
 // Run one level's filter for `nq` queries already staged in the workspace.
-void run_filter(mdh_index* ix, Shard& sh, const Level& lv, const QueryPlan& qp, const uint8_t* q_u8,
-                const int32_t* qn, const float* q_f32, int nq, const uint32_t* tk, const int32_t* ti, int cap) {
+// dense: every row of the level is a candidate (first level, infinite
+// thresholds, cap >= rows); the kernels write row r at slot r and the
+// counts are set to the row count here.
+// Returns the scan used: 1 CUDA cores, 2 tensor cores (one SM per tile),
+// 3 tensor cores (SM pairs).
+constexpr int kPairMinQueries = 1024;  // below this a 512-query pair group is mostly empty
+
+int run_filter(mdh_index* ix, Shard& sh, const Level& lv, const QueryPlan& qp, const uint8_t* q_u8,
+               const int32_t* qn, const float* q_f32, int nq, const uint32_t* tk, const int32_t* ti, int cap,
+               bool dense) {
     Workspace& w = sh.ws;
+    const int d = dense ? 1 : 0;
+    int used = 1;
     if (qp.integer) {
         if (ix->metric == MDH_METRIC_L2) {
-            bool use_tc = g_scan_path != 1 && lv.has_tmap && tc_supported(ix, lv) && (g_scan_path == 2 || nq >= 64);
-            if (use_tc) {
-                MDH_CUDA(cudaMemsetAsync(w.status, 0, sizeof(int32_t), sh.stream));
-                launch_filter_tc_u8_l2(lv, ix->dpad, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, w.status, sh.stream);
-            } else {
-                launch_filter_simt_u8_l2(lv, ix->dpad, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, sh.stream);
-            }
+            const bool can1 = lv.has_tmap && tc_supported(ix, lv);
+            const bool can2 = lv.has_tmap_pair && tc2_supported(ix, lv);
+            if (g_scan_path == 3 && can2)
+                used = 3;
+            else if (g_scan_path == 2 && can1)
+                used = 2;
+            else if (g_scan_path == 0)
+                used = (can2 && nq >= kPairMinQueries) ? 3 : ((can1 && nq >= 64) ? 2 : 1);
+            if (used == 3)
+                launch_filter_tc2_u8_l2(lv, ix->dpad, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, d, w.status,
+                                        sh.stream);
+            else if (used == 2)
+                launch_filter_tc_u8_l2(lv, ix->dpad, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, d, w.status, sh.stream);
+            else
+                launch_filter_simt_u8_l2(lv, ix->dpad, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, d, sh.stream);
         } else {
-            launch_filter_simt_u8_cos(lv, ix->dpad, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, sh.stream);
+            launch_filter_simt_u8_cos(lv, ix->dpad, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, d, sh.stream);
         }
     } else {
-        launch_filter_f32(lv, ix->dim, ix->dpad, qp.kind, q_f32, nq, tk, ti, w.counts, w.cand, cap, sh.stream);
+        launch_filter_f32(lv, ix->dim, ix->dpad, qp.kind, q_f32, nq, tk, ti, w.counts, w.cand, cap, d, sh.stream);
     }
+    if (dense) launch_fill_u32(w.counts, nq, (uint32_t)lv.n, sh.stream);
+    return used;
 }
 
 struct ShardResult {
@@ -186,6 +206,7 @@ struct ShardResult {
     bool tc = false;
     double scan_ms = 0.0;     // event time of the full-shard filter
     int64_t scan_pairs = 0;
+    int scan_path = 0;        // run_filter's path for the full shard
 };
 
 // Exact top-k for nq staged queries on one shard.  Results: ws.out_key /
@@ -224,19 +245,19 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
             }
             MDH_CUDA(cudaEventRecord(w.ev0, st));
         }
-        run_filter(ix, sh, lv, qp, w.q_u8, w.qn, w.q_f32, nq, w.thr_key, w.thr_id, s.cap);
+        const int used = run_filter(ix, sh, lv, qp, w.q_u8, w.qn, w.q_f32, nq, w.thr_key, w.thr_id, s.cap,
+                                    s.dense && s.cap >= lv.n);
         if (last_level) {
             MDH_CUDA(cudaEventRecord(w.ev1, st));
             res.scan_pairs = lv.n * (int64_t)nq;
+            res.scan_path = used;
         }
         res.pairs += lv.n * (int64_t)nq;
-        if (qp.integer && ix->metric == MDH_METRIC_L2 && lv.has_tmap && g_scan_path != 1 &&
-            (g_scan_path == 2 || nq >= 64))
-            res.tc = true;
+        if (used >= 2) res.tc = true;
         const bool final_ = si + 1 == steps.size();
         if (final_) MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
-        launch_select(w.counts, w.cand, s.cap, nq, k, final_ ? 1 : 0, w.thr_key, w.thr_id, w.out_key, w.out_id,
-                      w.flags, w.status + 1, nullptr, st);
+        launch_select(w.counts, w.cand, s.cap, lv.ids, nq, k, final_ ? 1 : 0, w.thr_key, w.thr_id, w.out_key,
+                      w.out_id, w.flags, w.status + 1, nullptr, st);
     }
     // Status words: [0] device error of the tensor-core scan, [1] overflowed queries.
     MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
@@ -305,9 +326,9 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
             MDH_CUDA(cudaStreamSynchronize(st));
         }
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
-        run_filter(ix, sh, lv, qp, cq_u8, cqn, cq_f32, m, d_tk, d_ti, last.cap);
+        run_filter(ix, sh, lv, qp, cq_u8, cqn, cq_f32, m, d_tk, d_ti, last.cap, false);
         MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
-        launch_select(w.counts, w.cand, last.cap, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id, w.flags,
+        launch_select(w.counts, w.cand, last.cap, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id, w.flags,
                       w.status + 1, d_list, st);
         MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
         MDH_CUDA(cudaStreamSynchronize(st));
@@ -473,7 +494,7 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
         for (auto& r : sres) {
             st.pairs_scored += r.pairs;
             st.levels = std::max(st.levels, r.levels);
-            st.tensor_core_path |= r.tc ? 1 : 0;
+            st.tensor_core_path = std::max(st.tensor_core_path, r.scan_path - 1);
             st.full_scan_pairs += r.scan_pairs;
             chunk_scan_ms = std::max(chunk_scan_ms, r.scan_ms);  // shards run concurrently
         }
@@ -698,7 +719,7 @@ mdh_status mdh_search_u8_device(mdh_index* index, const uint8_t* dev_queries, in
                 if (kk > 0) r = search_shard(index, sh, qp, nq, kk, nullptr, nullptr, 0);
                 st.pairs_scored = r.pairs;
                 st.levels = r.levels;
-                st.tensor_core_path = r.tc ? 1 : 0;
+                st.tensor_core_path = std::max(0, r.scan_path - 1);
                 st.full_scan_ms = r.scan_ms;
                 st.full_scan_pairs = r.scan_pairs;
                 if (kk == k) {
@@ -743,7 +764,7 @@ mdh_status mdh_merge_topk_device(const int32_t* dev_dist_all, const int32_t* dev
 
 mdh_status mdh_set_scan_path(int32_t path) {
     return guard([&] {
-        MDH_REQUIRE(path >= 0 && path <= 2, MDH_ERR_INVALID_ARG, "path must be 0, 1 or 2");
+        MDH_REQUIRE(path >= 0 && path <= 3, MDH_ERR_INVALID_ARG, "path must be 0, 1, 2 or 3");
         g_scan_path = path;
     });
 }

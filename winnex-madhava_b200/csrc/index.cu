@@ -250,8 +250,10 @@ void build_shard_u8(mdh_index* ix, Shard& sh, const uint8_t* host_rows, int64_t 
     sh.levels.clear();
     sh.levels.push_back(full);
     build_samples(ix, sh, true, false);
-    for (Level& lv : sh.levels)
+    for (Level& lv : sh.levels) {
         if (tc_supported(ix, lv)) make_tmap_rows(lv, dpad);
+        if (tc2_supported(ix, lv)) make_tmap_rows_pair(lv, dpad);
+    }
     MDH_CUDA(cudaStreamSynchronize(st));
 }
 

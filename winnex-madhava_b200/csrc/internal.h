@@ -23,8 +23,10 @@ struct Level {
     int32_t* ids = nullptr;  // [n_pad] global row id
     float* rows_f32 = nullptr;   // [n_pad][dim] float rows (float corpora / float-score paths)
     float* norms_f32 = nullptr;  // [n_pad] float |v|^2 (SpeedEngine semantics)
-    CUtensorMap tmap_rows;   // TMA map over `rows` (tensor-core scan), valid if has_tmap
+    CUtensorMap tmap_rows;   // TMA map over `rows` (1-SM tensor-core scan), valid if has_tmap
     bool has_tmap = false;
+    CUtensorMap tmap_rows_pair;  // TMA map over `rows` with half-tile boxes (2-SM scan)
+    bool has_tmap_pair = false;
     bool owns = true;        // false when aliasing another level's buffers
 };
 
@@ -81,16 +83,19 @@ void ensure(void** p, size_t* have, size_t need);
 // ---- CUDA-core scan kernels (scan_simt.cu) ----
 void launch_query_norms_u8(const uint8_t* q, int nq, int dpad, int32_t* qn, cudaStream_t st);
 // Append every pair with (key, id) <= per-query threshold to the candidate lists.
+// dense = 1: every row is a candidate (infinite threshold, cap >= rows): the
+// candidate of row r is written at slot r without atomics and the caller
+// sets counts to the row count afterwards.
 void launch_filter_simt_u8_l2(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
                               const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts,
-                              uint2* cand, int cap, cudaStream_t st);
+                              uint2* cand, int cap, int dense, cudaStream_t st);
 void launch_filter_simt_u8_cos(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
                                const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts,
-                               uint2* cand, int cap, cudaStream_t st);
+                               uint2* cand, int cap, int dense, cudaStream_t st);
 // Float replicas of the reference arithmetic (float queries).
 void launch_filter_f32(const Level& lv, int dim, int dpad, int score_kind, const float* q, int nq,
                        const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts, uint2* cand,
-                       int cap, cudaStream_t st);
+                       int cap, int dense, cudaStream_t st);
 
 // score_kind values for launch_filter_f32
 enum ScoreKind : int {
@@ -102,11 +107,21 @@ enum ScoreKind : int {
 };
 
 // ---- tensor-core scan (scan_tc.cu) ----
+// TMA map over u8 rows [rows][dpad], 128-byte swizzle, boxes of box_rows rows.
+void encode_u8_rows_tmap(CUtensorMap* map, const void* base, int64_t rows, int dpad, int box_rows);
+// Corpus chunks per query group so that groups x chunks spreads evenly over workers.
+int choose_scan_chunks(int groups, int n_tiles, int workers);
 bool tc_supported(const mdh_index* ix, const Level& lv);
 void make_tmap_rows(Level& lv, int dpad);
 void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
                             const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts,
-                            uint2* cand, int cap, int32_t* status, cudaStream_t st);
+                            uint2* cand, int cap, int dense, int32_t* status, cudaStream_t st);
+// ---- tensor-core scan on SM pairs (scan_tc2.cu) ----
+bool tc2_supported(const mdh_index* ix, const Level& lv);
+void make_tmap_rows_pair(Level& lv, int dpad);
+void launch_filter_tc2_u8_l2(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
+                             const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts,
+                             uint2* cand, int cap, int dense, int32_t* status, cudaStream_t st);
 
 // ---- selection (select.cu) ----
 void launch_fill_threshold(uint32_t* thr_key, int32_t* thr_id, int nq, uint32_t key, int32_t id,
@@ -114,7 +129,9 @@ void launch_fill_threshold(uint32_t* thr_key, int32_t* thr_id, int nq, uint32_t 
 // final == 0: write the k-th smallest stored (key, id) per query into thr.
 // final == 1: write the sorted top-k to out_key/out_id; set flags[q] = 1 and
 //             thr[q] when the candidate list overflowed (result not final).
-void launch_select(const uint32_t* counts, const uint2* cand, int cap, int nq, int k, int final_,
+void launch_fill_u32(uint32_t* p, int n, uint32_t v, cudaStream_t st);
+// Candidates hold {key, row position in the scanned level}; ids maps positions to global ids.
+void launch_select(const uint32_t* counts, const uint2* cand, int cap, const int32_t* ids, int nq, int k, int final_,
                    uint32_t* thr_key, int32_t* thr_id, uint32_t* out_key, int32_t* out_id,
                    int32_t* flags, int32_t* n_flagged, const int32_t* qmap, cudaStream_t st);
 void launch_merge_topk(const uint32_t* key_all, const int32_t* id_all, int nshard, int nq, int k,

@@ -3,9 +3,11 @@
 // Contract shared by every filter kernel (CUDA-core here, tensor-core in
 // scan_tc.cu): for each query q and each real row r of a Level, compute the
 // rank key of (q, r); when (key, id[r]) <= (thr_key[q], thr_id[q]) append
-// {key, id} to query q's candidate list (slot = atomicAdd(counts[q]), stored
-// only while slot < cap).  The selection step (select.cu) turns candidate
-// lists into thresholds or final top-k lists.
+// {key, r} to query q's candidate list (slot = atomicAdd(counts[q]), stored
+// only while slot < cap).  On a dense level (infinite thresholds, cap >= rows)
+// row r goes to slot r with no atomics.  The selection step (select.cu) maps
+// row positions to ids and turns candidate lists into thresholds or final
+// top-k lists.
 //
 // Integer u8 kernels: 8 lanes cover one 128-byte row segment (16 bytes per
 // lane, 128-bit loads, a warp reads 512 contiguous bytes), __dp4a forms the
@@ -76,10 +78,18 @@ __device__ __forceinline__ void reduce_scatter8(uint32_t (&s)[QG], int l8, int& 
     active = act;
 }
 
-__device__ __forceinline__ void append_candidate(uint32_t* counts, uint2* cand, int cap, int q, uint32_t key,
-                                                 int32_t id) {
+// Offer row `pos` (key) of query q: dense levels write slot = pos; otherwise
+// rows within the threshold (ties resolved by global id) take the next slot.
+__device__ __forceinline__ void offer_candidate(uint32_t* counts, uint2* cand, int cap, int dense, int q, uint32_t key,
+                                                int64_t pos, const int32_t* ids, uint32_t tkey, int32_t tid) {
+    if (dense) {
+        cand[(size_t)q * cap + pos] = make_uint2(key, (uint32_t)pos);
+        return;
+    }
+    if (key > tkey) return;
+    if (key == tkey && __ldg(ids + pos) > tid) return;
     uint32_t slot = atomicAdd(counts + q, 1u);
-    if (slot < (uint32_t)cap) cand[(size_t)q * cap + slot] = make_uint2(key, (uint32_t)id);
+    if (slot < (uint32_t)cap) cand[(size_t)q * cap + slot] = make_uint2(key, (uint32_t)pos);
 }
 
 // MODE 0: L2 (key = |q|^2 + |v|^2 - 2 q.v, exact integer)
@@ -90,7 +100,7 @@ __global__ void __launch_bounds__(256) k_filter_u8(
     const uint8_t* __restrict__ rows, const int32_t* __restrict__ norms, const int32_t* __restrict__ ids,
     int64_t n, int64_t n_pad, int dpad, const uint8_t* __restrict__ q, const int32_t* __restrict__ qn, int nq,
     const uint32_t* __restrict__ thr_key, const int32_t* __restrict__ thr_id, uint32_t* __restrict__ counts,
-    uint2* __restrict__ cand, int cap) {
+    uint2* __restrict__ cand, int cap, int dense) {
     const int lane = threadIdx.x & 31;
     const int l8 = lane & 7;
     const int grp = lane >> 3;
@@ -173,10 +183,7 @@ __global__ void __launch_bounds__(256) k_filter_u8(
                     float sc = denom > 1e-10f ? __fdiv_rn((float)dot, denom) : 0.0f;
                     key = ordered_key_desc(sc);
                 }
-                if (key <= tkey) {
-                    const int32_t id = __ldg(ids + r[u]);
-                    if (within_threshold(key, id, tkey, tid)) append_candidate(counts, cand, cap, qi, key, id);
-                }
+                offer_candidate(counts, cand, cap, dense, qi, key, r[u], ids, tkey, tid);
             }
         }
     }
@@ -190,7 +197,7 @@ __global__ void __launch_bounds__(128) k_filter_f32(
     const uint8_t* __restrict__ rows_u8, const float* __restrict__ rows_f32, const int32_t* __restrict__ norms_i,
     const float* __restrict__ norms_f, const int32_t* __restrict__ ids, int64_t n, int dim, int dpad,
     const float* __restrict__ q, const float* __restrict__ qaux, int nq, const uint32_t* __restrict__ thr_key,
-    const int32_t* __restrict__ thr_id, uint32_t* __restrict__ counts, uint2* __restrict__ cand, int cap) {
+    const int32_t* __restrict__ thr_id, uint32_t* __restrict__ counts, uint2* __restrict__ cand, int cap, int dense) {
     extern __shared__ float sq[];  // [QG][dim]
     const int q0 = blockIdx.y * QG;
     for (int i = threadIdx.x; i < QG * dim; i += blockDim.x) {
@@ -266,7 +273,6 @@ __global__ void __launch_bounds__(128) k_filter_f32(
         }
     }
 
-    const int32_t id = __ldg(ids + r);
 #pragma unroll
     for (int j = 0; j < QG; j++) {
         const int qi = q0 + j;
@@ -325,13 +331,13 @@ __global__ void __launch_bounds__(128) k_filter_f32(
             }
             key = ordered_key_desc(s);
         }
-        if (within_threshold(key, id, thr_key[qi], thr_id[qi])) append_candidate(counts, cand, cap, qi, key, id);
+        offer_candidate(counts, cand, cap, dense, qi, key, r, ids, thr_key[qi], thr_id[qi]);
     }
 }
 
 template <int QG, int SEGS, int MODE>
 void launch_u8_t(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq, const uint32_t* tk,
-                 const int32_t* ti, uint32_t* counts, uint2* cand, int cap, cudaStream_t st) {
+                 const int32_t* ti, uint32_t* counts, uint2* cand, int cap, int dense, cudaStream_t st) {
     int dev;
     MDH_CUDA(cudaGetDevice(&dev));
     const int sms = device_sm_count(dev);
@@ -346,28 +352,28 @@ void launch_u8_t(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn,
     MDH_REQUIRE(groups <= 65535, MDH_ERR_INTERNAL, "too many query groups for one launch");
     dim3 grid((unsigned)bx, (unsigned)groups);
     k_filter_u8<QG, SEGS, MODE><<<grid, 256, 0, st>>>(lv.rows, lv.norms, lv.ids, lv.n, lv.n_pad, dpad, q, qn, nq, tk,
-                                                      ti, counts, cand, cap);
+                                                      ti, counts, cand, cap, dense);
     MDH_CUDA(cudaGetLastError());
 }
 
 template <int MODE>
 void launch_u8_dispatch(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq, const uint32_t* tk,
-                        const int32_t* ti, uint32_t* counts, uint2* cand, int cap, cudaStream_t st) {
+                        const int32_t* ti, uint32_t* counts, uint2* cand, int cap, int dense, cudaStream_t st) {
     const int segs = dpad / 128;
     if (segs == 1) {
         if (nq >= 8)
-            launch_u8_t<8, 1, MODE>(lv, dpad, q, qn, nq, tk, ti, counts, cand, cap, st);
+            launch_u8_t<8, 1, MODE>(lv, dpad, q, qn, nq, tk, ti, counts, cand, cap, dense, st);
         else if (nq >= 4)
-            launch_u8_t<4, 1, MODE>(lv, dpad, q, qn, nq, tk, ti, counts, cand, cap, st);
+            launch_u8_t<4, 1, MODE>(lv, dpad, q, qn, nq, tk, ti, counts, cand, cap, dense, st);
         else if (nq >= 2)
-            launch_u8_t<2, 1, MODE>(lv, dpad, q, qn, nq, tk, ti, counts, cand, cap, st);
+            launch_u8_t<2, 1, MODE>(lv, dpad, q, qn, nq, tk, ti, counts, cand, cap, dense, st);
         else
-            launch_u8_t<1, 1, MODE>(lv, dpad, q, qn, nq, tk, ti, counts, cand, cap, st);
+            launch_u8_t<1, 1, MODE>(lv, dpad, q, qn, nq, tk, ti, counts, cand, cap, dense, st);
     } else if (segs == 2) {
         if (nq >= 4)
-            launch_u8_t<4, 2, MODE>(lv, dpad, q, qn, nq, tk, ti, counts, cand, cap, st);
+            launch_u8_t<4, 2, MODE>(lv, dpad, q, qn, nq, tk, ti, counts, cand, cap, dense, st);
         else
-            launch_u8_t<1, 2, MODE>(lv, dpad, q, qn, nq, tk, ti, counts, cand, cap, st);
+            launch_u8_t<1, 2, MODE>(lv, dpad, q, qn, nq, tk, ti, counts, cand, cap, dense, st);
     } else {
         throw Error(MDH_ERR_INTERNAL, "integer u8 scan supports dim <= 256");
     }
@@ -375,7 +381,7 @@ void launch_u8_dispatch(const Level& lv, int dpad, const uint8_t* q, const int32
 
 template <int KIND>
 void launch_f32_t(const Level& lv, int dim, int dpad, const float* q, const float* qaux, int nq, const uint32_t* tk,
-                  const int32_t* ti, uint32_t* counts, uint2* cand, int cap, cudaStream_t st) {
+                  const int32_t* ti, uint32_t* counts, uint2* cand, int cap, int dense, cudaStream_t st) {
     constexpr int QG = 4;
     const int groups = (nq + QG - 1) / QG;
     MDH_REQUIRE(groups <= 65535, MDH_ERR_INTERNAL, "too many query groups for one launch");
@@ -386,7 +392,7 @@ void launch_f32_t(const Level& lv, int dim, int dpad, const float* q, const floa
     dim3 grid((unsigned)((lv.n + 127) / 128), (unsigned)groups);
     if (lv.n == 0) return;
     k_filter_f32<KIND, QG><<<grid, 128, smem, st>>>(lv.rows, lv.rows_f32, lv.norms, lv.norms_f32, lv.ids, lv.n, dim,
-                                                    dpad, q, qaux, nq, tk, ti, counts, cand, cap);
+                                                    dpad, q, qaux, nq, tk, ti, counts, cand, cap, dense);
     MDH_CUDA(cudaGetLastError());
 }
 
@@ -402,31 +408,31 @@ void launch_query_norms_u8(const uint8_t* q, int nq, int dpad, int32_t* qn, cuda
 
 void launch_filter_simt_u8_l2(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
                               const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts, uint2* cand,
-                              int cap, cudaStream_t st) {
+                              int cap, int dense, cudaStream_t st) {
     if (nq <= 0 || lv.n == 0) return;
-    launch_u8_dispatch<0>(lv, dpad, q, qn, nq, thr_key, thr_id, counts, cand, cap, st);
+    launch_u8_dispatch<0>(lv, dpad, q, qn, nq, thr_key, thr_id, counts, cand, cap, dense, st);
 }
 
 void launch_filter_simt_u8_cos(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
                                const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts, uint2* cand,
-                               int cap, cudaStream_t st) {
+                               int cap, int dense, cudaStream_t st) {
     if (nq <= 0 || lv.n == 0) return;
-    launch_u8_dispatch<1>(lv, dpad, q, qn, nq, thr_key, thr_id, counts, cand, cap, st);
+    launch_u8_dispatch<1>(lv, dpad, q, qn, nq, thr_key, thr_id, counts, cand, cap, dense, st);
 }
 
 void launch_filter_f32(const Level& lv, int dim, int dpad, int score_kind, const float* q, int nq,
                        const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts, uint2* cand, int cap,
-                       cudaStream_t st) {
+                       int dense, cudaStream_t st) {
     if (nq <= 0 || lv.n == 0) return;
     // qaux (per-query |q|^2 for the cosine scores) is stored right after the
     // nq x dim query block by the caller.
     const float* qaux = q + (size_t)nq * dim;
     switch (score_kind) {
-        case kScoreL2SqU8: launch_f32_t<kScoreL2SqU8>(lv, dim, dpad, q, qaux, nq, thr_key, thr_id, counts, cand, cap, st); break;
-        case kScoreCosU8: launch_f32_t<kScoreCosU8>(lv, dim, dpad, q, qaux, nq, thr_key, thr_id, counts, cand, cap, st); break;
-        case kScoreSpeedL2: launch_f32_t<kScoreSpeedL2>(lv, dim, dpad, q, qaux, nq, thr_key, thr_id, counts, cand, cap, st); break;
-        case kScoreSpeedCos: launch_f32_t<kScoreSpeedCos>(lv, dim, dpad, q, qaux, nq, thr_key, thr_id, counts, cand, cap, st); break;
-        case kScoreExactCosF32: launch_f32_t<kScoreExactCosF32>(lv, dim, dpad, q, qaux, nq, thr_key, thr_id, counts, cand, cap, st); break;
+        case kScoreL2SqU8: launch_f32_t<kScoreL2SqU8>(lv, dim, dpad, q, qaux, nq, thr_key, thr_id, counts, cand, cap, dense, st); break;
+        case kScoreCosU8: launch_f32_t<kScoreCosU8>(lv, dim, dpad, q, qaux, nq, thr_key, thr_id, counts, cand, cap, dense, st); break;
+        case kScoreSpeedL2: launch_f32_t<kScoreSpeedL2>(lv, dim, dpad, q, qaux, nq, thr_key, thr_id, counts, cand, cap, dense, st); break;
+        case kScoreSpeedCos: launch_f32_t<kScoreSpeedCos>(lv, dim, dpad, q, qaux, nq, thr_key, thr_id, counts, cand, cap, dense, st); break;
+        case kScoreExactCosF32: launch_f32_t<kScoreExactCosF32>(lv, dim, dpad, q, qaux, nq, thr_key, thr_id, counts, cand, cap, dense, st); break;
         default: throw Error(MDH_ERR_INTERNAL, "unknown score kind");
     }
 }

@@ -36,6 +36,11 @@ __device__ __forceinline__ int next_pow2(int x) {
     return p;
 }
 
+__global__ void k_fill_u32(uint32_t* p, int n, uint32_t v) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) p[i] = v;
+}
+
 __global__ void k_fill_threshold(uint32_t* tk, int32_t* ti, int nq, uint32_t key, int32_t id) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < nq) {
@@ -46,7 +51,10 @@ __global__ void k_fill_threshold(uint32_t* tk, int32_t* ti, int nq, uint32_t key
 
 // One CTA per query.  qmap (optional) maps the CTA's query to the slot its
 // threshold / output / flag is written to.
-__global__ void k_select(const uint32_t* __restrict__ counts, const uint2* __restrict__ cand, int cap, int k,
+// Candidates are {key, row position in the scanned level}; `ids` maps a
+// position to its global row id, which breaks ties.
+__global__ void k_select(const uint32_t* __restrict__ counts, const uint2* __restrict__ cand, int cap,
+                         const int32_t* __restrict__ ids, int k,
                          int final_, uint32_t* __restrict__ thr_key, int32_t* __restrict__ thr_id,
                          uint32_t* __restrict__ out_key, int32_t* __restrict__ out_id, int32_t* __restrict__ flags,
                          int32_t* __restrict__ n_flagged, const int32_t* __restrict__ qmap) {
@@ -60,7 +68,7 @@ __global__ void k_select(const uint32_t* __restrict__ counts, const uint2* __res
     for (int i = threadIdx.x; i < P; i += blockDim.x) {
         if (i < c) {
             uint2 e = src[i];
-            keys[i] = ((unsigned long long)e.x << 32) | e.y;
+            keys[i] = ((unsigned long long)e.x << 32) | (uint32_t)__ldg(ids + e.y);
         } else {
             keys[i] = ~0ull;
         }
@@ -149,13 +157,20 @@ size_t select_smem(int P) { return (size_t)P * sizeof(unsigned long long); }
 
 }  // namespace
 
+void launch_fill_u32(uint32_t* p, int n, uint32_t v, cudaStream_t st) {
+    if (n <= 0) return;
+    k_fill_u32<<<(n + 255) / 256, 256, 0, st>>>(p, n, v);
+    MDH_CUDA(cudaGetLastError());
+}
+
 void launch_fill_threshold(uint32_t* thr_key, int32_t* thr_id, int nq, uint32_t key, int32_t id, cudaStream_t st) {
     if (nq <= 0) return;
     k_fill_threshold<<<(nq + 255) / 256, 256, 0, st>>>(thr_key, thr_id, nq, key, id);
     MDH_CUDA(cudaGetLastError());
 }
 
-void launch_select(const uint32_t* counts, const uint2* cand, int cap, int nq, int k, int final_, uint32_t* thr_key,
+void launch_select(const uint32_t* counts, const uint2* cand, int cap, const int32_t* ids, int nq, int k, int final_,
+                   uint32_t* thr_key,
                    int32_t* thr_id, uint32_t* out_key, int32_t* out_id, int32_t* flags, int32_t* n_flagged,
                    const int32_t* qmap, cudaStream_t st) {
     if (nq <= 0) return;
@@ -165,7 +180,7 @@ void launch_select(const uint32_t* counts, const uint2* cand, int cap, int nq, i
     MDH_REQUIRE(smem <= 220 * 1024, MDH_ERR_UNSUPPORTED, "candidate list too large for the selection kernel");
     if (smem > 48 * 1024) MDH_CUDA(cudaFuncSetAttribute(k_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int threads = pmax >= 4096 ? 1024 : (pmax >= 1024 ? 512 : 256);
-    k_select<<<nq, threads, smem, st>>>(counts, cand, cap, k, final_, thr_key, thr_id, out_key, out_id, flags,
+    k_select<<<nq, threads, smem, st>>>(counts, cand, cap, ids, k, final_, thr_key, thr_id, out_key, out_id, flags,
                                         n_flagged, qmap);
     MDH_CUDA(cudaGetLastError());
 }
