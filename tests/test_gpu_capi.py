@@ -47,7 +47,7 @@ def test_search_u8_distances_exact(path):
         np.testing.assert_array_equal(ids, want_ids)
         np.testing.assert_array_equal(dist, want_d)
         assert s.bound_violations == 0 and s.pairs_scored >= C.shape[0] * len(Q)
-        assert s.tensor_core_path == {1: 0, 2: 1, 3: 2, 0: 2}[path]
+        assert s.tensor_core_path == {1: 0, 2: 1, 3: 2, 0: 1}[path]
         assert L.mdh_index_destroy(h) == 0
     finally:
         L.mdh_set_scan_path(0)

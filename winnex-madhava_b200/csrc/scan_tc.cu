@@ -6,29 +6,30 @@
 // (key, id) <= (thr_key[q], thr_id[q]) are appended to q's candidate list as
 // {key, r}; on a dense level (infinite thresholds) row r goes to slot r.
 //
-// Tile: 128 queries (TMEM lanes, the MMA's M) x 128 corpus rows (the MMA's N)
-// x 128 bytes (K: four kind::i8 MMAs of K = 32).  u8 x u8 products
-// accumulate exactly in s32 in tensor memory.  Operands are staged by TMA
-// with the 128-byte swizzle (one 128-byte row per vector = one swizzle row);
-// each tile's 128 row norms follow by a 512-byte bulk copy into a norm ring.
-// Four accumulator stages (all 512 TMEM columns) keep the MMA ahead of the
+// Tile: 128 queries (TMEM lanes, the MMA's M) x BN corpus rows (the MMA's N,
+// 128 or 256) x 128 bytes (K: four kind::i8 MMAs of K = 32).  u8 x u8
+// products accumulate exactly in s32 in tensor memory.  Operands are staged
+// by TMA with the 128-byte swizzle (one 128-byte row per vector = one swizzle
+// row).  512 / BN accumulator stages (all of TMEM) keep the MMA ahead of the
 // epilogue.
 //
 // Warp roles (576 threads, one CTA per SM, persistent):
 //   warps 0-15 epilogue: warp w reads TMEM lanes 32*(w%4).. (thread = one
-//              query) and the 32 columns [32*(w/4), +32) of each accumulator;
-//              the chunk is copied to registers and the accumulator released
-//              before the Cauchy-Schwarz chunk filter runs; passing rows are
-//              buffered per thread in shared memory, one atomic per flush;
-//   warp 16    TMA producer (query tile once per work unit, corpus tiles and
-//              their norms through a STAGES-deep ring);
+//              query) and columns [BN/4*(w/4), +BN/4) of each accumulator
+//              (one or two 32-column chunks); the chunks are copied to
+//              registers and the accumulator released before the
+//              Cauchy-Schwarz chunk filter runs; passing rows are buffered per
+//              thread in shared memory, one atomic per flush;
+//   warp 16    TMA producer (query tile once per work unit, corpus tiles
+//              through a STAGES-deep ring);
 //   warp 17    TMEM allocator + single-thread MMA issuer.
 //
 // Epilogue filter: rows are sorted by |v|^2, so the first row of each
 // 32-row chunk has the chunk's smallest norm n_min.  With m = max q.v over
 // the chunk, every key in the chunk is >= |q|^2 + n_min - 2m; when that
 // exceeds the query's threshold the whole chunk is skipped after one max
-// reduction (tc_ptx.cuh: max32).
+// reduction (tc_ptx.cuh: max32).  n_min is read from L2 one tile ahead; the
+// rare chunks that pass are expanded by a bit-mask loop.
 //
 // Work units: (query tile, corpus chunk), ordered chunk-major so the CTAs
 // running at the same time share corpus chunks through L2; each CTA takes
@@ -50,40 +51,37 @@ namespace {
 
 using namespace tc;
 
+#ifndef MDH_TC1_BN
+#define MDH_TC1_BN 256
+#endif
+
 constexpr int BM = 128;           // queries per tile (TMEM lanes)
-constexpr int BN = 128;           // corpus rows per tile
+constexpr int BN = MDH_TC1_BN;    // corpus rows per tile (MMA N)
 constexpr int BK = 128;           // bytes per row (K)
-constexpr int STAGES = 8;         // corpus tile ring depth
-constexpr int ACC_STAGES = 4;     // 4 x 128 accumulator columns = all of TMEM
 constexpr int TMEM_COLS = 512;
-constexpr int EPI_WARPS = 16;     // 4 per TMEM lane quarter, one 32-column chunk each
+constexpr int ACC_STAGES = TMEM_COLS / BN;
+constexpr int STAGES = 10 * 128 / BN;   // corpus tile ring: 160 KB
+constexpr int EPI_WARPS = 16;     // 4 per TMEM lane quarter
+constexpr int COLS_PER_WARP = BN / 4;
+constexpr int CHUNKS = COLS_PER_WARP / 32;
 constexpr int EPI_THREADS = 32 * EPI_WARPS;
 constexpr int PRODUCER_WARP = EPI_WARPS;
 constexpr int MMA_WARP = EPI_WARPS + 1;
 constexpr int NUM_THREADS = 32 * (EPI_WARPS + 2);
-static_assert(BN == 32 * (EPI_WARPS / 4), "one 32-column chunk per epilogue warp");
-// Norm slots: the producer issues tile i's norms only after the MMA of tile
-// i - STAGES finished, which needed every epilogue warp to release the
-// accumulator of tile i - STAGES - ACC_STAGES, i.e. to have finished every
-// earlier tile; one extra slot covers the tile whose accumulator was released
-// but whose chunk is still being filtered.
-constexpr int NSLOTS = STAGES + ACC_STAGES + 1;
+static_assert(BN == 128 || BN == 256, "one or two 32-column chunks per epilogue warp");
 constexpr int BUFN = 4;           // buffered candidates per epilogue thread
 constexpr uint32_t A_BYTES = BM * BK;
 constexpr uint32_t B_BYTES = BN * BK;
-constexpr uint32_t NORM_BYTES = BN * 4;
 constexpr uint32_t IDESC = idesc_u8(BM, BN);
 
 // Shared memory map (offsets from a 1024-byte aligned base).
 constexpr uint32_t OFF_A = 0;
 constexpr uint32_t OFF_B = OFF_A + A_BYTES;
-constexpr uint32_t OFF_NORM = OFF_B + STAGES * B_BYTES;
-constexpr uint32_t OFF_BUF = OFF_NORM + NSLOTS * NORM_BYTES;
+constexpr uint32_t OFF_BUF = OFF_B + STAGES * B_BYTES;
 constexpr uint32_t OFF_BAR = OFF_BUF + BUFN * EPI_THREADS * 8;
 constexpr uint32_t BAR_FULL = 0, BAR_EMPTY = STAGES, BAR_ACC_FULL = 2 * STAGES,
-                   BAR_ACC_EMPTY = 2 * STAGES + ACC_STAGES, BAR_NORM_FULL = 2 * STAGES + 2 * ACC_STAGES,
-                   BAR_A_FULL = BAR_NORM_FULL + NSLOTS, BAR_A_EMPTY = BAR_A_FULL + 1, BAR_DRAIN = BAR_A_FULL + 2,
-                   NUM_BARS = BAR_A_FULL + 3;
+                   BAR_ACC_EMPTY = 2 * STAGES + ACC_STAGES, BAR_A_FULL = 2 * STAGES + 2 * ACC_STAGES,
+                   BAR_A_EMPTY = BAR_A_FULL + 1, BAR_DRAIN = BAR_A_FULL + 2, NUM_BARS = BAR_A_FULL + 3;
 constexpr uint32_t OFF_TMEM_SLOT = OFF_BAR + NUM_BARS * 8;
 constexpr uint32_t OFF_ABORT = OFF_TMEM_SLOT + 4;
 constexpr uint32_t SMEM_USED = OFF_ABORT + 4;
@@ -116,7 +114,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t bars = sbase + OFF_BAR;
     volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + OFF_ABORT);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM_SLOT);
-    const int32_t* norm_smem = reinterpret_cast<const int32_t*>(smem + OFF_NORM);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
@@ -129,7 +126,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(bars + 8 * (BAR_ACC_FULL + s), 1);
             mbar_init(bars + 8 * (BAR_ACC_EMPTY + s), EPI_WARPS);
         }
-        for (int s = 0; s < NSLOTS; s++) mbar_init(bars + 8 * (BAR_NORM_FULL + s), 1);
         mbar_init(bars + 8 * BAR_A_FULL, 1);
         mbar_init(bars + 8 * BAR_A_EMPTY, 1);
         mbar_init(bars + 8 * BAR_DRAIN, 1);
@@ -149,7 +145,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_rows) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_q) : "memory");
             int stage = 0;
-            uint32_t phase = 0, a_iter = 0, tile_seq = 0;
+            uint32_t phase = 0, a_iter = 0;
             uint32_t issued_mask = 0, last_parity = 0;
             bool a_issued = false;
             bool ok = true;
@@ -162,16 +158,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tma_load_2d(sbase + OFF_A, &tmap_q, bars + 8 * BAR_A_FULL, 0, g * BM);
                 a_issued = true;
                 a_iter++;
-                for (int t = t0; t < t1; t++, tile_seq++) {
+                for (int t = t0; t < t1; t++) {
                     ok = mbar_wait<false>(bars + 8 * (BAR_EMPTY + stage), phase ^ 1, abort_flag, status);
                     if (!ok) break;
                     mbar_expect_tx(bars + 8 * (BAR_FULL + stage), B_BYTES);
                     tma_load_2d(sbase + OFF_B + stage * B_BYTES, &tmap_rows, bars + 8 * (BAR_FULL + stage), 0,
                                 t * BN);
-                    const uint32_t ns = tile_seq % NSLOTS;
-                    mbar_expect_tx(bars + 8 * (BAR_NORM_FULL + ns), NORM_BYTES);
-                    bulk_load(sbase + OFF_NORM + ns * NORM_BYTES, norms + (int64_t)t * BN, NORM_BYTES,
-                              bars + 8 * (BAR_NORM_FULL + ns));
                     issued_mask |= 1u << stage;
                     last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == STAGES) {
@@ -185,8 +177,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int s = 0; s < STAGES; s++)
                     if (issued_mask & (1u << s))
                         mbar_drain_wait<false>(bars + 8 * (BAR_FULL + s), (last_parity >> s) & 1);
-                for (uint32_t i = (tile_seq > NSLOTS ? tile_seq - NSLOTS : 0); i < tile_seq; i++)
-                    mbar_drain_wait<false>(bars + 8 * (BAR_NORM_FULL + i % NSLOTS), (i / NSLOTS) & 1);
                 if (a_issued) mbar_drain_wait<false>(bars + 8 * BAR_A_FULL, (a_iter - 1) & 1);
             }
         }
@@ -244,8 +234,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         buf.base = reinterpret_cast<uint2*>(smem + OFF_BUF) + threadIdx.x;
         buf.n = 0;
         int acc = 0;
-        uint32_t acc_phase = 0, tile_seq = 0;
+        uint32_t acc_phase = 0;
         bool ok = true;
+        const int32_t* nrm = norms + part * COLS_PER_WARP;
         for (long long u = blockIdx.x; u < sched.n_units && ok; u += gridDim.x) {
             int g, t0, t1;
             unit_coords(sched, u, g, t0, t1);
@@ -261,48 +252,63 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // A row passes when qn + n - 2v <= tkey; with n >= n_min,
             // 2v >= n_min + bias (bias = qn - tkey) is necessary.  Keys of real
             // rows are below 2^30: an infinite threshold maps to a bias that
-            // always passes, an invalid query to one that never does.
+            // always passes, an invalid query to one that never does (and
+            // keeps n_min + bias below 2^31 for pad rows of norm 2^30).
             int32_t bias;
             if (!qvalid)
-                bias = 1 << 30;
+                bias = 1 << 29;
             else if (tkey >= (1u << 30))
                 bias = -(1 << 30);
             else
                 bias = qnv - (int32_t)tkey;
-            for (int t = t0; t < t1; t++, tile_seq++) {
-                const uint32_t ns = tile_seq % NSLOTS;
-                ok = mbar_wait<false>(bars + 8 * (BAR_ACC_FULL + acc), acc_phase, abort_flag, status);
-                if (ok) ok = mbar_wait<false>(bars + 8 * (BAR_NORM_FULL + ns), (tile_seq / NSLOTS) & 1, abort_flag, status);
+            // n_min of this warp's chunks, one tile ahead of their use.
+            int32_t nx[CHUNKS];
+#pragma unroll
+            for (int c = 0; c < CHUNKS; c++) nx[c] = t0 < t1 ? __ldg(nrm + (int64_t)t0 * BN + 32 * c) : 0;
+            for (int t = t0; t < t1; t++) {
+                int32_t need[CHUNKS];
+#pragma unroll
+                for (int c = 0; c < CHUNKS; c++) {
+                    need[c] = nx[c] + bias;
+                    if (t + 1 < t1) nx[c] = __ldg(nrm + (int64_t)(t + 1) * BN + 32 * c);
+                }
+                ok = mbar_wait_inl<false>(bars + 8 * (BAR_ACC_FULL + acc), acc_phase, abort_flag, status);
                 if (!ok) break;
                 tc_fence_after();
-                const int32_t* tnorm = norm_smem + ns * BN + part * 32;
-                const int32_t rbase = t * BN + part * 32;  // rows < 2^31 (ids are int32)
-                uint32_t v[32];
+                const uint32_t tcol = tmem_base + lane_base + (uint32_t)(acc * BN + part * COLS_PER_WARP);
+                uint32_t v[CHUNKS][32];
                 __syncwarp();
-                tmem_ld32_issue(tmem_base + lane_base + (uint32_t)(acc * BN + part * 32), v);
-                tmem_ld_wait(v);
-                // The chunk is in registers: hand the accumulator back to the MMA.
+#pragma unroll
+                for (int c = 0; c < CHUNKS; c++) tmem_ld32_issue(tcol + 32 * c, v[c]);
+#pragma unroll
+                for (int c = 0; c < CHUNKS; c++) tmem_ld_wait(v[c]);  // the first wait covers every load
+                // The chunks are in registers: hand the accumulator back to the MMA.
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bars + 8 * (BAR_ACC_EMPTY + acc));
-                const int32_t need = tnorm[0] + bias;
-                if (2 * max32(v) >= need) {
-#pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        const int32_t r = rbase + j;
-                        if (2 * (int32_t)v[j] >= need && r < n_rows) {
-                            const uint32_t key = (uint32_t)(qnv + tnorm[j] - 2 * (int32_t)v[j]);
-                            if (dense) {
-                                cand[(size_t)qi * cap + r] = make_uint2(key, (uint32_t)r);
-                            } else if (key < tkey || (key == tkey && __ldg(ids + r) <= tid)) {
-                                buf.push(key, (uint32_t)r, counts, cand, cap, qi);
-                            }
-                        }
-                    }
-                }
                 if (++acc == ACC_STAGES) {
                     acc = 0;
                     acc_phase ^= 1;
+                }
+                bool any = false;
+#pragma unroll
+                for (int c = 0; c < CHUNKS; c++) any |= 2 * max32(v[c]) >= need[c];
+                if (!any) continue;
+                const int32_t row0 = t * BN + part * COLS_PER_WARP;  // rows < 2^31 (ids are int32)
+#pragma unroll
+                for (int c = 0; c < CHUNKS; c++) {
+                    uint32_t mask = pass_mask32(v[c], need[c]);
+                    while (mask) {
+                        const int j = __ffs(mask) - 1;
+                        mask &= mask - 1;
+                        const int32_t r = row0 + 32 * c + j;
+                        if (r >= n_rows) break;  // pad rows trail the level
+                        const uint32_t key = (uint32_t)(qnv + __ldg(norms + r) - 2 * (int32_t)pick32(v[c], j));
+                        if (dense)
+                            cand[(size_t)qi * cap + r] = make_uint2(key, (uint32_t)r);
+                        else if (key < tkey || (key == tkey && __ldg(ids + r) <= tid))
+                            buf.push(key, (uint32_t)r, counts, cand, cap, qi);
+                    }
                 }
             }
             if (qvalid) buf.flush(counts, cand, cap, qi);

@@ -18,9 +18,11 @@
 //              (w/4)%2, columns [64*(w/8), +64): both 32-column chunks are
 //              copied to registers and the accumulator released (a remote
 //              arrive on the even CTA's barrier) before the Cauchy-Schwarz
-//              chunk filter runs;
-//   warp 16    TMA producer: its own two query tiles per work unit, its half
-//              of each corpus tile, and the tile's 128 row norms;
+//              chunk filter runs.  The filter needs only the first (smallest)
+//              norm of each chunk, read from L2 one tile ahead; the rare
+//              chunks that pass are expanded by a bit-mask loop;
+//   warp 16    TMA producer: its own two query tiles per work unit and its
+//              half of each corpus tile;
 //   warp 17    TMEM allocator (both CTAs) and, in the even CTA only, the
 //              single-thread MMA issuer.
 // Barriers with cross-CTA producers live in the even CTA (FULL, A_FULL,
@@ -59,22 +61,19 @@ constexpr int EPI_THREADS = 32 * EPI_WARPS;
 constexpr int PRODUCER_WARP = EPI_WARPS;
 constexpr int MMA_WARP = EPI_WARPS + 1;
 constexpr int NUM_THREADS = 32 * (EPI_WARPS + 2);
-constexpr int NSLOTS = STAGES + ACC_STAGES + 1;  // norm ring (see scan_tc.cu for the argument)
 constexpr int BUFN = 4;
 constexpr uint32_t A_TILE_BYTES = BM * BK;
 constexpr uint32_t A_BYTES = QT * A_TILE_BYTES;
 constexpr uint32_t B_BYTES = BN_HALF * BK;
-constexpr uint32_t NORM_BYTES = BN * 4;
 constexpr uint32_t IDESC = idesc_u8(PAIR_M, BN);
 
 constexpr uint32_t OFF_A = 0;
 constexpr uint32_t OFF_B = OFF_A + A_BYTES;
-constexpr uint32_t OFF_NORM = OFF_B + STAGES * B_BYTES;
-constexpr uint32_t OFF_BUF = OFF_NORM + NSLOTS * NORM_BYTES;
+constexpr uint32_t OFF_BUF = OFF_B + STAGES * B_BYTES;
 constexpr uint32_t OFF_BAR = OFF_BUF + BUFN * EPI_THREADS * 8;
 constexpr uint32_t BAR_FULL = 0, BAR_EMPTY = STAGES, BAR_ACC_FULL = 2 * STAGES,
-                   BAR_ACC_EMPTY = 2 * STAGES + ACC_STAGES, BAR_NORM_FULL = 2 * STAGES + 2 * ACC_STAGES,
-                   BAR_A_FULL = BAR_NORM_FULL + NSLOTS, BAR_A_EMPTY = BAR_A_FULL + 1, BAR_DRAIN = BAR_A_FULL + 2,
+                   BAR_ACC_EMPTY = 2 * STAGES + ACC_STAGES,
+                   BAR_A_FULL = 2 * STAGES + 2 * ACC_STAGES, BAR_A_EMPTY = BAR_A_FULL + 1, BAR_DRAIN = BAR_A_FULL + 2,
                    NUM_BARS = BAR_A_FULL + 3;
 constexpr uint32_t OFF_TMEM_SLOT = OFF_BAR + NUM_BARS * 8;
 constexpr uint32_t OFF_ABORT = OFF_TMEM_SLOT + 4;
@@ -109,7 +108,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t bars = sbase + OFF_BAR;
     volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + OFF_ABORT);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM_SLOT);
-    const int32_t* norm_smem = reinterpret_cast<const int32_t*>(smem + OFF_NORM);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
@@ -124,7 +122,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(bars + 8 * (BAR_ACC_FULL + s), 1);
             mbar_init(bars + 8 * (BAR_ACC_EMPTY + s), 2 * EPI_WARPS);
         }
-        for (int s = 0; s < NSLOTS; s++) mbar_init(bars + 8 * (BAR_NORM_FULL + s), 1);
         mbar_init(bars + 8 * BAR_A_FULL, 1);
         mbar_init(bars + 8 * BAR_A_EMPTY, 1);
         mbar_init(bars + 8 * BAR_DRAIN, 1);
@@ -145,7 +142,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_q) : "memory");
             const uint32_t leader_bars = map_to_cta(bars, 0);  // the even CTA's barriers, cluster address
             int stage = 0;
-            uint32_t phase = 0, a_iter = 0, tile_seq = 0;
+            uint32_t phase = 0, a_iter = 0;
             bool ok = true;
             for (long long u = pair; u < sched.n_units && ok; u += n_pairs) {
                 int g, t0, t1;
@@ -157,29 +154,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     tma_load_2d_pair(sbase + OFF_A + qt * A_TILE_BYTES, &tmap_q, leader_bars + 8 * BAR_A_FULL, 0,
                                      g * QGROUP + qt * PAIR_M + (int)rank * BM);
                 a_iter++;
-                for (int t = t0; t < t1; t++, tile_seq++) {
+                for (int t = t0; t < t1; t++) {
                     ok = mbar_wait<true>(bars + 8 * (BAR_EMPTY + stage), phase ^ 1, abort_flag, status);
                     if (!ok) break;
                     if (rank == 0) mbar_expect_tx(bars + 8 * (BAR_FULL + stage), 2 * B_BYTES);
                     tma_load_2d_pair(sbase + OFF_B + stage * B_BYTES, &tmap_rows, leader_bars + 8 * (BAR_FULL + stage), 0,
                                      t * BN + (int)rank * BN_HALF);
-                    const uint32_t ns = tile_seq % NSLOTS;
-                    mbar_expect_tx(bars + 8 * (BAR_NORM_FULL + ns), NORM_BYTES);
-                    bulk_load(sbase + OFF_NORM + ns * NORM_BYTES, norms + (int64_t)t * BN, NORM_BYTES,
-                              bars + 8 * (BAR_NORM_FULL + ns));
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
             }
-            if (!ok) {
-                // Drain this CTA's own norm copies (local barriers).  Its tensor
-                // copies complete on the even CTA's barriers, which the cluster
-                // barrier at exit keeps alive.
-                for (uint32_t i = (tile_seq > NSLOTS ? tile_seq - NSLOTS : 0); i < tile_seq; i++)
-                    mbar_drain_wait<false>(bars + 8 * (BAR_NORM_FULL + i % NSLOTS), (i / NSLOTS) & 1);
-            }
+            // Tensor copies complete on the even CTA's barriers, which the
+            // cluster barrier at exit keeps alive until both CTAs are done.
         }
     } else if (warp == MMA_WARP) {
         // ------------------------------------------------------------ MMA issuer (even CTA)
@@ -239,7 +227,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         buf.base = reinterpret_cast<uint2*>(smem + OFF_BUF) + threadIdx.x;
         buf.n = 0;
         int acc = 0;
-        uint32_t acc_phase = 0, tile_seq = 0;
+        uint32_t acc_phase = 0;
         bool ok = true;
         for (long long u = pair; u < sched.n_units && ok; u += n_pairs) {
             int g, t0, t1;
@@ -259,19 +247,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // bias that always passes, an invalid query to one that never does.
             int32_t bias;
             if (!qvalid)
-                bias = 1 << 30;
+                bias = 1 << 29;  // need stays below 2^31 even for pad rows (norm 2^30)
             else if (tkey >= (1u << 30))
                 bias = -(1 << 30);
             else
                 bias = qnv - (int32_t)tkey;
-            for (int t = t0; t < t1; t++, tile_seq++) {
-                const uint32_t ns = tile_seq % NSLOTS;
-                ok = mbar_wait<true>(bars + 8 * (BAR_ACC_FULL + acc), acc_phase, abort_flag, status);
-                if (ok) ok = mbar_wait<false>(bars + 8 * (BAR_NORM_FULL + ns), (tile_seq / NSLOTS) & 1, abort_flag, status);
+            // n_min of this warp's two chunks, one tile ahead of their use.
+            const int32_t* nrm = norms + part * COLS_PER_WARP;
+            int32_t nx0 = 0, nx1 = 0;
+            if (t0 < t1) {
+                nx0 = __ldg(nrm + (int64_t)t0 * BN);
+                nx1 = __ldg(nrm + (int64_t)t0 * BN + 32);
+            }
+            for (int t = t0; t < t1; t++) {
+                const int32_t need0 = nx0 + bias, need1 = nx1 + bias;
+                if (t + 1 < t1) {
+                    nx0 = __ldg(nrm + (int64_t)(t + 1) * BN);
+                    nx1 = __ldg(nrm + (int64_t)(t + 1) * BN + 32);
+                }
+                ok = mbar_wait_inl<true>(bars + 8 * (BAR_ACC_FULL + acc), acc_phase, abort_flag, status);
                 if (!ok) break;
                 tc_fence_after();
-                const int32_t* tnorm = norm_smem + ns * BN + part * COLS_PER_WARP;
-                const int32_t row0 = t * BN + part * COLS_PER_WARP;  // rows < 2^31 (ids are int32)
                 const uint32_t tcol = tmem_base + lane_base + (uint32_t)(acc * QT * BN + qt * BN + part * COLS_PER_WARP);
                 uint32_t v[2][32];
                 __syncwarp();
@@ -282,32 +278,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 // Both chunks are in registers: release the accumulator to the MMA.
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(leader_acc_empty + 8 * acc);
-                const int32_t need0 = tnorm[0] + bias, need1 = tnorm[32] + bias;
-                const int32_t m0 = max32(v[0]), m1 = max32(v[1]);
-#pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    const uint32_t(&cur)[32] = v[c];
-                    const int32_t need = c ? need1 : need0;
-                    if (2 * (c ? m1 : m0) >= need) {
-                        const int32_t rbase = row0 + c * 32;
-#pragma unroll
-                        for (int j = 0; j < 32; j++) {
-                            const int32_t r = rbase + j;
-                            if (2 * (int32_t)cur[j] >= need && r < n_rows) {
-                                const uint32_t key = (uint32_t)(qnv + tnorm[c * 32 + j] - 2 * (int32_t)cur[j]);
-                                if (dense) {
-                                    cand[(size_t)qi * cap + r] = make_uint2(key, (uint32_t)r);
-                                } else if (key < tkey || (key == tkey && __ldg(ids + r) <= tid)) {
-                                    buf.push(key, (uint32_t)r, counts, cand, cap, qi);
-                                }
-                            }
-                        }
-                    }
-                }
+                if (lane == 0) mbar_arrive_remote(leader_acc_empty + 8 * acc);
                 if (++acc == ACC_STAGES) {
                     acc = 0;
                     acc_phase ^= 1;
+                }
+                const int32_t m0 = max32(v[0]), m1 = max32(v[1]);
+                if (2 * m0 < need0 && 2 * m1 < need1) continue;
+                const int32_t row0 = t * BN + part * COLS_PER_WARP;  // rows < 2^31 (ids are int32)
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    uint32_t mask = pass_mask32(v[c], c ? need1 : need0);
+                    while (mask) {
+                        const int j = __ffs(mask) - 1;
+                        mask &= mask - 1;
+                        const int32_t r = row0 + c * 32 + j;
+                        if (r >= n_rows) break;  // pad rows trail the level
+                        const uint32_t key = (uint32_t)(qnv + __ldg(norms + r) - 2 * (int32_t)pick32(v[c], j));
+                        if (dense)
+                            cand[(size_t)qi * cap + r] = make_uint2(key, (uint32_t)r);
+                        else if (key < tkey || (key == tkey && __ldg(ids + r) <= tid))
+                            buf.push(key, (uint32_t)r, counts, cand, cap, qi);
+                    }
                 }
             }
             if (qvalid) buf.flush(counts, cand, cap, qi);

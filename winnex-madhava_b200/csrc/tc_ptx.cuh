@@ -29,6 +29,12 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
+// Release at CTA scope on a shared::cluster address: enough to order this
+// thread's completed tensor-memory reads (tcgen05.wait::ld +
+// fence::before_thread_sync) before the peer's next MMA.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
 template <bool CLUSTER>
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
@@ -52,6 +58,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // another role's did).  On expiry the status word records kDevTimeout.
 template <bool CLUSTER>
 __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int32_t* abort_flag, int32_t* status) {
+    if (mbar_try_wait<CLUSTER>(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (;;) {
+        if (mbar_try_wait<CLUSTER>(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (clock64() - t0 > kWaitBudget) {
+            *abort_flag = 1;
+            atomicExch(status, (int32_t)kDevTimeout);
+            return false;
+        }
+    }
+}
+
+// The same bounded wait written inline, for loops that keep many values in
+// registers across the wait (an out-of-line call would spill them).
+template <bool CLUSTER>
+__device__ __forceinline__ bool mbar_wait_inl(uint32_t bar, uint32_t parity, volatile int32_t* abort_flag,
+                                              int32_t* status) {
     if (mbar_try_wait<CLUSTER>(bar, parity)) return true;
     const long long t0 = clock64();
     for (;;) {
@@ -224,6 +248,28 @@ __device__ __forceinline__ int32_t max32(const uint32_t (&v)[32]) {
     float u0 = fmax3(t[0], t[1], t[2]), u1 = fmax3(t[3], t[4], t[5]), u2 = fmax3(t[6], t[7], t[8]);
     float u3 = fmaxf(t[9], t[10]);
     return (int32_t)__float_as_uint(fmaxf(fmax3(u0, u1, u2), u3));
+}
+
+// Bit j set when 2 * v[j] >= need (v[j] < 2^23, so 2 * v[j] does not overflow).
+__device__ __forceinline__ uint32_t pass_mask32(const uint32_t (&v)[32], int32_t need) {
+    uint32_t m = 0;
+#pragma unroll
+    for (int j = 0; j < 32; j++) m |= (uint32_t)(need - 1 - 2 * (int32_t)v[j]) >> 31 << j;
+    return m;
+}
+
+// v[j] for a run-time j, by a five-level select tree (no local memory).
+__device__ __forceinline__ uint32_t pick32(const uint32_t (&v)[32], int j) {
+    uint32_t a[16], b[8], c[4], d[2];
+#pragma unroll
+    for (int i = 0; i < 16; i++) a[i] = (j & 1) ? v[2 * i + 1] : v[2 * i];
+#pragma unroll
+    for (int i = 0; i < 8; i++) b[i] = (j & 2) ? a[2 * i + 1] : a[2 * i];
+#pragma unroll
+    for (int i = 0; i < 4; i++) c[i] = (j & 4) ? b[2 * i + 1] : b[2 * i];
+#pragma unroll
+    for (int i = 0; i < 2; i++) d[i] = (j & 8) ? c[2 * i + 1] : c[2 * i];
+    return (j & 16) ? d[1] : d[0];
 }
 
 // Per-thread candidate buffer in shared memory, entry-major (bank-conflict
