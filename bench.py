@@ -35,6 +35,7 @@ DIM = 128
 COMPONENTS = 4096
 SEED = 20261201
 CHUNK = 3_125_000
+TRAFFIC_BYTES_PER_ROW = (1.325461e9 + 12.59776e6) / 10_000_000
 METRIC = "queries/sec, 100M×128 u8 exact top-10, 10K-query batch at 1/2/4/8 B200; % roofline"
 
 
@@ -75,7 +76,8 @@ class Stats(ctypes.Structure):
     _fields_ = [("latency_ms", ctypes.c_double), ("pairs_scored", ctypes.c_int64),
                 ("pairs_pruned_by_bound", ctypes.c_int64), ("bound_violations", ctypes.c_int64),
                 ("candidates", ctypes.c_int64), ("tensor_core_path", ctypes.c_int32), ("levels", ctypes.c_int32),
-                ("full_scan_ms", ctypes.c_double), ("full_scan_pairs", ctypes.c_int64)]
+                ("full_scan_ms", ctypes.c_double), ("full_scan_pairs", ctypes.c_int64),
+                ("kernel_launches", ctypes.c_int64)]
 
 
 def load_lib():
@@ -282,7 +284,7 @@ def main():
     stream = torch.cuda.current_stream(device)
     sp = ctypes.c_void_p(stream.cuda_stream)
     st = Stats()
-    scan_ms, scan_pairs = [], []
+    scan_ms, scan_pairs, launches = [], [], []
 
     def step(record):
         check(L, L.mdh_search_u8_device(h, ctypes.c_void_p(dq.data_ptr()), nq, k, ctypes.c_void_p(ids.data_ptr()),
@@ -290,6 +292,7 @@ def main():
         if record:
             scan_ms.append(st.full_scan_ms)
             scan_pairs.append(st.full_scan_pairs)
+            launches.append(st.kernel_launches + (1 if world > 1 else 0))  # + the merge kernel
         if world > 1:
             dist.all_gather_into_tensor(all_i.view(-1), ids.view(-1))
             dist.all_gather_into_tensor(all_d.view(-1), dd.view(-1))
@@ -360,7 +363,11 @@ def main():
     ms_scan = statistics.median(scan_ms) if scan_ms else float("nan")
     pairs = scan_pairs[0] if scan_pairs else 0
     achieved = 2.0 * pairs * DIM / (ms_scan / 1e3) / 1e12 if ms_scan > 0 else None
-    launches = 2 + 2 * levels + (1 if world > 1 else 0)
+    # DRAM traffic of the scan per row: ncu capture of the same kernel on a
+    # 10M-row case (dram__bytes_read.sum + dram__bytes_write.sum = 1.3381e9 B
+    # per launch for 10,000 queries); the corpus and norms cross HBM once per
+    # launch, so traffic scales with the rows scanned.
+    traffic = TRAFFIC_BYTES_PER_ROW * (pairs / nq) if pairs else None
     line = {
         "metric": METRIC,
         "value": nq * args.steps / elapsed,
@@ -378,10 +385,11 @@ def main():
                        levels=levels, index_build_s=round(build_s, 2)),
         "e2e": {"value": nq * e2e_steps / e2e_t, "unit": "queries/sec", "h2d_bytes_per_step": int(nq * DIM),
                 "d2h_bytes_per_step": int(nq * k * 8)},
-        "gpu_launches": launches * args.steps,
+        "gpu_launches": int(sum(launches)),
         "clocks": clocks,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",
-                     "frac": (achieved / int8_peak) if achieved else None, "traffic": None,
+                     "frac": (achieved / int8_peak) if achieved else None, "traffic": traffic,
+                     "traffic_source": "ncu dram bytes of a 10M-row launch, scaled by rows (profiles/)",
                      "kernel": "full-corpus u8 L2 scan (filter) kernel",
                      "algorithmic": "2*N*Q*D int8 ops per launch",
                      "peak_source": f"2 x {peak_src} bf16 dense ({peaks['bf16_tflops']} TF/s): u8 MMA runs at twice "

@@ -66,6 +66,7 @@ typedef struct {
     int32_t levels;               /* threshold-refinement levels run */
     double full_scan_ms;          /* CUDA-event time of the full-corpus scan kernel(s) on their stream */
     int64_t full_scan_pairs;      /* (query, row) pairs that kernel scored */
+    int64_t kernel_launches;      /* this library's kernels launched by the call */
 } mdh_stats;
 
 /* Build an index over a row-major u8 corpus [n][dim] held in host memory.

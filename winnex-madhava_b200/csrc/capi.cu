@@ -208,6 +208,7 @@ struct ShardResult {
     double scan_ms = 0.0;     // event time of the full-shard filter
     int64_t scan_pairs = 0;
     int scan_path = 0;        // run_filter's path for the full shard
+    int64_t launches = 0;     // kernels launched
 };
 
 // Exact top-k for nq staged queries on one shard.  Results: ws.out_key /
@@ -236,7 +237,10 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
     for (size_t si = 0; si < steps.size(); si++) {
         const LevelStep& s = steps[si];
         const Level& lv = sh.levels[s.level];
-        if (s.dense) launch_fill_threshold(w.thr_key, w.thr_id, nq, kKeyInf, kIdInf, st);
+        if (s.dense) {
+            launch_fill_threshold(w.thr_key, w.thr_id, nq, kKeyInf, kIdInf, st);
+            res.launches++;
+        }
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)nq * 4, st));
         const bool last_level = si + 1 == steps.size();
         if (last_level) {
@@ -246,8 +250,9 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
             }
             MDH_CUDA(cudaEventRecord(w.ev0, st));
         }
-        const int used = run_filter(ix, sh, lv, qp, w.q_u8, w.qn, w.q_f32, nq, w.thr_key, w.thr_id, s.cap,
-                                    s.dense && s.cap >= lv.n);
+        const bool dense = s.dense && s.cap >= lv.n;
+        const int used = run_filter(ix, sh, lv, qp, w.q_u8, w.qn, w.q_f32, nq, w.thr_key, w.thr_id, s.cap, dense);
+        res.launches += dense ? 2 : 1;
         if (last_level) {
             MDH_CUDA(cudaEventRecord(w.ev1, st));
             res.scan_pairs = lv.n * (int64_t)nq;
@@ -259,6 +264,7 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
         if (final_) MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
         launch_select(w.counts, w.cand, s.cap, lv.ids, nq, k, final_ ? 1 : 0, w.thr_key, w.thr_id, w.out_key,
                       w.out_id, w.flags, w.status + 1, nullptr, st);
+        res.launches++;
     }
     // Status words: [0] device error of the tensor-core scan, [1] overflowed queries.
     MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
@@ -314,6 +320,7 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
             cq_u8 = static_cast<uint8_t*>(tmpbuf);
             cqn = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(tmpbuf) + round_up((size_t)m * ix->dpad, 256));
             launch_gather_queries_u8(w.q_u8, w.qn, d_list, m, ix->dpad, cq_u8, cqn, st);
+            res.launches++;
         } else {
             // Host copy of the flagged float queries: [m][dim] then [m] aux.
             std::vector<float> hq((size_t)m * ix->dim + (size_t)m);
@@ -331,6 +338,7 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
         MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
         launch_select(w.counts, w.cand, last.cap, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id, w.flags,
                       w.status + 1, d_list, st);
+        res.launches += 2;  // filter + select
         MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
         MDH_CUDA(cudaStreamSynchronize(st));
         if (w.h_status[0] != kDevOk)
@@ -458,6 +466,7 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
         std::vector<ShardResult> sres((size_t)nshard);
         std::vector<std::string> errs((size_t)nshard);
         std::vector<mdh_status> codes((size_t)nshard, MDH_OK);
+        std::vector<int64_t> st_launch((size_t)nshard, 0);
         auto run = [&](int si) {
             try {
                 Shard& sh = ix->shards[(size_t)si];
@@ -468,6 +477,7 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
                     growT(&w.qn, &w.qn_bytes, (size_t)m * 4);
                     MDH_CUDA(cudaMemcpyAsync(w.q_u8, qbuf_u8.data(), (size_t)m * dpad, cudaMemcpyHostToDevice, sh.stream));
                     launch_query_norms_u8(w.q_u8, m, dpad, w.qn, sh.stream);
+                    st_launch[(size_t)si] = 1;
                 } else {
                     growT(&w.q_f32, &w.q_f32_bytes, qbuf_f32.size() * 4);
                     MDH_CUDA(cudaMemcpyAsync(w.q_f32, qbuf_f32.data(), qbuf_f32.size() * 4, cudaMemcpyHostToDevice,
@@ -497,9 +507,11 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
             st.levels = std::max(st.levels, r.levels);
             st.tensor_core_path = std::max(st.tensor_core_path, r.scan_path - 1);
             st.full_scan_pairs += r.scan_pairs;
+            st.kernel_launches += r.launches;
             chunk_scan_ms = std::max(chunk_scan_ms, r.scan_ms);  // shards run concurrently
         }
         st.full_scan_ms += chunk_scan_ms;
+        for (int64_t l : st_launch) st.kernel_launches += l;
         // Gather / merge to the first shard's device.
         Shard& s0 = ix->shards[0];
         MDH_CUDA(cudaSetDevice(s0.device));
@@ -520,6 +532,7 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
                 MDH_CUDA(cudaMemcpyPeerAsync(all_id + per * si, s0.device, sh.ws.out_id, sh.device, per * 4, s0.stream));
             }
             launch_merge_topk(all_key, all_id, nshard, m, kk, mkey, mid, s0.stream);
+            st.kernel_launches++;
             fkey = mkey;
             fid = mid;
         }
@@ -723,6 +736,7 @@ mdh_status mdh_search_u8_device(mdh_index* index, const uint8_t* dev_queries, in
                 st.tensor_core_path = std::max(0, r.scan_path - 1);
                 st.full_scan_ms = r.scan_ms;
                 st.full_scan_pairs = r.scan_pairs;
+                st.kernel_launches = 1 + r.launches;  // query norms + the shard's search
                 if (kk == k) {
                     MDH_CUDA(cudaMemcpyAsync(dev_ids, w.out_id, (size_t)nq * k * 4, cudaMemcpyDeviceToDevice, sh.stream));
                     if (dev_dist)

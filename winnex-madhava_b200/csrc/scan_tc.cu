@@ -397,11 +397,8 @@ void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const i
     s.n_chunks = choose_scan_chunks(s.n_qtiles, s.n_tiles, ctas);
     s.n_units = (long long)s.n_qtiles * s.n_chunks;
     if (s.n_units < ctas) ctas = (int)s.n_units;
-    static bool attr_set = false;
-    if (!attr_set) {
-        MDH_CUDA(cudaFuncSetAttribute(k_filter_tc_u8_l2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
-        attr_set = true;
-    }
+    // A function attribute belongs to the current device: set it on every launch.
+    MDH_CUDA(cudaFuncSetAttribute(k_filter_tc_u8_l2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
     k_filter_tc_u8_l2<<<ctas, NUM_THREADS, SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n, qn, nq,
                                                             thr_key, thr_id, counts, cand, cap, dense, s, status);
     MDH_CUDA(cudaGetLastError());

@@ -336,11 +336,8 @@ void launch_filter_tc2_u8_l2(const Level& lv, int dpad, const uint8_t* q, const 
     MDH_REQUIRE((reinterpret_cast<uintptr_t>(lv.norms) & 15) == 0, MDH_ERR_INTERNAL, "norms must be 16-byte aligned");
     CUtensorMap tq;
     encode_u8_rows_tmap(&tq, q, nq, dpad, BM);
-    static bool attr_set = false;
-    if (!attr_set) {
-        MDH_CUDA(cudaFuncSetAttribute(k_filter_tc2_u8_l2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
-        attr_set = true;
-    }
+    // A function attribute belongs to the current device: set it on every launch.
+    MDH_CUDA(cudaFuncSetAttribute(k_filter_tc2_u8_l2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
     int dev;
     MDH_CUDA(cudaGetDevice(&dev));
     cudaLaunchConfig_t cfg = {};
@@ -354,13 +351,15 @@ void launch_filter_tc2_u8_l2(const Level& lv, int dpad, const uint8_t* q, const 
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    static int max_pairs = 0;
+    static int max_pairs_dev[64] = {0};  // per device; a racing double query is harmless
+    int max_pairs = (dev >= 0 && dev < 64) ? max_pairs_dev[dev] : 0;
     if (!max_pairs) {
         cfg.gridDim = dim3(2 * device_sm_count(dev) / 2, 1, 1);
         int clusters = 0;
         MDH_CUDA(cudaOccupancyMaxActiveClusters(&clusters, k_filter_tc2_u8_l2, &cfg));
         MDH_REQUIRE(clusters > 0, MDH_ERR_CUDA, "no SM pair can host the pair scan kernel");
         max_pairs = clusters;
+        if (dev >= 0 && dev < 64) max_pairs_dev[dev] = clusters;
     }
     Sched2 s;
     s.n_groups = (nq + QGROUP - 1) / QGROUP;
