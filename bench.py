@@ -261,8 +261,11 @@ def main():
         return
 
     L = load_lib()
+    sys.path.insert(0, os.path.join(ROOT, "winnex-madhava_b200"))
+    from winnex_madhava.sharding import gather_topk, merge_topk_device, row_range
+
     check(L, L.mdh_set_scan_path(args.scan_path), "set_scan_path")
-    start, end = args.n * rank // world, args.n * (rank + 1) // world
+    start, end = row_range(args.n, rank, world)
     rows = make_rows_gpu(torch, start, end, device)
     torch.cuda.synchronize()
     h = ctypes.c_void_p()
@@ -277,10 +280,6 @@ def main():
     dq = torch.from_numpy(queries).to(device)
     ids = torch.empty((nq, k), dtype=torch.int32, device=device)
     dd = torch.empty((nq, k), dtype=torch.int32, device=device)
-    all_i = torch.empty((world, nq, k), dtype=torch.int32, device=device)
-    all_d = torch.empty((world, nq, k), dtype=torch.int32, device=device)
-    out_i = torch.empty((nq, k), dtype=torch.int32, device=device)
-    out_d = torch.empty((nq, k), dtype=torch.int32, device=device)
     stream = torch.cuda.current_stream(device)
     sp = ctypes.c_void_p(stream.cuda_stream)
     st = Stats()
@@ -294,11 +293,8 @@ def main():
             scan_pairs.append(st.full_scan_pairs)
             launches.append(st.kernel_launches + (1 if world > 1 else 0))  # + the merge kernel
         if world > 1:
-            dist.all_gather_into_tensor(all_i.view(-1), ids.view(-1))
-            dist.all_gather_into_tensor(all_d.view(-1), dd.view(-1))
-            check(L, L.mdh_merge_topk_device(ctypes.c_void_p(all_d.data_ptr()), ctypes.c_void_p(all_i.data_ptr()),
-                                             world, nq, k, ctypes.c_void_p(out_d.data_ptr()),
-                                             ctypes.c_void_p(out_i.data_ptr()), sp), "merge")
+            all_d, all_i = gather_topk(dd, ids)
+            merge_topk_device(L, all_d, all_i, stream)
 
     for _ in range(warmup):
         step(False)
@@ -336,11 +332,8 @@ def main():
         if world > 1:
             ids.copy_(hid, non_blocking=True)
             dd.copy_(hdist, non_blocking=True)
-            dist.all_gather_into_tensor(all_i.view(-1), ids.view(-1))
-            dist.all_gather_into_tensor(all_d.view(-1), dd.view(-1))
-            check(L, L.mdh_merge_topk_device(ctypes.c_void_p(all_d.data_ptr()), ctypes.c_void_p(all_i.data_ptr()),
-                                             world, nq, k, ctypes.c_void_p(out_d.data_ptr()),
-                                             ctypes.c_void_p(out_i.data_ptr()), sp), "merge")
+            all_d, all_i = gather_topk(dd, ids)
+            out_d, out_i = merge_topk_device(L, all_d, all_i, stream)
             hid.copy_(out_i)
             hdist.copy_(out_d)
 

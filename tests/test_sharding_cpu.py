@@ -1,0 +1,96 @@
+"""The row-sharded path's host logic on a 2-rank gloo group (CPU).
+
+Each rank takes its rows with ``sharding.row_range``, ranks them with the
+oracle under global ids, and exchanges its [Q][k] lists with
+``sharding.gather_topk``; merging the gathered lists by (distance, id) must
+give the single-shard oracle result exactly.  The GPU merge kernel
+(mdh_merge_topk_device) is tested against the same rule in
+test_gpu_capi.py.
+"""
+import datetime
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+
+import cases
+import oracle
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, n, nq, k, out):
+    import torch
+    import torch.distributed as dist
+
+    from winnex_madhava.sharding import gather_topk, row_range
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        C = cases.gmm_u8(n, 32, 8, seed=61)
+        Q = cases.gmm_u8_queries(nq, 32, 8, seed_means=61, seed_q=62)
+        s, e = row_range(n, rank, world)
+        ids, d = oracle.l2_exact_u8_int(C[s:e], Q, k)
+        ids = np.where(ids >= 0, ids + s, -1).astype(np.int32)
+        d = np.where(ids >= 0, d, -1).astype(np.int32)
+        all_d, all_i = gather_topk(torch.from_numpy(d), torch.from_numpy(ids))
+        if rank == 0:
+            np.savez(out, d=all_d.numpy(), i=all_i.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def _merge(all_d, all_i, k):
+    world, nq, kk = all_d.shape
+    out_i = np.full((nq, k), -1, np.int32)
+    out_d = np.full((nq, k), -1, np.int64)
+    for q in range(nq):
+        pairs = [(int(all_d[r, q, j]), int(all_i[r, q, j])) for r in range(world) for j in range(kk)
+                 if all_i[r, q, j] >= 0]
+        pairs.sort()
+        for j, (dd, ii) in enumerate(pairs[:k]):
+            out_d[q, j], out_i[q, j] = dd, ii
+    return out_d, out_i
+
+
+@pytest.mark.parametrize("n,k", [(3001, 10), (7, 10)])
+def test_two_rank_shards_merge_to_single_shard(n, k):
+    mp = pytest.importorskip("torch.multiprocessing")
+    nq, world = 24, 2
+    with tempfile.TemporaryDirectory() as tmp:
+        out = os.path.join(tmp, "gathered.npz")
+        mp.spawn(_worker, args=(world, _free_port(), n, nq, k, out), nprocs=world, join=True)
+        g = np.load(out)
+        assert g["d"].shape == (world, nq, k) and g["i"].shape == (world, nq, k)
+        # rank-major: rank r's ids lie in its own row range
+        from winnex_madhava.sharding import row_range
+        for r in range(world):
+            s, e = row_range(n, r, world)
+            v = g["i"][r][g["i"][r] >= 0]
+            assert ((v >= s) & (v < e)).all()
+        got_d, got_i = _merge(g["d"], g["i"], k)
+    C = cases.gmm_u8(n, 32, 8, seed=61)
+    Q = cases.gmm_u8_queries(nq, 32, 8, seed_means=61, seed_q=62)
+    want_i, want_d = oracle.l2_exact_u8_int(C, Q, k)
+    np.testing.assert_array_equal(got_i, want_i)
+    np.testing.assert_array_equal(got_d[want_i >= 0], want_d[want_i >= 0])
+
+
+def test_row_range_partitions():
+    from winnex_madhava.sharding import row_range
+    for n in (0, 1, 7, 100_000_000):
+        for world in (1, 2, 4, 8):
+            spans = [row_range(n, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+            assert max(e - s for s, e in spans) - min(e - s for s, e in spans) <= 1
+    with pytest.raises(ValueError):
+        row_range(10, 2, 2)

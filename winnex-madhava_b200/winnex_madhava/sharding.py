@@ -1,0 +1,65 @@
+"""Row sharding of one corpus over the ranks of a process group (one process
+per GPU) and the exchange step of the sharded exact scan.
+
+Rank r of G owns the contiguous rows [r*N//G, (r+1)*N//G) and builds its
+index with ``id_offset`` = its first row, so its top-k lists carry global
+ids.  After the local search every rank all-gathers the ``[Q][k]`` (distance,
+id) lists -- the only collective of the path, 8*Q*k bytes per rank -- and
+merges them with ``mdh_merge_topk_device``, which orders by (distance,
+global id).  The merged lists therefore do not depend on G.
+
+The reference has no multi-GPU path; its single-device GPU search is
+``SpeedEngine::scores_gpu_topk`` (src/speed_gpu.cu:170-233).
+"""
+from __future__ import annotations
+
+import ctypes
+
+
+def row_range(n: int, rank: int, world: int) -> tuple[int, int]:
+    """Rows [start, end) owned by ``rank`` of ``world``."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    if n < 0:
+        raise ValueError("n must be >= 0")
+    return n * rank // world, n * (rank + 1) // world
+
+
+def gather_topk(dist, ids, group=None):
+    """All-gather this rank's ``[Q][k]`` int32 (distance, id) tensors.
+
+    Returns ``(all_dist, all_ids)`` shaped ``[world][Q][k]``, rank-major,
+    on the inputs' device.  Works with any backend that implements
+    ``all_gather`` (NCCL on GPUs, gloo on CPU).
+    """
+    import torch
+    import torch.distributed as tdist
+
+    if dist.shape != ids.shape or dist.dtype != torch.int32 or ids.dtype != torch.int32:
+        raise ValueError("dist and ids must be int32 tensors of the same shape")
+    world = tdist.get_world_size(group)
+    out_d = torch.empty((world,) + tuple(dist.shape), dtype=torch.int32, device=dist.device)
+    out_i = torch.empty_like(out_d)
+    tdist.all_gather(list(out_d.unbind(0)), dist.contiguous(), group=group)
+    tdist.all_gather(list(out_i.unbind(0)), ids.contiguous(), group=group)
+    return out_d, out_i
+
+
+def merge_topk_device(lib, all_dist, all_ids, stream=None):
+    """Merge gathered lists on the GPU (``mdh_merge_topk_device``).
+
+    ``lib`` is the loaded ``libwinnex_madhava_b200.so`` (ctypes); inputs are
+    CUDA tensors ``[world][Q][k]``.  Returns ``(dist, ids)`` ``[Q][k]``.
+    """
+    import torch
+
+    world, nq, k = all_dist.shape
+    out_d = torch.empty((nq, k), dtype=torch.int32, device=all_dist.device)
+    out_i = torch.empty_like(out_d)
+    sp = ctypes.c_void_p(stream.cuda_stream if stream is not None else 0)
+    st = lib.mdh_merge_topk_device(ctypes.c_void_p(all_dist.data_ptr()), ctypes.c_void_p(all_ids.data_ptr()),
+                                   world, nq, k, ctypes.c_void_p(out_d.data_ptr()), ctypes.c_void_p(out_i.data_ptr()),
+                                   sp)
+    if st != 0:
+        raise RuntimeError(lib.mdh_last_error().decode() if lib.mdh_last_error() else f"merge failed ({st})")
+    return out_d, out_i
