@@ -131,6 +131,19 @@ mdh_status mdh_search_u8(mdh_index* index, const uint8_t* host_queries, int32_t 
 mdh_status mdh_search_u8_device(mdh_index* index, const uint8_t* dev_queries, int32_t nq, int32_t k,
                                 int32_t* dev_ids, int32_t* dev_dist, void* stream, mdh_stats* stats);
 
+/* mdh_search_u8_device without any allocation: no cudaMalloc / cudaFree
+ * or allocating library call; scratch is a fixed 9 MiB __device__ array per
+ * device.  For callers that must not allocate (a serving loop beside a
+ * caching allocator that holds most of HBM; a latency-bound loop where
+ * cudaFree would synchronize the device).  Limits: L2 index on one device,
+ * dim <= 256, nq <= 256, k <= 256 (MDH_ERR_UNSUPPORTED beyond).  The first
+ * call on a device resolves the scratch address (cudaGetSymbolAddress): make
+ * it before any stream capture.  Calls share the scratch, so they are
+ * serialized by a process-wide lock; each returns after its work on `stream`
+ * completed.  No counterpart in the reference. */
+mdh_status mdh_search_u8_device_noalloc(mdh_index* index, const uint8_t* dev_queries, int32_t nq, int32_t k,
+                                        int32_t* dev_ids, int32_t* dev_dist, void* stream, mdh_stats* stats);
+
 /* Merge per-shard top-k lists (device pointers on the current device):
  * dist_all/ids_all are [nshard][nq][k] (int32 squared distance, int32 row id,
  * id -1 = empty), the output [nq][k] keeps the k smallest (dist, id).

@@ -633,6 +633,10 @@ int device_sm_count(int dev) {
 
 void ensure(void** p, size_t* have, size_t need) { grow(p, have, need); }
 
+mdh_status run_guarded(void (*fn)(void*), void* ctx) {
+    return guard([&] { fn(ctx); });
+}
+
 }  // namespace mdh
 
 using namespace mdh;

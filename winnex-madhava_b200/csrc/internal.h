@@ -141,4 +141,8 @@ void launch_gather_queries_u8(const uint8_t* src, const int32_t* qn_src, const i
 
 int device_sm_count(int dev);
 
+// Runs fn(ctx) under the C ABI's error convention (status code, and the
+// message for mdh_last_error) without allocating on success.
+mdh_status run_guarded(void (*fn)(void*), void* ctx);
+
 }  // namespace mdh
