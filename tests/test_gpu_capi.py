@@ -53,6 +53,25 @@ def test_search_u8_distances_exact(path):
         L.mdh_set_scan_path(0)
 
 
+@pytest.mark.parametrize("nq", [64, 100, 255, 256, 300, 513])
+def test_tensor_scan_batch_shapes(nq):
+    """Both tensor tile shapes (128 and 256 queries per CTA) and partial query groups."""
+    L = capi()
+    L.mdh_set_scan_path(2)
+    try:
+        C = cases.gmm_u8(70_001, 128, 128, seed=23)
+        Q = cases.gmm_u8_queries(nq, 128, 128, seed_means=23, seed_q=24)
+        h = _create_u8(L, C)
+        ids, dist, s = _search_u8(L, h, Q, 16)
+        want_ids, want_d = oracle.l2_exact_u8_int(C, Q, 16)
+        np.testing.assert_array_equal(ids, want_ids)
+        np.testing.assert_array_equal(dist, want_d)
+        assert s.tensor_core_path == 1
+        assert L.mdh_index_destroy(h) == 0
+    finally:
+        L.mdh_set_scan_path(0)
+
+
 def test_device_api_and_merge():
     torch = pytest.importorskip("torch")
     L = capi()

@@ -1,27 +1,31 @@
-// Tensor-core (tcgen05) u8 L2 scan on single SMs, sm_100a -- the small-batch
-// tensor path (the SM-pair kernel in scan_tc2.cu takes large batches).
+// Tensor-core (tcgen05) u8 L2 scan on single SMs, sm_100a.
 //
 // Same contract as the CUDA-core filter (scan_simt.cu): for each query q and
 // real row r of a Level, key = |q|^2 + |v|^2 - 2 q.v; pairs with
 // (key, id) <= (thr_key[q], thr_id[q]) are appended to q's candidate list as
 // {key, r}; on a dense level (infinite thresholds) row r goes to slot r.
 //
-// Tile: 128 queries (TMEM lanes, the MMA's M) x BN corpus rows (the MMA's N,
-// 128 or 256) x 128 bytes (K: four kind::i8 MMAs of K = 32).  u8 x u8
+// Tile: QT query tiles of 128 queries (TMEM lanes, the MMA's M) x BN corpus
+// rows (the MMA's N) x 128 bytes (K: four kind::i8 MMAs of K = 32).  u8 x u8
 // products accumulate exactly in s32 in tensor memory.  Operands are staged
 // by TMA with the 128-byte swizzle (one 128-byte row per vector = one swizzle
-// row).  512 / BN accumulator stages (all of TMEM) keep the MMA ahead of the
-// epilogue.
+// row).  An accumulator stage holds QT x BN columns; all 512 TMEM columns
+// form 512 / (QT x BN) stages.  Two shapes are built:
+//   QT = 2, BN = 128 (256 queries per CTA): each corpus tile read from L2
+//     feeds 256 queries, so the L2 -> SM stream is 32 B per SM-cycle at the
+//     full MMA rate -- half of what 128 queries per CTA would need, which
+//     is at the L2's limit with 148 SMs reading;
+//   QT = 1, BN = 256 (128 queries per CTA): batches below 256 queries.
 //
 // Warp roles (576 threads, one CTA per SM, persistent):
 //   warps 0-15 epilogue: warp w reads TMEM lanes 32*(w%4).. (thread = one
-//              query) and columns [BN/4*(w/4), +BN/4) of each accumulator
-//              (one or two 32-column chunks); the chunks are copied to
-//              registers and the accumulator released before the
-//              Cauchy-Schwarz chunk filter runs; passing rows are buffered per
-//              thread in shared memory, one atomic per flush;
-//   warp 16    TMA producer (query tile once per work unit, corpus tiles
-//              through a STAGES-deep ring);
+//              query) and the 64 columns [64*(w/4), +64) of each
+//              accumulator stage (query tile 64*(w/4) / BN); both 32-column
+//              chunks are copied to registers and the stage released before
+//              the Cauchy-Schwarz chunk filter runs; passing rows are buffered
+//              per thread in shared memory, one atomic per flush;
+//   warp 16    TMA producer (the QT query tiles once per work unit, corpus
+//              tiles through a STAGES-deep ring);
 //   warp 17    TMEM allocator + single-thread MMA issuer.
 //
 // Epilogue filter: rows are sorted by |v|^2, so the first row of each
@@ -31,7 +35,7 @@
 // reduction (tc_ptx.cuh: max32).  n_min is read from L2 one tile ahead; the
 // rare chunks that pass are expanded by a bit-mask loop.
 //
-// Work units: (query tile, corpus chunk), ordered chunk-major so the CTAs
+// Work units: (query group, corpus chunk), ordered chunk-major so the CTAs
 // running at the same time share corpus chunks through L2; each CTA takes
 // units blockIdx.x, blockIdx.x + gridDim.x, ...
 //
@@ -51,84 +55,92 @@ namespace {
 
 using namespace tc;
 
-#ifndef MDH_TC1_BN
-#define MDH_TC1_BN 256
-#endif
-
-constexpr int BM = 128;           // queries per tile (TMEM lanes)
-constexpr int BN = MDH_TC1_BN;    // corpus rows per tile (MMA N)
+constexpr int BM = 128;           // queries per query tile (TMEM lanes)
 constexpr int BK = 128;           // bytes per row (K)
+constexpr int BOX_ROWS = 128;     // corpus rows per TMA box (BN / BOX_ROWS boxes per stage)
 constexpr int TMEM_COLS = 512;
-constexpr int ACC_STAGES = TMEM_COLS / BN;
-constexpr int STAGES = 10 * 128 / BN;   // corpus tile ring: 160 KB
 constexpr int EPI_WARPS = 16;     // 4 per TMEM lane quarter
-constexpr int COLS_PER_WARP = BN / 4;
-constexpr int CHUNKS = COLS_PER_WARP / 32;
+constexpr int COLS_PER_WARP = 64; // two 32-column chunks
 constexpr int EPI_THREADS = 32 * EPI_WARPS;
 constexpr int PRODUCER_WARP = EPI_WARPS;
 constexpr int MMA_WARP = EPI_WARPS + 1;
 constexpr int NUM_THREADS = 32 * (EPI_WARPS + 2);
-static_assert(BN == 128 || BN == 256, "one or two 32-column chunks per epilogue warp");
 constexpr int BUFN = 4;           // buffered candidates per epilogue thread
-constexpr uint32_t A_BYTES = BM * BK;
-constexpr uint32_t B_BYTES = BN * BK;
-constexpr uint32_t IDESC = idesc_u8(BM, BN);
+constexpr uint32_t A_TILE_BYTES = BM * BK;
 
-// Shared memory map (offsets from a 1024-byte aligned base).
-constexpr uint32_t OFF_A = 0;
-constexpr uint32_t OFF_B = OFF_A + A_BYTES;
-constexpr uint32_t OFF_BUF = OFF_B + STAGES * B_BYTES;
-constexpr uint32_t OFF_BAR = OFF_BUF + BUFN * EPI_THREADS * 8;
-constexpr uint32_t BAR_FULL = 0, BAR_EMPTY = STAGES, BAR_ACC_FULL = 2 * STAGES,
-                   BAR_ACC_EMPTY = 2 * STAGES + ACC_STAGES, BAR_A_FULL = 2 * STAGES + 2 * ACC_STAGES,
-                   BAR_A_EMPTY = BAR_A_FULL + 1, BAR_DRAIN = BAR_A_FULL + 2, NUM_BARS = BAR_A_FULL + 3;
-constexpr uint32_t OFF_TMEM_SLOT = OFF_BAR + NUM_BARS * 8;
-constexpr uint32_t OFF_ABORT = OFF_TMEM_SLOT + 4;
-constexpr uint32_t SMEM_USED = OFF_ABORT + 4;
-constexpr uint32_t SMEM_BYTES = SMEM_USED + 1024;  // alignment slack
-static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+template <int BN_, int QT_>
+struct TcCfg {
+    static constexpr int BN = BN_;
+    static constexpr int QT = QT_;
+    static constexpr int QGROUP = QT * BM;             // queries per work unit
+    static constexpr int ACC_COLS = QT * BN;           // TMEM columns per accumulator stage
+    static constexpr int ACC_STAGES = TMEM_COLS / ACC_COLS;
+    static constexpr int STAGES = 10 * 128 / BN;       // corpus tile ring: 160 KB
+    static constexpr uint32_t A_BYTES = QT * A_TILE_BYTES;
+    static constexpr uint32_t B_BYTES = BN * BK;
+    static constexpr uint32_t IDESC = idesc_u8(BM, BN);
+    // Shared memory map (offsets from a 1024-byte aligned base).
+    static constexpr uint32_t OFF_A = 0;
+    static constexpr uint32_t OFF_B = OFF_A + A_BYTES;
+    static constexpr uint32_t OFF_BUF = OFF_B + STAGES * B_BYTES;
+    static constexpr uint32_t OFF_BAR = OFF_BUF + BUFN * EPI_THREADS * 8;
+    static constexpr uint32_t BAR_FULL = 0, BAR_EMPTY = STAGES, BAR_ACC_FULL = 2 * STAGES,
+                              BAR_ACC_EMPTY = 2 * STAGES + ACC_STAGES, BAR_A_FULL = 2 * STAGES + 2 * ACC_STAGES,
+                              BAR_A_EMPTY = BAR_A_FULL + 1, BAR_DRAIN = BAR_A_FULL + 2, NUM_BARS = BAR_A_FULL + 3;
+    static constexpr uint32_t OFF_TMEM_SLOT = OFF_BAR + NUM_BARS * 8;
+    static constexpr uint32_t OFF_ABORT = OFF_TMEM_SLOT + 4;
+    static constexpr uint32_t SMEM_BYTES = OFF_ABORT + 4 + 1024;  // + alignment slack
+    static_assert(ACC_COLS == 4 * COLS_PER_WARP && ACC_STAGES >= 2, "four 64-column parts per accumulator stage");
+    static_assert(BN % BOX_ROWS == 0 && BN <= 256 && (COLS_PER_WARP % BN == 0 || BN % COLS_PER_WARP == 0),
+                  "tile shape");
+    static_assert(STAGES <= 32, "issued-stage mask is 32 bits");
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+    static_assert(A_TILE_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "swizzle alignment");
+};
 
 struct Sched {
-    int n_qtiles;     // query tiles of BM
+    int n_groups;     // query groups of QT x BM
     int n_tiles;      // corpus tiles of BN rows
-    int n_chunks;     // corpus chunks per query tile
+    int n_chunks;     // corpus chunks per query group
     long long n_units;
 };
 
 __device__ __forceinline__ void unit_coords(const Sched& s, long long u, int& g, int& t0, int& t1) {
-    const int c = (int)(u / s.n_qtiles);
-    g = (int)(u - (long long)c * s.n_qtiles);
+    const int c = (int)(u / s.n_groups);
+    g = (int)(u - (long long)c * s.n_groups);
     t0 = (int)((long long)c * s.n_tiles / s.n_chunks);
     t1 = (int)((long long)(c + 1) * s.n_tiles / s.n_chunks);
 }
 
+template <class C>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_filter_tc_u8_l2(const __grid_constant__ CUtensorMap tmap_rows, const __grid_constant__ CUtensorMap tmap_q,
                       const int32_t* __restrict__ norms, const int32_t* __restrict__ ids, int32_t n_rows,
                       const int32_t* __restrict__ qn, int nq, const uint32_t* __restrict__ thr_key,
                       const int32_t* __restrict__ thr_id, uint32_t* __restrict__ counts, uint2* __restrict__ cand,
                       int cap, int dense, Sched sched, int32_t* __restrict__ status) {
+    constexpr int BN = C::BN, QT = C::QT, STAGES = C::STAGES, ACC_STAGES = C::ACC_STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t bars = sbase + OFF_BAR;
-    volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + OFF_ABORT);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM_SLOT);
+    const uint32_t bars = sbase + C::OFF_BAR;
+    volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + C::OFF_ABORT);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_TMEM_SLOT);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
-            mbar_init(bars + 8 * (BAR_FULL + s), 1);
-            mbar_init(bars + 8 * (BAR_EMPTY + s), 1);
+            mbar_init(bars + 8 * (C::BAR_FULL + s), 1);
+            mbar_init(bars + 8 * (C::BAR_EMPTY + s), 1);
         }
         for (int s = 0; s < ACC_STAGES; s++) {
-            mbar_init(bars + 8 * (BAR_ACC_FULL + s), 1);
-            mbar_init(bars + 8 * (BAR_ACC_EMPTY + s), EPI_WARPS);
+            mbar_init(bars + 8 * (C::BAR_ACC_FULL + s), 1);
+            mbar_init(bars + 8 * (C::BAR_ACC_EMPTY + s), EPI_WARPS);
         }
-        mbar_init(bars + 8 * BAR_A_FULL, 1);
-        mbar_init(bars + 8 * BAR_A_EMPTY, 1);
-        mbar_init(bars + 8 * BAR_DRAIN, 1);
+        mbar_init(bars + 8 * C::BAR_A_FULL, 1);
+        mbar_init(bars + 8 * C::BAR_A_EMPTY, 1);
+        mbar_init(bars + 8 * C::BAR_DRAIN, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -152,18 +164,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (long long u = blockIdx.x; u < sched.n_units && ok; u += gridDim.x) {
                 int g, t0, t1;
                 unit_coords(sched, u, g, t0, t1);
-                ok = mbar_wait<false>(bars + 8 * BAR_A_EMPTY, (a_iter & 1) ^ 1, abort_flag, status);
+                ok = mbar_wait<false>(bars + 8 * C::BAR_A_EMPTY, (a_iter & 1) ^ 1, abort_flag, status);
                 if (!ok) break;
-                mbar_expect_tx(bars + 8 * BAR_A_FULL, A_BYTES);
-                tma_load_2d(sbase + OFF_A, &tmap_q, bars + 8 * BAR_A_FULL, 0, g * BM);
+                mbar_expect_tx(bars + 8 * C::BAR_A_FULL, C::A_BYTES);
+#pragma unroll
+                for (int qt = 0; qt < QT; qt++)
+                    tma_load_2d(sbase + C::OFF_A + qt * A_TILE_BYTES, &tmap_q, bars + 8 * C::BAR_A_FULL, 0,
+                                g * C::QGROUP + qt * BM);
                 a_issued = true;
                 a_iter++;
                 for (int t = t0; t < t1; t++) {
-                    ok = mbar_wait<false>(bars + 8 * (BAR_EMPTY + stage), phase ^ 1, abort_flag, status);
+                    ok = mbar_wait<false>(bars + 8 * (C::BAR_EMPTY + stage), phase ^ 1, abort_flag, status);
                     if (!ok) break;
-                    mbar_expect_tx(bars + 8 * (BAR_FULL + stage), B_BYTES);
-                    tma_load_2d(sbase + OFF_B + stage * B_BYTES, &tmap_rows, bars + 8 * (BAR_FULL + stage), 0,
-                                t * BN);
+                    mbar_expect_tx(bars + 8 * (C::BAR_FULL + stage), C::B_BYTES);
+#pragma unroll
+                    for (int b = 0; b < BN / BOX_ROWS; b++)
+                        tma_load_2d(sbase + C::OFF_B + stage * C::B_BYTES + b * BOX_ROWS * BK, &tmap_rows,
+                                    bars + 8 * (C::BAR_FULL + stage), 0, t * BN + b * BOX_ROWS);
                     issued_mask |= 1u << stage;
                     last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == STAGES) {
@@ -176,12 +193,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 // Drain: every issued copy completes its barrier phase.
                 for (int s = 0; s < STAGES; s++)
                     if (issued_mask & (1u << s))
-                        mbar_drain_wait<false>(bars + 8 * (BAR_FULL + s), (last_parity >> s) & 1);
-                if (a_issued) mbar_drain_wait<false>(bars + 8 * BAR_A_FULL, (a_iter - 1) & 1);
+                        mbar_drain_wait<false>(bars + 8 * (C::BAR_FULL + s), (last_parity >> s) & 1);
+                if (a_issued) mbar_drain_wait<false>(bars + 8 * C::BAR_A_FULL, (a_iter - 1) & 1);
             }
         }
     } else if (warp == MMA_WARP) {
         // ------------------------------------------------------------ MMA issuer
+        // tcgen05.mma issue blocks while the tensor pipe is busy and the pipe
+        // queues little more than one MMA, so a wait between tiles leaves the
+        // pipe idle.  The barriers of tile t+1 are therefore probed between
+        // tile t's MMAs (test_wait does not block) and, when both are already
+        // complete, tile t+1 is issued without waiting.
         if (lane == 0) {
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0, a_iter = 0;
@@ -189,58 +211,75 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (long long u = blockIdx.x; u < sched.n_units && ok; u += gridDim.x) {
                 int g, t0, t1;
                 unit_coords(sched, u, g, t0, t1);
-                ok = mbar_wait<false>(bars + 8 * BAR_A_FULL, a_iter & 1, abort_flag, status);
+                ok = mbar_wait<false>(bars + 8 * C::BAR_A_FULL, a_iter & 1, abort_flag, status);
                 if (!ok) break;
                 a_iter++;
                 tc_fence_after();
-                const uint64_t adesc = sw128_desc(sbase + OFF_A);
+                bool ready = false;  // tile t's barriers were seen complete while issuing tile t-1
                 for (int t = t0; t < t1; t++) {
-                    ok = mbar_wait<false>(bars + 8 * (BAR_ACC_EMPTY + acc), acc_phase ^ 1, abort_flag, status);
-                    if (!ok) break;
-                    ok = mbar_wait<false>(bars + 8 * (BAR_FULL + stage), phase, abort_flag, status);
-                    if (!ok) break;
+                    if (!ready) {
+                        ok = mbar_wait_inl<false>(bars + 8 * (C::BAR_ACC_EMPTY + acc), acc_phase ^ 1, abort_flag,
+                                                  status);
+                        if (!ok) break;
+                        ok = mbar_wait_inl<false>(bars + 8 * (C::BAR_FULL + stage), phase, abort_flag, status);
+                        if (!ok) break;
+                    }
                     tc_fence_after();
-                    const uint64_t bdesc = sw128_desc(sbase + OFF_B + stage * B_BYTES);
-                    const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+                    const int nstage = stage + 1 == STAGES ? 0 : stage + 1;
+                    const uint32_t nphase = stage + 1 == STAGES ? phase ^ 1 : phase;
+                    const int nacc = acc + 1 == ACC_STAGES ? 0 : acc + 1;
+                    const uint32_t nacc_phase = acc + 1 == ACC_STAGES ? acc_phase ^ 1 : acc_phase;
+                    const bool more = t + 1 < t1;
+                    bool pe = false, pf = false;
+                    const uint64_t bdesc = sw128_desc(sbase + C::OFF_B + stage * C::B_BYTES);
 #pragma unroll
-                    for (int kk = 0; kk < BK / 32; kk++)
-                        umma_i8<1>(d, adesc + (uint64_t)((kk * 32) >> 4), bdesc + (uint64_t)((kk * 32) >> 4), IDESC,
-                                   kk > 0 ? 1u : 0u);
+                    for (int qt = 0; qt < QT; qt++) {
+                        const uint64_t adesc = sw128_desc(sbase + C::OFF_A + qt * A_TILE_BYTES);
+                        const uint32_t d = tmem_base + (uint32_t)(acc * C::ACC_COLS + qt * BN);
+#pragma unroll
+                        for (int kk = 0; kk < BK / 32; kk++) {
+                            umma_i8<1>(d, adesc + (uint64_t)((kk * 32) >> 4), bdesc + (uint64_t)((kk * 32) >> 4),
+                                       C::IDESC, kk > 0 ? 1u : 0u);
+                            if (more && qt == QT - 1 && kk == 1)
+                                pe = mbar_test_wait(bars + 8 * (C::BAR_ACC_EMPTY + nacc), nacc_phase ^ 1);
+                            if (more && qt == QT - 1 && kk == 2)
+                                pf = mbar_test_wait(bars + 8 * (C::BAR_FULL + nstage), nphase);
+                        }
+                    }
                     issued = true;
-                    umma_commit(bars + 8 * (BAR_EMPTY + stage));
-                    umma_commit(bars + 8 * (BAR_ACC_FULL + acc));
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1;
-                    }
-                    if (++acc == ACC_STAGES) {
-                        acc = 0;
-                        acc_phase ^= 1;
-                    }
+                    umma_commit(bars + 8 * (C::BAR_EMPTY + stage));
+                    umma_commit(bars + 8 * (C::BAR_ACC_FULL + acc));
+                    ready = pe && pf;
+                    stage = nstage;
+                    phase = nphase;
+                    acc = nacc;
+                    acc_phase = nacc_phase;
                 }
                 if (!ok) break;
-                umma_commit(bars + 8 * BAR_A_EMPTY);
+                umma_commit(bars + 8 * C::BAR_A_EMPTY);
             }
             if (!ok && issued) {
-                umma_commit(bars + 8 * BAR_DRAIN);
-                mbar_drain_wait<false>(bars + 8 * BAR_DRAIN, 0);
+                umma_commit(bars + 8 * C::BAR_DRAIN);
+                mbar_drain_wait<false>(bars + 8 * C::BAR_DRAIN, 0);
             }
         }
     } else {
         // ------------------------------------------------------------ epilogue (warps 0-15)
         const int quarter = warp & 3, part = warp >> 2;
+        const int qt = part * COLS_PER_WARP / BN;              // query tile of this warp's columns
+        const int rowoff = part * COLS_PER_WARP - qt * BN;     // their first row within a corpus tile
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         CandBuf<EPI_THREADS, BUFN> buf;
-        buf.base = reinterpret_cast<uint2*>(smem + OFF_BUF) + threadIdx.x;
+        buf.base = reinterpret_cast<uint2*>(smem + C::OFF_BUF) + threadIdx.x;
         buf.n = 0;
         int acc = 0;
         uint32_t acc_phase = 0;
         bool ok = true;
-        const int32_t* nrm = norms + part * COLS_PER_WARP;
+        const int32_t* nrm = norms + rowoff;
         for (long long u = blockIdx.x; u < sched.n_units && ok; u += gridDim.x) {
             int g, t0, t1;
             unit_coords(sched, u, g, t0, t1);
-            const int qi = g * BM + quarter * 32 + lane;
+            const int qi = g * C::QGROUP + qt * BM + quarter * 32 + lane;
             const bool qvalid = qi < nq;
             uint32_t tkey = 0;
             int32_t tid = 0, qnv = 0;
@@ -261,43 +300,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 bias = -(1 << 30);
             else
                 bias = qnv - (int32_t)tkey;
-            // n_min of this warp's chunks, one tile ahead of their use.
-            int32_t nx[CHUNKS];
-#pragma unroll
-            for (int c = 0; c < CHUNKS; c++) nx[c] = t0 < t1 ? __ldg(nrm + (int64_t)t0 * BN + 32 * c) : 0;
+            // n_min of this warp's two chunks, one tile ahead of their use.
+            int32_t nx0 = 0, nx1 = 0;
+            if (t0 < t1) {
+                nx0 = __ldg(nrm + (int64_t)t0 * BN);
+                nx1 = __ldg(nrm + (int64_t)t0 * BN + 32);
+            }
             for (int t = t0; t < t1; t++) {
-                int32_t need[CHUNKS];
-#pragma unroll
-                for (int c = 0; c < CHUNKS; c++) {
-                    need[c] = nx[c] + bias;
-                    if (t + 1 < t1) nx[c] = __ldg(nrm + (int64_t)(t + 1) * BN + 32 * c);
+                const int32_t need0 = nx0 + bias, need1 = nx1 + bias;
+                if (t + 1 < t1) {
+                    nx0 = __ldg(nrm + (int64_t)(t + 1) * BN);
+                    nx1 = __ldg(nrm + (int64_t)(t + 1) * BN + 32);
                 }
-                ok = mbar_wait_inl<false>(bars + 8 * (BAR_ACC_FULL + acc), acc_phase, abort_flag, status);
+                ok = mbar_wait_inl<false>(bars + 8 * (C::BAR_ACC_FULL + acc), acc_phase, abort_flag, status);
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t tcol = tmem_base + lane_base + (uint32_t)(acc * BN + part * COLS_PER_WARP);
-                uint32_t v[CHUNKS][32];
+                const uint32_t tcol = tmem_base + lane_base + (uint32_t)(acc * C::ACC_COLS + part * COLS_PER_WARP);
+                uint32_t v[2][32];
                 __syncwarp();
-#pragma unroll
-                for (int c = 0; c < CHUNKS; c++) tmem_ld32_issue(tcol + 32 * c, v[c]);
-#pragma unroll
-                for (int c = 0; c < CHUNKS; c++) tmem_ld_wait(v[c]);  // the first wait covers every load
+                tmem_ld32_issue(tcol, v[0]);
+                tmem_ld32_issue(tcol + 32, v[1]);
+                tmem_ld_wait(v[0]);  // waits for both loads
+                tmem_ld_wait(v[1]);
                 // The chunks are in registers: hand the accumulator back to the MMA.
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(bars + 8 * (BAR_ACC_EMPTY + acc));
+                if (lane == 0) mbar_arrive(bars + 8 * (C::BAR_ACC_EMPTY + acc));
                 if (++acc == ACC_STAGES) {
                     acc = 0;
                     acc_phase ^= 1;
                 }
-                bool any = false;
+                const int32_t m0 = max32(v[0]), m1 = max32(v[1]);
+                if (2 * m0 < need0 && 2 * m1 < need1) continue;
+                const int32_t row0 = t * BN + rowoff;  // rows < 2^31 (ids are int32)
 #pragma unroll
-                for (int c = 0; c < CHUNKS; c++) any |= 2 * max32(v[c]) >= need[c];
-                if (!any) continue;
-                const int32_t row0 = t * BN + part * COLS_PER_WARP;  // rows < 2^31 (ids are int32)
-#pragma unroll
-                for (int c = 0; c < CHUNKS; c++) {
-                    uint32_t mask = pass_mask32(v[c], need[c]);
+                for (int c = 0; c < 2; c++) {
+                    uint32_t mask = pass_mask32(v[c], c ? need1 : need0);
                     while (mask) {
                         const int j = __ffs(mask) - 1;
                         mask &= mask - 1;
@@ -322,6 +360,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_dealloc<1>(tmem_base, TMEM_COLS);
     }
 }
+
+using CfgWide = TcCfg<128, 2>;    // 256 queries per CTA
+using CfgNarrow = TcCfg<256, 1>;  // 128 queries per CTA
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -368,14 +409,37 @@ int choose_scan_chunks(int groups, int n_tiles, int workers) {
 }
 
 bool tc_supported(const mdh_index* ix, const Level& lv) {
-    return ix && !ix->is_f32 && ix->dpad == BK && ix->dim <= BK && lv.rows && lv.norms && lv.n_pad % BN == 0 &&
-           lv.n_pad < (int64_t(1) << 31);
+    return ix && !ix->is_f32 && ix->dpad == BK && ix->dim <= BK && lv.rows && lv.norms &&
+           lv.n_pad % CfgWide::BN == 0 && lv.n_pad % CfgNarrow::BN == 0 && lv.n_pad < (int64_t(1) << 31);
 }
 
 void make_tmap_rows(Level& lv, int dpad) {
     if (dpad != BK || !lv.rows) return;
-    encode_u8_rows_tmap(&lv.tmap_rows, lv.rows, lv.n_pad, dpad, BN);
+    encode_u8_rows_tmap(&lv.tmap_rows, lv.rows, lv.n_pad, dpad, BOX_ROWS);
     lv.has_tmap = true;
+}
+
+template <class C>
+void launch_tc(const Level& lv, const CUtensorMap& tq, const int32_t* qn, int nq, const uint32_t* thr_key,
+               const int32_t* thr_id, uint32_t* counts, uint2* cand, int cap, int dense, int32_t* status,
+               cudaStream_t st) {
+    int dev;
+    MDH_CUDA(cudaGetDevice(&dev));
+    const int sms = device_sm_count(dev);
+    Sched s;
+    s.n_groups = (nq + C::QGROUP - 1) / C::QGROUP;
+    s.n_tiles = (int)(lv.n_pad / C::BN);
+    int ctas = sms;
+    s.n_chunks = choose_scan_chunks(s.n_groups, s.n_tiles, ctas);
+    s.n_units = (long long)s.n_groups * s.n_chunks;
+    if (s.n_units < ctas) ctas = (int)s.n_units;
+    // A function attribute belongs to the current device: set it on every launch.
+    MDH_CUDA(cudaFuncSetAttribute(k_filter_tc_u8_l2<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)C::SMEM_BYTES));
+    k_filter_tc_u8_l2<C><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
+                                                                   qn, nq, thr_key, thr_id, counts, cand, cap, dense,
+                                                                   s, status);
+    MDH_CUDA(cudaGetLastError());
 }
 
 void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
@@ -384,24 +448,15 @@ void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const i
     if (nq <= 0 || lv.n == 0) return;
     MDH_REQUIRE(dpad == BK && lv.has_tmap, MDH_ERR_INTERNAL, "tensor-core scan needs 128-byte rows and a TMA map");
     MDH_REQUIRE(!dense || cap >= lv.n, MDH_ERR_INTERNAL, "dense scan needs cap >= rows");
-    MDH_REQUIRE((reinterpret_cast<uintptr_t>(lv.norms) & 15) == 0, MDH_ERR_INTERNAL, "norms must be 16-byte aligned");
     CUtensorMap tq;
     encode_u8_rows_tmap(&tq, q, nq, dpad, BM);
-    int dev;
-    MDH_CUDA(cudaGetDevice(&dev));
-    const int sms = device_sm_count(dev);
-    Sched s;
-    s.n_qtiles = (nq + BM - 1) / BM;
-    s.n_tiles = (int)(lv.n_pad / BN);
-    int ctas = sms;
-    s.n_chunks = choose_scan_chunks(s.n_qtiles, s.n_tiles, ctas);
-    s.n_units = (long long)s.n_qtiles * s.n_chunks;
-    if (s.n_units < ctas) ctas = (int)s.n_units;
-    // A function attribute belongs to the current device: set it on every launch.
-    MDH_CUDA(cudaFuncSetAttribute(k_filter_tc_u8_l2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
-    k_filter_tc_u8_l2<<<ctas, NUM_THREADS, SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n, qn, nq,
-                                                            thr_key, thr_id, counts, cand, cap, dense, s, status);
-    MDH_CUDA(cudaGetLastError());
+#ifdef MDH_TC_WIDE
+    if (nq >= CfgWide::QGROUP) {
+        launch_tc<CfgWide>(lv, tq, qn, nq, thr_key, thr_id, counts, cand, cap, dense, status, st);
+        return;
+    }
+#endif
+    launch_tc<CfgNarrow>(lv, tq, qn, nq, thr_key, thr_id, counts, cand, cap, dense, status, st);
 }
 
 }  // namespace mdh
