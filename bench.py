@@ -352,15 +352,39 @@ def main():
         e2e_t = float(t.item())
 
     peaks, peak_src = measured_peaks()
-    int8_peak = 2.0 * peaks["bf16_tflops"]
     ms_scan = statistics.median(scan_ms) if scan_ms else float("nan")
     pairs = scan_pairs[0] if scan_pairs else 0
-    achieved = 2.0 * pairs * DIM / (ms_scan / 1e3) / 1e12 if ms_scan > 0 else None
-    # DRAM traffic of the scan per row: ncu capture of the same kernel on a
-    # 10M-row case (dram__bytes_read.sum + dram__bytes_write.sum = 1.3381e9 B
-    # per launch for 10,000 queries); the corpus and norms cross HBM once per
-    # launch, so traffic scales with the rows scanned.
-    traffic = TRAFFIC_BYTES_PER_ROW * (pairs / nq) if pairs else None
+    rows_scanned = pairs // nq if nq else 0
+    if tensor_path:
+        # Batched path: u8 x u8 -> s32 on tcgen05, compute-bound at 2*N*Q*D ops.
+        int8_peak = 2.0 * peaks["bf16_tflops"]
+        achieved = 2.0 * pairs * DIM / (ms_scan / 1e3) / 1e12 if ms_scan > 0 else None
+        # DRAM traffic of the scan: ncu capture of the same kernel on a
+        # 10M-row case (dram__bytes_read.sum + dram__bytes_write.sum =
+        # 1.3381e9 B per launch for 10,000 queries); the corpus and norms cross
+        # HBM once per launch, so traffic scales with the rows scanned.
+        traffic = TRAFFIC_BYTES_PER_ROW * rows_scanned if pairs else None
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",
+                    "frac": (achieved / int8_peak) if achieved else None, "traffic": traffic,
+                    "traffic_source": "ncu dram bytes of a 10M-row launch, scaled by rows (profiles/)",
+                    "kernel": "full-corpus u8 L2 scan (filter) kernel, k_filter_tc_u8_l2",
+                    "algorithmic": "2*N*Q*D int8 ops per launch",
+                    "peak_source": f"2 x {peak_src} bf16 dense ({peaks['bf16_tflops']} TF/s): u8 MMA runs at twice "
+                                   "the bf16 rate on sm_100",
+                    "kernel_ms": ms_scan}
+    else:
+        # Small batches (the single-query GEMV path): CUDA-core dp4a scan,
+        # bound by reading the u8 corpus (N*D bytes per launch) from HBM.
+        bytes_alg = rows_scanned * DIM
+        achieved = bytes_alg / (ms_scan / 1e3) / 1e9 if ms_scan > 0 else None
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": (achieved / peaks["hbm_gbs"]) if achieved else None,
+                    "traffic": rows_scanned * (DIM + 4) if pairs else None,
+                    "traffic_source": "corpus + norms once per launch (rows x (D + 4) B)",
+                    "kernel": "full-corpus u8 L2 scan (filter) kernel, k_filter_u8",
+                    "algorithmic": "N*D corpus bytes per launch",
+                    "peak_source": f"{peak_src} HBM copy bandwidth",
+                    "kernel_ms": ms_scan}
     line = {
         "metric": METRIC,
         "value": nq * args.steps / elapsed,
@@ -380,14 +404,7 @@ def main():
                 "d2h_bytes_per_step": int(nq * k * 8)},
         "gpu_launches": int(sum(launches)),
         "clocks": clocks,
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",
-                     "frac": (achieved / int8_peak) if achieved else None, "traffic": traffic,
-                     "traffic_source": "ncu dram bytes of a 10M-row launch, scaled by rows (profiles/)",
-                     "kernel": "full-corpus u8 L2 scan (filter) kernel",
-                     "algorithmic": "2*N*Q*D int8 ops per launch",
-                     "peak_source": f"2 x {peak_src} bf16 dense ({peaks['bf16_tflops']} TF/s): u8 MMA runs at twice "
-                                    "the bf16 rate on sm_100",
-                     "kernel_ms": ms_scan},
+        "roofline": roofline,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:

@@ -92,6 +92,12 @@ void launch_filter_simt_u8_l2(const Level& lv, int dpad, const uint8_t* q, const
 void launch_filter_simt_u8_cos(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
                                const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts,
                                uint2* cand, int cap, int dense, cudaStream_t st);
+// Streaming CUDA-core scan for small batches over 128-byte rows
+// (scan_stream.cu): mode 0 = L2, 1 = integer cosine.
+bool stream_supported(int dpad, const Level& lv);
+void launch_scan_stream_u8(const Level& lv, int dpad, int mode, const uint8_t* q, const int32_t* qn, int nq,
+                           const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts, uint2* cand, int cap,
+                           int dense, int32_t* status, cudaStream_t st);
 // Float replicas of the reference arithmetic (float queries).
 void launch_filter_f32(const Level& lv, int dim, int dpad, int score_kind, const float* q, int nq,
                        const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts, uint2* cand,

@@ -120,6 +120,9 @@ void filter(mdh_index* ix, const Level& lv, const uint8_t* q, const int32_t* qn,
     if (lv.has_tmap && tc_supported(ix, lv) && nq >= 64) {
         launch_filter_tc_u8_l2(lv, ix->dpad, q, qn, nq, tk, ti, counts, cand, cap, d, status, st);
         *path = 1;
+    } else if (stream_supported(ix->dpad, lv)) {
+        launch_scan_stream_u8(lv, ix->dpad, 0, q, qn, nq, tk, ti, counts, cand, cap, d, status, st);
+        *path = 0;
     } else {
         launch_filter_simt_u8_l2(lv, ix->dpad, q, qn, nq, tk, ti, counts, cand, cap, d, st);
         *path = 0;
