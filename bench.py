@@ -355,9 +355,13 @@ def main():
     ms_scan = statistics.median(scan_ms) if scan_ms else float("nan")
     pairs = scan_pairs[0] if scan_pairs else 0
     rows_scanned = pairs // nq if nq else 0
-    if tensor_path:
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    # Which roof bounds the scan: it does 2*Q int ops per corpus byte, so
+    # below the ridge point (peak ops / peak bytes) it is HBM-bound.
+    hbm_bound = 2.0 * nq < int8_peak * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    kernel_name = "k_filter_tc_u8_l2" if tensor_path else "k_scan_stream_u8"
+    if not hbm_bound:
         # Batched path: u8 x u8 -> s32 on tcgen05, compute-bound at 2*N*Q*D ops.
-        int8_peak = 2.0 * peaks["bf16_tflops"]
         achieved = 2.0 * pairs * DIM / (ms_scan / 1e3) / 1e12 if ms_scan > 0 else None
         # DRAM traffic of the scan: ncu capture of the same kernel on a
         # 10M-row case (dram__bytes_read.sum + dram__bytes_write.sum =
@@ -367,23 +371,23 @@ def main():
         roofline = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",
                     "frac": (achieved / int8_peak) if achieved else None, "traffic": traffic,
                     "traffic_source": "ncu dram bytes of a 10M-row launch, scaled by rows (profiles/)",
-                    "kernel": "full-corpus u8 L2 scan (filter) kernel, k_filter_tc_u8_l2",
+                    "kernel": f"full-corpus u8 L2 scan (filter) kernel, {kernel_name}",
                     "algorithmic": "2*N*Q*D int8 ops per launch",
                     "peak_source": f"2 x {peak_src} bf16 dense ({peaks['bf16_tflops']} TF/s): u8 MMA runs at twice "
                                    "the bf16 rate on sm_100",
                     "kernel_ms": ms_scan}
     else:
-        # Small batches (the single-query GEMV path): CUDA-core dp4a scan,
-        # bound by reading the u8 corpus (N*D bytes per launch) from HBM.
+        # Small batches (the single-query GEMV end): bound by reading the u8
+        # corpus (N*D bytes per launch) from HBM.
         bytes_alg = rows_scanned * DIM
         achieved = bytes_alg / (ms_scan / 1e3) / 1e9 if ms_scan > 0 else None
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                     "frac": (achieved / peaks["hbm_gbs"]) if achieved else None,
                     "traffic": rows_scanned * (DIM + 4) if pairs else None,
                     "traffic_source": "corpus + norms once per launch (rows x (D + 4) B)",
-                    "kernel": "full-corpus u8 L2 scan (filter) kernel, k_filter_u8",
+                    "kernel": f"full-corpus u8 L2 scan (filter) kernel, {kernel_name}",
                     "algorithmic": "N*D corpus bytes per launch",
-                    "peak_source": f"{peak_src} HBM copy bandwidth",
+                    "peak_source": f"{peak_src} HBM copy bandwidth (read + write)",
                     "kernel_ms": ms_scan}
     line = {
         "metric": METRIC,

@@ -53,7 +53,7 @@ def test_search_u8_distances_exact(path):
         L.mdh_set_scan_path(0)
 
 
-@pytest.mark.parametrize("nq", [64, 100, 255, 256, 300, 513])
+@pytest.mark.parametrize("nq", [1, 5, 64, 100, 255, 256, 300, 513])
 def test_tensor_scan_batch_shapes(nq):
     """Both tensor tile shapes (128 and 256 queries per CTA) and partial query groups."""
     L = capi()
@@ -67,6 +67,29 @@ def test_tensor_scan_batch_shapes(nq):
         np.testing.assert_array_equal(ids, want_ids)
         np.testing.assert_array_equal(dist, want_d)
         assert s.tensor_core_path == 1
+        assert L.mdh_index_destroy(h) == 0
+    finally:
+        L.mdh_set_scan_path(0)
+
+
+@pytest.mark.parametrize("nq", [1, 3, 8, 9, 40])
+@pytest.mark.parametrize("metric", [1, 0])
+def test_stream_scan_batch_shapes(nq, metric):
+    """The streaming CUDA-core scan (query groups of 1/2/4/8, partial last group), L2 and cosine."""
+    L = capi()
+    L.mdh_set_scan_path(1)
+    try:
+        C = cases.gmm_u8(50_001, 128, 128, seed=25)
+        Q = cases.gmm_u8_queries(nq, 128, 128, seed_means=25, seed_q=26)
+        h = _create_u8(L, C, metric=metric)
+        ids, dist, s = _search_u8(L, h, Q, 12)
+        if metric == 1:
+            want_ids, want_d = oracle.l2_exact_u8_int(C, Q, 12)
+            np.testing.assert_array_equal(dist, want_d)
+        else:
+            want_ids = oracle.cosine_exact_u8(C, Q.astype(np.float32), 12)[0]
+        np.testing.assert_array_equal(ids, want_ids)
+        assert s.tensor_core_path == 0
         assert L.mdh_index_destroy(h) == 0
     finally:
         L.mdh_set_scan_path(0)

@@ -163,9 +163,10 @@ void ensure_status(Workspace& w) {
 // thresholds, cap >= rows); the kernels write row r at slot r and the
 // counts are set to the row count here.
 // Returns the scan used: 1 CUDA cores, 2 tensor cores (one SM per tile),
-// 3 tensor cores (SM pairs).  Auto takes the single-SM tensor scan from 64
-// queries up (measured faster than the SM-pair scan at every batch size on
-// B200); the pair scan runs only when selected.
+// 3 tensor cores (SM pairs).  Auto takes the single-SM tensor scan for every
+// batch size: on B200 it was measured faster than the SM-pair scan at every
+// batch and faster than the streaming CUDA-core scan even for one query (at
+// one query both read the corpus from HBM; TMA keeps more of it in flight).
 
 int run_filter(mdh_index* ix, Shard& sh, const Level& lv, const QueryPlan& qp, const uint8_t* q_u8,
                const int32_t* qn, const float* q_f32, int nq, const uint32_t* tk, const int32_t* ti, int cap,
@@ -182,7 +183,7 @@ int run_filter(mdh_index* ix, Shard& sh, const Level& lv, const QueryPlan& qp, c
             else if (g_scan_path == 2 && can1)
                 used = 2;
             else if (g_scan_path == 0)
-                used = (can1 && nq >= 64) ? 2 : 1;
+                used = can1 ? 2 : 1;
             if (used == 3)
                 launch_filter_tc2_u8_l2(lv, ix->dpad, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, d, w.status,
                                         sh.stream);

@@ -117,7 +117,7 @@ void filter(mdh_index* ix, const Level& lv, const uint8_t* q, const int32_t* qn,
             const int32_t* ti, uint32_t* counts, uint2* cand, int cap, bool dense, int32_t* status, cudaStream_t st,
             int* path) {
     const int d = dense ? 1 : 0;
-    if (lv.has_tmap && tc_supported(ix, lv) && nq >= 64) {
+    if (lv.has_tmap && tc_supported(ix, lv)) {
         launch_filter_tc_u8_l2(lv, ix->dpad, q, qn, nq, tk, ti, counts, cand, cap, d, status, st);
         *path = 1;
     } else if (stream_supported(ix->dpad, lv)) {
