@@ -60,13 +60,15 @@ typedef struct {
     double latency_ms;            /* host wall time of the call (SearchResult::latency_ms) */
     int64_t pairs_scored;         /* (query, row) pairs evaluated (bound_pairs / exact_evals) */
     int64_t pairs_pruned_by_bound;/* pairs skipped by the norm lower bound */
-    int64_t bound_violations;     /* pruned pairs that belonged in the top-K: measured, must be 0 */
+    int64_t bound_violations;     /* rows misplaced relative to the returned top-K, counted for the
+                                     verified queries by an exact unpruned scan (mdh_set_verify); 0 */
     int64_t candidates;           /* pairs that passed the threshold filter into the final selection */
     int32_t tensor_core_path;     /* full-corpus scan: 0 CUDA cores, 1 tcgen05 per SM, 2 tcgen05 on SM pairs */
     int32_t levels;               /* threshold-refinement levels run */
     double full_scan_ms;          /* CUDA-event time of the full-corpus scan kernel(s) on their stream */
     int64_t full_scan_pairs;      /* (query, row) pairs that kernel scored */
     int64_t kernel_launches;      /* this library's kernels launched by the call */
+    int64_t verified_queries;     /* queries re-checked by the verification scan (mdh_set_verify) */
 } mdh_stats;
 
 /* Build an index over a row-major u8 corpus [n][dim] held in host memory.
@@ -157,6 +159,15 @@ mdh_status mdh_merge_topk_device(const int32_t* dev_dist_all, const int32_t* dev
  * single SMs, 3 = tensor-core scan on SM pairs (each whenever the shape
  * allows; otherwise the CUDA-core scan). */
 mdh_status mdh_set_scan_path(int32_t path);
+
+/* Options (process-wide): verification.  max_queries > 0 makes every u8
+ * integer search re-check up to that many of its queries (spread evenly over
+ * the batch) with an exact CUDA-core scan that prunes nothing: it counts the
+ * rows at or before each query's k-th result by (distance, id), and any count
+ * other than k adds to mdh_stats.bound_violations.  0 = off (default).  The
+ * reference declares bound_violations but never measures it
+ * (include/winnex_madhava/winnex_madhava.hpp:125). */
+mdh_status mdh_set_verify(int32_t max_queries);
 
 /* Options (process-wide): upper bound on a query's candidate list length
  * (a power of two in [64, 16384]; 0 = automatic).  A list that overflows is

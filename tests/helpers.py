@@ -32,7 +32,7 @@ class Stats(ctypes.Structure):
                 ("pairs_pruned_by_bound", ctypes.c_int64), ("bound_violations", ctypes.c_int64),
                 ("candidates", ctypes.c_int64), ("tensor_core_path", ctypes.c_int32), ("levels", ctypes.c_int32),
                 ("full_scan_ms", ctypes.c_double), ("full_scan_pairs", ctypes.c_int64),
-                ("kernel_launches", ctypes.c_int64)]
+                ("kernel_launches", ctypes.c_int64), ("verified_queries", ctypes.c_int64)]
 
 
 def capi():
@@ -49,12 +49,14 @@ def capi():
     L.mdh_search_u8_device_noalloc.argtypes = [P, P, i32, i32, P, P, P, ctypes.POINTER(Stats)]
     L.mdh_merge_topk_device.argtypes = [P, P, i32, i32, i32, P, P, P]
     L.mdh_set_scan_path.argtypes = [i32]
+    L.mdh_set_verify.argtypes = [i32]
     L.mdh_set_candidate_cap_limit.argtypes = [i32]
     L.mdh_last_error.restype = ctypes.c_char_p
     L.mdh_version.restype = ctypes.c_char_p
     L.mdh_device_count.restype = i32
     for fn in ("mdh_index_create_u8", "mdh_index_create_u8_device", "mdh_index_create_f32", "mdh_index_destroy", "mdh_index_info", "mdh_search_f32",
                "mdh_search_u8", "mdh_search_u8_device", "mdh_search_u8_device_noalloc", "mdh_merge_topk_device", "mdh_set_scan_path",
+               "mdh_set_verify",
                "mdh_set_candidate_cap_limit"):
         getattr(L, fn).restype = ctypes.c_int
     return L

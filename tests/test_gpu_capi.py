@@ -95,6 +95,27 @@ def test_stream_scan_batch_shapes(nq, metric):
         L.mdh_set_scan_path(0)
 
 
+@pytest.mark.parametrize("metric", [1, 0])
+def test_verification_counts_zero_violations(metric):
+    """mdh_set_verify: an exact unpruned re-scan of sampled queries finds no misplaced rows."""
+    L = capi()
+    assert L.mdh_set_verify(48) == 0
+    try:
+        C = cases.gmm_u8(150_000, 128, 64, seed=27)
+        Q = cases.gmm_u8_queries(300, 128, 64, seed_means=27, seed_q=28)
+        h = _create_u8(L, C, metric=metric)
+        ids, _, s = _search_u8(L, h, Q, 10)
+        assert s.verified_queries == 48
+        assert s.bound_violations == 0
+        assert 300 * 10 <= s.candidates <= 300 * 16384
+        if metric == 1:
+            np.testing.assert_array_equal(ids, oracle.l2_exact_u8_int(C, Q, 10)[0])
+        assert L.mdh_index_destroy(h) == 0
+    finally:
+        assert L.mdh_set_verify(0) == 0
+    assert L.mdh_set_verify(-1) != 0
+
+
 def test_device_api_and_merge():
     torch = pytest.importorskip("torch")
     L = capi()

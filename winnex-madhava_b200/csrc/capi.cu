@@ -32,6 +32,7 @@ namespace {
 thread_local std::string g_last_error;
 int g_scan_path = 0;  // 0 auto, 1 CUDA cores only, 2 tensor cores when possible
 int g_cap_limit = 0;  // 0 = default candidate capacities
+int g_verify = 0;     // queries per search re-checked by an exact unpruned scan (0 = off)
 
 constexpr int kCapMax = 16384;          // largest candidate list the selection kernel sorts
 constexpr size_t kCandBudget = size_t(2) << 30;  // bytes of candidate lists per query chunk
@@ -153,8 +154,8 @@ void growT(T** p, size_t* have, size_t need_bytes) {
 
 void ensure_status(Workspace& w) {
     if (!w.status) {
-        MDH_CUDA(cudaMalloc(&w.status, 4 * sizeof(int32_t)));
-        MDH_CUDA(cudaHostAlloc(&w.h_status, 4 * sizeof(int32_t), cudaHostAllocDefault));
+        MDH_CUDA(cudaMalloc(&w.status, 8 * sizeof(int32_t)));
+        MDH_CUDA(cudaHostAlloc(&w.h_status, 8 * sizeof(int32_t), cudaHostAllocDefault));
     }
 }
 
@@ -208,13 +209,15 @@ int run_filter(mdh_index* ix, Shard& sh, const Level& lv, const QueryPlan& qp, c
 
 struct ShardResult {
     int64_t pairs = 0;
-    int64_t candidates = 0;
     int levels = 0;
     bool tc = false;
     double scan_ms = 0.0;     // event time of the full-shard filter
     int64_t scan_pairs = 0;
     int scan_path = 0;        // run_filter's path for the full shard
     int64_t launches = 0;     // kernels launched
+    int64_t candidates = 0;   // entries of the final candidate lists
+    int64_t violations = 0;   // verification: rows misplaced relative to the results
+    int64_t verified = 0;     // verification: queries re-checked
 };
 
 // Exact top-k for nq staged queries on one shard.  Results: ws.out_key /
@@ -237,7 +240,9 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
     growT(&w.out_id, &w.out_id_bytes, (size_t)nq * k * 4);
     growT(&w.flags, &w.flags_bytes, (size_t)nq * 4);
     ensure_status(w);
-    MDH_CUDA(cudaMemsetAsync(w.status, 0, 2 * sizeof(int32_t), st));
+    MDH_CUDA(cudaMemsetAsync(w.status, 0, 6 * sizeof(int32_t), st));
+    unsigned long long* n_cand = reinterpret_cast<unsigned long long*>(w.status + 2);
+    unsigned long long* n_viol = reinterpret_cast<unsigned long long*>(w.status + 4);
 
     res.levels = (int)steps.size();
     for (size_t si = 0; si < steps.size(); si++) {
@@ -269,7 +274,7 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
         const bool final_ = si + 1 == steps.size();
         if (final_) MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
         launch_select(w.counts, w.cand, s.cap, lv.ids, nq, k, final_ ? 1 : 0, w.thr_key, w.thr_id, w.out_key,
-                      w.out_id, w.flags, w.status + 1, nullptr, st);
+                      w.out_id, w.flags, w.status + 1, nullptr, final_ ? n_cand : nullptr, st);
         res.launches++;
     }
     // Status words: [0] device error of the tensor-core scan, [1] overflowed queries.
@@ -343,7 +348,7 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
         run_filter(ix, sh, lv, qp, cq_u8, cqn, cq_f32, m, d_tk, d_ti, last.cap, false);
         MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
         launch_select(w.counts, w.cand, last.cap, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id, w.flags,
-                      w.status + 1, d_list, st);
+                      w.status + 1, d_list, n_cand, st);
         res.launches += 2;  // filter + select
         MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
         MDH_CUDA(cudaStreamSynchronize(st));
@@ -351,6 +356,47 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
             throw Error(MDH_ERR_TIMEOUT, "tensor-core scan reported device status " + std::to_string(w.h_status[0]));
         flagged = w.h_status[1];
         res.pairs += lv.n * (int64_t)m;
+    }
+    // Verification (opt-in): for up to g_verify queries, an exact scan with no
+    // pruning (the CUDA-core kernels compare every row) counts the rows at or
+    // before each query's k-th result by (key, id).  An exact result has
+    // exactly k of them; any other count is reported as violations.
+    if (g_verify > 0 && qp.integer && nq > 0) {
+        const int m = std::min(nq, g_verify);
+        std::vector<int32_t> list((size_t)m);
+        for (int i = 0; i < m; i++) list[(size_t)i] = (int32_t)((int64_t)i * nq / m);
+        growT(&w.qlist, &w.qlist_bytes, (size_t)m * 4 * 3);
+        int32_t* d_list = w.qlist;
+        uint32_t* d_tk = reinterpret_cast<uint32_t*>(w.qlist + m);
+        int32_t* d_ti = w.qlist + 2 * m;
+        MDH_CUDA(cudaMemcpyAsync(d_list, list.data(), (size_t)m * 4, cudaMemcpyHostToDevice, st));
+        grow(&w.tmp, &w.tmp_bytes, round_up((size_t)m * ix->dpad, 256) + (size_t)m * 4 + 256);
+        uint8_t* cq_u8 = static_cast<uint8_t*>(w.tmp);
+        int32_t* cqn = reinterpret_cast<int32_t*>(cq_u8 + round_up((size_t)m * ix->dpad, 256));
+        launch_gather_queries_u8(w.q_u8, w.qn, d_list, m, ix->dpad, cq_u8, cqn, st);
+        launch_verify_thresholds(d_list, m, w.out_key, w.out_id, k, k, d_tk, d_ti, st);
+        MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
+        const int mode = ix->metric == MDH_METRIC_L2 ? 0 : 1;
+        if (stream_supported(ix->dpad, lv))
+            launch_scan_stream_u8(lv, ix->dpad, mode, cq_u8, cqn, m, d_tk, d_ti, w.counts, w.cand, 0, 0, w.status, st);
+        else if (mode == 0)
+            launch_filter_simt_u8_l2(lv, ix->dpad, cq_u8, cqn, m, d_tk, d_ti, w.counts, w.cand, 0, 0, st);
+        else
+            launch_filter_simt_u8_cos(lv, ix->dpad, cq_u8, cqn, m, d_tk, d_ti, w.counts, w.cand, 0, 0, st);
+        launch_count_violations(w.counts, m, k, n_viol, st);
+        res.launches += 4;
+        res.verified = m;
+    }
+    MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 6 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    MDH_CUDA(cudaStreamSynchronize(st));
+    if (w.h_status[0] != kDevOk)
+        throw Error(MDH_ERR_TIMEOUT, "scan reported device status " + std::to_string(w.h_status[0]));
+    {
+        unsigned long long cand_n = 0, viol_n = 0;
+        std::memcpy(&cand_n, w.h_status + 2, 8);
+        std::memcpy(&viol_n, w.h_status + 4, 8);
+        res.candidates = (int64_t)cand_n;
+        res.violations = (int64_t)viol_n;
     }
     (void)host_q_u8;
     return res;
@@ -514,6 +560,9 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
             st.tensor_core_path = std::max(st.tensor_core_path, r.scan_path - 1);
             st.full_scan_pairs += r.scan_pairs;
             st.kernel_launches += r.launches;
+            st.candidates += r.candidates;
+            st.bound_violations += r.violations;
+            st.verified_queries += r.verified;
             chunk_scan_ms = std::max(chunk_scan_ms, r.scan_ms);  // shards run concurrently
         }
         st.full_scan_ms += chunk_scan_ms;
@@ -747,6 +796,9 @@ mdh_status mdh_search_u8_device(mdh_index* index, const uint8_t* dev_queries, in
                 st.full_scan_ms = r.scan_ms;
                 st.full_scan_pairs = r.scan_pairs;
                 st.kernel_launches = 1 + r.launches;  // query norms + the shard's search
+                st.candidates = r.candidates;
+                st.bound_violations = r.violations;
+                st.verified_queries = r.verified;
                 if (kk == k) {
                     MDH_CUDA(cudaMemcpyAsync(dev_ids, w.out_id, (size_t)nq * k * 4, cudaMemcpyDeviceToDevice, sh.stream));
                     if (dev_dist)
@@ -791,6 +843,13 @@ mdh_status mdh_set_scan_path(int32_t path) {
     return guard([&] {
         MDH_REQUIRE(path >= 0 && path <= 3, MDH_ERR_INVALID_ARG, "path must be 0, 1, 2 or 3");
         g_scan_path = path;
+    });
+}
+
+mdh_status mdh_set_verify(int32_t max_queries) {
+    return guard([&] {
+        MDH_REQUIRE(max_queries >= 0 && max_queries <= 65536, MDH_ERR_INVALID_ARG, "max_queries must be in [0, 65536]");
+        g_verify = max_queries;
     });
 }
 

@@ -43,7 +43,8 @@ struct Workspace {
     int32_t* out_id = nullptr;   size_t out_id_bytes = 0;   // [nq][k]
     int32_t* flags = nullptr;    size_t flags_bytes = 0;    // [nq] overflow flags
     int32_t* qlist = nullptr;    size_t qlist_bytes = 0;    // [nq] query index list
-    int32_t* status = nullptr;                               // [4] device status words
+    int32_t* status = nullptr;   // [8] device status words: [0] scan error, [1] overflowed
+                                 // queries, [2..3] u64 final candidates, [4..5] u64 violations
     int32_t* h_status = nullptr;                             // pinned mirror
     void* tmp = nullptr;         size_t tmp_bytes = 0;      // CUB / misc scratch
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;               // brackets the full-shard scan
@@ -139,7 +140,12 @@ void launch_fill_u32(uint32_t* p, int n, uint32_t v, cudaStream_t st);
 // Candidates hold {key, row position in the scanned level}; ids maps positions to global ids.
 void launch_select(const uint32_t* counts, const uint2* cand, int cap, const int32_t* ids, int nq, int k, int final_,
                    uint32_t* thr_key, int32_t* thr_id, uint32_t* out_key, int32_t* out_id,
-                   int32_t* flags, int32_t* n_flagged, const int32_t* qmap, cudaStream_t st);
+                   int32_t* flags, int32_t* n_flagged, const int32_t* qmap, unsigned long long* n_cand,
+                   cudaStream_t st);
+// Verification of results (capi.cu, search with verification on).
+void launch_verify_thresholds(const int32_t* list, int m, const uint32_t* out_key, const int32_t* out_id, int k, int kk,
+                              uint32_t* thr_key, int32_t* thr_id, cudaStream_t st);
+void launch_count_violations(const uint32_t* counts, int m, int kk, unsigned long long* violations, cudaStream_t st);
 void launch_merge_topk(const uint32_t* key_all, const int32_t* id_all, int nshard, int nq, int k,
                        uint32_t* key_out, int32_t* id_out, cudaStream_t st);
 void launch_gather_queries_u8(const uint8_t* src, const int32_t* qn_src, const int32_t* list, int m,

@@ -193,7 +193,7 @@ void search_noalloc(mdh_index* ix, const uint8_t* dev_q, int nq, int k, int32_t*
                 s.pairs_scored += lv.n * (int64_t)nq;
                 const bool final_ = si + 1 == ns;
                 launch_select(counts, cand, p.cap, lv.ids, nq, kk, final_ ? 1 : 0, thr_key, thr_id, out_key, out_id,
-                              flags, status + 1, nullptr, st);
+                              flags, status + 1, nullptr, nullptr, st);
                 s.kernel_launches++;
                 if (final_) {
                     s.full_scan_pairs = lv.n * (int64_t)nq;
@@ -213,7 +213,7 @@ void search_noalloc(mdh_index* ix, const uint8_t* dev_q, int nq, int k, int32_t*
                 MDH_CUDA(cudaMemsetAsync(status + 1, 0, sizeof(int32_t), st));
                 filter(ix, lv, q, qn, nq, thr_key, thr_id, counts, cand, last.cap, false, status, st, &path);
                 launch_select(counts, cand, last.cap, lv.ids, nq, kk, 1, thr_key, thr_id, out_key, out_id, flags,
-                              status + 1, nullptr, st);
+                              status + 1, nullptr, nullptr, st);
                 s.kernel_launches += 2;
                 s.pairs_scored += lv.n * (int64_t)nq;
                 read_status(status, st);

@@ -515,4 +515,7 @@ PYBIND11_MODULE(_winnex_madhava, m) {
     m.def("device_count", &mdh_device_count);
     m.def("version", &mdh_version);
     m.def("set_scan_path", [](int p) { check(mdh_set_scan_path(p)); }, py::arg("path"));
+    m.def("set_verify", [](int n) { check(mdh_set_verify(n)); }, py::arg("max_queries"),
+          "Re-check up to max_queries queries of every search with an exact unpruned scan; misplaced rows are "
+          "counted in bound_violations (0 = off).");
 }

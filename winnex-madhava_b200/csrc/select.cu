@@ -57,7 +57,8 @@ __global__ void k_select(const uint32_t* __restrict__ counts, const uint2* __res
                          const int32_t* __restrict__ ids, int k,
                          int final_, uint32_t* __restrict__ thr_key, int32_t* __restrict__ thr_id,
                          uint32_t* __restrict__ out_key, int32_t* __restrict__ out_id, int32_t* __restrict__ flags,
-                         int32_t* __restrict__ n_flagged, const int32_t* __restrict__ qmap) {
+                         int32_t* __restrict__ n_flagged, const int32_t* __restrict__ qmap,
+                         unsigned long long* __restrict__ n_cand) {
     extern __shared__ unsigned long long keys[];
     const int q = blockIdx.x;
     const int qo = qmap ? qmap[q] : q;
@@ -109,7 +110,33 @@ __global__ void k_select(const uint32_t* __restrict__ counts, const uint2* __res
             out_id[(size_t)qo * k + j] = -1;
         }
     }
-    if (threadIdx.x == 0 && flags) flags[qo] = 0;
+    if (threadIdx.x == 0) {
+        if (flags) flags[qo] = 0;
+        if (n_cand) atomicAdd(n_cand, (unsigned long long)c);
+    }
+}
+
+// Verification: query i of a compact list gets the threshold (key, id) of the
+// kk-th entry of its result (an empty entry, id -1, means no threshold).
+__global__ void k_verify_thresholds(const int32_t* __restrict__ list, int m, const uint32_t* __restrict__ out_key,
+                                    const int32_t* __restrict__ out_id, int k, int kk, uint32_t* __restrict__ thr_key,
+                                    int32_t* __restrict__ thr_id) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= m) return;
+    const size_t e = (size_t)list[i] * k + (kk - 1);
+    const int32_t id = out_id[e];
+    thr_key[i] = id >= 0 ? out_key[e] : kKeyInf;
+    thr_id[i] = id >= 0 ? id : kIdInf;
+}
+
+// Every row at or before the kk-th result, by (key, id), was counted by an
+// exact scan; an exact result has exactly kk of them.
+__global__ void k_count_violations(const uint32_t* __restrict__ counts, int m, int kk,
+                                   unsigned long long* __restrict__ violations) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= m) return;
+    const long long d = (long long)counts[i] - kk;
+    if (d != 0) atomicAdd(violations, (unsigned long long)(d > 0 ? d : -d));
 }
 
 // Merge [nshard][nq][k] lists into [nq][k]; id -1 marks an empty entry.
@@ -172,7 +199,7 @@ void launch_fill_threshold(uint32_t* thr_key, int32_t* thr_id, int nq, uint32_t 
 void launch_select(const uint32_t* counts, const uint2* cand, int cap, const int32_t* ids, int nq, int k, int final_,
                    uint32_t* thr_key,
                    int32_t* thr_id, uint32_t* out_key, int32_t* out_id, int32_t* flags, int32_t* n_flagged,
-                   const int32_t* qmap, cudaStream_t st) {
+                   const int32_t* qmap, unsigned long long* n_cand, cudaStream_t st) {
     if (nq <= 0) return;
     int pmax = 1;
     while (pmax < (cap > k ? cap : k)) pmax <<= 1;
@@ -181,7 +208,20 @@ void launch_select(const uint32_t* counts, const uint2* cand, int cap, const int
     if (smem > 48 * 1024) MDH_CUDA(cudaFuncSetAttribute(k_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int threads = pmax >= 4096 ? 1024 : (pmax >= 1024 ? 512 : 256);
     k_select<<<nq, threads, smem, st>>>(counts, cand, cap, ids, k, final_, thr_key, thr_id, out_key, out_id, flags,
-                                        n_flagged, qmap);
+                                        n_flagged, qmap, n_cand);
+    MDH_CUDA(cudaGetLastError());
+}
+
+void launch_verify_thresholds(const int32_t* list, int m, const uint32_t* out_key, const int32_t* out_id, int k, int kk,
+                              uint32_t* thr_key, int32_t* thr_id, cudaStream_t st) {
+    if (m <= 0) return;
+    k_verify_thresholds<<<(m + 255) / 256, 256, 0, st>>>(list, m, out_key, out_id, k, kk, thr_key, thr_id);
+    MDH_CUDA(cudaGetLastError());
+}
+
+void launch_count_violations(const uint32_t* counts, int m, int kk, unsigned long long* violations, cudaStream_t st) {
+    if (m <= 0) return;
+    k_count_violations<<<(m + 255) / 256, 256, 0, st>>>(counts, m, kk, violations);
     MDH_CUDA(cudaGetLastError());
 }
 

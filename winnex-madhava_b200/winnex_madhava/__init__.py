@@ -67,6 +67,9 @@ recall_at_k = _native.recall_at_k
 ndcg_at_k = _native.ndcg_at_k
 read_bigann_groundtruth = _native.read_bigann_groundtruth
 l2_sq = _native.l2_sq
+# Not in the reference API: re-check up to n queries of every search with an
+# exact unpruned scan and report misplaced rows in bound_violations (0 = off).
+set_verify = _native.set_verify
 
 __version__ = "1.9.3+b200"
 __all__ = [
@@ -84,6 +87,7 @@ __all__ = [
     "build_engine",
     "retrieve",
     "benchmark_vs_groundtruth",
+    "set_verify",
     "__version__",
 ]
 
