@@ -154,6 +154,31 @@ mdh_status mdh_merge_topk_device(const int32_t* dev_dist_all, const int32_t* dev
                                  int32_t nq, int32_t k, int32_t* dev_dist_out, int32_t* dev_ids_out,
                                  void* stream);
 
+/* ---------------------------------------------------------------- IVF
+ * Clustered index over a u8 corpus: the GPU form of MadHybrid's uint8 path
+ * (python/winnex_madhava/__init__.py:547-654).  The caller supplies the
+ * cells: centroids [nlist][dim] float32 and one label per row (the reference
+ * computes them with MiniBatchKMeans, __init__.py:577-593).  A query goes to
+ * the nprobe cells with the largest centroid inner product (the reference's
+ * `centroids @ q`, :631-632; here in fp64, ties to the lower cell id) and the
+ * result is the exact top-k over the union of those cells by (squared L2
+ * distance, row id).  dim <= 128, nlist <= 8192, nprobe <= 1024, k <= 4096. */
+typedef struct mdh_ivf mdh_ivf;
+
+/* device: GPU ordinal, -1 = the current device.  Row ids are 0..n-1. */
+mdh_status mdh_ivf_create_u8(const uint8_t* host_corpus, int64_t n, int32_t dim, const float* centroids,
+                             int32_t nlist, const int32_t* labels, int32_t device, mdh_ivf** out);
+/* out_cells [nq][nprobe]: the cells each query probes, best first. */
+mdh_status mdh_ivf_route_u8(mdh_ivf* index, const uint8_t* host_queries, int32_t nq, int32_t nprobe,
+                            int32_t* out_cells);
+/* u8 host queries [nq][dim]; out_ids / out_dist (exact squared L2, NULL
+ * allowed) [nq][k], -1 past the rows of the probed cells. */
+mdh_status mdh_ivf_search_u8(mdh_ivf* index, const uint8_t* host_queries, int32_t nq, int32_t k, int32_t nprobe,
+                             int32_t* out_ids, int32_t* out_dist, mdh_stats* stats);
+/* cell_rows (NULL allowed): [nlist] rows per cell. */
+mdh_status mdh_ivf_info(const mdh_ivf* index, int64_t* n, int32_t* dim, int32_t* nlist, int64_t* cell_rows);
+mdh_status mdh_ivf_destroy(mdh_ivf* index);
+
 /* Options (process-wide): force the scan path for testing and measurement.
  * path: 0 = automatic, 1 = CUDA-core scan only, 2 = tensor-core scan on
  * single SMs, 3 = tensor-core scan on SM pairs (each whenever the shape

@@ -353,6 +353,38 @@ void oracle_score_ids(int kind, int is_cosine, const uint8_t* corpus_u8, const f
     free(qbuf);
 }
 
+/* MadHybrid routing, python/winnex_madhava/__init__.py:631-632:
+ * sims = centroids @ q, then the nprobe largest (argsort(-sims)[:nprobe]).
+ * The reference evaluates the product in float32 through BLAS, whose
+ * summation order is unspecified; this restatement fixes it: fp64
+ * multiply-adds in dimension order from 0.0, ties to the lower cell id.
+ * out_cells: [nq][nprobe], best first. */
+void oracle_ivf_route(const float* centroids, int nlist, int d, const uint8_t* queries, int nq, int nprobe,
+                      int32_t* out_cells) {
+#pragma omp parallel
+    {
+        double* sims = (double*)malloc(sizeof(double) * (size_t)nlist);
+#pragma omp for schedule(dynamic, 4)
+        for (int qi = 0; qi < nq; qi++) {
+            const uint8_t* q = queries + (size_t)qi * d;
+            for (int c = 0; c < nlist; c++) {
+                const float* cr = centroids + (size_t)c * d;
+                double acc = 0.0;
+                for (int j = 0; j < d; j++) acc = fma((double)q[j], (double)cr[j], acc);
+                sims[c] = acc;
+            }
+            for (int p = 0; p < nprobe; p++) {
+                int bi = -1;
+                for (int c = 0; c < nlist; c++)
+                    if (bi < 0 || sims[c] > sims[bi]) bi = c; /* first maximum = lower id */
+                out_cells[(size_t)qi * nprobe + p] = bi;
+                sims[bi] = -INFINITY;
+            }
+        }
+        free(sims);
+    }
+}
+
 int oracle_num_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

@@ -58,6 +58,7 @@ def lib() -> ctypes.CDLL:
         L.oracle_l2_sq_u8.restype = f32
         L.oracle_num_threads.restype = i32
         L.oracle_score_ids.argtypes = [i32, i32, P, P, P, i32, P, P, i32, P]
+        L.oracle_ivf_route.argtypes = [P, i32, i32, P, i32, i32, P]
         L.oracle_score_ids.restype = None
         for fn in ("oracle_l2_exact_u8", "oracle_l2_exact_u8_int", "oracle_cosine_exact_u8",
                    "oracle_speed_exact", "oracle_speed_prepare_u8", "oracle_speed_prepare_f32"):
@@ -189,6 +190,37 @@ def equivalent_topk(kind: str, corpus, queries, got, want, prepared=None) -> lis
         if strict_w != strict_g:
             bad.append(i)
     return bad
+
+
+def ivf_route(centroids, queries_u8, nprobe):
+    """[nq, nprobe] cells per query, best first (MadHybrid routing,
+    python/winnex_madhava/__init__.py:631-632, fp64 in dimension order)."""
+    Cn = np.ascontiguousarray(centroids, dtype=np.float32)
+    Q = np.ascontiguousarray(queries_u8, dtype=np.uint8)
+    if Q.ndim == 1:
+        Q = Q[None, :]
+    out = np.empty((Q.shape[0], nprobe), np.int32)
+    lib().oracle_ivf_route(_p(Cn), Cn.shape[0], Cn.shape[1], _p(Q), Q.shape[0], nprobe, _p(out))
+    return out
+
+
+def ivf_exact(corpus, labels, centroids, queries_u8, k, nprobe):
+    """(ids, dist) [nq, k]: exact top-k by (squared L2, row id) over the union
+    of each query's probed cells; -1 past the rows available."""
+    C = np.ascontiguousarray(corpus, dtype=np.uint8)
+    Q = np.ascontiguousarray(queries_u8, dtype=np.uint8)
+    probe = ivf_route(centroids, Q, nprobe)
+    labels = np.asarray(labels)
+    ids = np.full((Q.shape[0], k), -1, np.int32)
+    dist = np.full((Q.shape[0], k), -1, np.int64)
+    C64 = C.astype(np.int64)
+    for i in range(Q.shape[0]):
+        rows = np.flatnonzero(np.isin(labels, probe[i]))
+        d = ((C64[rows] - Q[i].astype(np.int64)) ** 2).sum(axis=1)
+        order = np.lexsort((rows, d))[:k]
+        ids[i, :len(order)] = rows[order]
+        dist[i, :len(order)] = d[order]
+    return ids, dist
 
 
 def num_threads() -> int:

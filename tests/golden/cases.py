@@ -113,6 +113,17 @@ def case_small():
     return corpus, queries
 
 
+def case_hybrid():
+    """MadHybrid (uint8, L2): 24,000 x 64 clipped-GMM rows, 96 queries from the
+    same mixture; the reference clusters them into nlist=16 cells."""
+    C = gmm_u8(24_000, 64, 32, seed=71)
+    Q = gmm_u8_queries(96, 64, 32, seed_means=71, seed_q=72)
+    return C, Q
+
+
+HYBRID = {"nlist": 16, "nprobe": 4, "seed": 42}
+
+
 def case_f32_corpus():
     X = clustered_f32(n=12_000, d=96, n_clusters=24, seed=13)
     rng = np.random.default_rng(14)

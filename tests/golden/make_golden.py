@@ -55,6 +55,42 @@ def speed(R, C, Q, k, metric, batch=False):
     return out
 
 
+def reference_hybrid(C, Q):
+    """The reference's own MadHybrid (python/winnex_madhava/__init__.py:547-654)
+    built on the u8 case: its MiniBatchKMeans centroids and cell labels, and
+    its routing expression `argsort(-(centroids @ q))[:nprobe]` (:631-632)
+    evaluated here on those centroids."""
+    import shutil
+    import tempfile
+
+    ref_py = "/root/reference/python/winnex_madhava/__init__.py"
+    so = [f for f in os.listdir(oracle.REF_DIR) if f.startswith("_winnex_madhava") and f.endswith(".so")][0]
+    tmp = tempfile.mkdtemp()
+    try:
+        pkg = os.path.join(tmp, "winnex_madhava")
+        os.mkdir(pkg)
+        os.symlink(ref_py, os.path.join(pkg, "__init__.py"))
+        os.symlink(os.path.join(oracle.REF_DIR, so), os.path.join(pkg, so))
+        sys.path.insert(0, tmp)
+        import winnex_madhava as refwm  # the reference package, not this repository's
+
+        h = cases.HYBRID
+        eng = refwm.build_engine(np.ascontiguousarray(C), dim=C.shape[1], metric="l2", hybrid=True,
+                                 nlist=h["nlist"], nprobe=h["nprobe"], seed=h["seed"])
+        centroids = np.asarray(eng._centroids, dtype=np.float32)
+        labels = np.full(C.shape[0], -1, np.int32)
+        for cid, idxs in eng._members.items():
+            labels[np.asarray(idxs)] = cid
+        assert (labels >= 0).all()
+        route = np.stack([np.argsort(-(centroids @ np.ascontiguousarray(q, dtype=np.float32).flatten()))[:h["nprobe"]]
+                          for q in Q]).astype(np.int32)
+        sims = (centroids.astype(np.float64) @ Q.astype(np.float64).T).T
+        return {"centroids": centroids, "labels": labels, "route_ref": route, "sims64": sims}
+    finally:
+        sys.path.remove(tmp)
+        shutil.rmtree(tmp)
+
+
 def main():
     R = oracle.reference_module()
     if R is None:
@@ -105,6 +141,9 @@ def main():
     X, Q = cases.case_f32_corpus()
     todo["f32_corpus"] = ((X, Q), {"speed_cos_k10": speed(R, X, Q, 10, 0), "speed_l2_k10": speed(R, X, Q, 10, 1),
                                    "speedb_cos_k10": speed(R, X, Q, 10, 0, True)})
+
+    C, Q = cases.case_hybrid()
+    todo["hybrid"] = ((C, Q), reference_hybrid(C, Q))
 
     for name, ((C, Q), res) in todo.items():
         meta = {"case": name, "sha256": cases.sha(C, Q), "corpus_shape": list(C.shape), "corpus_dtype": str(C.dtype),

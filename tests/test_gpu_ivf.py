@@ -1,0 +1,98 @@
+"""GPU parity of the clustered (IVF) search against the oracle.
+
+The cells are the reference's own: MiniBatchKMeans centroids and labels from
+its MadHybrid build (tests/golden/hybrid.npz).  Routing must equal the
+oracle's cell lists exactly (same fp64 order); results must equal the exact
+top-k over the union of the probed cells, ids and squared distances.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import cases
+import oracle
+from helpers import Stats, capi, load_fixture, ptr
+
+pytestmark = pytest.mark.gpu
+
+
+def _ivf(L, C, cen, labels):
+    C = np.ascontiguousarray(C, dtype=np.uint8)
+    cen = np.ascontiguousarray(cen, dtype=np.float32)
+    labels = np.ascontiguousarray(labels, dtype=np.int32)
+    h = ctypes.c_void_p()
+    st = L.mdh_ivf_create_u8(ptr(C), C.shape[0], C.shape[1], ptr(cen), cen.shape[0], ptr(labels), -1,
+                             ctypes.byref(h))
+    assert st == 0, L.mdh_last_error()
+    return h
+
+
+def _search(L, h, Q, k, nprobe):
+    Q = np.ascontiguousarray(Q, dtype=np.uint8)
+    ids = np.empty((len(Q), k), np.int32)
+    dist = np.empty((len(Q), k), np.int32)
+    s = Stats()
+    st = L.mdh_ivf_search_u8(h, ptr(Q), len(Q), k, nprobe, ptr(ids), ptr(dist), ctypes.byref(s))
+    assert st == 0, L.mdh_last_error()
+    return ids, dist, s
+
+
+def test_ivf_matches_oracle_on_reference_cells():
+    L = capi()
+    _, res = load_fixture("hybrid")
+    C, Q = cases.case_hybrid()
+    cen, labels, nprobe = res["centroids"], res["labels"], cases.HYBRID["nprobe"]
+    h = _ivf(L, C, cen, labels)
+    cells = np.empty((len(Q), nprobe), np.int32)
+    assert L.mdh_ivf_route_u8(h, ptr(Q), len(Q), nprobe, ptr(cells)) == 0, L.mdh_last_error()
+    np.testing.assert_array_equal(cells, oracle.ivf_route(cen, Q, nprobe))
+    for k in (1, 10, 100):
+        ids, dist, s = _search(L, h, Q, k, nprobe)
+        want_ids, want_d = oracle.ivf_exact(C, labels, cen, Q, k, nprobe)
+        np.testing.assert_array_equal(ids, want_ids)
+        np.testing.assert_array_equal(dist[want_ids >= 0], want_d[want_ids >= 0])
+        assert s.levels == 2 and s.tensor_core_path == 1 and s.full_scan_pairs > 0
+    # probing every cell is the plain exact search
+    ids, dist, _ = _search(L, h, Q, 10, cases.HYBRID["nlist"])
+    want_ids, want_d = oracle.l2_exact_u8_int(C, Q, 10)
+    np.testing.assert_array_equal(ids, want_ids)
+    np.testing.assert_array_equal(dist, want_d)
+    n = ctypes.c_int64()
+    nl = ctypes.c_int32()
+    rows = np.empty(cases.HYBRID["nlist"], np.int64)
+    assert L.mdh_ivf_info(h, ctypes.byref(n), None, ctypes.byref(nl), ptr(rows)) == 0
+    assert n.value == len(C) and nl.value == cases.HYBRID["nlist"]
+    np.testing.assert_array_equal(rows, np.bincount(labels, minlength=cases.HYBRID["nlist"]))
+    assert L.mdh_ivf_destroy(h) == 0
+
+
+def test_ivf_edge_cells_and_batches():
+    """Empty cells, cells smaller than k, a cell larger than a unit's 64 tiles,
+    one query and a 700-query batch."""
+    L = capi()
+    C = cases.gmm_u8(60_000, 128, 64, seed=73)
+    Q = cases.gmm_u8_queries(700, 128, 64, seed_means=73, seed_q=74)
+    rng = np.random.default_rng(75)
+    nlist = 40
+    cen = rng.uniform(0, 60, (nlist, 128)).astype(np.float32)
+    labels = rng.integers(0, 30, len(C)).astype(np.int32)  # cells 30..39 stay empty
+    labels[:20_000] = 5                                    # one cell of 20,000 rows (> 64 tiles)
+    labels[20_000:20_003] = 31                             # a 3-row cell
+    h = _ivf(L, C, cen, labels)
+    for nq, k, nprobe in ((1, 10, 3), (700, 10, 6), (64, 16, 40)):
+        ids, dist, _ = _search(L, h, Q[:nq], k, nprobe)
+        want_ids, want_d = oracle.ivf_exact(C, labels, cen, Q[:nq], k, nprobe)
+        np.testing.assert_array_equal(ids, want_ids)
+        np.testing.assert_array_equal(dist[want_ids >= 0], want_d[want_ids >= 0])
+    assert L.mdh_ivf_destroy(h) == 0
+
+
+def test_ivf_rejects_bad_input():
+    L = capi()
+    C = np.zeros((100, 16), np.uint8)
+    cen = np.zeros((4, 16), np.float32)
+    labels = np.full(100, 4, np.int32)  # out of range
+    h = ctypes.c_void_p()
+    assert L.mdh_ivf_create_u8(ptr(C), 100, 16, ptr(cen), 4, ptr(labels), -1, ctypes.byref(h)) != 0
+    assert b"label" in L.mdh_last_error()

@@ -121,3 +121,38 @@ def test_oracle_edge_cases():
     np.testing.assert_array_equal(ids, [[0, 1, 2, -1, -1]])
     ids, _ = oracle.l2_exact_u8(C[:0], np.zeros((1, 16), np.float32), 3)  # empty corpus
     np.testing.assert_array_equal(ids, [[-1, -1, -1]])
+
+
+def test_ivf_routing_matches_reference():
+    """The routing restatement (fp64, fixed order, lower cell id on ties) picks
+    the reference's cells, `argsort(-(centroids @ q))[:nprobe]`
+    (python/winnex_madhava/__init__.py:631-632), on the reference's own
+    MiniBatchKMeans centroids; positions where the reference's float32 sums
+    leave two cells within rounding of each other are the only exemptions."""
+    meta, res = load_fixture("hybrid")
+    C, Q = cases.case_hybrid()
+    assert cases.sha(C, Q) == meta["sha256"]
+    got = oracle.ivf_route(res["centroids"], Q, cases.HYBRID["nprobe"])
+    want = res["route_ref"]
+    sims = res["sims64"]
+    differ = 0
+    for i in range(len(Q)):
+        if (got[i] == want[i]).all():
+            continue
+        s = np.sort(sims[i])[::-1]
+        gaps = np.abs(np.diff(s[: cases.HYBRID["nprobe"] + 1]))
+        assert gaps.min() < 1e-3 * abs(s[0]), (i, got[i], want[i])
+        differ += 1
+    assert differ <= 2
+    # every row has a cell, every cell index is valid
+    assert res["labels"].min() >= 0 and res["labels"].max() < cases.HYBRID["nlist"]
+
+
+def test_ivf_exact_oracle_full_probe_is_brute_force():
+    """Probing every cell makes the IVF oracle the plain exact search."""
+    meta, res = load_fixture("hybrid")
+    C, Q = cases.case_hybrid()
+    ids, dist = oracle.ivf_exact(C, res["labels"], res["centroids"], Q[:12], 10, cases.HYBRID["nlist"])
+    want_ids, want_d = oracle.l2_exact_u8_int(C, Q[:12], 10)
+    np.testing.assert_array_equal(ids, want_ids)
+    np.testing.assert_array_equal(dist, want_d)

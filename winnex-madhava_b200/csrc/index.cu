@@ -301,25 +301,32 @@ void ensure_speed_rows_u8(mdh_index* ix, Shard& sh) {
     MDH_CUDA(cudaStreamSynchronize(sh.stream));
 }
 
-void free_shard(Shard& sh) {
-    cudaSetDevice(sh.device);
-    for (Level& lv : sh.levels) {
-        if (!lv.owns) continue;
+void free_level_buffers(Level& lv) {
+    if (lv.owns) {
         cudaFree(lv.rows);
         cudaFree(lv.norms);
         cudaFree(lv.ids);
         cudaFree(lv.rows_f32);
         cudaFree(lv.norms_f32);
     }
-    sh.levels.clear();
-    Workspace& w = sh.ws;
+    lv = Level();
+}
+
+void free_workspace(Workspace& w) {
     void* ptrs[] = {w.q_u8, w.q_f32, w.qn, w.thr_key, w.thr_id, w.counts, w.cand, w.out_key, w.out_id, w.flags,
                     w.qlist, w.status, w.tmp};
     for (void* p : ptrs) cudaFree(p);
     if (w.h_status) cudaFreeHost(w.h_status);
     if (w.ev0) cudaEventDestroy(w.ev0);
     if (w.ev1) cudaEventDestroy(w.ev1);
-    sh.ws = Workspace();
+    w = Workspace();
+}
+
+void free_shard(Shard& sh) {
+    cudaSetDevice(sh.device);
+    for (Level& lv : sh.levels) free_level_buffers(lv);
+    sh.levels.clear();
+    free_workspace(sh.ws);
     if (sh.stream) cudaStreamDestroy(sh.stream);
     sh.stream = nullptr;
 }

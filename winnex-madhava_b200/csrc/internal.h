@@ -77,6 +77,8 @@ namespace mdh {
 void build_shard_u8(mdh_index* ix, Shard& sh, const uint8_t* host_rows, int64_t n);
 void build_shard_f32(mdh_index* ix, Shard& sh, const float* host_rows, int64_t n);
 void free_shard(Shard& sh);
+void free_level_buffers(Level& lv);   // frees owned buffers, resets lv
+void free_workspace(Workspace& w);    // frees every buffer, resets w
 
 // ---- workspace (capi.cu) ----
 void ensure(void** p, size_t* have, size_t need);
@@ -123,6 +125,21 @@ void make_tmap_rows(Level& lv, int dpad);
 void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
                             const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts,
                             uint2* cand, int cap, int dense, int32_t* status, cudaStream_t st);
+// Unit-table form of the tensor-core scan (used by the IVF search, ivf.cu):
+// unit u scans query rows [q_row, q_row + q_count) of `qmat` (row i is query
+// qmap[i]; thresholds, norms and candidate lists are indexed by that query)
+// against corpus tiles [t0, t1) of 256 rows, rows at or past row_end masked.
+struct ScanUnit {
+    int32_t q_row;
+    int32_t q_count;   // <= 128
+    int32_t t0, t1;
+    int32_t row_end;
+    int32_t pad;
+};
+void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat, int qmat_rows, const int32_t* qmap,
+                                  const int32_t* qn, const ScanUnit* units, int n_units, const uint32_t* thr_key,
+                                  const int32_t* thr_id, uint32_t* counts, uint2* cand, int cap, int32_t* status,
+                                  cudaStream_t st);
 // ---- tensor-core scan on SM pairs (scan_tc2.cu) ----
 bool tc2_supported(const mdh_index* ix, const Level& lv);
 void make_tmap_rows_pair(Level& lv, int dpad);

@@ -1,0 +1,614 @@
+// Clustered (IVF) exact L2 search over a u8 corpus: the GPU form of
+// MadHybrid's uint8 path (python/winnex_madhava/__init__.py:547-654).
+//
+// Semantics: a query is routed to the nprobe cells whose centroids have the
+// largest inner product with it (the reference's `centroids @ q`,
+// __init__.py:631-632; here in fp64 with a fixed multiply-add order and ties
+// to the lower cell id), and the result is the exact top-k over the union of
+// those cells' rows, ranked by (squared L2 distance, row id).
+//
+// Layout: rows are grouped by cell (cell-major), sorted by (|v|^2, id)
+// inside a cell, and every cell starts on a 256-row boundary (pad rows: zero
+// bytes, norm 2^30, id -1).  So a cell is a run of whole corpus tiles and
+// every 32-row chunk of it starts with its smallest norm, which the tensor
+// scan's chunk bound needs.
+//
+// Search, per batch of queries:
+//   1. route (k_route): fp64 dot products with every centroid, top nprobe;
+//   2. pass 1: each query against its nearest cell with an infinite
+//      threshold; the k-th smallest (key, id) is a valid threshold for the
+//      union (that cell is part of it);
+//   3. pass 2: each query against all its cells with that threshold; the
+//      candidates' first k are exact.  Overflowed lists rerun with their
+//      k-th stored entry, strictly tighter, until they fit.
+// Both passes run the tcgen05 scan (scan_tc.cu) over a unit table: a unit
+// is one cell (or a run of at most 64 of its tiles) against up to 128 of the
+// queries that probe it, gathered into a per-pass query matrix.
+#include <cub/cub.cuh>
+
+#include <algorithm>
+#include <cmath>
+#include <chrono>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "internal.h"
+
+namespace mdh {
+// Device buffers of one IVF pass: gathered query matrix, its norms, its map
+// to batch queries, and the unit table.
+struct IvfPassBufs {
+    uint8_t* g = nullptr;      size_t g_bytes = 0;
+    int32_t* gqn = nullptr;    size_t gqn_bytes = 0;
+    int32_t* gmap = nullptr;   size_t gmap_bytes = 0;
+    ScanUnit* units = nullptr; size_t units_bytes = 0;
+    void free_all() {
+        for (void* p : {(void*)g, (void*)gqn, (void*)gmap, (void*)units})
+            if (p) cudaFree(p);
+        *this = IvfPassBufs();
+    }
+};
+}  // namespace mdh
+
+struct mdh_ivf {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int64_t n = 0;
+    int32_t dim = 0;
+    int32_t dpad = 0;
+    int32_t nlist = 0;
+    mdh::Level rows;                     // all cells, padded
+    std::vector<int64_t> cell_start;     // first row of cell c
+    std::vector<int64_t> cell_count;     // real rows of cell c
+    float* centroids = nullptr;          // [nlist][dim]
+    mdh::Workspace ws;
+    mdh::IvfPassBufs pass[2];            // pass 1 (nearest cell) and pass 2 (all probed cells)
+    std::mutex mu;
+};
+
+namespace mdh {
+
+namespace {
+
+constexpr int kIvfTileRows = 256;     // tile of the tensor scan (CfgNarrow::BN)
+constexpr int kIvfMaxTilesPerUnit = 64;
+constexpr int kIvfMaxNlist = 8192;    // routing keeps all similarities in shared memory
+constexpr int kIvfMaxProbe = 1024;
+constexpr int kIvfCap1 = 16384;       // pass 1 candidate lists (whole nearest cell)
+constexpr int kIvfCap2 = 16384;       // pass 2 candidate lists
+
+template <class T>
+T* dalloc(size_t count) {
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, count * sizeof(T) + 16);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        throw Error(MDH_ERR_OOM, std::string("device allocation failed: ") + cudaGetErrorString(e));
+    }
+    return static_cast<T*>(p);
+}
+
+// key = label << 32 | |v|^2 for row r (8 lanes per row); value = r.
+__global__ void k_ivf_keys(const uint8_t* __restrict__ rows, const int32_t* __restrict__ labels, int64_t n, int dpad,
+                           unsigned long long* __restrict__ keys, int32_t* __restrict__ vals) {
+    const int lane = threadIdx.x & 31;
+    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+    const int l8 = lane & 7;
+    uint32_t s = 0;
+    if (r < n) {
+        const uint8_t* row = rows + (size_t)r * dpad;
+        for (int off = l8 * 16; off < dpad; off += 128) {
+            uint4 v = *reinterpret_cast<const uint4*>(row + off);
+            s = __dp4a(v.x, v.x, s);
+            s = __dp4a(v.y, v.y, s);
+            s = __dp4a(v.z, v.z, s);
+            s = __dp4a(v.w, v.w, s);
+        }
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    if (r < n && l8 == 0) {
+        keys[r] = ((unsigned long long)(uint32_t)labels[r] << 32) | (unsigned long long)s;
+        vals[r] = (int32_t)r;
+    }
+}
+
+// Sorted position p (cell l = key >> 32) goes to row cell_start[l] + p - cell_first[l].
+__global__ void k_ivf_gather(const uint8_t* __restrict__ src, const unsigned long long* __restrict__ keys,
+                             const int32_t* __restrict__ vals, int64_t n, int dpad,
+                             const int64_t* __restrict__ cell_start, const int64_t* __restrict__ cell_first,
+                             uint8_t* __restrict__ rows, int32_t* __restrict__ norms, int32_t* __restrict__ ids) {
+    const int64_t p = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+    const int l8 = threadIdx.x & 7;
+    if (p >= n) return;
+    const unsigned long long key = keys[p];
+    const int l = (int)(key >> 32);
+    const int64_t dst = cell_start[l] + (p - cell_first[l]);
+    const int64_t s = vals[p];
+    for (int off = l8 * 16; off < dpad; off += 128)
+        *reinterpret_cast<uint4*>(rows + (size_t)dst * dpad + off) =
+            *reinterpret_cast<const uint4*>(src + (size_t)s * dpad + off);
+    if (l8 == 0) {
+        norms[dst] = (int32_t)(key & 0xffffffffull);
+        ids[dst] = (int32_t)s;
+    }
+}
+
+__global__ void k_ivf_fill(int32_t* __restrict__ p, int64_t n, int32_t v) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) p[i] = v;
+}
+
+// One block per query: fp64 similarities with every centroid (multiply-adds
+// in dimension order from 0.0), then nprobe rounds of a block arg-max with
+// ties to the lower cell id.
+__global__ void __launch_bounds__(256) k_route(const uint8_t* __restrict__ q, int dpad, int dim,
+                                               const float* __restrict__ centroids, int nlist, int nprobe,
+                                               int32_t* __restrict__ probe) {
+    extern __shared__ double sims[];
+    __shared__ double best_v[256];
+    __shared__ int best_i[256];
+    const int qi = blockIdx.x;
+    const uint8_t* qrow = q + (size_t)qi * dpad;
+    for (int c = threadIdx.x; c < nlist; c += blockDim.x) {
+        const float* cr = centroids + (size_t)c * dim;
+        double acc = 0.0;
+        for (int j = 0; j < dim; j++) acc = __fma_rn((double)qrow[j], (double)cr[j], acc);
+        sims[c] = acc;
+    }
+    __syncthreads();
+    for (int p = 0; p < nprobe; p++) {
+        double bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int c = threadIdx.x; c < nlist; c += blockDim.x) {
+            const double v = sims[c];
+            if (v > bv || (v == bv && c < bi)) {
+                bv = v;
+                bi = c;
+            }
+        }
+        best_v[threadIdx.x] = bv;
+        best_i[threadIdx.x] = bi;
+        __syncthreads();
+        for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+            if (threadIdx.x < s) {
+                const double ov = best_v[threadIdx.x + s];
+                const int oi = best_i[threadIdx.x + s];
+                if (ov > best_v[threadIdx.x] || (ov == best_v[threadIdx.x] && oi < best_i[threadIdx.x])) {
+                    best_v[threadIdx.x] = ov;
+                    best_i[threadIdx.x] = oi;
+                }
+            }
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) {
+            const int c = best_i[0];
+            probe[(size_t)qi * nprobe + p] = c;
+            sims[c] = -INFINITY;  // taken
+        }
+        __syncthreads();
+    }
+}
+
+void launch_route(const uint8_t* q, int nq, int dpad, int dim, const float* centroids, int nlist, int nprobe,
+                  int32_t* probe, cudaStream_t st) {
+    if (nq <= 0) return;
+    const size_t smem = (size_t)nlist * sizeof(double);
+    if (smem > 48 * 1024) MDH_CUDA(cudaFuncSetAttribute(k_route, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k_route<<<nq, 256, smem, st>>>(q, dpad, dim, centroids, nlist, nprobe, probe);
+    MDH_CUDA(cudaGetLastError());
+}
+
+template <class T>
+void grow_dev(T** p, size_t* have, size_t bytes) {
+    void* v = *p;
+    ensure(&v, have, bytes);
+    *p = static_cast<T*>(v);
+}
+
+// Query lists per cell for one pass and the unit table over them.
+// probe_of(qi) -> list of cells; gmap = concatenated per-cell query lists.
+struct PassPlan {
+    std::vector<int32_t> gmap;
+    std::vector<ScanUnit> units;
+    int64_t pairs = 0;
+};
+
+PassPlan plan_pass(const mdh_ivf* ix, const std::vector<int32_t>& probe, int m, int nprobe, int use) {
+    const int nl = ix->nlist;
+    std::vector<int64_t> cnt((size_t)nl + 1, 0);
+    for (int i = 0; i < m; i++)
+        for (int j = 0; j < use; j++) {
+            const int32_t c = probe[(size_t)i * nprobe + j];
+            MDH_REQUIRE(c >= 0 && c < nl, MDH_ERR_INTERNAL, "routing produced an invalid cell");
+            cnt[(size_t)c + 1]++;
+        }
+    for (int c = 0; c < nl; c++) cnt[(size_t)c + 1] += cnt[(size_t)c];
+    PassPlan pp;
+    pp.gmap.resize((size_t)cnt[(size_t)nl]);
+    std::vector<int64_t> fill(cnt.begin(), cnt.end() - 1);
+    for (int i = 0; i < m; i++)
+        for (int j = 0; j < use; j++) pp.gmap[(size_t)fill[(size_t)probe[(size_t)i * nprobe + j]]++] = i;
+    for (int c = 0; c < nl; c++) {
+        const int64_t qn = cnt[(size_t)c + 1] - cnt[(size_t)c];
+        const int64_t rows = ix->cell_count[(size_t)c];
+        if (qn == 0 || rows == 0) continue;
+        const int64_t t_first = ix->cell_start[(size_t)c] / kIvfTileRows;
+        const int64_t t_end = t_first + (rows + kIvfTileRows - 1) / kIvfTileRows;
+        for (int64_t q0 = 0; q0 < qn; q0 += 128) {
+            for (int64_t t0 = t_first; t0 < t_end; t0 += kIvfMaxTilesPerUnit) {
+                ScanUnit u;
+                u.q_row = (int32_t)(cnt[(size_t)c] + q0);
+                u.q_count = (int32_t)std::min<int64_t>(128, qn - q0);
+                u.t0 = (int32_t)t0;
+                u.t1 = (int32_t)std::min<int64_t>(t_end, t0 + kIvfMaxTilesPerUnit);
+                u.row_end = (int32_t)(ix->cell_start[(size_t)c] + rows);
+                u.pad = 0;
+                pp.units.push_back(u);
+            }
+        }
+        pp.pairs += qn * rows;
+    }
+    // Longest units first, so the tail of the persistent grid is short.
+    std::stable_sort(pp.units.begin(), pp.units.end(), [](const ScanUnit& a, const ScanUnit& b) {
+        return (int64_t)(a.t1 - a.t0) * a.q_count > (int64_t)(b.t1 - b.t0) * b.q_count;
+    });
+    return pp;
+}
+
+void check_ivf_device(int dev) {
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0) {
+        cudaGetLastError();
+        throw Error(MDH_ERR_CUDA, "no CUDA device is available (this library has no CPU fallback)");
+    }
+    MDH_REQUIRE(dev >= 0 && dev < count, MDH_ERR_INVALID_ARG, "device ordinal out of range");
+    cudaDeviceProp p;
+    MDH_CUDA(cudaGetDeviceProperties(&p, dev));
+    MDH_REQUIRE(p.major == 10 && p.minor == 0, MDH_ERR_CUDA, "this library is built for sm_100a (B200)");
+}
+
+void ivf_create(const uint8_t* host, int64_t n, int32_t dim, const float* centroids, int32_t nlist,
+                const int32_t* labels, int32_t device, mdh_ivf** out) {
+    MDH_REQUIRE(out, MDH_ERR_INVALID_ARG, "null output pointer");
+    *out = nullptr;
+    MDH_REQUIRE(n >= 1 && host && labels && centroids, MDH_ERR_INVALID_ARG, "null or empty corpus");
+    MDH_REQUIRE(n <= 0x7FFFFFFF - 256 * (int64_t)kIvfMaxNlist, MDH_ERR_INVALID_ARG, "too many rows");
+    MDH_REQUIRE(dim >= 1 && dim <= 128, MDH_ERR_UNSUPPORTED, "the IVF scan supports dim <= 128");
+    MDH_REQUIRE(nlist >= 1 && nlist <= kIvfMaxNlist, MDH_ERR_UNSUPPORTED, "nlist must be in [1, 8192]");
+    int dev = device;
+    if (dev < 0) {
+        if (cudaGetDevice(&dev) != cudaSuccess) {
+            cudaGetLastError();
+            throw Error(MDH_ERR_CUDA, "no CUDA device is available (this library has no CPU fallback)");
+        }
+    }
+    check_ivf_device(dev);
+    for (int64_t i = 0; i < (int64_t)nlist * dim; i++)
+        MDH_REQUIRE(std::isfinite(centroids[i]), MDH_ERR_INVALID_ARG, "centroids must be finite");
+    std::vector<int64_t> count((size_t)nlist, 0);
+    for (int64_t i = 0; i < n; i++) {
+        const int32_t l = labels[i];
+        MDH_REQUIRE(l >= 0 && l < nlist, MDH_ERR_INVALID_ARG, "label out of range [0, nlist)");
+        count[(size_t)l]++;
+    }
+    std::unique_ptr<mdh_ivf> ix(new mdh_ivf());
+    ix->device = dev;
+    ix->n = n;
+    ix->dim = dim;
+    ix->dpad = 128;
+    ix->nlist = nlist;
+    ix->cell_count = count;
+    ix->cell_start.resize((size_t)nlist);
+    std::vector<int64_t> first((size_t)nlist);
+    int64_t off = 0, pos = 0;
+    for (int c = 0; c < nlist; c++) {
+        ix->cell_start[(size_t)c] = off;
+        first[(size_t)c] = pos;
+        off += (count[(size_t)c] + kIvfTileRows - 1) / kIvfTileRows * kIvfTileRows;
+        pos += count[(size_t)c];
+    }
+    const int64_t total = std::max<int64_t>(off, kIvfTileRows);
+    MDH_CUDA(cudaSetDevice(dev));
+    MDH_CUDA(cudaStreamCreateWithFlags(&ix->stream, cudaStreamNonBlocking));
+    cudaStream_t st = ix->stream;
+    const int dpad = ix->dpad;
+    uint8_t* stage = nullptr;
+    int32_t* dlabels = nullptr;
+    unsigned long long *keys = nullptr, *keys2 = nullptr;
+    int32_t *vals = nullptr, *vals2 = nullptr;
+    int64_t *dstart = nullptr, *dfirst = nullptr;
+    void* tmp = nullptr;
+    auto release_tmp = [&]() {
+        for (void* p : {(void*)stage, (void*)dlabels, (void*)keys, (void*)keys2, (void*)vals, (void*)vals2,
+                        (void*)dstart, (void*)dfirst, tmp})
+            if (p) cudaFree(p);
+    };
+    try {
+        stage = dalloc<uint8_t>((size_t)n * dpad);
+        MDH_CUDA(cudaMemsetAsync(stage, 0, (size_t)n * dpad, st));
+        MDH_CUDA(cudaMemcpy2DAsync(stage, dpad, host, dim, dim, n, cudaMemcpyHostToDevice, st));
+        dlabels = dalloc<int32_t>(n);
+        MDH_CUDA(cudaMemcpyAsync(dlabels, labels, (size_t)n * 4, cudaMemcpyHostToDevice, st));
+        keys = dalloc<unsigned long long>(n);
+        keys2 = dalloc<unsigned long long>(n);
+        vals = dalloc<int32_t>(n);
+        vals2 = dalloc<int32_t>(n);
+        k_ivf_keys<<<(unsigned)((n * 8 + 255) / 256), 256, 0, st>>>(stage, dlabels, n, dpad, keys, vals);
+        MDH_CUDA(cudaGetLastError());
+        size_t tmp_bytes = 0;
+        MDH_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tmp_bytes, keys, keys2, vals, vals2, (int)n, 0, 64, st));
+        tmp = dalloc<uint8_t>(tmp_bytes);
+        MDH_CUDA(cub::DeviceRadixSort::SortPairs(tmp, tmp_bytes, keys, keys2, vals, vals2, (int)n, 0, 64, st));
+        Level& lv = ix->rows;
+        lv.n = total;
+        lv.n_pad = total;
+        lv.rows = dalloc<uint8_t>((size_t)total * dpad);
+        lv.norms = dalloc<int32_t>(total);
+        lv.ids = dalloc<int32_t>(total);
+        MDH_CUDA(cudaMemsetAsync(lv.rows, 0, (size_t)total * dpad, st));
+        k_ivf_fill<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(lv.norms, total, kNormPad);
+        k_ivf_fill<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(lv.ids, total, -1);
+        dstart = dalloc<int64_t>(nlist);
+        dfirst = dalloc<int64_t>(nlist);
+        MDH_CUDA(cudaMemcpyAsync(dstart, ix->cell_start.data(), (size_t)nlist * 8, cudaMemcpyHostToDevice, st));
+        MDH_CUDA(cudaMemcpyAsync(dfirst, first.data(), (size_t)nlist * 8, cudaMemcpyHostToDevice, st));
+        k_ivf_gather<<<(unsigned)((n * 8 + 255) / 256), 256, 0, st>>>(stage, keys2, vals2, n, dpad, dstart, dfirst,
+                                                                       lv.rows, lv.norms, lv.ids);
+        MDH_CUDA(cudaGetLastError());
+        ix->centroids = dalloc<float>((size_t)nlist * dim);
+        MDH_CUDA(cudaMemcpyAsync(ix->centroids, centroids, (size_t)nlist * dim * 4, cudaMemcpyHostToDevice, st));
+        MDH_CUDA(cudaStreamSynchronize(st));
+        make_tmap_rows(lv, dpad);
+    } catch (...) {
+        cudaStreamSynchronize(st);
+        release_tmp();
+        free_level_buffers(ix->rows);
+        if (ix->centroids) cudaFree(ix->centroids);
+        cudaStreamDestroy(ix->stream);
+        throw;
+    }
+    release_tmp();
+    *out = ix.release();
+}
+
+void ivf_route_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int nprobe, std::vector<int32_t>& probe,
+                    int32_t** d_probe_out) {
+    Workspace& w = ix->ws;
+    cudaStream_t st = ix->stream;
+    grow_dev(&w.q_u8, &w.q_u8_bytes, (size_t)nq * ix->dpad);
+    grow_dev(&w.qn, &w.qn_bytes, (size_t)nq * 4);
+    grow_dev(&w.flags, &w.flags_bytes, (size_t)nq * nprobe * 4);  // probe matrix
+    MDH_CUDA(cudaMemsetAsync(w.q_u8, 0, (size_t)nq * ix->dpad, st));
+    MDH_CUDA(cudaMemcpy2DAsync(w.q_u8, ix->dpad, host_q, ix->dim, ix->dim, nq, cudaMemcpyHostToDevice, st));
+    launch_query_norms_u8(w.q_u8, nq, ix->dpad, w.qn, st);
+    launch_route(w.q_u8, nq, ix->dpad, ix->dim, ix->centroids, ix->nlist, nprobe, w.flags, st);
+    probe.resize((size_t)nq * nprobe);
+    MDH_CUDA(cudaMemcpyAsync(probe.data(), w.flags, probe.size() * 4, cudaMemcpyDeviceToHost, st));
+    MDH_CUDA(cudaStreamSynchronize(st));
+    if (d_probe_out) *d_probe_out = w.flags;
+}
+
+void upload_pass(mdh_ivf* ix, IvfPassBufs& b, const PassPlan& pp, cudaStream_t st) {
+    const size_t gr = std::max<size_t>(pp.gmap.size(), 1);
+    grow_dev(&b.g, &b.g_bytes, gr * ix->dpad);
+    grow_dev(&b.gqn, &b.gqn_bytes, gr * 4);
+    grow_dev(&b.gmap, &b.gmap_bytes, gr * 4);
+    grow_dev(&b.units, &b.units_bytes, std::max<size_t>(pp.units.size(), 1) * sizeof(ScanUnit));
+    if (!pp.gmap.empty()) {
+        MDH_CUDA(cudaMemcpyAsync(b.gmap, pp.gmap.data(), pp.gmap.size() * 4, cudaMemcpyHostToDevice, st));
+        launch_gather_queries_u8(ix->ws.q_u8, ix->ws.qn, b.gmap, (int)pp.gmap.size(), ix->dpad, b.g, b.gqn, st);
+    }
+    if (!pp.units.empty())
+        MDH_CUDA(cudaMemcpyAsync(b.units, pp.units.data(), pp.units.size() * sizeof(ScanUnit), cudaMemcpyHostToDevice,
+                                 st));
+}
+
+void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int nprobe, int32_t* out_ids,
+                     int32_t* out_dist, mdh_stats* stats) {
+    auto t_start = std::chrono::high_resolution_clock::now();
+    MDH_REQUIRE(ix, MDH_ERR_INVALID_ARG, "null index");
+    MDH_REQUIRE(nq >= 0 && k >= 0, MDH_ERR_INVALID_ARG, "nq and k must be >= 0");
+    MDH_REQUIRE(nq == 0 || k == 0 || (host_q && out_ids), MDH_ERR_INVALID_ARG, "null buffer");
+    MDH_REQUIRE(nprobe >= 1, MDH_ERR_INVALID_ARG, "nprobe must be >= 1");
+    MDH_REQUIRE(k <= 4096, MDH_ERR_UNSUPPORTED, "the IVF search supports k <= 4096");
+    nprobe = std::min(nprobe, ix->nlist);
+    MDH_REQUIRE(nprobe <= kIvfMaxProbe, MDH_ERR_UNSUPPORTED, "nprobe must be <= 1024");
+    std::lock_guard<std::mutex> lock(ix->mu);
+    MDH_CUDA(cudaSetDevice(ix->device));
+    mdh_stats s{};
+    for (size_t i = 0; i < (size_t)nq * k; i++) out_ids[i] = -1;
+    if (out_dist)
+        for (size_t i = 0; i < (size_t)nq * k; i++) out_dist[i] = -1;
+    if (nq == 0 || k == 0) {
+        if (stats) *stats = s;
+        return;
+    }
+    cudaStream_t st = ix->stream;
+    Workspace& w = ix->ws;
+    const Level& lv = ix->rows;
+    const int chunk = (int)std::max<int64_t>(1, std::min<int64_t>(nq, (int64_t(2) << 30) / ((int64_t)kIvfCap2 * 8)));
+    std::vector<uint32_t> hkey;
+    std::vector<int32_t> hid;
+    for (int c0 = 0; c0 < nq; c0 += chunk) {
+        const int m = std::min(chunk, nq - c0);
+        std::vector<int32_t> probe;
+        ivf_route_impl(ix, host_q + (size_t)c0 * ix->dim, m, nprobe, probe, nullptr);
+        s.kernel_launches += 2;
+        PassPlan p1 = plan_pass(ix, probe, m, nprobe, 1);
+        PassPlan p2 = plan_pass(ix, probe, m, nprobe, nprobe);
+        upload_pass(ix, ix->pass[0], p1, st);
+        upload_pass(ix, ix->pass[1], p2, st);
+        s.kernel_launches += 2;
+        grow_dev(&w.thr_key, &w.thr_key_bytes, (size_t)m * 4);
+        grow_dev(&w.thr_id, &w.thr_id_bytes, (size_t)m * 4);
+        grow_dev(&w.counts, &w.counts_bytes, (size_t)m * 4);
+        grow_dev(&w.cand, &w.cand_bytes, (size_t)m * std::max(kIvfCap1, kIvfCap2) * sizeof(uint2));
+        grow_dev(&w.out_key, &w.out_key_bytes, (size_t)m * k * 4);
+        grow_dev(&w.out_id, &w.out_id_bytes, (size_t)m * k * 4);
+        grow_dev(&w.qlist, &w.qlist_bytes, (size_t)m * 4);  // overflow flags
+        if (!w.status) {
+            MDH_CUDA(cudaMalloc(&w.status, 8 * sizeof(int32_t)));
+            MDH_CUDA(cudaHostAlloc(&w.h_status, 8 * sizeof(int32_t), cudaHostAllocDefault));
+        }
+        if (!w.ev0) {
+            MDH_CUDA(cudaEventCreate(&w.ev0));
+            MDH_CUDA(cudaEventCreate(&w.ev1));
+        }
+        MDH_CUDA(cudaMemsetAsync(w.status, 0, 6 * sizeof(int32_t), st));
+        unsigned long long* n_cand = reinterpret_cast<unsigned long long*>(w.status + 2);
+        // Pass 1: nearest cell, infinite thresholds -> k-th entry thresholds.
+        launch_fill_threshold(w.thr_key, w.thr_id, m, kKeyInf, kIdInf, st);
+        MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
+        launch_filter_tc_u8_l2_units(lv, ix->dpad, ix->pass[0].g, (int)p1.gmap.size(), ix->pass[0].gmap, w.qn,
+                                     ix->pass[0].units, (int)p1.units.size(), w.thr_key, w.thr_id, w.counts, w.cand,
+                                     kIvfCap1, w.status, st);
+        launch_select(w.counts, w.cand, kIvfCap1, lv.ids, m, k, 0, w.thr_key, w.thr_id, w.out_key, w.out_id, w.qlist,
+                      w.status + 1, nullptr, nullptr, st);
+        s.kernel_launches += 3;
+        // Pass 2: every probed cell with those thresholds.
+        MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
+        MDH_CUDA(cudaEventRecord(w.ev0, st));
+        launch_filter_tc_u8_l2_units(lv, ix->dpad, ix->pass[1].g, (int)p2.gmap.size(), ix->pass[1].gmap, w.qn,
+                                     ix->pass[1].units, (int)p2.units.size(), w.thr_key, w.thr_id, w.counts, w.cand,
+                                     kIvfCap2, w.status, st);
+        MDH_CUDA(cudaEventRecord(w.ev1, st));
+        launch_select(w.counts, w.cand, kIvfCap2, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id, w.qlist,
+                      w.status + 1, nullptr, n_cand, st);
+        s.kernel_launches += 2;
+        s.pairs_scored += p1.pairs + p2.pairs;
+        s.full_scan_pairs += p2.pairs;
+        MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 6 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+        MDH_CUDA(cudaStreamSynchronize(st));
+        if (w.h_status[0] != kDevOk)
+            throw Error(MDH_ERR_TIMEOUT, "IVF scan reported device status " + std::to_string(w.h_status[0]));
+        {
+            float ms = 0.0f;
+            MDH_CUDA(cudaEventElapsedTime(&ms, w.ev0, w.ev1));
+            s.full_scan_ms += ms;
+        }
+        int rounds = 0;
+        while (w.h_status[1] > 0) {
+            // Overflowed lists got a strictly tighter threshold; the others keep
+            // theirs and reproduce their result.
+            MDH_REQUIRE(++rounds < 64, MDH_ERR_INTERNAL, "candidate overflow did not converge");
+            MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
+            MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
+            launch_filter_tc_u8_l2_units(lv, ix->dpad, ix->pass[1].g, (int)p2.gmap.size(), ix->pass[1].gmap, w.qn,
+                                         ix->pass[1].units, (int)p2.units.size(), w.thr_key, w.thr_id, w.counts,
+                                         w.cand, kIvfCap2, w.status, st);
+            launch_select(w.counts, w.cand, kIvfCap2, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id,
+                          w.qlist, w.status + 1, nullptr, n_cand, st);
+            s.kernel_launches += 2;
+            s.pairs_scored += p2.pairs;
+            MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 6 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+            MDH_CUDA(cudaStreamSynchronize(st));
+            if (w.h_status[0] != kDevOk)
+                throw Error(MDH_ERR_TIMEOUT, "IVF scan reported device status " + std::to_string(w.h_status[0]));
+        }
+        {
+            unsigned long long cand_n = 0;
+            std::memcpy(&cand_n, w.h_status + 2, 8);
+            s.candidates += (int64_t)cand_n;
+        }
+        hkey.resize((size_t)m * k);
+        hid.resize((size_t)m * k);
+        MDH_CUDA(cudaMemcpyAsync(hkey.data(), w.out_key, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
+        MDH_CUDA(cudaMemcpyAsync(hid.data(), w.out_id, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
+        MDH_CUDA(cudaStreamSynchronize(st));
+        for (size_t i = 0; i < (size_t)m * k; i++) {
+            out_ids[(size_t)c0 * k + i] = hid[i];
+            if (out_dist) out_dist[(size_t)c0 * k + i] = hid[i] >= 0 ? (int32_t)hkey[i] : -1;
+        }
+    }
+    s.levels = 2;
+    s.tensor_core_path = 1;
+    s.latency_ms = std::chrono::duration<double, std::milli>(std::chrono::high_resolution_clock::now() - t_start).count();
+    if (stats) *stats = s;
+}
+
+}  // namespace
+
+}  // namespace mdh
+
+using namespace mdh;
+
+extern "C" {
+
+mdh_status mdh_ivf_create_u8(const uint8_t* host_corpus, int64_t n, int32_t dim, const float* centroids,
+                             int32_t nlist, const int32_t* labels, int32_t device, mdh_ivf** out) {
+    struct A {
+        const uint8_t* c; int64_t n; int32_t dim; const float* cen; int32_t nl; const int32_t* lab; int32_t dev;
+        mdh_ivf** out;
+    } a{host_corpus, n, dim, centroids, nlist, labels, device, out};
+    return run_guarded([](void* p) {
+        A& x = *static_cast<A*>(p);
+        ivf_create(x.c, x.n, x.dim, x.cen, x.nl, x.lab, x.dev, x.out);
+    }, &a);
+}
+
+mdh_status mdh_ivf_route_u8(mdh_ivf* index, const uint8_t* host_queries, int32_t nq, int32_t nprobe,
+                            int32_t* out_cells) {
+    struct A {
+        mdh_ivf* ix; const uint8_t* q; int32_t nq, np; int32_t* out;
+    } a{index, host_queries, nq, nprobe, out_cells};
+    return run_guarded([](void* p) {
+        A& x = *static_cast<A*>(p);
+        MDH_REQUIRE(x.ix, MDH_ERR_INVALID_ARG, "null index");
+        MDH_REQUIRE(x.nq >= 0 && (x.nq == 0 || (x.q && x.out)), MDH_ERR_INVALID_ARG, "null buffer");
+        MDH_REQUIRE(x.np >= 1 && x.np <= x.ix->nlist && x.np <= kIvfMaxProbe, MDH_ERR_INVALID_ARG,
+                    "nprobe must be in [1, min(nlist, 1024)]");
+        if (x.nq == 0) return;
+        std::lock_guard<std::mutex> lock(x.ix->mu);
+        MDH_CUDA(cudaSetDevice(x.ix->device));
+        std::vector<int32_t> probe;
+        ivf_route_impl(x.ix, x.q, x.nq, x.np, probe, nullptr);
+        std::memcpy(x.out, probe.data(), probe.size() * 4);
+    }, &a);
+}
+
+mdh_status mdh_ivf_search_u8(mdh_ivf* index, const uint8_t* host_queries, int32_t nq, int32_t k, int32_t nprobe,
+                             int32_t* out_ids, int32_t* out_dist, mdh_stats* stats) {
+    struct A {
+        mdh_ivf* ix; const uint8_t* q; int32_t nq, k, np; int32_t *ids, *dist; mdh_stats* st;
+    } a{index, host_queries, nq, k, nprobe, out_ids, out_dist, stats};
+    return run_guarded([](void* p) {
+        A& x = *static_cast<A*>(p);
+        ivf_search_impl(x.ix, x.q, x.nq, x.k, x.np, x.ids, x.dist, x.st);
+    }, &a);
+}
+
+mdh_status mdh_ivf_info(const mdh_ivf* index, int64_t* n, int32_t* dim, int32_t* nlist, int64_t* cell_rows) {
+    struct A {
+        const mdh_ivf* ix; int64_t* n; int32_t *dim, *nlist; int64_t* cells;
+    } a{index, n, dim, nlist, cell_rows};
+    return run_guarded([](void* p) {
+        A& x = *static_cast<A*>(p);
+        MDH_REQUIRE(x.ix, MDH_ERR_INVALID_ARG, "null index");
+        if (x.n) *x.n = x.ix->n;
+        if (x.dim) *x.dim = x.ix->dim;
+        if (x.nlist) *x.nlist = x.ix->nlist;
+        if (x.cells) std::memcpy(x.cells, x.ix->cell_count.data(), x.ix->cell_count.size() * 8);
+    }, &a);
+}
+
+mdh_status mdh_ivf_destroy(mdh_ivf* index) {
+    return run_guarded([](void* p) {
+        mdh_ivf* ix = static_cast<mdh_ivf*>(p);
+        if (!ix) return;
+        cudaSetDevice(ix->device);
+        if (ix->stream) cudaStreamSynchronize(ix->stream);
+        ix->pass[0].free_all();
+        ix->pass[1].free_all();
+        free_level_buffers(ix->rows);
+        if (ix->centroids) cudaFree(ix->centroids);
+        free_workspace(ix->ws);
+        if (ix->stream) cudaStreamDestroy(ix->stream);
+        delete ix;
+    }, index);
+}
+
+}  // extern "C"

@@ -43,6 +43,8 @@
 // *status, raises a shared abort flag so every role leaves its loop, drains
 // its own outstanding copies and MMAs with bounded waits, frees its tensor
 // memory and returns.
+#include <algorithm>
+
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -112,13 +114,43 @@ __device__ __forceinline__ void unit_coords(const Sched& s, long long u, int& g,
     t1 = (int)((long long)(c + 1) * s.n_tiles / s.n_chunks);
 }
 
+// A work unit: query rows [q_row, q_row + q_count) of the query matrix
+// (padded to the group size with rows that are masked) against corpus tiles
+// [t0, t1), rows at or past row_end masked.  Without a unit table, unit u is
+// (query group, corpus chunk) from the schedule; with one (the IVF scan), it
+// is units[u] and query row i belongs to query qmap[i].
+struct UnitView {
+    int q_row, q_count, t0, t1, row_end;
+};
+
+template <class C>
+__device__ __forceinline__ UnitView unit_view(const Sched& s, const ScanUnit* units, long long u, int n_rows, int nq) {
+    UnitView v;
+    if (units) {
+        const ScanUnit x = units[u];
+        v.q_row = x.q_row;
+        v.q_count = x.q_count;
+        v.t0 = x.t0;
+        v.t1 = x.t1;
+        v.row_end = x.row_end;
+    } else {
+        int g;
+        unit_coords(s, u, g, v.t0, v.t1);
+        v.q_row = g * C::QGROUP;
+        v.q_count = nq - v.q_row < C::QGROUP ? nq - v.q_row : C::QGROUP;
+        v.row_end = n_rows;
+    }
+    return v;
+}
+
 template <class C>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_filter_tc_u8_l2(const __grid_constant__ CUtensorMap tmap_rows, const __grid_constant__ CUtensorMap tmap_q,
                       const int32_t* __restrict__ norms, const int32_t* __restrict__ ids, int32_t n_rows,
                       const int32_t* __restrict__ qn, int nq, const uint32_t* __restrict__ thr_key,
                       const int32_t* __restrict__ thr_id, uint32_t* __restrict__ counts, uint2* __restrict__ cand,
-                      int cap, int dense, Sched sched, int32_t* __restrict__ status) {
+                      int cap, int dense, Sched sched, int32_t* __restrict__ status,
+                      const ScanUnit* __restrict__ units, const int32_t* __restrict__ qmap) {
     constexpr int BN = C::BN, QT = C::QT, STAGES = C::STAGES, ACC_STAGES = C::ACC_STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -162,15 +194,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             bool a_issued = false;
             bool ok = true;
             for (long long u = blockIdx.x; u < sched.n_units && ok; u += gridDim.x) {
-                int g, t0, t1;
-                unit_coords(sched, u, g, t0, t1);
+                const UnitView uv = unit_view<C>(sched, units, u, n_rows, nq);
+                const int t0 = uv.t0, t1 = uv.t1;
                 ok = mbar_wait<false>(bars + 8 * C::BAR_A_EMPTY, (a_iter & 1) ^ 1, abort_flag, status);
                 if (!ok) break;
                 mbar_expect_tx(bars + 8 * C::BAR_A_FULL, C::A_BYTES);
 #pragma unroll
                 for (int qt = 0; qt < QT; qt++)
                     tma_load_2d(sbase + C::OFF_A + qt * A_TILE_BYTES, &tmap_q, bars + 8 * C::BAR_A_FULL, 0,
-                                g * C::QGROUP + qt * BM);
+                                uv.q_row + qt * BM);
                 a_issued = true;
                 a_iter++;
                 for (int t = t0; t < t1; t++) {
@@ -209,8 +241,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t phase = 0, acc_phase = 0, a_iter = 0;
             bool ok = true, issued = false;
             for (long long u = blockIdx.x; u < sched.n_units && ok; u += gridDim.x) {
-                int g, t0, t1;
-                unit_coords(sched, u, g, t0, t1);
+                const UnitView uv = unit_view<C>(sched, units, u, n_rows, nq);
+                const int t0 = uv.t0, t1 = uv.t1;
                 ok = mbar_wait<false>(bars + 8 * C::BAR_A_FULL, a_iter & 1, abort_flag, status);
                 if (!ok) break;
                 a_iter++;
@@ -277,10 +309,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         bool ok = true;
         const int32_t* nrm = norms + rowoff;
         for (long long u = blockIdx.x; u < sched.n_units && ok; u += gridDim.x) {
-            int g, t0, t1;
-            unit_coords(sched, u, g, t0, t1);
-            const int qi = g * C::QGROUP + qt * BM + quarter * 32 + lane;
-            const bool qvalid = qi < nq;
+            const UnitView uv = unit_view<C>(sched, units, u, n_rows, nq);
+            const int t0 = uv.t0, t1 = uv.t1, row_end = uv.row_end;
+            const int qlocal = qt * BM + quarter * 32 + lane;
+            const bool qvalid = qlocal < uv.q_count;
+            const int qi = qvalid ? (qmap ? qmap[uv.q_row + qlocal] : uv.q_row + qlocal) : 0;
             uint32_t tkey = 0;
             int32_t tid = 0, qnv = 0;
             if (qvalid) {
@@ -340,7 +373,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         const int j = __ffs(mask) - 1;
                         mask &= mask - 1;
                         const int32_t r = row0 + 32 * c + j;
-                        if (r >= n_rows) break;  // pad rows trail the level
+                        if (r >= row_end) break;  // pad rows trail the level (or the cell)
                         const uint32_t key = (uint32_t)(qnv + __ldg(norms + r) - 2 * (int32_t)pick32(v[c], j));
                         if (dense)
                             cand[(size_t)qi * cap + r] = make_uint2(key, (uint32_t)r);
@@ -438,7 +471,7 @@ void launch_tc(const Level& lv, const CUtensorMap& tq, const int32_t* qn, int nq
                                   (int)C::SMEM_BYTES));
     k_filter_tc_u8_l2<C><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
                                                                    qn, nq, thr_key, thr_id, counts, cand, cap, dense,
-                                                                   s, status);
+                                                                   s, status, nullptr, nullptr);
     MDH_CUDA(cudaGetLastError());
 }
 
@@ -457,6 +490,28 @@ void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const i
     }
 #endif
     launch_tc<CfgNarrow>(lv, tq, qn, nq, thr_key, thr_id, counts, cand, cap, dense, status, st);
+}
+
+void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat, int qmat_rows, const int32_t* qmap,
+                                  const int32_t* qn, const ScanUnit* units, int n_units, const uint32_t* thr_key,
+                                  const int32_t* thr_id, uint32_t* counts, uint2* cand, int cap, int32_t* status,
+                                  cudaStream_t st) {
+    using C = CfgNarrow;
+    if (n_units <= 0 || qmat_rows <= 0 || lv.n == 0) return;
+    MDH_REQUIRE(dpad == BK && lv.has_tmap, MDH_ERR_INTERNAL, "tensor-core scan needs 128-byte rows and a TMA map");
+    CUtensorMap tq;
+    encode_u8_rows_tmap(&tq, qmat, qmat_rows, dpad, BM);
+    int dev;
+    MDH_CUDA(cudaGetDevice(&dev));
+    Sched s{};
+    s.n_units = n_units;
+    const int ctas = std::min(device_sm_count(dev), n_units);
+    MDH_CUDA(cudaFuncSetAttribute(k_filter_tc_u8_l2<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)C::SMEM_BYTES));
+    k_filter_tc_u8_l2<C><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
+                                                                   qn, qmat_rows, thr_key, thr_id, counts, cand, cap,
+                                                                   0, s, status, units, qmap);
+    MDH_CUDA(cudaGetLastError());
 }
 
 }  // namespace mdh
