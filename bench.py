@@ -40,27 +40,27 @@ METRIC = "queries/sec, 100M×128 u8 exact top-10, 10K-query batch at 1/2/4/8 B20
 
 
 # --------------------------------------------------------------------------- data
-def mixture_means():
-    return np.random.default_rng(SEED).uniform(0, 60, size=(COMPONENTS, DIM))
+def mixture_means(comps=COMPONENTS):
+    return np.random.default_rng(SEED).uniform(0, 60, size=(comps, DIM))
 
 
-def make_queries(nq):
-    means = mixture_means()
+def make_queries(nq, comps=COMPONENTS):
+    means = mixture_means(comps)
     rng = np.random.default_rng(SEED + 1)
-    lab = rng.integers(0, COMPONENTS, size=nq)
+    lab = rng.integers(0, comps, size=nq)
     return np.clip(np.rint(means[lab] + rng.normal(0, 15, size=(nq, DIM))), 0, 255).astype(np.uint8)
 
 
-def make_rows_gpu(torch, start, end, device):
+def make_rows_gpu(torch, start, end, device, comps=COMPONENTS):
     """Rows [start, end) of the corpus on `device` (u8 [end-start][128])."""
-    means = torch.tensor(mixture_means(), dtype=torch.float32, device=device)
+    means = torch.tensor(mixture_means(comps), dtype=torch.float32, device=device)
     out = torch.empty((end - start, DIM), dtype=torch.uint8, device=device)
     c0, c1 = start // CHUNK, (end + CHUNK - 1) // CHUNK
     g = torch.Generator(device=device)
     for c in range(c0, c1):
         s, e = c * CHUNK, (c + 1) * CHUNK
         g.manual_seed(SEED * 1000 + c)
-        lab = torch.randint(0, COMPONENTS, (CHUNK,), generator=g, device=device)
+        lab = torch.randint(0, comps, (CHUNK,), generator=g, device=device)
         x = means[lab]
         x.add_(torch.randn((CHUNK, DIM), generator=g, device=device), alpha=15.0)
         x = x.round_().clamp_(0, 255).to(torch.uint8)
@@ -89,12 +89,19 @@ def load_lib():
     L.mdh_index_create_u8_device.argtypes = [P, i64, i32, i32, i64, ctypes.POINTER(P)]
     L.mdh_index_destroy.argtypes = [P]
     L.mdh_search_u8.argtypes = [P, P, i32, i32, P, P, ctypes.POINTER(Stats)]
+    L.mdh_index_create_u8.argtypes = [P, i64, i32, i32, P, i32, i64, ctypes.POINTER(P)]
+    L.mdh_index_create_u8.restype = ctypes.c_int
     L.mdh_search_u8_device.argtypes = [P, P, i32, i32, P, P, P, ctypes.POINTER(Stats)]
     L.mdh_merge_topk_device.argtypes = [P, P, i32, i32, i32, P, P, P]
     L.mdh_set_scan_path.argtypes = [i32]
+    L.mdh_ivf_create_u8.argtypes = [P, i64, i32, P, i32, P, i32, ctypes.POINTER(P)]
+    L.mdh_ivf_search_u8.argtypes = [P, P, i32, i32, i32, P, P, ctypes.POINTER(Stats)]
+    L.mdh_ivf_destroy.argtypes = [P]
+    L.mdh_search_u8.restype = ctypes.c_int
     L.mdh_last_error.restype = ctypes.c_char_p
     for f in ("mdh_index_create_u8_device", "mdh_index_destroy", "mdh_search_u8", "mdh_search_u8_device",
-              "mdh_merge_topk_device", "mdh_set_scan_path"):
+              "mdh_merge_topk_device", "mdh_set_scan_path", "mdh_ivf_create_u8", "mdh_ivf_search_u8",
+              "mdh_ivf_destroy"):
         getattr(L, f).restype = ctypes.c_int
     return L
 
@@ -201,6 +208,106 @@ def cpu_reference_qps(corpus_slice, n_total, queries, k, steps=1, warmup=0):
                  "seconds_per_step": t}
 
 
+# --------------------------------------------------------------------------- IVF workload
+IVF_COMPS, IVF_NLIST, IVF_NPROBE = 1024, 1024, 16
+
+
+def run_ivf(args, torch, device, L, warmup):
+    """Clustered search: 10M x 128 u8 clipped GMM (1,024 components), nlist
+    1,024, nprobe 16, exact top-k over the probed cells; one GPU."""
+    from sklearn.cluster import MiniBatchKMeans
+
+    n = args.n if args.n != N_DEFAULT else 10_000_000
+    nq, k = args.nq, args.k
+    rows = make_rows_gpu(torch, 0, n, device, IVF_COMPS)
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED + 7)
+    sample = rows[torch.randperm(n, generator=g, device=device)[:200_000]].cpu().numpy().astype(np.float32)
+    t0 = time.time()
+    km = MiniBatchKMeans(n_clusters=IVF_NLIST, random_state=42, batch_size=10_000, n_init=1, max_iter=20)
+    km.fit(sample)
+    cen = km.cluster_centers_.astype(np.float32)
+    cen_t = torch.from_numpy(cen).to(device)
+    cn = (cen_t * cen_t).sum(1)
+    labels = torch.empty(n, dtype=torch.int32, device=device)
+    for s in range(0, n, 1_000_000):  # nearest centroid, as MiniBatchKMeans.predict
+        x = rows[s:s + 1_000_000].float()
+        labels[s:s + 1_000_000] = (cn[None, :] - 2.0 * (x @ cen_t.T)).argmin(dim=1).to(torch.int32)
+    host_rows = rows.cpu().numpy()
+    host_labels = labels.cpu().numpy()
+    cluster_s = time.time() - t0
+    del rows, labels, x
+    torch.cuda.empty_cache()
+    h = ctypes.c_void_p()
+    t0 = time.time()
+    check(L, L.mdh_ivf_create_u8(ctypes.c_void_p(host_rows.ctypes.data), n, DIM, ctypes.c_void_p(cen.ctypes.data),
+                                 IVF_NLIST, ctypes.c_void_p(host_labels.ctypes.data), device.index or 0,
+                                 ctypes.byref(h)), "ivf build")
+    build_s = time.time() - t0
+    queries = make_queries(nq, IVF_COMPS)
+    ids = np.empty((nq, k), np.int32)
+    dist = np.empty((nq, k), np.int32)
+    st = Stats()
+
+    def step():
+        check(L, L.mdh_ivf_search_u8(h, ctypes.c_void_p(queries.ctypes.data), nq, k, IVF_NPROBE,
+                                     ctypes.c_void_p(ids.ctypes.data), ctypes.c_void_p(dist.ctypes.data),
+                                     ctypes.byref(st)), "ivf search")
+
+    for _ in range(warmup):
+        step()
+    sampler = ClockSampler(device.index or 0)
+    sampler.start()
+    scan_ms, pairs = [], []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+        scan_ms.append(st.full_scan_ms)
+        pairs.append(st.full_scan_pairs)
+    elapsed = time.perf_counter() - t0
+    clocks = sampler.stop()
+    launches = int(st.kernel_launches) * args.steps
+    # Recall of the clustered search against the exact scan, on 1,000 queries.
+    m = min(nq, 1000)
+    flat = ctypes.c_void_p()
+    check(L, L.mdh_index_create_u8(ctypes.c_void_p(host_rows.ctypes.data), n, DIM, 1, None, 0, 0, ctypes.byref(flat)),
+          "flat build")
+    fids = np.empty((m, k), np.int32)
+    check(L, L.mdh_search_u8(flat, ctypes.c_void_p(queries.ctypes.data), m, k, ctypes.c_void_p(fids.ctypes.data),
+                             None, None), "flat search")
+    check(L, L.mdh_index_destroy(flat), "flat destroy")
+    recall = float(np.mean([len(set(ids[i]) & set(fids[i])) / k for i in range(m)]))
+    check(L, L.mdh_ivf_destroy(h), "ivf destroy")
+    peaks, peak_src = measured_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    ms = statistics.median(scan_ms)
+    achieved = 2.0 * pairs[0] * DIM / (ms / 1e3) / 1e12 if ms > 0 else None
+    qps = nq * args.steps / elapsed
+    line = {
+        "metric": f"queries/sec, {n // 1_000_000}M x {DIM} u8 IVF (nlist {IVF_NLIST}, nprobe {IVF_NPROBE}) "
+                  f"exact top-{k} over the probed cells, {nq}-query batch",
+        "value": qps, "unit": "queries/sec", "n_gpus": 1, "steps": args.steps, "warmup": warmup,
+        "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": {"workload": f"IVF: {n} x {DIM} u8 clipped-GMM ({IVF_COMPS} comps), nlist {IVF_NLIST}, "
+                               f"nprobe {IVF_NPROBE}, {nq} queries, k={k}",
+                   "centroids": "MiniBatchKMeans on a 200,000-row sample (n_init 1, max_iter 20); labels = nearest "
+                                "centroid", "recall_at_k_vs_exact": recall, "cluster_s": round(cluster_s, 1),
+                   "index_build_s": round(build_s, 2),
+                   "timing": "wall clock around the host-buffer call (queries in, ids and distances out)"},
+        "e2e": {"value": qps, "unit": "queries/sec", "h2d_bytes_per_step": int(nq * DIM),
+                "d2h_bytes_per_step": int(nq * k * 8)},
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",
+                     "frac": (achieved / int8_peak) if achieved else None, "traffic": None,
+                     "kernel": "pass-2 scan over the probed cells (k_filter_tc_u8_l2, unit table)",
+                     "algorithmic": "2 * (query, row) pairs of the probed cells * D",
+                     "peak_source": f"2 x {peak_src} bf16 dense ({peaks['bf16_tflops']} TF/s)", "kernel_ms": ms},
+    }
+    print(json.dumps(line), flush=True)
+
+
 # --------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -215,6 +322,8 @@ def main():
     ap.add_argument("--cpu-slice", type=int, default=4_000_000)
     ap.add_argument("--cpu-queries", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="flat", choices=["flat", "ivf"],
+                    help="flat: exact scan (the headline); ivf: clustered search (nlist 1024, nprobe 16)")
     args = ap.parse_args()
     warmup = max(3, args.warmup)
 
@@ -261,6 +370,9 @@ def main():
         return
 
     L = load_lib()
+    if args.workload == "ivf":
+        run_ivf(args, torch, device, L, warmup)
+        return
     sys.path.insert(0, os.path.join(ROOT, "winnex-madhava_b200"))
     from winnex_madhava.sharding import gather_topk, merge_topk_device, row_range
 

@@ -96,3 +96,40 @@ def test_ivf_rejects_bad_input():
     h = ctypes.c_void_p()
     assert L.mdh_ivf_create_u8(ptr(C), 100, 16, ptr(cen), 4, ptr(labels), -1, ctypes.byref(h)) != 0
     assert b"label" in L.mdh_last_error()
+
+
+def _structured(n=20_000, d=64, n_clusters=16, seed=7):
+    """The reference's hybrid test corpus shape (tests/python/test_hybrid.py:23-38)."""
+    rng = np.random.RandomState(seed)
+    centers = rng.randn(n_clusters, d).astype(np.float32) * 5.0
+    labels = rng.randint(0, n_clusters, n)
+    X = centers[labels] + rng.randn(n, d).astype(np.float32) * 0.5
+    X /= np.linalg.norm(X, axis=1, keepdims=True)
+    Xq = (X - X.min()) / (X.max() - X.min()) * 255
+    return X.astype(np.float32), Xq.astype(np.uint8)
+
+
+def test_hybrid_facade_uint8_l2():
+    """build_engine(hybrid=True) on u8/L2 runs on the GPU IVF index; its results
+    are the exact top-k over the probed cells of its own clustering, and the
+    reference test assertions hold (tests/python/test_hybrid.py:57-67,121-128)."""
+    pytest.importorskip("sklearn")
+    import winnex_madhava as wm
+    _, Xu = _structured()
+    eng = wm.build_engine(Xu, dim=Xu.shape[1], k=10, hybrid=True, nlist=16, nprobe=5, metric="l2")
+    assert type(eng).__name__ == "MadHybrid" and eng._ivf is not None
+    assert eng.num_vectors() == Xu.shape[0] and eng.dim() == Xu.shape[1] and eng.built() is True
+    res = eng.search(Xu[0].astype(np.float32), k=10)
+    assert len(res.indices) == 10 and all(0 <= int(i) < Xu.shape[0] for i in res.indices)
+    Q = Xu[:40]
+    got = np.array(eng.search_batch(Q.astype(np.float32), k=10).indices).reshape(40, 10)
+    want, _ = oracle.ivf_exact(Xu, eng._labels, eng._centroids, Q, 10, 5)
+    np.testing.assert_array_equal(got, want)
+    for i in range(5):
+        assert eng.search(Q[i].astype(np.float32), k=10).indices == [int(v) for v in want[i] if v >= 0]
+    # non-integral queries take the per-cell engines and rank the union by float L2
+    qf = Xu[1].astype(np.float32) + 0.25
+    r = eng.search(qf, k=10)
+    assert len(r.indices) == 10
+    default = wm.build_engine(Xu, dim=Xu.shape[1], k=10, metric="l2")
+    assert type(default).__name__ == "MadhavaL2" and default.search(Xu[0].astype(np.float32)).bound_violations == 0

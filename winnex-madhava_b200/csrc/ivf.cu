@@ -15,9 +15,11 @@
 //
 // Search, per batch of queries:
 //   1. route (k_route): fp64 dot products with every centroid, top nprobe;
-//   2. pass 1: each query against its nearest cell with an infinite
-//      threshold; the k-th smallest (key, id) is a valid threshold for the
-//      union (that cell is part of it);
+//   2. pass 1: each query against a sample of its cells (every row whose
+//      id hashes below 1/32, and the 8 lowest-norm rows of each cell) with an
+//      infinite threshold; the k-th smallest (key, id) is a valid threshold
+//      for the union (the sample is part of it) and about 32 k of the
+//      union's rows lie at or below it;
 //   3. pass 2: each query against all its cells with that threshold; the
 //      candidates' first k are exact.  Overflowed lists rerun with their
 //      k-th stored entry, strictly tighter, until they fit.
@@ -61,9 +63,12 @@ struct mdh_ivf {
     mdh::Level rows;                     // all cells, padded
     std::vector<int64_t> cell_start;     // first row of cell c
     std::vector<int64_t> cell_count;     // real rows of cell c
+    mdh::Level sample;                   // per-cell samples, same layout
+    std::vector<int64_t> sample_start;
+    std::vector<int64_t> sample_count;
     float* centroids = nullptr;          // [nlist][dim]
     mdh::Workspace ws;
-    mdh::IvfPassBufs pass[2];            // pass 1 (nearest cell) and pass 2 (all probed cells)
+    mdh::IvfPassBufs pass[2];            // pass 1 (cell samples) and pass 2 (whole cells)
     std::mutex mu;
 };
 
@@ -75,7 +80,9 @@ constexpr int kIvfTileRows = 256;     // tile of the tensor scan (CfgNarrow::BN)
 constexpr int kIvfMaxTilesPerUnit = 64;
 constexpr int kIvfMaxNlist = 8192;    // routing keeps all similarities in shared memory
 constexpr int kIvfMaxProbe = 1024;
-constexpr int kIvfCap1 = 16384;       // pass 1 candidate lists (whole nearest cell)
+constexpr int kIvfCap1 = 16384;       // pass 1 candidate lists (samples of the probed cells)
+constexpr uint32_t kIvfSampleThresh = 0x08000000u;  // id hash below this: in the sample (1/32)
+constexpr int kIvfSampleHead = 8;     // lowest-norm rows of every cell always in the sample
 constexpr int kIvfCap2 = 16384;       // pass 2 candidate lists
 
 template <class T>
@@ -134,6 +141,32 @@ __global__ void k_ivf_gather(const uint8_t* __restrict__ src, const unsigned lon
         norms[dst] = (int32_t)(key & 0xffffffffull);
         ids[dst] = (int32_t)s;
     }
+}
+
+// Sample row p copies main row pos[p] (pos -1: a pad row).
+__global__ void k_ivf_gather_rows(const int32_t* __restrict__ pos, int64_t m, int dpad,
+                                  const uint8_t* __restrict__ src_rows, const int32_t* __restrict__ src_norms,
+                                  const int32_t* __restrict__ src_ids, uint8_t* __restrict__ rows,
+                                  int32_t* __restrict__ norms, int32_t* __restrict__ ids) {
+    const int64_t p = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+    const int l8 = threadIdx.x & 7;
+    if (p >= m) return;
+    const int32_t s = pos[p];
+    for (int off = l8 * 16; off < dpad; off += 128)
+        *reinterpret_cast<uint4*>(rows + (size_t)p * dpad + off) =
+            s >= 0 ? *reinterpret_cast<const uint4*>(src_rows + (size_t)s * dpad + off) : make_uint4(0, 0, 0, 0);
+    if (l8 == 0) {
+        norms[p] = s >= 0 ? src_norms[s] : kNormPad;
+        ids[p] = s >= 0 ? src_ids[s] : -1;
+    }
+}
+
+uint32_t sample_hash_host(int32_t id) {
+    uint64_t z = (uint64_t)(uint32_t)id + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    return (uint32_t)(z >> 32);
 }
 
 __global__ void k_ivf_fill(int32_t* __restrict__ p, int64_t n, int32_t v) {
@@ -216,7 +249,8 @@ struct PassPlan {
     int64_t pairs = 0;
 };
 
-PassPlan plan_pass(const mdh_ivf* ix, const std::vector<int32_t>& probe, int m, int nprobe, int use) {
+PassPlan plan_pass(const mdh_ivf* ix, const std::vector<int64_t>& start, const std::vector<int64_t>& count,
+                   const std::vector<int32_t>& probe, int m, int nprobe, int use) {
     const int nl = ix->nlist;
     std::vector<int64_t> cnt((size_t)nl + 1, 0);
     for (int i = 0; i < m; i++)
@@ -233,9 +267,9 @@ PassPlan plan_pass(const mdh_ivf* ix, const std::vector<int32_t>& probe, int m, 
         for (int j = 0; j < use; j++) pp.gmap[(size_t)fill[(size_t)probe[(size_t)i * nprobe + j]]++] = i;
     for (int c = 0; c < nl; c++) {
         const int64_t qn = cnt[(size_t)c + 1] - cnt[(size_t)c];
-        const int64_t rows = ix->cell_count[(size_t)c];
+        const int64_t rows = count[(size_t)c];
         if (qn == 0 || rows == 0) continue;
-        const int64_t t_first = ix->cell_start[(size_t)c] / kIvfTileRows;
+        const int64_t t_first = start[(size_t)c] / kIvfTileRows;
         const int64_t t_end = t_first + (rows + kIvfTileRows - 1) / kIvfTileRows;
         for (int64_t q0 = 0; q0 < qn; q0 += 128) {
             for (int64_t t0 = t_first; t0 < t_end; t0 += kIvfMaxTilesPerUnit) {
@@ -244,7 +278,7 @@ PassPlan plan_pass(const mdh_ivf* ix, const std::vector<int32_t>& probe, int m, 
                 u.q_count = (int32_t)std::min<int64_t>(128, qn - q0);
                 u.t0 = (int32_t)t0;
                 u.t1 = (int32_t)std::min<int64_t>(t_end, t0 + kIvfMaxTilesPerUnit);
-                u.row_end = (int32_t)(ix->cell_start[(size_t)c] + rows);
+                u.row_end = (int32_t)(start[(size_t)c] + rows);
                 u.pad = 0;
                 pp.units.push_back(u);
             }
@@ -269,6 +303,49 @@ void check_ivf_device(int dev) {
     cudaDeviceProp p;
     MDH_CUDA(cudaGetDeviceProperties(&p, dev));
     MDH_REQUIRE(p.major == 10 && p.minor == 0, MDH_ERR_CUDA, "this library is built for sm_100a (B200)");
+}
+
+// Per-cell samples in the main layout: rows whose id hashes below 1/32 plus
+// the first kIvfSampleHead rows of each cell, in the cell's norm order, each
+// cell padded to whole tiles.
+void build_ivf_sample(mdh_ivf* ix, cudaStream_t st) {
+    const Level& lv = ix->rows;
+    std::vector<int32_t> ids((size_t)lv.n_pad);
+    MDH_CUDA(cudaMemcpyAsync(ids.data(), lv.ids, ids.size() * 4, cudaMemcpyDeviceToHost, st));
+    MDH_CUDA(cudaStreamSynchronize(st));
+    const int nl = ix->nlist;
+    ix->sample_start.assign((size_t)nl, 0);
+    ix->sample_count.assign((size_t)nl, 0);
+    std::vector<int32_t> pos;
+    for (int c = 0; c < nl; c++) {
+        ix->sample_start[(size_t)c] = (int64_t)pos.size();
+        const int64_t s0 = ix->cell_start[(size_t)c], cnt = ix->cell_count[(size_t)c];
+        for (int64_t r = s0; r < s0 + cnt; r++)
+            if (r - s0 < kIvfSampleHead || sample_hash_host(ids[(size_t)r]) < kIvfSampleThresh)
+                pos.push_back((int32_t)r);
+        const int64_t taken = (int64_t)pos.size() - ix->sample_start[(size_t)c];
+        ix->sample_count[(size_t)c] = taken;
+        while (pos.size() % kIvfTileRows) pos.push_back(-1);
+    }
+    if (pos.empty())
+        for (int i = 0; i < kIvfTileRows; i++) pos.push_back(-1);
+    const int64_t m = (int64_t)pos.size();
+    Level& sv = ix->sample;
+    sv.n = m;
+    sv.n_pad = m;
+    sv.rows = dalloc<uint8_t>((size_t)m * ix->dpad);
+    sv.norms = dalloc<int32_t>(m);
+    sv.ids = dalloc<int32_t>(m);
+    int32_t* dpos = dalloc<int32_t>(m);
+    MDH_CUDA(cudaMemcpyAsync(dpos, pos.data(), (size_t)m * 4, cudaMemcpyHostToDevice, st));
+    k_ivf_gather_rows<<<(unsigned)((m * 8 + 255) / 256), 256, 0, st>>>(dpos, m, ix->dpad, lv.rows, lv.norms, lv.ids,
+                                                                        sv.rows, sv.norms, sv.ids);
+    cudaError_t e = cudaGetLastError();
+    cudaError_t e2 = cudaStreamSynchronize(st);
+    cudaFree(dpos);
+    MDH_CUDA(e);
+    MDH_CUDA(e2);
+    make_tmap_rows(sv, ix->dpad);
 }
 
 void ivf_create(const uint8_t* host, int64_t n, int32_t dim, const float* centroids, int32_t nlist,
@@ -363,10 +440,12 @@ void ivf_create(const uint8_t* host, int64_t n, int32_t dim, const float* centro
         MDH_CUDA(cudaMemcpyAsync(ix->centroids, centroids, (size_t)nlist * dim * 4, cudaMemcpyHostToDevice, st));
         MDH_CUDA(cudaStreamSynchronize(st));
         make_tmap_rows(lv, dpad);
+        build_ivf_sample(ix.get(), st);
     } catch (...) {
         cudaStreamSynchronize(st);
         release_tmp();
         free_level_buffers(ix->rows);
+        free_level_buffers(ix->sample);
         if (ix->centroids) cudaFree(ix->centroids);
         cudaStreamDestroy(ix->stream);
         throw;
@@ -438,10 +517,15 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         std::vector<int32_t> probe;
         ivf_route_impl(ix, host_q + (size_t)c0 * ix->dim, m, nprobe, probe, nullptr);
         s.kernel_launches += 2;
-        PassPlan p1 = plan_pass(ix, probe, m, nprobe, 1);
-        PassPlan p2 = plan_pass(ix, probe, m, nprobe, nprobe);
-        upload_pass(ix, ix->pass[0], p1, st);
+        PassPlan p1 = plan_pass(ix, ix->sample_start, ix->sample_count, probe, m, nprobe, nprobe);
+        PassPlan p2 = plan_pass(ix, ix->cell_start, ix->cell_count, probe, m, nprobe, nprobe);
+        // Both passes probe the same cells, so they share the gathered query
+        // matrix (pass 2's); pass 1 only has its own unit table.
         upload_pass(ix, ix->pass[1], p2, st);
+        grow_dev(&ix->pass[0].units, &ix->pass[0].units_bytes, std::max<size_t>(p1.units.size(), 1) * sizeof(ScanUnit));
+        if (!p1.units.empty())
+            MDH_CUDA(cudaMemcpyAsync(ix->pass[0].units, p1.units.data(), p1.units.size() * sizeof(ScanUnit),
+                                     cudaMemcpyHostToDevice, st));
         s.kernel_launches += 2;
         grow_dev(&w.thr_key, &w.thr_key_bytes, (size_t)m * 4);
         grow_dev(&w.thr_id, &w.thr_id_bytes, (size_t)m * 4);
@@ -460,13 +544,13 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         }
         MDH_CUDA(cudaMemsetAsync(w.status, 0, 6 * sizeof(int32_t), st));
         unsigned long long* n_cand = reinterpret_cast<unsigned long long*>(w.status + 2);
-        // Pass 1: nearest cell, infinite thresholds -> k-th entry thresholds.
+        // Pass 1: samples of the probed cells, infinite thresholds -> k-th entry thresholds.
         launch_fill_threshold(w.thr_key, w.thr_id, m, kKeyInf, kIdInf, st);
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
-        launch_filter_tc_u8_l2_units(lv, ix->dpad, ix->pass[0].g, (int)p1.gmap.size(), ix->pass[0].gmap, w.qn,
+        launch_filter_tc_u8_l2_units(ix->sample, ix->dpad, ix->pass[1].g, (int)p2.gmap.size(), ix->pass[1].gmap, w.qn,
                                      ix->pass[0].units, (int)p1.units.size(), w.thr_key, w.thr_id, w.counts, w.cand,
                                      kIvfCap1, w.status, st);
-        launch_select(w.counts, w.cand, kIvfCap1, lv.ids, m, k, 0, w.thr_key, w.thr_id, w.out_key, w.out_id, w.qlist,
+        launch_select(w.counts, w.cand, kIvfCap1, ix->sample.ids, m, k, 0, w.thr_key, w.thr_id, w.out_key, w.out_id, w.qlist,
                       w.status + 1, nullptr, nullptr, st);
         s.kernel_launches += 3;
         // Pass 2: every probed cell with those thresholds.
@@ -604,6 +688,7 @@ mdh_status mdh_ivf_destroy(mdh_ivf* index) {
         ix->pass[0].free_all();
         ix->pass[1].free_all();
         free_level_buffers(ix->rows);
+        free_level_buffers(ix->sample);
         if (ix->centroids) cudaFree(ix->centroids);
         free_workspace(ix->ws);
         if (ix->stream) cudaStreamDestroy(ix->stream);

@@ -216,6 +216,79 @@ private:
 };
 
 // ---------------------------------------------------------------------------
+// GPU IVF index (MadHybrid's uint8 L2 path): cells given as centroids + labels.
+class IvfIndex {
+public:
+    IvfIndex(const U8Array& corpus, const F32Array& centroids, py::array_t<int32_t, py::array::c_style |
+                                                                             py::array::forcecast> labels,
+             int device) {
+        auto ic = corpus.request(), ie = centroids.request(), il = labels.request();
+        if (ic.ndim != 2) throw std::runtime_error("corpus must be a 2-D uint8 array");
+        if (ie.ndim != 2 || ie.shape[1] != ic.shape[1]) throw std::runtime_error("centroids must be [nlist][dim]");
+        if (il.size != ic.shape[0]) throw std::runtime_error("labels must hold one cell per row");
+        n_ = (int64_t)ic.shape[0];
+        dim_ = (int)ic.shape[1];
+        nlist_ = (int)ie.shape[0];
+        mdh_ivf* p = nullptr;
+        mdh_status s;
+        {
+            py::gil_scoped_release nogil;
+            s = mdh_ivf_create_u8((const uint8_t*)ic.ptr, n_, dim_, (const float*)ie.ptr, nlist_,
+                                  (const int32_t*)il.ptr, device, &p);
+        }
+        check(s);
+        ix_ = p;
+    }
+    ~IvfIndex() {
+        if (ix_) mdh_ivf_destroy(ix_);
+    }
+    IvfIndex(const IvfIndex&) = delete;
+    IvfIndex& operator=(const IvfIndex&) = delete;
+
+    // queries [nq][dim] u8 -> (ids, dists) [nq][k] and the call's stats
+    py::tuple search(const U8Array& q, int k, int nprobe) const {
+        auto info = q.request();
+        const int nq = info.ndim == 1 ? 1 : (int)info.shape[0];
+        if ((size_t)info.size != (size_t)nq * dim_) throw std::runtime_error("queries must be uint8 [nq][dim]");
+        py::array_t<int32_t> ids({nq, k}), dist({nq, k});
+        mdh_stats st{};
+        mdh_status s;
+        {
+            py::gil_scoped_release nogil;
+            s = mdh_ivf_search_u8(ix_, (const uint8_t*)info.ptr, nq, k, nprobe, ids.mutable_data(),
+                                  dist.mutable_data(), &st);
+        }
+        check(s);
+        py::dict d;
+        d["latency_ms"] = st.latency_ms;
+        d["pairs_scored"] = (long long)st.pairs_scored;
+        d["full_scan_ms"] = st.full_scan_ms;
+        d["kernel_launches"] = (long long)st.kernel_launches;
+        return py::make_tuple(ids, dist, d);
+    }
+    py::array_t<int32_t> route(const U8Array& q, int nprobe) const {
+        auto info = q.request();
+        const int nq = info.ndim == 1 ? 1 : (int)info.shape[0];
+        if ((size_t)info.size != (size_t)nq * dim_) throw std::runtime_error("queries must be uint8 [nq][dim]");
+        py::array_t<int32_t> cells({nq, nprobe});
+        mdh_status s;
+        {
+            py::gil_scoped_release nogil;
+            s = mdh_ivf_route_u8(ix_, (const uint8_t*)info.ptr, nq, nprobe, cells.mutable_data());
+        }
+        check(s);
+        return cells;
+    }
+    int64_t num_vectors() const { return n_; }
+    int nlist() const { return nlist_; }
+
+private:
+    mdh_ivf* ix_ = nullptr;
+    int64_t n_ = 0;
+    int dim_ = 0, nlist_ = 0;
+};
+
+// ---------------------------------------------------------------------------
 class SpeedEngine {
 public:
     SpeedEngine(const void* data, bool is_f32, int n, int dim, int metric, std::vector<int32_t> devices)
@@ -482,6 +555,15 @@ PYBIND11_MODULE(_winnex_madhava, m) {
         .def("residuals1", [](const MadhavaL2&) -> py::array { not_implemented("MadhavaL2.residuals1: the exact engine has no projection residuals"); })
         .def("residuals2", [](const MadhavaL2&) -> py::array { not_implemented("MadhavaL2.residuals2: the exact engine has no projection residuals"); })
         .def("_set_devices", [](MadhavaL2& self, py::object d) { self.set_devices(parse_devices(d)); }, py::arg("devices"));
+
+    py::class_<IvfIndex>(m, "IvfIndex")
+        .def(py::init<const U8Array&, const F32Array&, py::array_t<int32_t, py::array::c_style | py::array::forcecast>,
+                      int>(),
+             py::arg("corpus"), py::arg("centroids"), py::arg("labels"), py::arg("device") = -1)
+        .def("search", &IvfIndex::search, py::arg("queries"), py::arg("k"), py::arg("nprobe"))
+        .def("route", &IvfIndex::route, py::arg("queries"), py::arg("nprobe"))
+        .def("num_vectors", &IvfIndex::num_vectors)
+        .def("nlist", &IvfIndex::nlist);
 
     py::class_<SpeedEngine>(m, "SpeedEngine")
         .def(py::init([](py::array_t<float, py::array::c_style> arr, int dim, int metric, int n_anchors, int nprobe,

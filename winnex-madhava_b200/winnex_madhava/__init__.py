@@ -326,7 +326,10 @@ class MadHybrid:
     (python/winnex_madhava/__init__.py:577-593); a query is routed to the
     ``nprobe`` cells whose centroids have the largest inner product with it
     (:631-632), and the result is the exact top-k over the union of those
-    cells, computed on the GPU (one exact engine per cell).
+    cells.  For a uint8 corpus under L2 (dim <= 128) with integral queries
+    that runs entirely on the GPU index ``IvfIndex`` (routing in fp64, ties to
+    the lower cell id; ranking by (squared distance, row id)); other corpora
+    and float queries use one exact GPU engine per cell.
     """
 
     def __init__(self, corpus, *, nlist: int = 64, nprobe: int = 5, dtype: str | None = None,
@@ -355,7 +358,25 @@ class MadHybrid:
         self._labels = labels
         self._members = {}
         self._cells = {}
+        self._devices = devices
+        self._ivf = None
         t0 = time.time()
+        if self._dtype == "uint8" and self._metric != "cosine" and self._dim <= 128:
+            dev = int(devices[0]) if devices else -1
+            self._ivf = _native.IvfIndex(np.ascontiguousarray(arr, dtype=np.uint8), self._centroids,
+                                         np.ascontiguousarray(labels, dtype=np.int32), dev)
+            for cid in range(self._nlist):
+                idxs = np.where(labels == cid)[0]
+                if len(idxs):
+                    self._members[cid] = idxs
+            self._build_time = time.time() - t0
+            return
+        self._build_cells()
+        self._build_time = time.time() - t0
+
+    def _build_cells(self):
+        arr, labels, devices = self._corpus, self._labels, self._devices
+        E = arr.astype(np.float32)
         for cid in range(self._nlist):
             idxs = np.where(labels == cid)[0]
             if len(idxs) == 0:
@@ -368,7 +389,6 @@ class MadHybrid:
                 cell = np.ascontiguousarray(E[idxs], dtype=np.float32)
                 self._cells[cid] = MadhavaSpeed(cell, k=self._k, metric="cosine" if self._metric == "cosine" else "l2",
                                                 devices=devices)
-        self._build_time = time.time() - t0
 
     def _probe(self, q, nprobe):
         sims = self._centroids @ q
@@ -378,6 +398,13 @@ class MadHybrid:
         np_ = min(self._nprobe if nprobe is None else int(nprobe), self._nlist)
         kk = k or self._k
         q = np.ascontiguousarray(query, dtype=np.float32).reshape(-1)
+        if self._ivf is not None and np.all((q >= 0) & (q <= 255) & (q == np.round(q))):
+            ids, _, st = self._ivf.search(q.astype(np.uint8)[None, :], kk, np_)
+            r = _SimpleResult([int(i) for i in ids[0] if i >= 0], 0)
+            r.latency_ms = float(st["latency_ms"])
+            return r
+        if not self._cells:
+            self._build_cells()
         cands = []
         for cid in self._probe(q, np_):
             cell = self._cells.get(int(cid))
@@ -404,6 +431,23 @@ class MadHybrid:
             s = self._corpus[ids].astype(np.float64) @ q.astype(np.float64)
             order = np.lexsort((ids, -s))
         return [int(i) for i in ids[order[:kk]]]
+
+    def search_batch(self, queries, k: int | None = None, nprobe: int | None = None):
+        """Batch form of ``search`` (not in the reference API): ``indices`` is
+        the flat [nq * k] list, -1 where the probed cells hold fewer than k rows."""
+        np_ = min(self._nprobe if nprobe is None else int(nprobe), self._nlist)
+        kk = k or self._k
+        Q = np.ascontiguousarray(queries, dtype=np.float32).reshape(-1, self._dim)
+        if self._ivf is not None and np.all((Q >= 0) & (Q <= 255) & (Q == np.round(Q))):
+            ids, _, st = self._ivf.search(Q.astype(np.uint8), kk, np_)
+            r = _SimpleResult([int(i) for i in ids.reshape(-1)], 0)
+            r.latency_ms = float(st["latency_ms"])
+            return r
+        out = []
+        for q in Q:
+            got = self.search(q, k=kk, nprobe=np_).indices
+            out.extend(list(got) + [-1] * (kk - len(got)))
+        return _SimpleResult(out, 0)
 
     def search_exact(self, query, k: int | None = None):
         """Exact scan of the whole corpus (the recall ceiling), on the GPU."""
