@@ -14,7 +14,8 @@
 // scan's chunk bound needs.
 //
 // Search, per batch of queries:
-//   1. route (k_route): fp64 dot products with every centroid, top nprobe;
+//   1. route (k_route_sims, k_route_select): fp64 dot products with every
+//      centroid, top nprobe;
 //   2. pass 1: each query against a sample of its cells (every row whose
 //      id hashes below 1/32, and the 8 lowest-norm rows of each cell) with an
 //      infinite threshold; the k-th smallest (key, id) is a valid threshold
@@ -78,7 +79,7 @@ namespace {
 
 constexpr int kIvfTileRows = 256;     // tile of the tensor scan (CfgNarrow::BN)
 constexpr int kIvfMaxTilesPerUnit = 64;
-constexpr int kIvfMaxNlist = 8192;    // routing keeps all similarities in shared memory
+constexpr int kIvfMaxNlist = 8192;
 constexpr int kIvfMaxProbe = 1024;
 constexpr int kIvfCap1 = 16384;       // pass 1 candidate lists (samples of the probed cells)
 constexpr uint32_t kIvfSampleThresh = 0x08000000u;  // id hash below this: in the sample (1/32)
@@ -174,63 +175,83 @@ __global__ void k_ivf_fill(int32_t* __restrict__ p, int64_t n, int32_t v) {
     if (i < n) p[i] = v;
 }
 
-// One block per query: fp64 similarities with every centroid (multiply-adds
-// in dimension order from 0.0), then nprobe rounds of a block arg-max with
-// ties to the lower cell id.
-__global__ void __launch_bounds__(256) k_route(const uint8_t* __restrict__ q, int dpad, int dim,
-                                               const float* __restrict__ centroids, int nlist, int nprobe,
-                                               int32_t* __restrict__ probe) {
-    extern __shared__ double sims[];
-    __shared__ double best_v[256];
-    __shared__ int best_i[256];
-    const int qi = blockIdx.x;
-    const uint8_t* qrow = q + (size_t)qi * dpad;
-    for (int c = threadIdx.x; c < nlist; c += blockDim.x) {
-        const float* cr = centroids + (size_t)c * dim;
-        double acc = 0.0;
-        for (int j = 0; j < dim; j++) acc = __fma_rn((double)qrow[j], (double)cr[j], acc);
-        sims[c] = acc;
+// Routing, step 1: sims[q][c] = sum_j q[j] * centroid[c][j] in fp64, one
+// fused multiply-add per j in dimension order from 0.0 (deterministic, so the
+// cell order is reproducible).  Block tile: 16 queries x 64 centroids in
+// shared memory; each thread forms 4 of the 1024 dot products.
+constexpr int kRouteQ = 16, kRouteC = 64, kRouteDim = 128;
+constexpr int kRoutePerThread = kRouteQ * kRouteC / 256;
+__global__ void __launch_bounds__(256) k_route_sims(const uint8_t* __restrict__ q, int nq, int dpad, int dim,
+                                                    const float* __restrict__ centroids, int nlist,
+                                                    double* __restrict__ sims) {
+    __shared__ float cs[kRouteC][kRouteDim + 1];
+    __shared__ uint8_t qs[kRouteQ][kRouteDim];
+    const int q0 = blockIdx.y * kRouteQ, c0 = blockIdx.x * kRouteC;
+    for (int i = threadIdx.x; i < kRouteC * dim; i += blockDim.x) {
+        const int c = i / dim, j = i - c * dim;
+        cs[c][j] = c0 + c < nlist ? centroids[(size_t)(c0 + c) * dim + j] : 0.0f;
+    }
+    for (int i = threadIdx.x; i < kRouteQ * dim; i += blockDim.x) {
+        const int r = i / dim, j = i - r * dim;
+        qs[r][j] = q0 + r < nq ? q[(size_t)(q0 + r) * dpad + j] : 0;
     }
     __syncthreads();
+    const int c = threadIdx.x % kRouteC;
+    const int rbase = (threadIdx.x / kRouteC) * kRoutePerThread;
+    double acc[kRoutePerThread];
+#pragma unroll
+    for (int r = 0; r < kRoutePerThread; r++) acc[r] = 0.0;
+    for (int j = 0; j < dim; j++) {
+        const double cv = (double)cs[c][j];
+#pragma unroll
+        for (int r = 0; r < kRoutePerThread; r++) acc[r] = __fma_rn((double)qs[rbase + r][j], cv, acc[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < kRoutePerThread; r++)
+        if (q0 + rbase + r < nq && c0 + c < nlist) sims[(size_t)(q0 + rbase + r) * nlist + c0 + c] = acc[r];
+}
+
+// Routing, step 2: one warp per query takes the nprobe largest similarities,
+// ties to the lower cell id, best first.
+__global__ void __launch_bounds__(256) k_route_select(double* __restrict__ sims, int nq, int nlist, int nprobe,
+                                                      int32_t* __restrict__ probe) {
+    const int qi = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (qi >= nq) return;
+    double* row = sims + (size_t)qi * nlist;
     for (int p = 0; p < nprobe; p++) {
         double bv = -INFINITY;
         int bi = 0x7fffffff;
-        for (int c = threadIdx.x; c < nlist; c += blockDim.x) {
-            const double v = sims[c];
+        for (int c = lane; c < nlist; c += 32) {
+            const double v = row[c];
             if (v > bv || (v == bv && c < bi)) {
                 bv = v;
                 bi = c;
             }
         }
-        best_v[threadIdx.x] = bv;
-        best_i[threadIdx.x] = bi;
-        __syncthreads();
-        for (int s = blockDim.x / 2; s > 0; s >>= 1) {
-            if (threadIdx.x < s) {
-                const double ov = best_v[threadIdx.x + s];
-                const int oi = best_i[threadIdx.x + s];
-                if (ov > best_v[threadIdx.x] || (ov == best_v[threadIdx.x] && oi < best_i[threadIdx.x])) {
-                    best_v[threadIdx.x] = ov;
-                    best_i[threadIdx.x] = oi;
-                }
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) {
+            const double ov = __shfl_xor_sync(0xffffffffu, bv, m);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
             }
-            __syncthreads();
         }
-        if (threadIdx.x == 0) {
-            const int c = best_i[0];
-            probe[(size_t)qi * nprobe + p] = c;
-            sims[c] = -INFINITY;  // taken
-        }
-        __syncthreads();
+        if (lane == 0) probe[(size_t)qi * nprobe + p] = bi;
+        if (lane == (bi & 31)) row[bi] = -INFINITY;  // taken
+        __syncwarp();
     }
 }
 
 void launch_route(const uint8_t* q, int nq, int dpad, int dim, const float* centroids, int nlist, int nprobe,
-                  int32_t* probe, cudaStream_t st) {
+                  double* sims, int32_t* probe, cudaStream_t st) {
     if (nq <= 0) return;
-    const size_t smem = (size_t)nlist * sizeof(double);
-    if (smem > 48 * 1024) MDH_CUDA(cudaFuncSetAttribute(k_route, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k_route<<<nq, 256, smem, st>>>(q, dpad, dim, centroids, nlist, nprobe, probe);
+    MDH_REQUIRE(dim <= kRouteDim, MDH_ERR_INTERNAL, "routing supports dim <= 128");
+    dim3 grid((unsigned)((nlist + kRouteC - 1) / kRouteC), (unsigned)((nq + kRouteQ - 1) / kRouteQ));
+    k_route_sims<<<grid, 256, 0, st>>>(q, nq, dpad, dim, centroids, nlist, sims);
+    MDH_CUDA(cudaGetLastError());
+    k_route_select<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, st>>>(sims, nq, nlist, nprobe, probe);
     MDH_CUDA(cudaGetLastError());
 }
 
@@ -464,7 +485,9 @@ void ivf_route_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int nprobe, std:
     MDH_CUDA(cudaMemsetAsync(w.q_u8, 0, (size_t)nq * ix->dpad, st));
     MDH_CUDA(cudaMemcpy2DAsync(w.q_u8, ix->dpad, host_q, ix->dim, ix->dim, nq, cudaMemcpyHostToDevice, st));
     launch_query_norms_u8(w.q_u8, nq, ix->dpad, w.qn, st);
-    launch_route(w.q_u8, nq, ix->dpad, ix->dim, ix->centroids, ix->nlist, nprobe, w.flags, st);
+    grow_dev(&w.tmp, &w.tmp_bytes, (size_t)nq * ix->nlist * sizeof(double));  // similarities
+    launch_route(w.q_u8, nq, ix->dpad, ix->dim, ix->centroids, ix->nlist, nprobe, static_cast<double*>(w.tmp), w.flags,
+                 st);
     probe.resize((size_t)nq * nprobe);
     MDH_CUDA(cudaMemcpyAsync(probe.data(), w.flags, probe.size() * 4, cudaMemcpyDeviceToHost, st));
     MDH_CUDA(cudaStreamSynchronize(st));

@@ -49,6 +49,62 @@ __global__ void k_fill_threshold(uint32_t* tk, int32_t* ti, int nq, uint32_t key
     }
 }
 
+// k-th smallest (1-based rank k <= c) of keys[0, c) by an 8-bit radix select
+// from the most significant digit: O(8 c) instead of a full sort.  Every
+// thread of the block calls it and gets the result.
+__device__ unsigned long long radix_select_kth(const unsigned long long* keys, int c, int k) {
+    __shared__ unsigned int hist[256];
+    __shared__ unsigned long long s_prefix;
+    __shared__ int s_rem;
+    unsigned long long prefix = 0, mask = 0;
+    int rem = k;
+    for (int d = 7; d >= 0; d--) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        const int sh = 8 * d;
+        for (int i = threadIdx.x; i < c; i += blockDim.x) {
+            const unsigned long long v = keys[i];
+            if ((v & mask) == prefix) atomicAdd(&hist[(v >> sh) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            // Lane l owns bins [8l, 8l + 8); find the bin where the count reaches rem.
+            const int l = threadIdx.x;
+            unsigned int own = 0;
+#pragma unroll
+            for (int b = 0; b < 8; b++) own += hist[8 * l + b];
+            unsigned int incl = own;
+#pragma unroll
+            for (int m = 1; m < 32; m <<= 1) {
+                const unsigned int o = __shfl_up_sync(0xffffffffu, incl, m);
+                if (l >= m) incl += o;
+            }
+            const unsigned int excl = incl - own;
+            const unsigned int hit = __ballot_sync(0xffffffffu, incl >= (unsigned int)rem);
+            if (l == __ffs(hit) - 1) {
+                unsigned int cum = excl;
+                for (int b = 0; b < 8; b++) {
+                    const unsigned int h = hist[8 * l + b];
+                    if (cum + h >= (unsigned int)rem) {
+                        s_prefix = prefix | ((unsigned long long)(8 * l + b) << sh);
+                        s_rem = rem - (int)cum;
+                        break;
+                    }
+                    cum += h;
+                }
+            }
+        }
+        __syncthreads();
+        prefix = s_prefix;
+        rem = s_rem;
+        mask |= 0xFFull << sh;
+        __syncthreads();
+    }
+    return prefix;
+}
+
+constexpr int kRadixMinCount = 1024;  // below this the bitonic sort is as fast
+
 // One CTA per query.  qmap (optional) maps the CTA's query to the slot its
 // threshold / output / flag is written to.
 // Candidates are {key, row position in the scanned level}; `ids` maps a
@@ -73,6 +129,16 @@ __global__ void k_select(const uint32_t* __restrict__ counts, const uint2* __res
         } else {
             keys[i] = ~0ull;
         }
+    }
+    if (!final_ && c >= k && c > kRadixMinCount) {
+        // Only the k-th entry is needed: select it without sorting.
+        __syncthreads();
+        const unsigned long long kth = radix_select_kth(keys, c, k);
+        if (threadIdx.x == 0) {
+            thr_key[qo] = (uint32_t)(kth >> 32);
+            thr_id[qo] = (int32_t)(kth & 0xffffffffu);
+        }
+        return;
     }
     bitonic_sort_smem(keys, P);
     if (!final_) {
