@@ -97,6 +97,10 @@ def load_lib():
     L.mdh_ivf_create_u8.argtypes = [P, i64, i32, P, i32, P, i32, ctypes.POINTER(P)]
     L.mdh_ivf_search_u8.argtypes = [P, P, i32, i32, i32, P, P, ctypes.POINTER(Stats)]
     L.mdh_ivf_destroy.argtypes = [P]
+    L.mdh_index_create_f32.argtypes = [P, i64, i32, i32, P, i32, i64, ctypes.POINTER(P)]
+    L.mdh_index_create_f32.restype = ctypes.c_int
+    L.mdh_search_f32.argtypes = [P, P, i32, i32, i32, P, P, ctypes.POINTER(Stats)]
+    L.mdh_search_f32.restype = ctypes.c_int
     L.mdh_search_u8.restype = ctypes.c_int
     L.mdh_last_error.restype = ctypes.c_char_p
     for f in ("mdh_index_create_u8_device", "mdh_index_destroy", "mdh_search_u8", "mdh_search_u8_device",
@@ -308,6 +312,93 @@ def run_ivf(args, torch, device, L, warmup):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- float cosine workload
+COS_DIM, COS_COMPS = 768, 1024
+
+
+def make_cos_rows_gpu(torch, n, device, seed):
+    """Row-normalized isotropic Gaussian mixture (1,024 unit-normalized random
+    means, component std 0.3), float32 [n][768], generated on the GPU."""
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED + 11)
+    means = torch.randn((COS_COMPS, COS_DIM), generator=g, device=device)
+    means /= means.norm(dim=1, keepdim=True)
+    out = torch.empty((n, COS_DIM), dtype=torch.float32, device=device)
+    g.manual_seed(seed)
+    step = 1_000_000
+    for s in range(0, n, step):
+        e = min(n, s + step)
+        lab = torch.randint(0, COS_COMPS, (e - s,), generator=g, device=device)
+        x = means[lab] + 0.3 * torch.randn((e - s, COS_DIM), generator=g, device=device)
+        out[s:e] = x / x.norm(dim=1, keepdim=True)
+    return out
+
+
+def run_cos(args, torch, device, L, warmup):
+    """Float32 cosine (SpeedEngine cosine semantics) over 10M x 768, batch
+    4,096, k=10: bf16 tcgen05 pass + exact fp32 rescore."""
+    n = args.n if args.n != N_DEFAULT else 10_000_000
+    nq = args.nq if args.nq != 10_000 else 4096
+    k = args.k
+    rows = make_cos_rows_gpu(torch, n, device, SEED + 12).cpu().numpy()
+    queries = make_cos_rows_gpu(torch, nq, device, SEED + 13).cpu().numpy()
+    torch.cuda.empty_cache()
+    check(L, L.mdh_set_scan_path(args.scan_path), "set_scan_path")
+    h = ctypes.c_void_p()
+    t0 = time.time()
+    check(L, L.mdh_index_create_f32(ctypes.c_void_p(rows.ctypes.data), n, COS_DIM, 0, None, 0, 0, ctypes.byref(h)),
+          "index build")
+    build_s = time.time() - t0
+    del rows
+    ids = np.empty((nq, k), np.int32)
+    score = np.empty((nq, k), np.float32)
+    st = Stats()
+
+    def step():
+        check(L, L.mdh_search_f32(h, ctypes.c_void_p(queries.ctypes.data), nq, k, 2, ctypes.c_void_p(ids.ctypes.data),
+                                  ctypes.c_void_p(score.ctypes.data), ctypes.byref(st)), "search")
+
+    for _ in range(warmup):
+        step()
+    sampler = ClockSampler(device.index or 0)
+    sampler.start()
+    scan_ms, pairs = [], []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+        scan_ms.append(st.full_scan_ms)
+        pairs.append(st.full_scan_pairs)
+    elapsed = time.perf_counter() - t0
+    clocks = sampler.stop()
+    check(L, L.mdh_index_destroy(h), "destroy")
+    peaks, peak_src = measured_peaks()
+    ms = statistics.median(scan_ms)
+    achieved = 2.0 * pairs[0] * COS_DIM / (ms / 1e3) / 1e12 if ms > 0 else None
+    qps = nq * args.steps / elapsed
+    path = {0: "CUDA cores (fp32 replica)", 3: "bf16 tcgen05 pass + exact fp32 rescore"}.get(int(st.tensor_core_path),
+                                                                                           str(st.tensor_core_path))
+    line = {
+        "metric": f"queries/sec, {n // 1_000_000}M x {COS_DIM} f32 cosine top-{k}, {nq}-query batch",
+        "value": qps, "unit": "queries/sec", "n_gpus": 1, "steps": args.steps, "warmup": warmup,
+        "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32 (bf16 tensor pass, fp32 rescore)", "data": "synthetic",
+        "config": {"workload": f"{n} x {COS_DIM} f32 row-normalized GMM ({COS_COMPS} comps, std 0.3), {nq} queries, "
+                               f"k={k}, SpeedEngine cosine semantics", "scan": path,
+                   "index_build_s": round(build_s, 1), "levels": int(st.levels),
+                   "timing": "wall clock around the host-buffer call (queries in, ids and scores out)"},
+        "e2e": {"value": qps, "unit": "queries/sec", "h2d_bytes_per_step": int(nq * COS_DIM * 4),
+                "d2h_bytes_per_step": int(nq * k * 8)},
+        "gpu_launches": int(st.kernel_launches) * args.steps,
+        "clocks": clocks,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": (achieved / peaks["bf16_tflops"]) if achieved else None, "traffic": None,
+                     "kernel": "full-corpus scan (k_filter_tc_bf16_cos + k_rescore_speed_cos)",
+                     "algorithmic": "2*N*Q*D flop per launch", "peak_source": f"{peak_src} bf16 dense",
+                     "kernel_ms": ms},
+    }
+    print(json.dumps(line), flush=True)
+
+
 # --------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -318,12 +409,14 @@ def main():
     ap.add_argument("--n", type=int, default=N_DEFAULT)
     ap.add_argument("--nq", type=int, default=10_000)
     ap.add_argument("--k", type=int, default=10)
+    ap.add_argument("--comps", type=int, default=COMPONENTS, help="mixture components of the synthetic corpus")
     ap.add_argument("--scan-path", type=int, default=0, help="0 auto, 1 CUDA cores, 2 tensor cores")
     ap.add_argument("--cpu-slice", type=int, default=4_000_000)
     ap.add_argument("--cpu-queries", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="flat", choices=["flat", "ivf"],
-                    help="flat: exact scan (the headline); ivf: clustered search (nlist 1024, nprobe 16)")
+    ap.add_argument("--workload", default="flat", choices=["flat", "ivf", "cos"],
+                    help="flat: exact u8 L2 scan (the headline); ivf: clustered search (nlist 1024, nprobe 16); "
+                         "cos: float32 cosine scan (10M x 768, 4,096 queries)")
     args = ap.parse_args()
     warmup = max(3, args.warmup)
 
@@ -343,8 +436,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    queries = make_queries(args.nq)
-    config = {"workload": f"{args.n // 1_000_000}M x {DIM} u8 clipped-GMM ({COMPONENTS} comps), {args.nq} queries, "
+    queries = make_queries(args.nq, args.comps)
+    config = {"workload": f"{args.n // 1_000_000}M x {DIM} u8 clipped-GMM ({args.comps} comps), {args.nq} queries, "
                           f"exact top-{args.k} L2",
               "n": args.n, "dim": DIM, "nq": args.nq, "k": args.k,
               "parallelism": f"row-shard x{n_gpus} + NCCL all_gather of top-k",
@@ -356,7 +449,7 @@ def main():
                 dist.destroy_process_group()
             return
         n_slice = min(args.cpu_slice, args.n)
-        rows = make_rows_gpu(torch, 0, n_slice, device).cpu().numpy()
+        rows = make_rows_gpu(torch, 0, n_slice, device, args.comps).cpu().numpy()
         qps, cb = cpu_reference_qps(rows, args.n, queries[:args.cpu_queries], args.k, steps=args.steps,
                                     warmup=min(warmup, 1))
         line = {"metric": METRIC, "value": qps, "unit": "queries/sec", "n_gpus": n_gpus, "steps": args.steps,
@@ -373,12 +466,15 @@ def main():
     if args.workload == "ivf":
         run_ivf(args, torch, device, L, warmup)
         return
+    if args.workload == "cos":
+        run_cos(args, torch, device, L, warmup)
+        return
     sys.path.insert(0, os.path.join(ROOT, "winnex-madhava_b200"))
     from winnex_madhava.sharding import gather_topk, merge_topk_device, row_range
 
     check(L, L.mdh_set_scan_path(args.scan_path), "set_scan_path")
     start, end = row_range(args.n, rank, world)
-    rows = make_rows_gpu(torch, start, end, device)
+    rows = make_rows_gpu(torch, start, end, device, args.comps)
     torch.cuda.synchronize()
     h = ctypes.c_void_p()
     t0 = time.time()
@@ -525,7 +621,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             n_slice = min(args.cpu_slice, args.n)
-            rows = make_rows_gpu(torch, 0, n_slice, device).cpu().numpy()
+            rows = make_rows_gpu(torch, 0, n_slice, device, args.comps).cpu().numpy()
             _, cb = cpu_reference_qps(rows, args.n, queries[:args.cpu_queries], k, steps=1, warmup=0)
             line["cpu_baseline"] = cb
         except Exception as exc:  # the baseline must not hide the GPU number

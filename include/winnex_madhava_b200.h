@@ -63,7 +63,8 @@ typedef struct {
     int64_t bound_violations;     /* rows misplaced relative to the returned top-K, counted for the
                                      verified queries by an exact unpruned scan (mdh_set_verify); 0 */
     int64_t candidates;           /* pairs that passed the threshold filter into the final selection */
-    int32_t tensor_core_path;     /* full-corpus scan: 0 CUDA cores, 1 tcgen05 per SM, 2 tcgen05 on SM pairs */
+    int32_t tensor_core_path;     /* full-corpus scan: 0 CUDA cores, 1 tcgen05 per SM, 2 tcgen05 on SM pairs,
+                                     3 bf16 tcgen05 pass + exact fp32 rescore (float cosine scores) */
     int32_t levels;               /* threshold-refinement levels run */
     double full_scan_ms;          /* CUDA-event time of the full-corpus scan kernel(s) on their stream */
     int64_t full_scan_pairs;      /* (query, row) pairs that kernel scored */

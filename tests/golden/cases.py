@@ -131,4 +131,18 @@ def case_f32_corpus():
     return X, Q
 
 
+def cos_gmm_f32(n, d, comps, seed, stream=0):
+    """Row-normalized isotropic Gaussian mixture: unit-normalized random means,
+    component std 0.3 (the float cosine workload's generator); `stream`
+    selects an independent draw of rows from the same means."""
+    rng = np.random.default_rng(seed)
+    means = rng.standard_normal((comps, d))
+    means /= np.linalg.norm(means, axis=1, keepdims=True)
+    r = np.random.default_rng([seed, stream])
+    lab = r.integers(0, comps, n)
+    X = means[lab] + r.normal(0, 0.3, (n, d))
+    X /= np.linalg.norm(X, axis=1, keepdims=True)
+    return X.astype(np.float32)
+
+
 DIMS = (48, 7, 200, 300)

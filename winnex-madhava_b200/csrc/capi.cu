@@ -169,12 +169,31 @@ void ensure_status(Workspace& w) {
 // batch and faster than the streaming CUDA-core scan even for one query (at
 // one query both read the corpus from HBM; TMA keeps more of it in flight).
 
+// Error bound of the bf16 cosine pass for unit vectors: bf16 products carry a
+// relative error of at most 2u + u^2 (u = 2^-8) and |sum q_j v_j| <= 1; the
+// fp32 sums of the tensor core and of the reference add at most dim * 2^-24
+// each.
+float bf16_cos_eps(int dim) {
+    return (float)((1.0 / 128 + 1.0 / 65536) * 1.001 + 2.0 * dim / 16777216.0 + 1e-6);
+}
+
 int run_filter(mdh_index* ix, Shard& sh, const Level& lv, const QueryPlan& qp, const uint8_t* q_u8,
                const int32_t* qn, const float* q_f32, int nq, const uint32_t* tk, const int32_t* ti, int cap,
-               bool dense) {
+               bool dense, const uint16_t* q_bf16 = nullptr, bool exact_only = false) {
     Workspace& w = sh.ws;
     const int d = dense ? 1 : 0;
     int used = 1;
+    if (!qp.integer && qp.kind == kScoreSpeedCos && q_bf16 && !exact_only && g_scan_path != 1 &&
+        lv.has_tmap_bf16 && tc_bf16_supported(ix, lv)) {
+        // bf16 tensor pass keeps every pair within the error bound of the
+        // threshold; the kept pairs are then rescored with the reference's
+        // fp32 arithmetic.
+        launch_filter_tc_bf16_cos(lv, ix->dim, q_bf16, nq, tk, w.counts, w.cand, cap, d, bf16_cos_eps(ix->dim),
+                                  w.status, sh.stream);
+        if (dense) launch_fill_u32(w.counts, nq, (uint32_t)lv.n, sh.stream);
+        launch_rescore_speed_cos(w.counts, w.cand, cap, lv.rows_f32, ix->dim, q_f32, nq, sh.stream);
+        return 4;
+    }
     if (qp.integer) {
         if (ix->metric == MDH_METRIC_L2) {
             const bool can1 = lv.has_tmap && tc_supported(ix, lv);
@@ -262,8 +281,9 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
             MDH_CUDA(cudaEventRecord(w.ev0, st));
         }
         const bool dense = s.dense && s.cap >= lv.n;
-        const int used = run_filter(ix, sh, lv, qp, w.q_u8, w.qn, w.q_f32, nq, w.thr_key, w.thr_id, s.cap, dense);
-        res.launches += dense ? 2 : 1;
+        const int used = run_filter(ix, sh, lv, qp, w.q_u8, w.qn, w.q_f32, nq, w.thr_key, w.thr_id, s.cap, dense,
+                                    w.q_bf16);
+        res.launches += (dense ? 2 : 1) + (used == 4 ? 1 : 0);
         if (last_level) {
             MDH_CUDA(cudaEventRecord(w.ev1, st));
             res.scan_pairs = lv.n * (int64_t)nq;
@@ -345,7 +365,7 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
             MDH_CUDA(cudaStreamSynchronize(st));
         }
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
-        run_filter(ix, sh, lv, qp, cq_u8, cqn, cq_f32, m, d_tk, d_ti, last.cap, false);
+        run_filter(ix, sh, lv, qp, cq_u8, cqn, cq_f32, m, d_tk, d_ti, last.cap, false, nullptr, true);
         MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
         launch_select(w.counts, w.cand, last.cap, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id, w.flags,
                       w.status + 1, d_list, n_cand, st);
@@ -492,6 +512,8 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
     MDH_REQUIRE(qp.integer || host_f32, MDH_ERR_NOT_INTEGRAL, "u8 queries need the integer path");
     if (qp.kind == kScoreSpeedCos && !ix->is_f32)
         for (auto& sh : ix->shards) ensure_speed_rows_u8(ix, sh);
+    if (qp.kind == kScoreSpeedCos && g_scan_path != 1)
+        for (auto& sh : ix->shards) ensure_bf16_rows(ix, sh);
     if (qp.kind == kScoreExactCosF32)
         throw Error(MDH_ERR_UNSUPPORTED, "float-row exact cosine is not built in this version");
 
@@ -534,6 +556,10 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
                     growT(&w.q_f32, &w.q_f32_bytes, qbuf_f32.size() * 4);
                     MDH_CUDA(cudaMemcpyAsync(w.q_f32, qbuf_f32.data(), qbuf_f32.size() * 4, cudaMemcpyHostToDevice,
                                              sh.stream));
+                    if (qp.kind == kScoreSpeedCos && ix->dim % 8 == 0) {
+                        growT(&w.q_bf16, &w.q_bf16_bytes, (size_t)m * dim * 2);
+                        launch_convert_bf16(w.q_f32, (int64_t)m * dim, w.q_bf16, sh.stream);
+                    }
                 }
                 sres[(size_t)si] = search_shard(ix, sh, qp, m, kk, qbuf_u8.data(), qbuf_f32.data(), (size_t)dim);
             } catch (const Error& e) {

@@ -303,6 +303,7 @@ void ensure_speed_rows_u8(mdh_index* ix, Shard& sh) {
 
 void free_level_buffers(Level& lv) {
     if (lv.owns) {
+        cudaFree(lv.rows_bf16);
         cudaFree(lv.rows);
         cudaFree(lv.norms);
         cudaFree(lv.ids);
@@ -313,7 +314,7 @@ void free_level_buffers(Level& lv) {
 }
 
 void free_workspace(Workspace& w) {
-    void* ptrs[] = {w.q_u8, w.q_f32, w.qn, w.thr_key, w.thr_id, w.counts, w.cand, w.out_key, w.out_id, w.flags,
+    void* ptrs[] = {w.q_u8, w.q_f32, w.q_bf16, w.qn, w.thr_key, w.thr_id, w.counts, w.cand, w.out_key, w.out_id, w.flags,
                     w.qlist, w.status, w.tmp};
     for (void* p : ptrs) cudaFree(p);
     if (w.h_status) cudaFreeHost(w.h_status);

@@ -27,6 +27,9 @@ struct Level {
     bool has_tmap = false;
     CUtensorMap tmap_rows_pair;  // TMA map over `rows` with half-tile boxes (2-SM scan)
     bool has_tmap_pair = false;
+    uint16_t* rows_bf16 = nullptr;  // [n_pad][dim] bf16 copy of rows_f32 (approximate tensor scan)
+    CUtensorMap tmap_bf16;          // TMA map over rows_bf16, 64 x 128 boxes, 128-byte swizzle
+    bool has_tmap_bf16 = false;
     bool owns = true;        // false when aliasing another level's buffers
 };
 
@@ -34,6 +37,7 @@ struct Level {
 struct Workspace {
     uint8_t* q_u8 = nullptr;     size_t q_u8_bytes = 0;     // [nq][dpad]
     float* q_f32 = nullptr;      size_t q_f32_bytes = 0;    // [nq][dim]
+    uint16_t* q_bf16 = nullptr;  size_t q_bf16_bytes = 0;   // [nq][dim] bf16 of q_f32
     int32_t* qn = nullptr;       size_t qn_bytes = 0;       // [nq] |q|^2
     uint32_t* thr_key = nullptr; size_t thr_key_bytes = 0;  // [nq]
     int32_t* thr_id = nullptr;   size_t thr_id_bytes = 0;   // [nq]
@@ -116,6 +120,10 @@ enum ScoreKind : int {
 };
 
 // ---- tensor-core scan (scan_tc.cu) ----
+// TMA map over a row-major 2-D array of u8 (bf16 = 0) or bf16 (bf16 = 1)
+// elements, 128-byte swizzle, boxes of box_inner x box_rows elements.
+void encode_tmap_2d_sw128(CUtensorMap* map, int bf16, const void* base, uint64_t inner, uint64_t rows,
+                         uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows);
 // TMA map over u8 rows [rows][dpad], 128-byte swizzle, boxes of box_rows rows.
 void encode_u8_rows_tmap(CUtensorMap* map, const void* base, int64_t rows, int dpad, int box_rows);
 // Corpus chunks per query group so that groups x chunks spreads evenly over workers.
@@ -146,6 +154,19 @@ void make_tmap_rows_pair(Level& lv, int dpad);
 void launch_filter_tc2_u8_l2(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
                              const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts,
                              uint2* cand, int cap, int dense, int32_t* status, cudaStream_t st);
+
+// ---- approximate bf16 tensor-core scan for float cosine scores (scan_tc_bf16.cu) ----
+// Every row whose bf16 score is >= T - eps (T = the query's threshold score)
+// is appended with its row position; launch_rescore_speed_cos then replaces
+// the candidates' keys by the exact float score of the reference.
+bool tc_bf16_supported(const mdh_index* ix, const Level& lv);
+void ensure_bf16_rows(mdh_index* ix, Shard& sh);
+void launch_convert_bf16(const float* src, int64_t count, uint16_t* dst, cudaStream_t st);
+void launch_filter_tc_bf16_cos(const Level& lv, int dim, const uint16_t* q_bf16, int nq, const uint32_t* thr_key,
+                               uint32_t* counts, uint2* cand, int cap, int dense, float eps, int32_t* status,
+                               cudaStream_t st);
+void launch_rescore_speed_cos(const uint32_t* counts, uint2* cand, int cap, const float* rows_f32, int dim,
+                              const float* q_f32, int nq, cudaStream_t st);
 
 // ---- selection (select.cu) ----
 void launch_fill_threshold(uint32_t* thr_key, int32_t* thr_id, int nq, uint32_t key, int32_t id,

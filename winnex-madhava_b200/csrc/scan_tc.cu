@@ -411,6 +411,21 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 
 }  // namespace
 
+void encode_tmap_2d_sw128(CUtensorMap* map, int bf16, const void* base, uint64_t inner, uint64_t rows,
+                         uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
+    MDH_REQUIRE((reinterpret_cast<uintptr_t>(base) & 15) == 0, MDH_ERR_INTERNAL, "TMA base must be 16-byte aligned");
+    MDH_REQUIRE(row_stride_bytes % 16 == 0, MDH_ERR_INTERNAL, "TMA row stride must be a multiple of 16 bytes");
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)row_stride_bytes};
+    cuuint32_t box[2] = {box_inner, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = get_encode()(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                              const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    MDH_REQUIRE(r == CUDA_SUCCESS, MDH_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+}
+
 void encode_u8_rows_tmap(CUtensorMap* map, const void* base, int64_t rows, int dpad, int box_rows) {
     MDH_REQUIRE((reinterpret_cast<uintptr_t>(base) & 15) == 0, MDH_ERR_INTERNAL, "TMA base must be 16-byte aligned");
     MDH_REQUIRE(dpad == BK, MDH_ERR_INTERNAL, "tensor-core rows are 128 bytes");
