@@ -32,8 +32,9 @@
 // 32-row chunk has the chunk's smallest norm n_min.  With m = max q.v over
 // the chunk, every key in the chunk is >= |q|^2 + n_min - 2m; when that
 // exceeds the query's threshold the whole chunk is skipped after one max
-// reduction (tc_ptx.cuh: max32).  n_min is read from L2 one tile ahead; the
-// rare chunks that pass are expanded by a bit-mask loop.
+// reduction (tc_ptx.cuh: max32).  The rows' norms are read one tile ahead,
+// one per lane; the rare chunks that pass are expanded by a warp-uniform walk
+// over the passing columns, so no global load sits on that path.
 //
 // Work units: (query group, corpus chunk), ordered chunk-major so the CTAs
 // running at the same time share corpus chunks through L2; each CTA takes
@@ -123,10 +124,10 @@ struct UnitView {
     int q_row, q_count, t0, t1, row_end;
 };
 
-template <class C>
+template <class C, bool UNITS>
 __device__ __forceinline__ UnitView unit_view(const Sched& s, const ScanUnit* units, long long u, int n_rows, int nq) {
     UnitView v;
-    if (units) {
+    if (UNITS) {
         const ScanUnit x = units[u];
         v.q_row = x.q_row;
         v.q_count = x.q_count;
@@ -143,7 +144,12 @@ __device__ __forceinline__ UnitView unit_view(const Sched& s, const ScanUnit* un
     return v;
 }
 
-template <class C>
+// UNITS: the unit-table form.  Its query rows are different queries probing
+// one cell, whose passing columns rarely coincide, so its slow path walks
+// each lane's own columns (reading the row norm from memory); the schedule
+// form walks the columns any lane keeps, warp-uniformly, with the norms
+// already in registers.
+template <class C, bool UNITS>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_filter_tc_u8_l2(const __grid_constant__ CUtensorMap tmap_rows, const __grid_constant__ CUtensorMap tmap_q,
                       const int32_t* __restrict__ norms, const int32_t* __restrict__ ids, int32_t n_rows,
@@ -194,7 +200,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             bool a_issued = false;
             bool ok = true;
             for (long long u = blockIdx.x; u < sched.n_units && ok; u += gridDim.x) {
-                const UnitView uv = unit_view<C>(sched, units, u, n_rows, nq);
+                const UnitView uv = unit_view<C, UNITS>(sched, units, u, n_rows, nq);
                 const int t0 = uv.t0, t1 = uv.t1;
                 ok = mbar_wait<false>(bars + 8 * C::BAR_A_EMPTY, (a_iter & 1) ^ 1, abort_flag, status);
                 if (!ok) break;
@@ -241,7 +247,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t phase = 0, acc_phase = 0, a_iter = 0;
             bool ok = true, issued = false;
             for (long long u = blockIdx.x; u < sched.n_units && ok; u += gridDim.x) {
-                const UnitView uv = unit_view<C>(sched, units, u, n_rows, nq);
+                const UnitView uv = unit_view<C, UNITS>(sched, units, u, n_rows, nq);
                 const int t0 = uv.t0, t1 = uv.t1;
                 ok = mbar_wait<false>(bars + 8 * C::BAR_A_FULL, a_iter & 1, abort_flag, status);
                 if (!ok) break;
@@ -309,7 +315,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         bool ok = true;
         const int32_t* nrm = norms + rowoff;
         for (long long u = blockIdx.x; u < sched.n_units && ok; u += gridDim.x) {
-            const UnitView uv = unit_view<C>(sched, units, u, n_rows, nq);
+            const UnitView uv = unit_view<C, UNITS>(sched, units, u, n_rows, nq);
             const int t0 = uv.t0, t1 = uv.t1, row_end = uv.row_end;
             const int qlocal = qt * BM + quarter * 32 + lane;
             const bool qvalid = qlocal < uv.q_count;
@@ -333,17 +339,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 bias = -(1 << 30);
             else
                 bias = qnv - (int32_t)tkey;
-            // n_min of this warp's two chunks, one tile ahead of their use.
+            // Lane l holds the norms of rows l and 32 + l of this warp's two
+            // chunks, loaded (coalesced) one tile ahead of their use; a chunk's
+            // n_min is its lane-0 value.
             int32_t nx0 = 0, nx1 = 0;
             if (t0 < t1) {
-                nx0 = __ldg(nrm + (int64_t)t0 * BN);
-                nx1 = __ldg(nrm + (int64_t)t0 * BN + 32);
+                nx0 = __ldg(nrm + (int64_t)t0 * BN + lane);
+                nx1 = __ldg(nrm + (int64_t)t0 * BN + 32 + lane);
             }
             for (int t = t0; t < t1; t++) {
-                const int32_t need0 = nx0 + bias, need1 = nx1 + bias;
+                const int32_t nr0 = nx0, nr1 = nx1;
+                const int32_t need0 = __shfl_sync(0xffffffffu, nr0, 0) + bias;
+                const int32_t need1 = __shfl_sync(0xffffffffu, nr1, 0) + bias;
                 if (t + 1 < t1) {
-                    nx0 = __ldg(nrm + (int64_t)(t + 1) * BN);
-                    nx1 = __ldg(nrm + (int64_t)(t + 1) * BN + 32);
+                    nx0 = __ldg(nrm + (int64_t)(t + 1) * BN + lane);
+                    nx1 = __ldg(nrm + (int64_t)(t + 1) * BN + 32 + lane);
                 }
                 ok = mbar_wait_inl<false>(bars + 8 * (C::BAR_ACC_FULL + acc), acc_phase, abort_flag, status);
                 if (!ok) break;
@@ -364,21 +374,46 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     acc_phase ^= 1;
                 }
                 const int32_t m0 = max32(v[0]), m1 = max32(v[1]);
-                if (2 * m0 < need0 && 2 * m1 < need1) continue;
+                const bool pass0 = 2 * m0 >= need0, pass1 = 2 * m1 >= need1;
                 const int32_t row0 = t * BN + rowoff;  // rows < 2^31 (ids are int32)
+                if (UNITS) {
+                    if (!pass0 && !pass1) continue;
+#pragma unroll
+                    for (int c = 0; c < 2; c++) {
+                        uint32_t mask = (c ? pass1 : pass0) ? pass_mask32(v[c], c ? need1 : need0) : 0u;
+                        while (mask) {
+                            const int j = __ffs(mask) - 1;
+                            mask &= mask - 1;
+                            const int32_t r = row0 + 32 * c + j;
+                            if (r >= row_end) break;  // pad rows trail the cell
+                            const uint32_t key =
+                                (uint32_t)(qnv + __ldg(norms + r) - 2 * (int32_t)pick32(v[c], j));
+                            if (key < tkey || (key == tkey && __ldg(ids + r) <= tid))
+                                buf.push(key, (uint32_t)r, counts, cand, cap, qi);
+                        }
+                    }
+                    continue;
+                }
+                if (!__any_sync(0xffffffffu, pass0 || pass1)) continue;
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
-                    uint32_t mask = pass_mask32(v[c], c ? need1 : need0);
-                    while (mask) {
-                        const int j = __ffs(mask) - 1;
-                        mask &= mask - 1;
+                    // A warp-uniform walk over the columns any lane keeps; the
+                    // row's norm comes from the lane that loaded it.
+                    const uint32_t mask = (c ? pass1 : pass0) ? pass_mask32(v[c], c ? need1 : need0) : 0u;
+                    uint32_t any = __reduce_or_sync(0xffffffffu, mask);
+                    while (any) {
+                        const int j = __ffs(any) - 1;
+                        any &= any - 1;
                         const int32_t r = row0 + 32 * c + j;
                         if (r >= row_end) break;  // pad rows trail the level (or the cell)
-                        const uint32_t key = (uint32_t)(qnv + __ldg(norms + r) - 2 * (int32_t)pick32(v[c], j));
-                        if (dense)
-                            cand[(size_t)qi * cap + r] = make_uint2(key, (uint32_t)r);
-                        else if (key < tkey || (key == tkey && __ldg(ids + r) <= tid))
-                            buf.push(key, (uint32_t)r, counts, cand, cap, qi);
+                        const int32_t nr = __shfl_sync(0xffffffffu, c ? nr1 : nr0, j);
+                        if ((mask >> j) & 1u) {
+                            const uint32_t key = (uint32_t)(qnv + nr - 2 * (int32_t)pick32(v[c], j));
+                            if (dense)
+                                cand[(size_t)qi * cap + r] = make_uint2(key, (uint32_t)r);
+                            else if (key < tkey || (key == tkey && __ldg(ids + r) <= tid))
+                                buf.push(key, (uint32_t)r, counts, cand, cap, qi);
+                        }
                     }
                 }
             }
@@ -482,9 +517,9 @@ void launch_tc(const Level& lv, const CUtensorMap& tq, const int32_t* qn, int nq
     s.n_units = (long long)s.n_groups * s.n_chunks;
     if (s.n_units < ctas) ctas = (int)s.n_units;
     // A function attribute belongs to the current device: set it on every launch.
-    MDH_CUDA(cudaFuncSetAttribute(k_filter_tc_u8_l2<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    MDH_CUDA(cudaFuncSetAttribute(k_filter_tc_u8_l2<C, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)C::SMEM_BYTES));
-    k_filter_tc_u8_l2<C><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
+    k_filter_tc_u8_l2<C, false><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
                                                                    qn, nq, thr_key, thr_id, counts, cand, cap, dense,
                                                                    s, status, nullptr, nullptr);
     MDH_CUDA(cudaGetLastError());
@@ -521,9 +556,9 @@ void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat
     Sched s{};
     s.n_units = n_units;
     const int ctas = std::min(device_sm_count(dev), n_units);
-    MDH_CUDA(cudaFuncSetAttribute(k_filter_tc_u8_l2<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    MDH_CUDA(cudaFuncSetAttribute(k_filter_tc_u8_l2<C, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)C::SMEM_BYTES));
-    k_filter_tc_u8_l2<C><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
+    k_filter_tc_u8_l2<C, true><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
                                                                    qn, qmat_rows, thr_key, thr_id, counts, cand, cap,
                                                                    0, s, status, units, qmap);
     MDH_CUDA(cudaGetLastError());
