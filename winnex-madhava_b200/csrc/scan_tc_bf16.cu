@@ -295,11 +295,15 @@ __global__ void k_convert_bf16(const float* __restrict__ src, int64_t count, __n
 }
 
 // The reference's SpeedEngine score of a normalized float row against a
-// normalized float query (dot_f32, src/speed_cpu.cpp:60-76): 8 lanes of
-// fused multiply-adds over steps of 8, lanes summed left to right, then the
-// scalar tail -- the same operations as k_filter_f32 (scan_simt.cu).
-__global__ void k_rescore_speed_cos(const uint32_t* __restrict__ counts, uint2* __restrict__ cand, int cap,
-                                    const float* __restrict__ rows, int dim, const float* __restrict__ q, int nq) {
+// normalized float query (dot_f32, src/speed_cpu.cpp:60-76): lane l of 8
+// accumulates fused multiply-adds of elements l, l + 8, l + 16, ...; the 8
+// lanes are summed left to right, then the scalar tail -- the operations and
+// order of k_filter_f32 (scan_simt.cu).  Here the 8 lanes of one candidate are
+// 8 threads (each lane's chain is sequential, as in the reference), so a warp
+// rescores 4 candidates with coalesced 32-byte reads.
+__global__ void __launch_bounds__(256) k_rescore_speed_cos(const uint32_t* __restrict__ counts, uint2* __restrict__ cand,
+                                                           int cap, const float* __restrict__ rows, int dim,
+                                                           const float* __restrict__ q, int nq) {
     extern __shared__ float sq[];
     const int qi = blockIdx.x;
     if (qi >= nq) return;
@@ -308,22 +312,24 @@ __global__ void k_rescore_speed_cos(const uint32_t* __restrict__ counts, uint2* 
     const uint32_t c_all = counts[qi];
     const int c = (int)(c_all < (uint32_t)cap ? c_all : (uint32_t)cap);
     uint2* lst = cand + (size_t)qi * cap;
-    for (int i = threadIdx.x; i < c; i += blockDim.x) {
-        const uint2 e = lst[i];
-        const float* row = rows + (size_t)e.y * dim;
-        float acc[8];
+    const int l = threadIdx.x & 7;
+    const int gbase = (threadIdx.x & 31) & ~7;  // first lane of this candidate's group in the warp
+    const int jt_end = dim & ~7;
+    for (int i0 = 0; i0 < c; i0 += blockDim.x / 8) {
+        const int i = i0 + (threadIdx.x >> 3);
+        const bool valid = i < c;
+        const uint32_t r = valid ? lst[i].y : 0u;
+        const float* row = rows + (size_t)r * dim;
+        float acc = 0.0f;
+        if (valid)
+            for (int jt = 0; jt < jt_end; jt += 8) acc = __fmaf_rn(__ldg(row + jt + l), sq[jt + l], acc);
+        float sum = __shfl_sync(0xffffffffu, acc, gbase);
 #pragma unroll
-        for (int l = 0; l < 8; l++) acc[l] = 0.0f;
-        int jt = 0;
-        for (; jt + 8 <= dim; jt += 8) {
-#pragma unroll
-            for (int l = 0; l < 8; l++) acc[l] = __fmaf_rn(__ldg(row + jt + l), sq[jt + l], acc[l]);
+        for (int m = 1; m < 8; m++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, acc, gbase + m));
+        if (valid && l == 0) {
+            for (int t = jt_end; t < dim; t++) sum = __fmaf_rn(__ldg(row + t), sq[t], sum);
+            lst[i].x = ordered_key_desc(sum);
         }
-        float s = acc[0];
-#pragma unroll
-        for (int l = 1; l < 8; l++) s = __fadd_rn(s, acc[l]);
-        for (int t = jt; t < dim; t++) s = __fmaf_rn(__ldg(row + t), sq[t], s);
-        lst[i].x = ordered_key_desc(s);
     }
 }
 
