@@ -432,6 +432,9 @@ def main():
 
         import torch.distributed as dist
 
+        # Rank 0 prints exactly one JSON line: keep NCCL's version banner off stdout.
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
+
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
     device = torch.device("cuda", local)
