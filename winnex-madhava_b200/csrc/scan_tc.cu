@@ -5,36 +5,36 @@
 // (key, id) <= (thr_key[q], thr_id[q]) are appended to q's candidate list as
 // {key, r}; on a dense level (infinite thresholds) row r goes to slot r.
 //
-// Tile: QT query tiles of 128 queries (TMEM lanes, the MMA's M) x BN corpus
-// rows (the MMA's N) x 128 bytes (K: four kind::i8 MMAs of K = 32).  u8 x u8
-// products accumulate exactly in s32 in tensor memory.  Operands are staged
-// by TMA with the 128-byte swizzle (one 128-byte row per vector = one swizzle
-// row).  An accumulator stage holds QT x BN columns; all 512 TMEM columns
-// form 512 / (QT x BN) stages.  Two shapes are built:
-//   QT = 2, BN = 128 (256 queries per CTA): each corpus tile read from L2
-//     feeds 256 queries, so the L2 -> SM stream is 32 B per SM-cycle at the
-//     full MMA rate -- half of what 128 queries per CTA would need, which
-//     is at the L2's limit with 148 SMs reading;
-//   QT = 1, BN = 256 (128 queries per CTA): batches below 256 queries.
+// Tile: 128 queries (TMEM lanes, the MMA's M) x 256 corpus rows (the MMA's
+// N) x 128 bytes (K: four kind::i8 MMAs of K = 32).  u8 x u8 products
+// accumulate exactly in s32 in tensor memory.  Operands are staged by TMA
+// with the 128-byte swizzle (one 128-byte row per vector = one swizzle row).
+// An accumulator stage holds 256 columns; the 512 TMEM columns form two
+// stages, so the MMA of tile t+1 overlaps the epilogue of tile t.  (The
+// template keeps QT query tiles per stage as a parameter; only QT = 1 is
+// built: with QT = 2, BN = 128 every MMA re-reads its A tile and the shared
+// memory port, not the tensor pipe, set the pace.)
 //
 // Warp roles (576 threads, one CTA per SM, persistent):
 //   warps 0-15 epilogue: warp w reads TMEM lanes 32*(w%4).. (thread = one
 //              query) and the 64 columns [64*(w/4), +64) of each
-//              accumulator stage (query tile 64*(w/4) / BN); both 32-column
-//              chunks are copied to registers and the stage released before
-//              the Cauchy-Schwarz chunk filter runs; passing rows are buffered
-//              per thread in shared memory, one atomic per flush;
+//              accumulator stage; both 32-column chunks are copied to
+//              registers and the stage released before the Cauchy-Schwarz
+//              filter runs; passing rows are buffered per thread in shared
+//              memory, one atomic per flush;
 //   warp 16    TMA producer (the QT query tiles once per work unit, corpus
 //              tiles through a STAGES-deep ring);
 //   warp 17    TMEM allocator + single-thread MMA issuer.
 //
-// Epilogue filter: rows are sorted by |v|^2, so the first row of each
-// 32-row chunk has the chunk's smallest norm n_min.  With m = max q.v over
-// the chunk, every key in the chunk is >= |q|^2 + n_min - 2m; when that
-// exceeds the query's threshold the whole chunk is skipped after one max
-// reduction (tc_ptx.cuh: max32).  The rows' norms are read one tile ahead,
-// one per lane; the rare chunks that pass are expanded by a warp-uniform walk
-// over the passing columns, so no global load sits on that path.
+// Epilogue filter: rows are sorted by |v|^2, so a row block's first row has
+// its smallest norm n_min.  With m = max q.v over the block, every key in it
+// is >= |q|^2 + n_min - 2m; when that exceeds the query's threshold the whole
+// block is skipped after one max reduction (tc_ptx.cuh: max32).  The
+// schedule form bounds each warp's 64 columns with the tile's first norm
+// (neighbouring rows of a sorted level have nearly equal norms); the unit
+// table form (IVF cells, whose tiles span a wider norm range) bounds each
+// 32-row chunk with its own first norm.  Blocks that pass are expanded per
+// lane: each passing lane walks its own passing columns.
 //
 // Work units: (query group, corpus chunk), ordered chunk-major so the CTAs
 // running at the same time share corpus chunks through L2; each CTA takes
@@ -45,6 +45,7 @@
 // its own outstanding copies and MMAs with bounded waits, frees its tensor
 // memory and returns.
 #include <algorithm>
+#include <type_traits>
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -142,6 +143,31 @@ __device__ __forceinline__ UnitView unit_view(const Sched& s, const ScanUnit* un
         v.row_end = n_rows;
     }
     return v;
+}
+
+// The rows [row0, row0 + 32) of one 32-column chunk against this thread's
+// query: v[j] = q.v of row row0 + j.  Nothing passes unless 2 max(v) >= need
+// (need = n_min + |q|^2 - threshold for an n_min no larger than any of the
+// rows' norms); a passing lane walks its own passing columns, reads their
+// norms and appends the rows whose exact (key, id) reaches the threshold.
+__device__ __forceinline__ void chunk_filter(const uint32_t (&v)[32], int32_t need, int32_t row0, int row_end,
+                                             uint32_t tkey, int32_t tid, int32_t qnv, int qi,
+                                             const int32_t* __restrict__ norms, const int32_t* __restrict__ ids,
+                                             int dense, CandBuf<EPI_THREADS, BUFN>& buf, uint32_t* __restrict__ counts,
+                                             uint2* __restrict__ cand, int cap) {
+    if (2 * max32(v) < need) return;
+    uint32_t mask = pass_mask32(v, need);
+    while (mask) {
+        const int j = __ffs(mask) - 1;
+        mask &= mask - 1;
+        const int32_t r = row0 + j;
+        if (r >= row_end) break;  // pad rows trail the level
+        const uint32_t key = (uint32_t)(qnv + __ldg(norms + r) - 2 * (int32_t)pick32(v, j));
+        if (dense)
+            cand[(size_t)qi * cap + r] = make_uint2(key, (uint32_t)r);
+        else if (key < tkey || (key == tkey && __ldg(ids + r) <= tid))
+            buf.push(key, (uint32_t)r, counts, cand, cap, qi);
+    }
 }
 
 // UNITS: the unit-table form.  Its query rows are different queries probing
@@ -301,8 +327,103 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 mbar_drain_wait<false>(bars + 8 * C::BAR_DRAIN, 0);
             }
         }
+    } else if constexpr (!UNITS && QT == 1 && ACC_STAGES == 2) {
+        // ------------------------------------------------------------ epilogue (warps 0-15), schedule form
+        // Warp w reads TMEM lanes 32*(w%4) (thread = one query) and the 64
+        // columns [64*(w/4), +64) of each accumulator stage.  One bound per
+        // tile: n_min is the norm of the tile's first row (rows are sorted by
+        // norm), and one max reduction covers the warp's 64 columns.  The tile
+        // loop is unrolled over the two accumulator stages so each stage's
+        // barrier and TMEM address are constants.  This keeps the epilogue's
+        // ALU work -- which competes with the MMA issuer for the issue slots
+        // of its sub-partition -- near the reduction itself.
+        const int quarter = warp & 3, part = warp >> 2;
+        const int rowoff = part * COLS_PER_WARP;
+        const uint32_t tcol0 = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)rowoff;
+        CandBuf<EPI_THREADS, BUFN> buf;
+        buf.base = reinterpret_cast<uint2*>(smem + C::OFF_BUF) + threadIdx.x;
+        buf.n = 0;
+        int acc = 0;  // accumulator stage of the CTA's next tile
+        uint32_t ph0 = 0, ph1 = 0;
+        bool ok = true;
+        for (long long u = blockIdx.x; u < sched.n_units && ok; u += gridDim.x) {
+            const UnitView uv = unit_view<C, UNITS>(sched, units, u, n_rows, nq);
+            const int t0 = uv.t0, t1 = uv.t1, row_end = uv.row_end;
+            const int qlocal = quarter * 32 + lane;
+            const bool qvalid = qlocal < uv.q_count;
+            const int qi = qvalid ? uv.q_row + qlocal : 0;
+            uint32_t tkey = 0;
+            int32_t tid = 0, qnv = 0;
+            if (qvalid) {
+                tkey = thr_key[qi];
+                tid = thr_id[qi];
+                qnv = qn[qi];
+            }
+            // A row passes when qn + n - 2v <= tkey; with n >= n_min,
+            // 2v >= n_min + bias (bias = qn - tkey) is necessary.  Keys of real
+            // rows are below 2^30: an infinite threshold maps to a bias that
+            // always passes, an invalid query to one that never does (and
+            // keeps n_min + bias below 2^31 for pad rows of norm 2^30).
+            int32_t bias;
+            if (!qvalid)
+                bias = 1 << 29;
+            else if (tkey >= (1u << 30))
+                bias = -(1 << 30);
+            else
+                bias = qnv - (int32_t)tkey;
+            int32_t nm = t0 < t1 ? __ldg(norms + (int64_t)t0 * BN) : 0;  // n_min of the next tile
+            auto tile = [&](int t, auto stage_c, uint32_t ph) -> bool {
+                constexpr int A = decltype(stage_c)::value;
+                const int32_t need = nm + bias;
+                nm = __ldg(norms + (int64_t)min(t + 1, t1 - 1) * BN);
+                if (!mbar_wait_inl<false>(bars + 8 * (C::BAR_ACC_FULL + A), ph, abort_flag, status)) return false;
+                tc_fence_after();
+                uint32_t v[2][32];
+                __syncwarp();
+                tmem_ld32_issue(tcol0 + A * C::ACC_COLS, v[0]);
+                tmem_ld32_issue(tcol0 + A * C::ACC_COLS + 32, v[1]);
+                tmem_ld_wait(v[0]);  // waits for both loads
+                tmem_ld_wait(v[1]);
+                // The chunks are in registers: hand the accumulator back to the MMA.
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bars + 8 * (C::BAR_ACC_EMPTY + A));
+                const int32_t m = (int32_t)__float_as_uint(
+                    fmaxf(__uint_as_float((uint32_t)max32(v[0])), __uint_as_float((uint32_t)max32(v[1]))));
+                if (2 * m >= need) {
+                    const int32_t row0 = t * BN + rowoff;  // rows < 2^31 (ids are int32)
+                    chunk_filter(v[0], need, row0, row_end, tkey, tid, qnv, qi, norms, ids, dense, buf, counts, cand,
+                                 cap);
+                    chunk_filter(v[1], need, row0 + 32, row_end, tkey, tid, qnv, qi, norms, ids, dense, buf, counts,
+                                 cand, cap);
+                }
+                return true;
+            };
+            using S0 = std::integral_constant<int, 0>;
+            using S1 = std::integral_constant<int, 1>;
+            int t = t0;
+            if (acc == 1 && t < t1) {
+                ok = tile(t, S1{}, ph1);
+                ph1 ^= 1;
+                acc = 0;
+                t++;
+            }
+            for (; ok && t + 1 < t1; t += 2) {
+                ok = tile(t, S0{}, ph0);
+                ph0 ^= 1;
+                if (!ok) break;
+                ok = tile(t + 1, S1{}, ph1);
+                ph1 ^= 1;
+            }
+            if (ok && t < t1) {
+                ok = tile(t, S0{}, ph0);
+                ph0 ^= 1;
+                acc = 1;
+            }
+            if (qvalid) buf.flush(counts, cand, cap, qi);
+        }
     } else {
-        // ------------------------------------------------------------ epilogue (warps 0-15)
+        // ------------------------------------------------------------ epilogue (warps 0-15), unit tables
         const int quarter = warp & 3, part = warp >> 2;
         const int qt = part * COLS_PER_WARP / BN;              // query tile of this warp's columns
         const int rowoff = part * COLS_PER_WARP - qt * BN;     // their first row within a corpus tile
@@ -375,45 +496,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 const int32_t m0 = max32(v[0]), m1 = max32(v[1]);
                 const bool pass0 = 2 * m0 >= need0, pass1 = 2 * m1 >= need1;
+                if (!pass0 && !pass1) continue;
+                // The queries of a unit probe one cell but rarely keep the same
+                // columns: each passing lane walks its own columns.
                 const int32_t row0 = t * BN + rowoff;  // rows < 2^31 (ids are int32)
-                if (UNITS) {
-                    if (!pass0 && !pass1) continue;
-#pragma unroll
-                    for (int c = 0; c < 2; c++) {
-                        uint32_t mask = (c ? pass1 : pass0) ? pass_mask32(v[c], c ? need1 : need0) : 0u;
-                        while (mask) {
-                            const int j = __ffs(mask) - 1;
-                            mask &= mask - 1;
-                            const int32_t r = row0 + 32 * c + j;
-                            if (r >= row_end) break;  // pad rows trail the cell
-                            const uint32_t key =
-                                (uint32_t)(qnv + __ldg(norms + r) - 2 * (int32_t)pick32(v[c], j));
-                            if (key < tkey || (key == tkey && __ldg(ids + r) <= tid))
-                                buf.push(key, (uint32_t)r, counts, cand, cap, qi);
-                        }
-                    }
-                    continue;
-                }
-                if (!__any_sync(0xffffffffu, pass0 || pass1)) continue;
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
-                    // A warp-uniform walk over the columns any lane keeps; the
-                    // row's norm comes from the lane that loaded it.
-                    const uint32_t mask = (c ? pass1 : pass0) ? pass_mask32(v[c], c ? need1 : need0) : 0u;
-                    uint32_t any = __reduce_or_sync(0xffffffffu, mask);
-                    while (any) {
-                        const int j = __ffs(any) - 1;
-                        any &= any - 1;
+                    uint32_t mask = (c ? pass1 : pass0) ? pass_mask32(v[c], c ? need1 : need0) : 0u;
+                    while (mask) {
+                        const int j = __ffs(mask) - 1;
+                        mask &= mask - 1;
                         const int32_t r = row0 + 32 * c + j;
-                        if (r >= row_end) break;  // pad rows trail the level (or the cell)
-                        const int32_t nr = __shfl_sync(0xffffffffu, c ? nr1 : nr0, j);
-                        if ((mask >> j) & 1u) {
-                            const uint32_t key = (uint32_t)(qnv + nr - 2 * (int32_t)pick32(v[c], j));
-                            if (dense)
-                                cand[(size_t)qi * cap + r] = make_uint2(key, (uint32_t)r);
-                            else if (key < tkey || (key == tkey && __ldg(ids + r) <= tid))
-                                buf.push(key, (uint32_t)r, counts, cand, cap, qi);
-                        }
+                        if (r >= row_end) break;  // pad rows trail the cell
+                        const uint32_t key = (uint32_t)(qnv + __ldg(norms + r) - 2 * (int32_t)pick32(v[c], j));
+                        if (key < tkey || (key == tkey && __ldg(ids + r) <= tid))
+                            buf.push(key, (uint32_t)r, counts, cand, cap, qi);
                     }
                 }
             }
@@ -429,7 +526,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
 }
 
-using CfgWide = TcCfg<128, 2>;    // 256 queries per CTA
 using CfgNarrow = TcCfg<256, 1>;  // 128 queries per CTA
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
@@ -493,7 +589,7 @@ int choose_scan_chunks(int groups, int n_tiles, int workers) {
 
 bool tc_supported(const mdh_index* ix, const Level& lv) {
     return ix && !ix->is_f32 && ix->dpad == BK && ix->dim <= BK && lv.rows && lv.norms &&
-           lv.n_pad % CfgWide::BN == 0 && lv.n_pad % CfgNarrow::BN == 0 && lv.n_pad < (int64_t(1) << 31);
+           lv.n_pad % CfgNarrow::BN == 0 && lv.n_pad < (int64_t(1) << 31);
 }
 
 void make_tmap_rows(Level& lv, int dpad) {
@@ -533,12 +629,6 @@ void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const i
     MDH_REQUIRE(!dense || cap >= lv.n, MDH_ERR_INTERNAL, "dense scan needs cap >= rows");
     CUtensorMap tq;
     encode_u8_rows_tmap(&tq, q, nq, dpad, BM);
-#ifdef MDH_TC_WIDE
-    if (nq >= CfgWide::QGROUP) {
-        launch_tc<CfgWide>(lv, tq, qn, nq, thr_key, thr_id, counts, cand, cap, dense, status, st);
-        return;
-    }
-#endif
     launch_tc<CfgNarrow>(lv, tq, qn, nq, thr_key, thr_id, counts, cand, cap, dense, status, st);
 }
 
