@@ -35,7 +35,7 @@ DIM = 128
 COMPONENTS = 4096
 SEED = 20261201
 CHUNK = 3_125_000
-TRAFFIC_BYTES_PER_ROW = (1.325461e9 + 12.59776e6) / 10_000_000
+TRAFFIC_BYTES_PER_ROW = (1.322692e9 + 12.821248e6) / 10_000_000
 METRIC = "queries/sec, 100M×128 u8 exact top-10, 10K-query batch at 1/2/4/8 B200; % roofline"
 
 
