@@ -182,6 +182,105 @@ __global__ void k_select(const uint32_t* __restrict__ counts, const uint2* __res
     }
 }
 
+// The same contract as k_select for k <= kWarpSelectK, one warp per query:
+// each lane keeps the kWarpSelectK smallest composite keys of its stride of
+// the list in registers (ascending), reading a row's id only when its key
+// could enter; the warp then pops the k smallest in order by warp minima.
+// The block kernel sizes its shared memory by the list capacity, so on long
+// lists it runs one query per SM at a time; this one streams the list.
+constexpr int kWarpSelectK = 16;
+constexpr int kWarpSelectWarps = 8;  // queries per 256-thread block
+
+__global__ void __launch_bounds__(32 * kWarpSelectWarps)
+    k_select_warp(const uint32_t* __restrict__ counts, const uint2* __restrict__ cand, int cap,
+                  const int32_t* __restrict__ ids, int nq, int k, int final_, uint32_t* __restrict__ thr_key,
+                  int32_t* __restrict__ thr_id, uint32_t* __restrict__ out_key, int32_t* __restrict__ out_id,
+                  int32_t* __restrict__ flags, int32_t* __restrict__ n_flagged, const int32_t* __restrict__ qmap,
+                  unsigned long long* __restrict__ n_cand) {
+    constexpr int KM = kWarpSelectK;
+    const int q = blockIdx.x * kWarpSelectWarps + (int)(threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (q >= nq) return;  // whole warps leave together
+    const int qo = qmap ? qmap[q] : q;
+    const uint32_t c_all = counts[q];
+    const int c = (int)(c_all < (uint32_t)cap ? c_all : (uint32_t)cap);
+    const uint2* src = cand + (size_t)q * cap;
+    unsigned long long top[KM];
+#pragma unroll
+    for (int j = 0; j < KM; j++) top[j] = ~0ull;
+    unsigned long long worst = ~0ull;  // this lane's k-th smallest so far
+    for (int i = lane; i < c; i += 32) {
+        const uint2 e = src[i];
+        const unsigned long long hi = (unsigned long long)e.x << 32;
+        if (hi > worst) continue;  // its composite key is larger still
+        const unsigned long long v = hi | (uint32_t)__ldg(ids + e.y);
+        if (v >= worst) continue;
+        // Insert into the ascending list (the last slot drops out).
+#pragma unroll
+        for (int j = KM - 1; j > 0; j--) top[j] = top[j - 1] > v ? top[j - 1] : (top[j] > v ? v : top[j]);
+        top[0] = top[0] > v ? v : top[0];
+        unsigned long long w = top[0];
+#pragma unroll
+        for (int j = 1; j < KM; j++) w = (j == k - 1) ? top[j] : w;
+        worst = w;
+    }
+    // The k smallest of the warp, ascending: lane r ends with the r-th.
+    unsigned long long res = ~0ull;
+    for (int r = 0; r < k; r++) {
+        unsigned long long m = top[0];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, m, o);
+            m = other < m ? other : m;
+        }
+        if (lane == r) res = m;
+        if (m != ~0ull && top[0] == m) {  // composite keys are unique: one lane pops
+#pragma unroll
+            for (int j = 0; j < KM - 1; j++) top[j] = top[j + 1];
+            top[KM - 1] = ~0ull;
+        }
+    }
+    const unsigned long long kth = __shfl_sync(0xffffffffu, res, k - 1);
+    if (!final_) {
+        if (lane == 0) {
+            if (c >= k) {
+                thr_key[qo] = (uint32_t)(kth >> 32);
+                thr_id[qo] = (int32_t)(kth & 0xffffffffu);
+            } else {
+                // Fewer than k rows in this level: every row of the next
+                // level stays a candidate.
+                thr_key[qo] = kKeyInf;
+                thr_id[qo] = kIdInf;
+            }
+        }
+        return;
+    }
+    if (c_all > (uint32_t)cap) {
+        // Overflow: the stored lists are a subset; their k-th key is a valid
+        // (tighter) threshold for a rerun.  c == cap >= k here.
+        if (lane == 0) {
+            flags[qo] = 1;
+            thr_key[qo] = (uint32_t)(kth >> 32);
+            thr_id[qo] = (int32_t)(kth & 0xffffffffu);
+            atomicAdd(n_flagged, 1);
+        }
+        return;
+    }
+    if (lane < k) {
+        if (lane < c) {
+            out_key[(size_t)qo * k + lane] = (uint32_t)(res >> 32);
+            out_id[(size_t)qo * k + lane] = (int32_t)(res & 0xffffffffu);
+        } else {
+            out_key[(size_t)qo * k + lane] = kKeyInf;
+            out_id[(size_t)qo * k + lane] = -1;
+        }
+    }
+    if (lane == 0) {
+        if (flags) flags[qo] = 0;
+        if (n_cand) atomicAdd(n_cand, (unsigned long long)c);
+    }
+}
+
 // Verification: query i of a compact list gets the threshold (key, id) of the
 // kk-th entry of its result (an empty entry, id -1, means no threshold).
 __global__ void k_verify_thresholds(const int32_t* __restrict__ list, int m, const uint32_t* __restrict__ out_key,
@@ -267,6 +366,12 @@ void launch_select(const uint32_t* counts, const uint2* cand, int cap, const int
                    int32_t* thr_id, uint32_t* out_key, int32_t* out_id, int32_t* flags, int32_t* n_flagged,
                    const int32_t* qmap, unsigned long long* n_cand, cudaStream_t st) {
     if (nq <= 0) return;
+    if (k >= 1 && k <= kWarpSelectK) {
+        k_select_warp<<<(nq + kWarpSelectWarps - 1) / kWarpSelectWarps, 32 * kWarpSelectWarps, 0, st>>>(
+            counts, cand, cap, ids, nq, k, final_, thr_key, thr_id, out_key, out_id, flags, n_flagged, qmap, n_cand);
+        MDH_CUDA(cudaGetLastError());
+        return;
+    }
     int pmax = 1;
     while (pmax < (cap > k ? cap : k)) pmax <<= 1;
     size_t smem = select_smem(pmax);
