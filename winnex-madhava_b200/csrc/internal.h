@@ -137,6 +137,8 @@ void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const i
 // unit u scans query rows [q_row, q_row + q_count) of `qmat` (row i is query
 // qmap[i]; thresholds, norms and candidate lists are indexed by that query)
 // against corpus tiles [t0, t1) of 256 rows, rows at or past row_end masked.
+// n_units bounds the table (it sizes the grid); when n_units_dev is given the
+// kernel reads the table's length from it (tables built on the device).
 struct ScanUnit {
     int32_t q_row;
     int32_t q_count;   // <= 128
@@ -145,9 +147,9 @@ struct ScanUnit {
     int32_t pad;
 };
 void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat, int qmat_rows, const int32_t* qmap,
-                                  const int32_t* qn, const ScanUnit* units, int n_units, const uint32_t* thr_key,
-                                  const int32_t* thr_id, uint32_t* counts, uint2* cand, int cap, int32_t* status,
-                                  cudaStream_t st);
+                                  const int32_t* qn, const ScanUnit* units, int n_units, const int32_t* n_units_dev,
+                                  const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts, uint2* cand,
+                                  int cap, int32_t* status, cudaStream_t st);
 // ---- tensor-core scan on SM pairs (scan_tc2.cu) ----
 bool tc2_supported(const mdh_index* ix, const Level& lv);
 void make_tmap_rows_pair(Level& lv, int dpad);

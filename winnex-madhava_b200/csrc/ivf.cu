@@ -70,6 +70,16 @@ struct mdh_ivf {
     float* centroids = nullptr;          // [nlist][dim]
     mdh::Workspace ws;
     mdh::IvfPassBufs pass[2];            // pass 1 (cell samples) and pass 2 (whole cells)
+    // Device-side planning: per cell {first tile, tiles, row end} in the full
+    // layout, then in the sample layout; the cells in planning order (most
+    // tiles first); scratch for the plan (query counts, fill cursors, query
+    // offsets, unit offsets of both passes, table lengths) and pair counts.
+    int32_t* plan_info = nullptr;        // [nlist][6]
+    int32_t* plan_order = nullptr;       // [nlist]
+    int32_t* plan_scratch = nullptr;     // [6 * nlist + 2]
+    unsigned long long* plan_pairs = nullptr;  // [2]
+    int64_t unit_max_runs[2] = {0, 0};   // per pass: max over cells of ceil(tiles / 64)
+    int64_t unit_sum_runs[2] = {0, 0};   // per pass: sum over cells of ceil(tiles / 64)
     std::mutex mu;
 };
 
@@ -262,55 +272,228 @@ void grow_dev(T** p, size_t* have, size_t bytes) {
     *p = static_cast<T*>(v);
 }
 
-// Query lists per cell for one pass and the unit table over them.
-// probe_of(qi) -> list of cells; gmap = concatenated per-cell query lists.
-struct PassPlan {
-    std::vector<int32_t> gmap;
-    std::vector<ScanUnit> units;
-    int64_t pairs = 0;
-};
+// ---------------------------------------------------------------- planning
+// Both passes probe the same cells, so they share one grouped query matrix
+// (queries listed cell by cell) and differ in their unit tables.  The plan
+// is built on the device from the routing output, so routing, planning and
+// both passes run back to back on one stream.  The order of queries inside a
+// cell's list depends on atomics; results do not (candidates are selected by
+// (key, id)).
 
-PassPlan plan_pass(const mdh_ivf* ix, const std::vector<int64_t>& start, const std::vector<int64_t>& count,
-                   const std::vector<int32_t>& probe, int m, int nprobe, int use) {
-    const int nl = ix->nlist;
-    std::vector<int64_t> cnt((size_t)nl + 1, 0);
-    for (int i = 0; i < m; i++)
-        for (int j = 0; j < use; j++) {
-            const int32_t c = probe[(size_t)i * nprobe + j];
-            MDH_REQUIRE(c >= 0 && c < nl, MDH_ERR_INTERNAL, "routing produced an invalid cell");
-            cnt[(size_t)c + 1]++;
+constexpr int kPlanThreads = 1024;
+constexpr int kPlanItems = kIvfMaxNlist / kPlanThreads;  // cells per thread in k_plan_scan
+static_assert(kPlanItems * kPlanThreads == kIvfMaxNlist, "plan scan covers every cell");
+
+__global__ void k_plan_count(const int32_t* __restrict__ probe, int total, int32_t* __restrict__ cnt) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < total) atomicAdd(cnt + probe[i], 1);
+}
+
+// Block-wide exclusive scan of three counters (one block of kPlanThreads).
+__device__ __forceinline__ void block_scan3(int (&v)[3], int (&total)[3]) {
+    __shared__ int wsum[3][kPlanThreads / 32];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    int incl[3];
+#pragma unroll
+    for (int j = 0; j < 3; j++) {
+        incl[j] = v[j];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, incl[j], o);
+            if (lane >= o) incl[j] += t;
         }
-    for (int c = 0; c < nl; c++) cnt[(size_t)c + 1] += cnt[(size_t)c];
-    PassPlan pp;
-    pp.gmap.resize((size_t)cnt[(size_t)nl]);
-    std::vector<int64_t> fill(cnt.begin(), cnt.end() - 1);
-    for (int i = 0; i < m; i++)
-        for (int j = 0; j < use; j++) pp.gmap[(size_t)fill[(size_t)probe[(size_t)i * nprobe + j]]++] = i;
-    for (int c = 0; c < nl; c++) {
-        const int64_t qn = cnt[(size_t)c + 1] - cnt[(size_t)c];
-        const int64_t rows = count[(size_t)c];
-        if (qn == 0 || rows == 0) continue;
-        const int64_t t_first = start[(size_t)c] / kIvfTileRows;
-        const int64_t t_end = t_first + (rows + kIvfTileRows - 1) / kIvfTileRows;
-        for (int64_t q0 = 0; q0 < qn; q0 += 128) {
-            for (int64_t t0 = t_first; t0 < t_end; t0 += kIvfMaxTilesPerUnit) {
-                ScanUnit u;
-                u.q_row = (int32_t)(cnt[(size_t)c] + q0);
-                u.q_count = (int32_t)std::min<int64_t>(128, qn - q0);
-                u.t0 = (int32_t)t0;
-                u.t1 = (int32_t)std::min<int64_t>(t_end, t0 + kIvfMaxTilesPerUnit);
-                u.row_end = (int32_t)(start[(size_t)c] + rows);
-                u.pad = 0;
-                pp.units.push_back(u);
+        if (lane == 31) wsum[j][wid] = incl[j];
+    }
+    __syncthreads();
+    if (wid == 0) {
+#pragma unroll
+        for (int j = 0; j < 3; j++) {
+            int x = wsum[j][lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += t;
+            }
+            wsum[j][lane] = x;  // inclusive over warps
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 3; j++) {
+        total[j] = wsum[j][kPlanThreads / 32 - 1];
+        v[j] = incl[j] - v[j] + (wid > 0 ? wsum[j][wid - 1] : 0);
+    }
+}
+
+// One block.  For every cell, taken in planning order: the offset of its
+// query list in the grouped matrix (qstart) and of its first unit in each
+// pass's table (ustart[pass][cell]); the tables' lengths (nunits[2]) and the
+// (query, row) pairs each pass scans (pairs[2], zeroed by the caller).
+__global__ void __launch_bounds__(kPlanThreads)
+    k_plan_scan(const int32_t* __restrict__ cnt, const int32_t* __restrict__ order, const int32_t* __restrict__ info,
+                int nlist, int32_t* __restrict__ qstart, int32_t* __restrict__ ustart, int32_t* __restrict__ nunits,
+                unsigned long long* __restrict__ pairs) {
+    int item[kPlanItems][3];
+    int sum[3] = {0, 0, 0};
+    unsigned long long pr[2] = {0, 0};
+#pragma unroll
+    for (int j = 0; j < kPlanItems; j++) {
+        const int pos = threadIdx.x * kPlanItems + j;
+        int qn = 0, u[2] = {0, 0};
+        if (pos < nlist) {
+            const int32_t* f = info + 6 * order[pos];
+            qn = cnt[order[pos]];
+            if (qn > 0) {
+#pragma unroll
+                for (int p = 0; p < 2; p++) {
+                    const int32_t* g = f + (p == 0 ? 3 : 0);  // pass 0: sample layout, pass 1: full layout
+                    if (g[1] > 0) {
+                        u[p] = (qn + 127) / 128 * ((g[1] + kIvfMaxTilesPerUnit - 1) / kIvfMaxTilesPerUnit);
+                        pr[p] += (unsigned long long)qn * (unsigned long long)(g[2] - g[0] * kIvfTileRows);
+                    }
+                }
             }
         }
-        pp.pairs += qn * rows;
+        item[j][0] = qn;
+        item[j][1] = u[0];
+        item[j][2] = u[1];
+        sum[0] += qn;
+        sum[1] += u[0];
+        sum[2] += u[1];
     }
-    // Longest units first, so the tail of the persistent grid is short.
-    std::stable_sort(pp.units.begin(), pp.units.end(), [](const ScanUnit& a, const ScanUnit& b) {
-        return (int64_t)(a.t1 - a.t0) * a.q_count > (int64_t)(b.t1 - b.t0) * b.q_count;
+    int total[3];
+    block_scan3(sum, total);
+#pragma unroll
+    for (int j = 0; j < kPlanItems; j++) {
+        const int pos = threadIdx.x * kPlanItems + j;
+        if (pos < nlist) {
+            const int c = order[pos];
+            qstart[c] = sum[0];
+            ustart[c] = sum[1];
+            ustart[nlist + c] = sum[2];
+        }
+        sum[0] += item[j][0];
+        sum[1] += item[j][1];
+        sum[2] += item[j][2];
+    }
+    if (threadIdx.x == 0) {
+        nunits[0] = total[1];
+        nunits[1] = total[2];
+    }
+#pragma unroll
+    for (int p = 0; p < 2; p++) {
+        unsigned long long x = pr[p];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+        if ((threadIdx.x & 31) == 0 && x) atomicAdd(pairs + p, x);
+    }
+}
+
+// probe[i] = the j-th cell of query i / nprobe: list the query in its cell.
+__global__ void k_plan_fill(const int32_t* __restrict__ probe, int total, int nprobe,
+                            const int32_t* __restrict__ qstart, int32_t* __restrict__ fill,
+                            int32_t* __restrict__ gmap) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const int c = probe[i];
+    gmap[qstart[c] + atomicAdd(fill + c, 1)] = i / nprobe;
+}
+
+// One thread per (cell, pass): the cell's units, runs of at most 64 tiles
+// against at most 128 of its queries.
+__global__ void k_plan_units(const int32_t* __restrict__ cnt, const int32_t* __restrict__ info,
+                             const int32_t* __restrict__ qstart, const int32_t* __restrict__ ustart, int nlist,
+                             ScanUnit* __restrict__ units0, ScanUnit* __restrict__ units1) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    const int p = blockIdx.y;
+    if (c >= nlist) return;
+    const int qn = cnt[c];
+    const int32_t* g = info + 6 * c + (p == 0 ? 3 : 0);
+    const int tf = g[0], tiles = g[1], rend = g[2];
+    if (qn == 0 || tiles == 0) return;
+    ScanUnit* out = (p == 0 ? units0 : units1) + ustart[p * nlist + c];
+    int k = 0;
+    for (int q0 = 0; q0 < qn; q0 += 128)
+        for (int t0 = 0; t0 < tiles; t0 += kIvfMaxTilesPerUnit) {
+            ScanUnit u;
+            u.q_row = qstart[c] + q0;
+            u.q_count = min(128, qn - q0);
+            u.t0 = tf + t0;
+            u.t1 = tf + min(tiles, t0 + kIvfMaxTilesPerUnit);
+            u.row_end = rend;
+            u.pad = 0;
+            out[k++] = u;
+        }
+}
+
+// Per-cell planning facts, uploaded once per index.
+void build_ivf_plan_info(mdh_ivf* ix, cudaStream_t st) {
+    const int nl = ix->nlist;
+    std::vector<int32_t> info((size_t)nl * 6);
+    std::vector<int32_t> order((size_t)nl);
+    for (int c = 0; c < nl; c++) {
+        const int64_t fs = ix->cell_start[(size_t)c], fc = ix->cell_count[(size_t)c];
+        const int64_t ss = ix->sample_start[(size_t)c], sc = ix->sample_count[(size_t)c];
+        int32_t* f = info.data() + 6 * (size_t)c;
+        f[0] = (int32_t)(fs / kIvfTileRows);
+        f[1] = (int32_t)((fc + kIvfTileRows - 1) / kIvfTileRows);
+        f[2] = (int32_t)(fs + fc);
+        f[3] = (int32_t)(ss / kIvfTileRows);
+        f[4] = (int32_t)((sc + kIvfTileRows - 1) / kIvfTileRows);
+        f[5] = (int32_t)(ss + sc);
+        order[(size_t)c] = c;
+        for (int p = 0; p < 2; p++) {
+            const int64_t runs = ((p == 0 ? f[4] : f[1]) + kIvfMaxTilesPerUnit - 1) / kIvfMaxTilesPerUnit;
+            ix->unit_max_runs[p] = std::max(ix->unit_max_runs[p], runs);
+            ix->unit_sum_runs[p] += runs;
+        }
+    }
+    // Most tiles first, so the persistent grid's tail is short.
+    std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) {
+        return info[6 * (size_t)a + 1] > info[6 * (size_t)b + 1];
     });
-    return pp;
+    ix->plan_info = dalloc<int32_t>(info.size());
+    ix->plan_order = dalloc<int32_t>(order.size());
+    ix->plan_scratch = dalloc<int32_t>((size_t)6 * nl + 2);
+    ix->plan_pairs = dalloc<unsigned long long>(2);
+    MDH_CUDA(cudaMemcpyAsync(ix->plan_info, info.data(), info.size() * 4, cudaMemcpyHostToDevice, st));
+    MDH_CUDA(cudaMemcpyAsync(ix->plan_order, order.data(), order.size() * 4, cudaMemcpyHostToDevice, st));
+    MDH_CUDA(cudaStreamSynchronize(st));
+}
+
+// Plans both passes for `total` = m * nprobe probes in ws.flags: the grouped
+// query matrix in pass[1] (g, gqn, gmap) and the unit tables of both passes,
+// whose lengths land in nunits[0..1] on the device.  Returns per-pass upper
+// bounds of the table lengths (they size the buffers and the grids).
+void plan_passes(mdh_ivf* ix, int m, int nprobe, cudaStream_t st, int64_t bound[2], int32_t** nunits) {
+    const int nl = ix->nlist;
+    const int total = m * nprobe;
+    Workspace& w = ix->ws;
+    int32_t* cnt = ix->plan_scratch;
+    int32_t* fill = cnt + nl;
+    int32_t* qstart = fill + nl;
+    int32_t* ustart = qstart + nl;  // [2][nlist]
+    *nunits = ustart + 2 * nl;      // [2]
+    MDH_CUDA(cudaMemsetAsync(cnt, 0, (size_t)2 * nl * 4, st));
+    MDH_CUDA(cudaMemsetAsync(ix->plan_pairs, 0, 2 * sizeof(unsigned long long), st));
+    k_plan_count<<<(total + 255) / 256, 256, 0, st>>>(w.flags, total, cnt);
+    k_plan_scan<<<1, kPlanThreads, 0, st>>>(cnt, ix->plan_order, ix->plan_info, nl, qstart, ustart, *nunits,
+                                            ix->plan_pairs);
+    IvfPassBufs& g = ix->pass[1];
+    grow_dev(&g.g, &g.g_bytes, (size_t)total * ix->dpad);
+    grow_dev(&g.gqn, &g.gqn_bytes, (size_t)total * 4);
+    grow_dev(&g.gmap, &g.gmap_bytes, (size_t)total * 4);
+    k_plan_fill<<<(total + 255) / 256, 256, 0, st>>>(w.flags, total, nprobe, qstart, fill, g.gmap);
+    launch_gather_queries_u8(w.q_u8, w.qn, g.gmap, total, ix->dpad, g.g, g.gqn, st);
+    // sum_c ceil(q_c / 128) * runs_c <= sum_c (q_c / 128 + 1) * runs_c <= total * max_runs / 128 + sum_runs.
+    for (int p = 0; p < 2; p++) {
+        bound[p] = std::max<int64_t>(1, ((int64_t)total * ix->unit_max_runs[p] + 127) / 128 + ix->unit_sum_runs[p]);
+        MDH_REQUIRE(bound[p] < (int64_t(1) << 31), MDH_ERR_UNSUPPORTED, "IVF unit table too large");
+        grow_dev(&ix->pass[p].units, &ix->pass[p].units_bytes, (size_t)bound[p] * sizeof(ScanUnit));
+    }
+    k_plan_units<<<dim3((unsigned)((nl + 255) / 256), 2), 256, 0, st>>>(cnt, ix->plan_info, qstart, ustart, nl,
+                                                                        ix->pass[0].units, ix->pass[1].units);
+    MDH_CUDA(cudaGetLastError());
 }
 
 void check_ivf_device(int dev) {
@@ -462,12 +645,15 @@ void ivf_create(const uint8_t* host, int64_t n, int32_t dim, const float* centro
         MDH_CUDA(cudaStreamSynchronize(st));
         make_tmap_rows(lv, dpad);
         build_ivf_sample(ix.get(), st);
+        build_ivf_plan_info(ix.get(), st);
     } catch (...) {
         cudaStreamSynchronize(st);
         release_tmp();
         free_level_buffers(ix->rows);
         free_level_buffers(ix->sample);
         if (ix->centroids) cudaFree(ix->centroids);
+        for (void* p : {(void*)ix->plan_info, (void*)ix->plan_order, (void*)ix->plan_scratch, (void*)ix->plan_pairs})
+            if (p) cudaFree(p);
         cudaStreamDestroy(ix->stream);
         throw;
     }
@@ -475,8 +661,9 @@ void ivf_create(const uint8_t* host, int64_t n, int32_t dim, const float* centro
     *out = ix.release();
 }
 
-void ivf_route_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int nprobe, std::vector<int32_t>& probe,
-                    int32_t** d_probe_out) {
+// Routes nq host queries: staged u8 queries in ws.q_u8, norms in ws.qn, the
+// probe matrix [nq][nprobe] in ws.flags; copied to `probe` when it is given.
+void ivf_route_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int nprobe, std::vector<int32_t>* probe) {
     Workspace& w = ix->ws;
     cudaStream_t st = ix->stream;
     grow_dev(&w.q_u8, &w.q_u8_bytes, (size_t)nq * ix->dpad);
@@ -488,25 +675,11 @@ void ivf_route_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int nprobe, std:
     grow_dev(&w.tmp, &w.tmp_bytes, (size_t)nq * ix->nlist * sizeof(double));  // similarities
     launch_route(w.q_u8, nq, ix->dpad, ix->dim, ix->centroids, ix->nlist, nprobe, static_cast<double*>(w.tmp), w.flags,
                  st);
-    probe.resize((size_t)nq * nprobe);
-    MDH_CUDA(cudaMemcpyAsync(probe.data(), w.flags, probe.size() * 4, cudaMemcpyDeviceToHost, st));
-    MDH_CUDA(cudaStreamSynchronize(st));
-    if (d_probe_out) *d_probe_out = w.flags;
-}
-
-void upload_pass(mdh_ivf* ix, IvfPassBufs& b, const PassPlan& pp, cudaStream_t st) {
-    const size_t gr = std::max<size_t>(pp.gmap.size(), 1);
-    grow_dev(&b.g, &b.g_bytes, gr * ix->dpad);
-    grow_dev(&b.gqn, &b.gqn_bytes, gr * 4);
-    grow_dev(&b.gmap, &b.gmap_bytes, gr * 4);
-    grow_dev(&b.units, &b.units_bytes, std::max<size_t>(pp.units.size(), 1) * sizeof(ScanUnit));
-    if (!pp.gmap.empty()) {
-        MDH_CUDA(cudaMemcpyAsync(b.gmap, pp.gmap.data(), pp.gmap.size() * 4, cudaMemcpyHostToDevice, st));
-        launch_gather_queries_u8(ix->ws.q_u8, ix->ws.qn, b.gmap, (int)pp.gmap.size(), ix->dpad, b.g, b.gqn, st);
+    if (probe) {
+        probe->resize((size_t)nq * nprobe);
+        MDH_CUDA(cudaMemcpyAsync(probe->data(), w.flags, probe->size() * 4, cudaMemcpyDeviceToHost, st));
+        MDH_CUDA(cudaStreamSynchronize(st));
     }
-    if (!pp.units.empty())
-        MDH_CUDA(cudaMemcpyAsync(b.units, pp.units.data(), pp.units.size() * sizeof(ScanUnit), cudaMemcpyHostToDevice,
-                                 st));
 }
 
 void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int nprobe, int32_t* out_ids,
@@ -537,19 +710,13 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
     std::vector<int32_t> hid;
     for (int c0 = 0; c0 < nq; c0 += chunk) {
         const int m = std::min(chunk, nq - c0);
-        std::vector<int32_t> probe;
-        ivf_route_impl(ix, host_q + (size_t)c0 * ix->dim, m, nprobe, probe, nullptr);
-        s.kernel_launches += 2;
-        PassPlan p1 = plan_pass(ix, ix->sample_start, ix->sample_count, probe, m, nprobe, nprobe);
-        PassPlan p2 = plan_pass(ix, ix->cell_start, ix->cell_count, probe, m, nprobe, nprobe);
-        // Both passes probe the same cells, so they share the gathered query
-        // matrix (pass 2's); pass 1 only has its own unit table.
-        upload_pass(ix, ix->pass[1], p2, st);
-        grow_dev(&ix->pass[0].units, &ix->pass[0].units_bytes, std::max<size_t>(p1.units.size(), 1) * sizeof(ScanUnit));
-        if (!p1.units.empty())
-            MDH_CUDA(cudaMemcpyAsync(ix->pass[0].units, p1.units.data(), p1.units.size() * sizeof(ScanUnit),
-                                     cudaMemcpyHostToDevice, st));
-        s.kernel_launches += 2;
+        ivf_route_impl(ix, host_q + (size_t)c0 * ix->dim, m, nprobe, nullptr);
+        s.kernel_launches += 3;
+        int64_t bound[2];
+        int32_t* nunits = nullptr;
+        plan_passes(ix, m, nprobe, st, bound, &nunits);
+        const int total = m * nprobe;
+        s.kernel_launches += 5;
         grow_dev(&w.thr_key, &w.thr_key_bytes, (size_t)m * 4);
         grow_dev(&w.thr_id, &w.thr_id_bytes, (size_t)m * 4);
         grow_dev(&w.counts, &w.counts_bytes, (size_t)m * 4);
@@ -570,8 +737,8 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         // Pass 1: samples of the probed cells, infinite thresholds -> k-th entry thresholds.
         launch_fill_threshold(w.thr_key, w.thr_id, m, kKeyInf, kIdInf, st);
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
-        launch_filter_tc_u8_l2_units(ix->sample, ix->dpad, ix->pass[1].g, (int)p2.gmap.size(), ix->pass[1].gmap, w.qn,
-                                     ix->pass[0].units, (int)p1.units.size(), w.thr_key, w.thr_id, w.counts, w.cand,
+        launch_filter_tc_u8_l2_units(ix->sample, ix->dpad, ix->pass[1].g, total, ix->pass[1].gmap, w.qn,
+                                     ix->pass[0].units, (int)bound[0], nunits, w.thr_key, w.thr_id, w.counts, w.cand,
                                      kIvfCap1, w.status, st);
         launch_select(w.counts, w.cand, kIvfCap1, ix->sample.ids, m, k, 0, w.thr_key, w.thr_id, w.out_key, w.out_id, w.qlist,
                       w.status + 1, nullptr, nullptr, st);
@@ -579,17 +746,25 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         // Pass 2: every probed cell with those thresholds.
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
         MDH_CUDA(cudaEventRecord(w.ev0, st));
-        launch_filter_tc_u8_l2_units(lv, ix->dpad, ix->pass[1].g, (int)p2.gmap.size(), ix->pass[1].gmap, w.qn,
-                                     ix->pass[1].units, (int)p2.units.size(), w.thr_key, w.thr_id, w.counts, w.cand,
-                                     kIvfCap2, w.status, st);
+        launch_filter_tc_u8_l2_units(lv, ix->dpad, ix->pass[1].g, total, ix->pass[1].gmap, w.qn,
+                                     ix->pass[1].units, (int)bound[1], nunits + 1, w.thr_key, w.thr_id, w.counts,
+                                     w.cand, kIvfCap2, w.status, st);
         MDH_CUDA(cudaEventRecord(w.ev1, st));
         launch_select(w.counts, w.cand, kIvfCap2, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id, w.qlist,
                       w.status + 1, nullptr, n_cand, st);
         s.kernel_launches += 2;
-        s.pairs_scored += p1.pairs + p2.pairs;
-        s.full_scan_pairs += p2.pairs;
+        // Status, pair counts and the results come back with one synchronization
+        // (the results are copied again after an overflow round).
+        hkey.resize((size_t)m * k);
+        hid.resize((size_t)m * k);
+        unsigned long long pairs[2] = {0, 0};
         MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 6 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+        MDH_CUDA(cudaMemcpyAsync(pairs, ix->plan_pairs, sizeof(pairs), cudaMemcpyDeviceToHost, st));
+        MDH_CUDA(cudaMemcpyAsync(hkey.data(), w.out_key, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
+        MDH_CUDA(cudaMemcpyAsync(hid.data(), w.out_id, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
         MDH_CUDA(cudaStreamSynchronize(st));
+        s.pairs_scored += (int64_t)(pairs[0] + pairs[1]);
+        s.full_scan_pairs += (int64_t)pairs[1];
         if (w.h_status[0] != kDevOk)
             throw Error(MDH_ERR_TIMEOUT, "IVF scan reported device status " + std::to_string(w.h_status[0]));
         {
@@ -604,14 +779,16 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
             MDH_REQUIRE(++rounds < 64, MDH_ERR_INTERNAL, "candidate overflow did not converge");
             MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
             MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
-            launch_filter_tc_u8_l2_units(lv, ix->dpad, ix->pass[1].g, (int)p2.gmap.size(), ix->pass[1].gmap, w.qn,
-                                         ix->pass[1].units, (int)p2.units.size(), w.thr_key, w.thr_id, w.counts,
-                                         w.cand, kIvfCap2, w.status, st);
+            launch_filter_tc_u8_l2_units(lv, ix->dpad, ix->pass[1].g, total, ix->pass[1].gmap, w.qn,
+                                         ix->pass[1].units, (int)bound[1], nunits + 1, w.thr_key, w.thr_id,
+                                         w.counts, w.cand, kIvfCap2, w.status, st);
             launch_select(w.counts, w.cand, kIvfCap2, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id,
                           w.qlist, w.status + 1, nullptr, n_cand, st);
             s.kernel_launches += 2;
-            s.pairs_scored += p2.pairs;
+            s.pairs_scored += (int64_t)pairs[1];
             MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 6 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+            MDH_CUDA(cudaMemcpyAsync(hkey.data(), w.out_key, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
+            MDH_CUDA(cudaMemcpyAsync(hid.data(), w.out_id, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
             MDH_CUDA(cudaStreamSynchronize(st));
             if (w.h_status[0] != kDevOk)
                 throw Error(MDH_ERR_TIMEOUT, "IVF scan reported device status " + std::to_string(w.h_status[0]));
@@ -621,11 +798,6 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
             std::memcpy(&cand_n, w.h_status + 2, 8);
             s.candidates += (int64_t)cand_n;
         }
-        hkey.resize((size_t)m * k);
-        hid.resize((size_t)m * k);
-        MDH_CUDA(cudaMemcpyAsync(hkey.data(), w.out_key, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
-        MDH_CUDA(cudaMemcpyAsync(hid.data(), w.out_id, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
-        MDH_CUDA(cudaStreamSynchronize(st));
         for (size_t i = 0; i < (size_t)m * k; i++) {
             out_ids[(size_t)c0 * k + i] = hid[i];
             if (out_dist) out_dist[(size_t)c0 * k + i] = hid[i] >= 0 ? (int32_t)hkey[i] : -1;
@@ -672,7 +844,7 @@ mdh_status mdh_ivf_route_u8(mdh_ivf* index, const uint8_t* host_queries, int32_t
         std::lock_guard<std::mutex> lock(x.ix->mu);
         MDH_CUDA(cudaSetDevice(x.ix->device));
         std::vector<int32_t> probe;
-        ivf_route_impl(x.ix, x.q, x.nq, x.np, probe, nullptr);
+        ivf_route_impl(x.ix, x.q, x.nq, x.np, &probe);
         std::memcpy(x.out, probe.data(), probe.size() * 4);
     }, &a);
 }
@@ -713,6 +885,8 @@ mdh_status mdh_ivf_destroy(mdh_ivf* index) {
         free_level_buffers(ix->rows);
         free_level_buffers(ix->sample);
         if (ix->centroids) cudaFree(ix->centroids);
+        for (void* p : {(void*)ix->plan_info, (void*)ix->plan_order, (void*)ix->plan_scratch, (void*)ix->plan_pairs})
+            if (p) cudaFree(p);
         free_workspace(ix->ws);
         if (ix->stream) cudaStreamDestroy(ix->stream);
         delete ix;

@@ -182,8 +182,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                       const int32_t* __restrict__ qn, int nq, const uint32_t* __restrict__ thr_key,
                       const int32_t* __restrict__ thr_id, uint32_t* __restrict__ counts, uint2* __restrict__ cand,
                       int cap, int dense, Sched sched, int32_t* __restrict__ status,
-                      const ScanUnit* __restrict__ units, const int32_t* __restrict__ qmap) {
+                      const ScanUnit* __restrict__ units, const int32_t* __restrict__ qmap,
+                      const int32_t* __restrict__ n_units_dev) {
     constexpr int BN = C::BN, QT = C::QT, STAGES = C::STAGES, ACC_STAGES = C::ACC_STAGES;
+    // A unit table built on the device carries its own length.
+    const long long n_units = n_units_dev ? (long long)*n_units_dev : sched.n_units;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
@@ -225,7 +228,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t issued_mask = 0, last_parity = 0;
             bool a_issued = false;
             bool ok = true;
-            for (long long u = blockIdx.x; u < sched.n_units && ok; u += gridDim.x) {
+            for (long long u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
                 const UnitView uv = unit_view<C, UNITS>(sched, units, u, n_rows, nq);
                 const int t0 = uv.t0, t1 = uv.t1;
                 ok = mbar_wait<false>(bars + 8 * C::BAR_A_EMPTY, (a_iter & 1) ^ 1, abort_flag, status);
@@ -272,7 +275,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0, a_iter = 0;
             bool ok = true, issued = false;
-            for (long long u = blockIdx.x; u < sched.n_units && ok; u += gridDim.x) {
+            for (long long u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
                 const UnitView uv = unit_view<C, UNITS>(sched, units, u, n_rows, nq);
                 const int t0 = uv.t0, t1 = uv.t1;
                 ok = mbar_wait<false>(bars + 8 * C::BAR_A_FULL, a_iter & 1, abort_flag, status);
@@ -346,7 +349,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int acc = 0;  // accumulator stage of the CTA's next tile
         uint32_t ph0 = 0, ph1 = 0;
         bool ok = true;
-        for (long long u = blockIdx.x; u < sched.n_units && ok; u += gridDim.x) {
+        for (long long u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
             const UnitView uv = unit_view<C, UNITS>(sched, units, u, n_rows, nq);
             const int t0 = uv.t0, t1 = uv.t1, row_end = uv.row_end;
             const int qlocal = quarter * 32 + lane;
@@ -435,7 +438,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t acc_phase = 0;
         bool ok = true;
         const int32_t* nrm = norms + rowoff;
-        for (long long u = blockIdx.x; u < sched.n_units && ok; u += gridDim.x) {
+        for (long long u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
             const UnitView uv = unit_view<C, UNITS>(sched, units, u, n_rows, nq);
             const int t0 = uv.t0, t1 = uv.t1, row_end = uv.row_end;
             const int qlocal = qt * BM + quarter * 32 + lane;
@@ -617,7 +620,7 @@ void launch_tc(const Level& lv, const CUtensorMap& tq, const int32_t* qn, int nq
                                   (int)C::SMEM_BYTES));
     k_filter_tc_u8_l2<C, false><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
                                                                    qn, nq, thr_key, thr_id, counts, cand, cap, dense,
-                                                                   s, status, nullptr, nullptr);
+                                                                   s, status, nullptr, nullptr, nullptr);
     MDH_CUDA(cudaGetLastError());
 }
 
@@ -633,9 +636,9 @@ void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const i
 }
 
 void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat, int qmat_rows, const int32_t* qmap,
-                                  const int32_t* qn, const ScanUnit* units, int n_units, const uint32_t* thr_key,
-                                  const int32_t* thr_id, uint32_t* counts, uint2* cand, int cap, int32_t* status,
-                                  cudaStream_t st) {
+                                  const int32_t* qn, const ScanUnit* units, int n_units, const int32_t* n_units_dev,
+                                  const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts, uint2* cand,
+                                  int cap, int32_t* status, cudaStream_t st) {
     using C = CfgNarrow;
     if (n_units <= 0 || qmat_rows <= 0 || lv.n == 0) return;
     MDH_REQUIRE(dpad == BK && lv.has_tmap, MDH_ERR_INTERNAL, "tensor-core scan needs 128-byte rows and a TMA map");
@@ -650,7 +653,7 @@ void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat
                                   (int)C::SMEM_BYTES));
     k_filter_tc_u8_l2<C, true><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
                                                                    qn, qmat_rows, thr_key, thr_id, counts, cand, cap,
-                                                                   0, s, status, units, qmap);
+                                                                   0, s, status, units, qmap, n_units_dev);
     MDH_CUDA(cudaGetLastError());
 }
 
