@@ -69,7 +69,8 @@ constexpr int EPI_THREADS = 32 * EPI_WARPS;
 constexpr int PRODUCER_WARP = EPI_WARPS;
 constexpr int MMA_WARP = EPI_WARPS + 1;
 constexpr int NUM_THREADS = 32 * (EPI_WARPS + 2);
-constexpr int BUFN = 4;           // buffered candidates per epilogue thread
+constexpr int BUFN = 8;           // buffered candidates per epilogue thread
+constexpr int BUF_FLUSH_AT = 4;   // a warp flushes together once a lane holds this many
 constexpr uint32_t A_TILE_BYTES = BM * BK;
 
 template <int BN_, int QT_>
@@ -400,6 +401,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     chunk_filter(v[1], need, row0 + 32, row_end, tkey, tid, qnv, qi, norms, ids, dense, buf, counts,
                                  cand, cap);
                 }
+                buf.warp_flush_at(BUF_FLUSH_AT, counts, cand, cap, qi);
                 return true;
             };
             using S0 = std::integral_constant<int, 0>;
@@ -472,6 +474,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 nx1 = __ldg(nrm + (int64_t)t0 * BN + 32 + lane);
             }
             for (int t = t0; t < t1; t++) {
+                buf.warp_flush_at(BUF_FLUSH_AT, counts, cand, cap, qi);
                 const int32_t nr0 = nx0, nr1 = nx1;
                 const int32_t need0 = __shfl_sync(0xffffffffu, nr0, 0) + bias;
                 const int32_t need1 = __shfl_sync(0xffffffffu, nr1, 0) + bias;

@@ -300,6 +300,12 @@ struct CandBuf {
         base[n * STRIDE] = make_uint2(key, pos);
         if (++n == N) flush(counts, cand, cap, qi);
     }
+    // Called by a whole (converged) warp between tiles: once any lane holds
+    // `threshold` entries, every lane with entries flushes, so the warp waits
+    // for one round of atomics instead of one per lane as each fills up.
+    __device__ __forceinline__ void warp_flush_at(int threshold, uint32_t* counts, uint2* cand, int cap, int qi) {
+        if (__any_sync(0xffffffffu, n >= threshold)) flush(counts, cand, cap, qi);
+    }
 };
 
 }  // namespace tc
