@@ -187,38 +187,55 @@ __global__ void k_ivf_fill(int32_t* __restrict__ p, int64_t n, int32_t v) {
 
 // Routing, step 1: sims[q][c] = sum_j q[j] * centroid[c][j] in fp64, one
 // fused multiply-add per j in dimension order from 0.0 (deterministic, so the
-// cell order is reproducible).  Block tile: 16 queries x 64 centroids in
-// shared memory; each thread forms 4 of the 1024 dot products.
-constexpr int kRouteQ = 16, kRouteC = 64, kRouteDim = 128;
-constexpr int kRoutePerThread = kRouteQ * kRouteC / 256;
+// cell order is reproducible).  Block tile: 32 queries x 64 centroids, both
+// converted to fp64 once in shared memory; each thread forms 2 x 4 of the
+// 2048 dot products, so a step of j is 6 shared loads for 8 multiply-adds.
+constexpr int kRouteQ = 32, kRouteC = 64, kRouteDim = 128;
+constexpr size_t kRouteSmem = (size_t)(kRouteQ * kRouteDim + kRouteC * (kRouteDim + 1)) * sizeof(double);
 __global__ void __launch_bounds__(256) k_route_sims(const uint8_t* __restrict__ q, int nq, int dpad, int dim,
                                                     const float* __restrict__ centroids, int nlist,
                                                     double* __restrict__ sims) {
-    __shared__ float cs[kRouteC][kRouteDim + 1];
-    __shared__ uint8_t qs[kRouteQ][kRouteDim];
+    extern __shared__ double route_smem[];
+    double* qs = route_smem;                       // [kRouteQ][dim]
+    double* cs = route_smem + kRouteQ * kRouteDim;  // [kRouteC][dim + 1]
     const int q0 = blockIdx.y * kRouteQ, c0 = blockIdx.x * kRouteC;
+    const int cstride = dim + 1;
     for (int i = threadIdx.x; i < kRouteC * dim; i += blockDim.x) {
         const int c = i / dim, j = i - c * dim;
-        cs[c][j] = c0 + c < nlist ? centroids[(size_t)(c0 + c) * dim + j] : 0.0f;
+        cs[c * cstride + j] = c0 + c < nlist ? (double)centroids[(size_t)(c0 + c) * dim + j] : 0.0;
     }
     for (int i = threadIdx.x; i < kRouteQ * dim; i += blockDim.x) {
         const int r = i / dim, j = i - r * dim;
-        qs[r][j] = q0 + r < nq ? q[(size_t)(q0 + r) * dpad + j] : 0;
+        qs[r * dim + j] = q0 + r < nq ? (double)q[(size_t)(q0 + r) * dpad + j] : 0.0;
     }
     __syncthreads();
-    const int c = threadIdx.x % kRouteC;
-    const int rbase = (threadIdx.x / kRouteC) * kRoutePerThread;
-    double acc[kRoutePerThread];
+    // Thread: centroids cq + 16 b (b < 4), queries rp and rp + 16.  A warp
+    // reads 16 centroid rows 129 doubles apart (every bank once) and
+    // broadcasts two query rows.
+    const int cq = threadIdx.x & 15, rp = threadIdx.x >> 4;
+    double acc[2][4];
 #pragma unroll
-    for (int r = 0; r < kRoutePerThread; r++) acc[r] = 0.0;
+    for (int a = 0; a < 2; a++)
+#pragma unroll
+        for (int b = 0; b < 4; b++) acc[a][b] = 0.0;
     for (int j = 0; j < dim; j++) {
-        const double cv = (double)cs[c][j];
+        double qv[2], cv[4];
 #pragma unroll
-        for (int r = 0; r < kRoutePerThread; r++) acc[r] = __fma_rn((double)qs[rbase + r][j], cv, acc[r]);
+        for (int a = 0; a < 2; a++) qv[a] = qs[(rp + 16 * a) * dim + j];
+#pragma unroll
+        for (int b = 0; b < 4; b++) cv[b] = cs[(cq + 16 * b) * cstride + j];
+#pragma unroll
+        for (int a = 0; a < 2; a++)
+#pragma unroll
+            for (int b = 0; b < 4; b++) acc[a][b] = __fma_rn(qv[a], cv[b], acc[a][b]);
     }
 #pragma unroll
-    for (int r = 0; r < kRoutePerThread; r++)
-        if (q0 + rbase + r < nq && c0 + c < nlist) sims[(size_t)(q0 + rbase + r) * nlist + c0 + c] = acc[r];
+    for (int a = 0; a < 2; a++)
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            const int qi = q0 + rp + 16 * a, c = c0 + cq + 16 * b;
+            if (qi < nq && c < nlist) sims[(size_t)qi * nlist + c] = acc[a][b];
+        }
 }
 
 // Routing, step 2: one warp per query takes the nprobe largest similarities,
@@ -254,14 +271,62 @@ __global__ void __launch_bounds__(256) k_route_select(double* __restrict__ sims,
     }
 }
 
+// The same selection with the row held in registers (nlist <= 32 * PER):
+// lane l holds cells l, l + 32, ...; each round takes the warp's best
+// (largest similarity, lower id on ties) and retires it.
+template <int PER>
+__global__ void __launch_bounds__(256) k_route_select_reg(const double* __restrict__ sims, int nq, int nlist,
+                                                          int nprobe, int32_t* __restrict__ probe) {
+    const int qi = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (qi >= nq) return;
+    const double* row = sims + (size_t)qi * nlist;
+    double v[PER];
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const int c = lane + 32 * i;
+        v[i] = c < nlist ? row[c] : -INFINITY;
+    }
+    for (int p = 0; p < nprobe; p++) {
+        double bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            const int c = lane + 32 * i;  // ascending, so '>' keeps the lower id on ties
+            if (c < nlist && v[i] > bv) {
+                bv = v[i];
+                bi = c;
+            }
+        }
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) {
+            const double ov = __shfl_xor_sync(0xffffffffu, bv, m);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) probe[(size_t)qi * nprobe + p] = bi;
+#pragma unroll
+        for (int i = 0; i < PER; i++)
+            if (lane + 32 * i == bi) v[i] = -INFINITY;  // taken
+    }
+}
+
 void launch_route(const uint8_t* q, int nq, int dpad, int dim, const float* centroids, int nlist, int nprobe,
                   double* sims, int32_t* probe, cudaStream_t st) {
     if (nq <= 0) return;
     MDH_REQUIRE(dim <= kRouteDim, MDH_ERR_INTERNAL, "routing supports dim <= 128");
     dim3 grid((unsigned)((nlist + kRouteC - 1) / kRouteC), (unsigned)((nq + kRouteQ - 1) / kRouteQ));
-    k_route_sims<<<grid, 256, 0, st>>>(q, nq, dpad, dim, centroids, nlist, sims);
+    // A function attribute belongs to the current device: set it on every launch.
+    MDH_CUDA(cudaFuncSetAttribute(k_route_sims, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRouteSmem));
+    k_route_sims<<<grid, 256, kRouteSmem, st>>>(q, nq, dpad, dim, centroids, nlist, sims);
     MDH_CUDA(cudaGetLastError());
-    k_route_select<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, st>>>(sims, nq, nlist, nprobe, probe);
+    if (nlist <= 32 * 32)
+        k_route_select_reg<32><<<(unsigned)((nq * 32 + 255) / 256), 256, 0, st>>>(sims, nq, nlist, nprobe, probe);
+    else
+        k_route_select<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, st>>>(sims, nq, nlist, nprobe, probe);
     MDH_CUDA(cudaGetLastError());
 }
 

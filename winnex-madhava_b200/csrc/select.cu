@@ -209,20 +209,32 @@ __global__ void __launch_bounds__(32 * kWarpSelectWarps)
 #pragma unroll
     for (int j = 0; j < KM; j++) top[j] = ~0ull;
     unsigned long long worst = ~0ull;  // this lane's k-th smallest so far
-    for (int i = lane; i < c; i += 32) {
-        const uint2 e = src[i];
-        const unsigned long long hi = (unsigned long long)e.x << 32;
-        if (hi > worst) continue;  // its composite key is larger still
-        const unsigned long long v = hi | (uint32_t)__ldg(ids + e.y);
-        if (v >= worst) continue;
-        // Insert into the ascending list (the last slot drops out).
+    // Eight loads per lane in flight per round: the list is streamed, not
+    // walked one dependent load at a time.
+    constexpr int U = 8;
+    for (int i0 = lane; i0 < c; i0 += 32 * U) {
+        uint2 e[U];
 #pragma unroll
-        for (int j = KM - 1; j > 0; j--) top[j] = top[j - 1] > v ? top[j - 1] : (top[j] > v ? v : top[j]);
-        top[0] = top[0] > v ? v : top[0];
-        unsigned long long w = top[0];
+        for (int u = 0; u < U; u++) {
+            const int i = i0 + 32 * u;
+            e[u] = i < c ? src[i] : make_uint2(0u, 0u);
+        }
 #pragma unroll
-        for (int j = 1; j < KM; j++) w = (j == k - 1) ? top[j] : w;
-        worst = w;
+        for (int u = 0; u < U; u++) {
+            if (i0 + 32 * u >= c) break;
+            const unsigned long long hi = (unsigned long long)e[u].x << 32;
+            if (hi > worst) continue;  // its composite key is larger still
+            const unsigned long long v = hi | (uint32_t)__ldg(ids + e[u].y);
+            if (v >= worst) continue;
+            // Insert into the ascending list (the last slot drops out).
+#pragma unroll
+            for (int j = KM - 1; j > 0; j--) top[j] = top[j - 1] > v ? top[j - 1] : (top[j] > v ? v : top[j]);
+            top[0] = top[0] > v ? v : top[0];
+            unsigned long long w = top[0];
+#pragma unroll
+            for (int j = 1; j < KM; j++) w = (j == k - 1) ? top[j] : w;
+            worst = w;
+        }
     }
     // The k smallest of the warp, ascending: lane r ends with the r-th.
     unsigned long long res = ~0ull;
