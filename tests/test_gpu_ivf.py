@@ -52,7 +52,7 @@ def test_ivf_matches_oracle_on_reference_cells():
         want_ids, want_d = oracle.ivf_exact(C, labels, cen, Q, k, nprobe)
         np.testing.assert_array_equal(ids, want_ids)
         np.testing.assert_array_equal(dist[want_ids >= 0], want_d[want_ids >= 0])
-        assert s.levels == 2 and s.tensor_core_path == 1 and s.full_scan_pairs > 0
+        assert s.levels == 3 and s.tensor_core_path == 1 and s.full_scan_pairs > 0  # coarse, sample, full passes
     # probing every cell is the plain exact search
     ids, dist, _ = _search(L, h, Q, 10, cases.HYBRID["nlist"])
     want_ids, want_d = oracle.l2_exact_u8_int(C, Q, 10)

@@ -16,17 +16,22 @@
 // Search, per batch of queries:
 //   1. route (k_route_sims, k_route_select): fp64 dot products with every
 //      centroid, top nprobe;
-//   2. pass 1: each query against a sample of its cells (every row whose
-//      id hashes below 1/32, and the 8 lowest-norm rows of each cell) with an
-//      infinite threshold; the k-th smallest (key, id) is a valid threshold
-//      for the union (the sample is part of it) and about 32 k of the
-//      union's rows lie at or below it;
-//   3. pass 2: each query against all its cells with that threshold; the
+//   2. pass 0: each query against a coarse sample of its cells (rows whose
+//      id hashes below 1/256, and the 2 lowest-norm rows of each cell) with
+//      an infinite threshold; the k-th smallest (key, id) is a valid
+//      threshold for the union (the sample is part of it);
+//   3. pass 1: each query against a finer sample (1/32, and the 8
+//      lowest-norm rows of each cell) with that threshold; its k-th smallest
+//      candidate tightens the threshold so that about 32 k of the union's
+//      rows lie at or below it;
+//   4. pass 2: each query against all its cells with that threshold; the
 //      candidates' first k are exact.  Overflowed lists rerun with their
 //      k-th stored entry, strictly tighter, until they fit.
-// Both passes run the tcgen05 scan (scan_tc.cu) over a unit table: a unit
+// Every pass runs the tcgen05 scan (scan_tc.cu) over a unit table: a unit
 // is one cell (or a run of at most 64 of its tiles) against up to 128 of the
-// queries that probe it, gathered into a per-pass query matrix.
+// queries that probe it, gathered into one query matrix.  The coarse pass
+// keeps the first sample pass from handling every sampled pair as a
+// candidate.
 #include <cub/cub.cuh>
 
 #include <algorithm>
@@ -64,22 +69,25 @@ struct mdh_ivf {
     mdh::Level rows;                     // all cells, padded
     std::vector<int64_t> cell_start;     // first row of cell c
     std::vector<int64_t> cell_count;     // real rows of cell c
-    mdh::Level sample;                   // per-cell samples, same layout
+    mdh::Level sample;                   // per-cell samples (1/32), same layout
     std::vector<int64_t> sample_start;
     std::vector<int64_t> sample_count;
+    mdh::Level coarse;                   // per-cell coarse samples (1/256), same layout
+    std::vector<int64_t> coarse_start;
+    std::vector<int64_t> coarse_count;
     float* centroids = nullptr;          // [nlist][dim]
     mdh::Workspace ws;
-    mdh::IvfPassBufs pass[2];            // pass 1 (cell samples) and pass 2 (whole cells)
-    // Device-side planning: per cell {first tile, tiles, row end} in the full
-    // layout, then in the sample layout; the cells in planning order (most
-    // tiles first); scratch for the plan (query counts, fill cursors, query
-    // offsets, unit offsets of both passes, table lengths) and pair counts.
-    int32_t* plan_info = nullptr;        // [nlist][6]
+    mdh::IvfPassBufs pass[3];            // coarse samples, samples, whole cells (pass[2] holds the query matrix)
+    // Device-side planning: per cell and pass {first tile, tiles, row end} of
+    // the pass's layout; the cells in planning order (most tiles first);
+    // scratch for the plan (query counts, fill cursors, query offsets, unit
+    // offsets of each pass, table lengths) and pair counts.
+    int32_t* plan_info = nullptr;        // [nlist][3 passes][3]
     int32_t* plan_order = nullptr;       // [nlist]
-    int32_t* plan_scratch = nullptr;     // [6 * nlist + 2]
-    unsigned long long* plan_pairs = nullptr;  // [2]
-    int64_t unit_max_runs[2] = {0, 0};   // per pass: max over cells of ceil(tiles / 64)
-    int64_t unit_sum_runs[2] = {0, 0};   // per pass: sum over cells of ceil(tiles / 64)
+    int32_t* plan_scratch = nullptr;     // [6 * nlist + 3]
+    unsigned long long* plan_pairs = nullptr;  // [3]
+    int64_t unit_max_runs[3] = {0, 0, 0};  // per pass: max over cells of ceil(tiles / 64)
+    int64_t unit_sum_runs[3] = {0, 0, 0};  // per pass: sum over cells of ceil(tiles / 64)
     std::mutex mu;
 };
 
@@ -91,9 +99,13 @@ constexpr int kIvfTileRows = 256;     // tile of the tensor scan (CfgNarrow::BN)
 constexpr int kIvfMaxTilesPerUnit = 64;
 constexpr int kIvfMaxNlist = 8192;
 constexpr int kIvfMaxProbe = 1024;
-constexpr int kIvfCap1 = 16384;       // pass 1 candidate lists (samples of the probed cells)
+constexpr int kIvfPasses = 3;         // coarse samples, samples, whole cells
+constexpr int kIvfCap0 = 4096;        // coarse-sample pass candidate lists
+constexpr int kIvfCap1 = 16384;       // sample pass candidate lists
 constexpr uint32_t kIvfSampleThresh = 0x08000000u;  // id hash below this: in the sample (1/32)
 constexpr int kIvfSampleHead = 8;     // lowest-norm rows of every cell always in the sample
+constexpr uint32_t kIvfCoarseThresh = 0x01000000u;  // ... in the coarse sample (1/256)
+constexpr int kIvfCoarseHead = 2;
 constexpr int kIvfCap2 = 16384;       // pass 2 candidate lists
 
 template <class T>
@@ -338,15 +350,16 @@ void grow_dev(T** p, size_t* have, size_t bytes) {
 }
 
 // ---------------------------------------------------------------- planning
-// Both passes probe the same cells, so they share one grouped query matrix
+// All passes probe the same cells, so they share one grouped query matrix
 // (queries listed cell by cell) and differ in their unit tables.  The plan
 // is built on the device from the routing output, so routing, planning and
-// both passes run back to back on one stream.  The order of queries inside a
+// the passes run back to back on one stream.  The order of queries inside a
 // cell's list depends on atomics; results do not (candidates are selected by
-// (key, id)).
+// (key, id)).  Pass p uses layout p: coarse samples, samples, whole cells.
 
 constexpr int kPlanThreads = 1024;
 constexpr int kPlanItems = kIvfMaxNlist / kPlanThreads;  // cells per thread in k_plan_scan
+constexpr int kPlanCounters = 1 + kIvfPasses;            // queries, then units of each pass
 static_assert(kPlanItems * kPlanThreads == kIvfMaxNlist, "plan scan covers every cell");
 
 __global__ void k_plan_count(const int32_t* __restrict__ probe, int total, int32_t* __restrict__ cnt) {
@@ -354,13 +367,13 @@ __global__ void k_plan_count(const int32_t* __restrict__ probe, int total, int32
     if (i < total) atomicAdd(cnt + probe[i], 1);
 }
 
-// Block-wide exclusive scan of three counters (one block of kPlanThreads).
-__device__ __forceinline__ void block_scan3(int (&v)[3], int (&total)[3]) {
-    __shared__ int wsum[3][kPlanThreads / 32];
+// Block-wide exclusive scan of kPlanCounters counters (one block of kPlanThreads).
+__device__ __forceinline__ void block_scan(int (&v)[kPlanCounters], int (&total)[kPlanCounters]) {
+    __shared__ int wsum[kPlanCounters][kPlanThreads / 32];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    int incl[3];
+    int incl[kPlanCounters];
 #pragma unroll
-    for (int j = 0; j < 3; j++) {
+    for (int j = 0; j < kPlanCounters; j++) {
         incl[j] = v[j];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -372,7 +385,7 @@ __device__ __forceinline__ void block_scan3(int (&v)[3], int (&total)[3]) {
     __syncthreads();
     if (wid == 0) {
 #pragma unroll
-        for (int j = 0; j < 3; j++) {
+        for (int j = 0; j < kPlanCounters; j++) {
             int x = wsum[j][lane];
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -384,7 +397,7 @@ __device__ __forceinline__ void block_scan3(int (&v)[3], int (&total)[3]) {
     }
     __syncthreads();
 #pragma unroll
-    for (int j = 0; j < 3; j++) {
+    for (int j = 0; j < kPlanCounters; j++) {
         total[j] = wsum[j][kPlanThreads / 32 - 1];
         v[j] = incl[j] - v[j] + (wid > 0 ? wsum[j][wid - 1] : 0);
     }
@@ -392,61 +405,60 @@ __device__ __forceinline__ void block_scan3(int (&v)[3], int (&total)[3]) {
 
 // One block.  For every cell, taken in planning order: the offset of its
 // query list in the grouped matrix (qstart) and of its first unit in each
-// pass's table (ustart[pass][cell]); the tables' lengths (nunits[2]) and the
-// (query, row) pairs each pass scans (pairs[2], zeroed by the caller).
+// pass's table (ustart[pass][cell]); the tables' lengths (nunits[pass]) and
+// the (query, row) pairs each pass scans (pairs[pass], zeroed by the caller).
+// info[cell][pass] = {first tile, tiles, row end} of the pass's layout.
 __global__ void __launch_bounds__(kPlanThreads)
     k_plan_scan(const int32_t* __restrict__ cnt, const int32_t* __restrict__ order, const int32_t* __restrict__ info,
                 int nlist, int32_t* __restrict__ qstart, int32_t* __restrict__ ustart, int32_t* __restrict__ nunits,
                 unsigned long long* __restrict__ pairs) {
-    int item[kPlanItems][3];
-    int sum[3] = {0, 0, 0};
-    unsigned long long pr[2] = {0, 0};
+    int item[kPlanItems][kPlanCounters];
+    int sum[kPlanCounters] = {};
+    unsigned long long pr[kIvfPasses] = {};
 #pragma unroll
     for (int j = 0; j < kPlanItems; j++) {
         const int pos = threadIdx.x * kPlanItems + j;
-        int qn = 0, u[2] = {0, 0};
+        int x[kPlanCounters] = {};
         if (pos < nlist) {
-            const int32_t* f = info + 6 * order[pos];
-            qn = cnt[order[pos]];
+            const int c = order[pos];
+            const int qn = cnt[c];
+            x[0] = qn;
             if (qn > 0) {
 #pragma unroll
-                for (int p = 0; p < 2; p++) {
-                    const int32_t* g = f + (p == 0 ? 3 : 0);  // pass 0: sample layout, pass 1: full layout
+                for (int p = 0; p < kIvfPasses; p++) {
+                    const int32_t* g = info + 9 * c + 3 * p;
                     if (g[1] > 0) {
-                        u[p] = (qn + 127) / 128 * ((g[1] + kIvfMaxTilesPerUnit - 1) / kIvfMaxTilesPerUnit);
+                        x[1 + p] = (qn + 127) / 128 * ((g[1] + kIvfMaxTilesPerUnit - 1) / kIvfMaxTilesPerUnit);
                         pr[p] += (unsigned long long)qn * (unsigned long long)(g[2] - g[0] * kIvfTileRows);
                     }
                 }
             }
         }
-        item[j][0] = qn;
-        item[j][1] = u[0];
-        item[j][2] = u[1];
-        sum[0] += qn;
-        sum[1] += u[0];
-        sum[2] += u[1];
+#pragma unroll
+        for (int q = 0; q < kPlanCounters; q++) {
+            item[j][q] = x[q];
+            sum[q] += x[q];
+        }
     }
-    int total[3];
-    block_scan3(sum, total);
+    int total[kPlanCounters];
+    block_scan(sum, total);
 #pragma unroll
     for (int j = 0; j < kPlanItems; j++) {
         const int pos = threadIdx.x * kPlanItems + j;
         if (pos < nlist) {
             const int c = order[pos];
             qstart[c] = sum[0];
-            ustart[c] = sum[1];
-            ustart[nlist + c] = sum[2];
-        }
-        sum[0] += item[j][0];
-        sum[1] += item[j][1];
-        sum[2] += item[j][2];
-    }
-    if (threadIdx.x == 0) {
-        nunits[0] = total[1];
-        nunits[1] = total[2];
-    }
 #pragma unroll
-    for (int p = 0; p < 2; p++) {
+            for (int p = 0; p < kIvfPasses; p++) ustart[p * nlist + c] = sum[1 + p];
+        }
+#pragma unroll
+        for (int q = 0; q < kPlanCounters; q++) sum[q] += item[j][q];
+    }
+    if (threadIdx.x == 0)
+#pragma unroll
+        for (int p = 0; p < kIvfPasses; p++) nunits[p] = total[1 + p];
+#pragma unroll
+    for (int p = 0; p < kIvfPasses; p++) {
         unsigned long long x = pr[p];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
@@ -464,19 +476,23 @@ __global__ void k_plan_fill(const int32_t* __restrict__ probe, int total, int np
     gmap[qstart[c] + atomicAdd(fill + c, 1)] = i / nprobe;
 }
 
+struct PassUnits {
+    ScanUnit* u[kIvfPasses];
+};
+
 // One thread per (cell, pass): the cell's units, runs of at most 64 tiles
 // against at most 128 of its queries.
 __global__ void k_plan_units(const int32_t* __restrict__ cnt, const int32_t* __restrict__ info,
                              const int32_t* __restrict__ qstart, const int32_t* __restrict__ ustart, int nlist,
-                             ScanUnit* __restrict__ units0, ScanUnit* __restrict__ units1) {
+                             PassUnits tables) {
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     const int p = blockIdx.y;
     if (c >= nlist) return;
     const int qn = cnt[c];
-    const int32_t* g = info + 6 * c + (p == 0 ? 3 : 0);
+    const int32_t* g = info + 9 * c + 3 * p;
     const int tf = g[0], tiles = g[1], rend = g[2];
     if (qn == 0 || tiles == 0) return;
-    ScanUnit* out = (p == 0 ? units0 : units1) + ustart[p * nlist + c];
+    ScanUnit* out = tables.u[p] + ustart[p * nlist + c];
     int k = 0;
     for (int q0 = 0; q0 < qn; q0 += 128)
         for (int t0 = 0; t0 < tiles; t0 += kIvfMaxTilesPerUnit) {
@@ -494,70 +510,70 @@ __global__ void k_plan_units(const int32_t* __restrict__ cnt, const int32_t* __r
 // Per-cell planning facts, uploaded once per index.
 void build_ivf_plan_info(mdh_ivf* ix, cudaStream_t st) {
     const int nl = ix->nlist;
-    std::vector<int32_t> info((size_t)nl * 6);
+    std::vector<int32_t> info((size_t)nl * 9);
     std::vector<int32_t> order((size_t)nl);
+    const std::vector<int64_t>* starts[kIvfPasses] = {&ix->coarse_start, &ix->sample_start, &ix->cell_start};
+    const std::vector<int64_t>* counts[kIvfPasses] = {&ix->coarse_count, &ix->sample_count, &ix->cell_count};
     for (int c = 0; c < nl; c++) {
-        const int64_t fs = ix->cell_start[(size_t)c], fc = ix->cell_count[(size_t)c];
-        const int64_t ss = ix->sample_start[(size_t)c], sc = ix->sample_count[(size_t)c];
-        int32_t* f = info.data() + 6 * (size_t)c;
-        f[0] = (int32_t)(fs / kIvfTileRows);
-        f[1] = (int32_t)((fc + kIvfTileRows - 1) / kIvfTileRows);
-        f[2] = (int32_t)(fs + fc);
-        f[3] = (int32_t)(ss / kIvfTileRows);
-        f[4] = (int32_t)((sc + kIvfTileRows - 1) / kIvfTileRows);
-        f[5] = (int32_t)(ss + sc);
-        order[(size_t)c] = c;
-        for (int p = 0; p < 2; p++) {
-            const int64_t runs = ((p == 0 ? f[4] : f[1]) + kIvfMaxTilesPerUnit - 1) / kIvfMaxTilesPerUnit;
+        for (int p = 0; p < kIvfPasses; p++) {
+            const int64_t s0 = (*starts[p])[(size_t)c], cn = (*counts[p])[(size_t)c];
+            int32_t* f = info.data() + 9 * (size_t)c + 3 * p;
+            f[0] = (int32_t)(s0 / kIvfTileRows);
+            f[1] = (int32_t)((cn + kIvfTileRows - 1) / kIvfTileRows);
+            f[2] = (int32_t)(s0 + cn);
+            const int64_t runs = (f[1] + kIvfMaxTilesPerUnit - 1) / kIvfMaxTilesPerUnit;
             ix->unit_max_runs[p] = std::max(ix->unit_max_runs[p], runs);
             ix->unit_sum_runs[p] += runs;
         }
+        order[(size_t)c] = c;
     }
     // Most tiles first, so the persistent grid's tail is short.
     std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) {
-        return info[6 * (size_t)a + 1] > info[6 * (size_t)b + 1];
+        return info[9 * (size_t)a + 3 * (kIvfPasses - 1) + 1] > info[9 * (size_t)b + 3 * (kIvfPasses - 1) + 1];
     });
     ix->plan_info = dalloc<int32_t>(info.size());
     ix->plan_order = dalloc<int32_t>(order.size());
-    ix->plan_scratch = dalloc<int32_t>((size_t)6 * nl + 2);
-    ix->plan_pairs = dalloc<unsigned long long>(2);
+    ix->plan_scratch = dalloc<int32_t>((size_t)6 * nl + kIvfPasses);
+    ix->plan_pairs = dalloc<unsigned long long>(kIvfPasses);
     MDH_CUDA(cudaMemcpyAsync(ix->plan_info, info.data(), info.size() * 4, cudaMemcpyHostToDevice, st));
     MDH_CUDA(cudaMemcpyAsync(ix->plan_order, order.data(), order.size() * 4, cudaMemcpyHostToDevice, st));
     MDH_CUDA(cudaStreamSynchronize(st));
 }
 
-// Plans both passes for `total` = m * nprobe probes in ws.flags: the grouped
-// query matrix in pass[1] (g, gqn, gmap) and the unit tables of both passes,
-// whose lengths land in nunits[0..1] on the device.  Returns per-pass upper
+// Plans every pass for `total` = m * nprobe probes in ws.flags: the grouped
+// query matrix in pass[kIvfPasses - 1] (g, gqn, gmap) and the unit tables,
+// whose lengths land in nunits[pass] on the device.  Returns per-pass upper
 // bounds of the table lengths (they size the buffers and the grids).
-void plan_passes(mdh_ivf* ix, int m, int nprobe, cudaStream_t st, int64_t bound[2], int32_t** nunits) {
+void plan_passes(mdh_ivf* ix, int m, int nprobe, cudaStream_t st, int64_t bound[kIvfPasses], int32_t** nunits) {
     const int nl = ix->nlist;
     const int total = m * nprobe;
     Workspace& w = ix->ws;
     int32_t* cnt = ix->plan_scratch;
     int32_t* fill = cnt + nl;
     int32_t* qstart = fill + nl;
-    int32_t* ustart = qstart + nl;  // [2][nlist]
-    *nunits = ustart + 2 * nl;      // [2]
+    int32_t* ustart = qstart + nl;  // [kIvfPasses][nlist]
+    *nunits = ustart + kIvfPasses * nl;
     MDH_CUDA(cudaMemsetAsync(cnt, 0, (size_t)2 * nl * 4, st));
-    MDH_CUDA(cudaMemsetAsync(ix->plan_pairs, 0, 2 * sizeof(unsigned long long), st));
+    MDH_CUDA(cudaMemsetAsync(ix->plan_pairs, 0, kIvfPasses * sizeof(unsigned long long), st));
     k_plan_count<<<(total + 255) / 256, 256, 0, st>>>(w.flags, total, cnt);
     k_plan_scan<<<1, kPlanThreads, 0, st>>>(cnt, ix->plan_order, ix->plan_info, nl, qstart, ustart, *nunits,
                                             ix->plan_pairs);
-    IvfPassBufs& g = ix->pass[1];
+    IvfPassBufs& g = ix->pass[kIvfPasses - 1];
     grow_dev(&g.g, &g.g_bytes, (size_t)total * ix->dpad);
     grow_dev(&g.gqn, &g.gqn_bytes, (size_t)total * 4);
     grow_dev(&g.gmap, &g.gmap_bytes, (size_t)total * 4);
     k_plan_fill<<<(total + 255) / 256, 256, 0, st>>>(w.flags, total, nprobe, qstart, fill, g.gmap);
     launch_gather_queries_u8(w.q_u8, w.qn, g.gmap, total, ix->dpad, g.g, g.gqn, st);
     // sum_c ceil(q_c / 128) * runs_c <= sum_c (q_c / 128 + 1) * runs_c <= total * max_runs / 128 + sum_runs.
-    for (int p = 0; p < 2; p++) {
+    PassUnits tables;
+    for (int p = 0; p < kIvfPasses; p++) {
         bound[p] = std::max<int64_t>(1, ((int64_t)total * ix->unit_max_runs[p] + 127) / 128 + ix->unit_sum_runs[p]);
         MDH_REQUIRE(bound[p] < (int64_t(1) << 31), MDH_ERR_UNSUPPORTED, "IVF unit table too large");
         grow_dev(&ix->pass[p].units, &ix->pass[p].units_bytes, (size_t)bound[p] * sizeof(ScanUnit));
+        tables.u[p] = ix->pass[p].units;
     }
-    k_plan_units<<<dim3((unsigned)((nl + 255) / 256), 2), 256, 0, st>>>(cnt, ix->plan_info, qstart, ustart, nl,
-                                                                        ix->pass[0].units, ix->pass[1].units);
+    k_plan_units<<<dim3((unsigned)((nl + 255) / 256), kIvfPasses), 256, 0, st>>>(cnt, ix->plan_info, qstart, ustart,
+                                                                                 nl, tables);
     MDH_CUDA(cudaGetLastError());
 }
 
@@ -574,32 +590,27 @@ void check_ivf_device(int dev) {
     MDH_REQUIRE(p.major == 10 && p.minor == 0, MDH_ERR_CUDA, "this library is built for sm_100a (B200)");
 }
 
-// Per-cell samples in the main layout: rows whose id hashes below 1/32 plus
-// the first kIvfSampleHead rows of each cell, in the cell's norm order, each
+// Per-cell samples in the main layout: rows whose id hashes below `thresh`
+// plus the first `head` rows of each cell, in the cell's norm order, each
 // cell padded to whole tiles.
-void build_ivf_sample(mdh_ivf* ix, cudaStream_t st) {
+void build_ivf_sample(mdh_ivf* ix, const std::vector<int32_t>& ids, uint32_t thresh, int head, Level& sv,
+                      std::vector<int64_t>& start, std::vector<int64_t>& count, cudaStream_t st) {
     const Level& lv = ix->rows;
-    std::vector<int32_t> ids((size_t)lv.n_pad);
-    MDH_CUDA(cudaMemcpyAsync(ids.data(), lv.ids, ids.size() * 4, cudaMemcpyDeviceToHost, st));
-    MDH_CUDA(cudaStreamSynchronize(st));
     const int nl = ix->nlist;
-    ix->sample_start.assign((size_t)nl, 0);
-    ix->sample_count.assign((size_t)nl, 0);
+    start.assign((size_t)nl, 0);
+    count.assign((size_t)nl, 0);
     std::vector<int32_t> pos;
     for (int c = 0; c < nl; c++) {
-        ix->sample_start[(size_t)c] = (int64_t)pos.size();
+        start[(size_t)c] = (int64_t)pos.size();
         const int64_t s0 = ix->cell_start[(size_t)c], cnt = ix->cell_count[(size_t)c];
         for (int64_t r = s0; r < s0 + cnt; r++)
-            if (r - s0 < kIvfSampleHead || sample_hash_host(ids[(size_t)r]) < kIvfSampleThresh)
-                pos.push_back((int32_t)r);
-        const int64_t taken = (int64_t)pos.size() - ix->sample_start[(size_t)c];
-        ix->sample_count[(size_t)c] = taken;
+            if (r - s0 < head || sample_hash_host(ids[(size_t)r]) < thresh) pos.push_back((int32_t)r);
+        count[(size_t)c] = (int64_t)pos.size() - start[(size_t)c];
         while (pos.size() % kIvfTileRows) pos.push_back(-1);
     }
     if (pos.empty())
         for (int i = 0; i < kIvfTileRows; i++) pos.push_back(-1);
     const int64_t m = (int64_t)pos.size();
-    Level& sv = ix->sample;
     sv.n = m;
     sv.n_pad = m;
     sv.rows = dalloc<uint8_t>((size_t)m * ix->dpad);
@@ -615,6 +626,15 @@ void build_ivf_sample(mdh_ivf* ix, cudaStream_t st) {
     MDH_CUDA(e);
     MDH_CUDA(e2);
     make_tmap_rows(sv, ix->dpad);
+}
+
+void build_ivf_samples(mdh_ivf* ix, cudaStream_t st) {
+    const Level& lv = ix->rows;
+    std::vector<int32_t> ids((size_t)lv.n_pad);
+    MDH_CUDA(cudaMemcpyAsync(ids.data(), lv.ids, ids.size() * 4, cudaMemcpyDeviceToHost, st));
+    MDH_CUDA(cudaStreamSynchronize(st));
+    build_ivf_sample(ix, ids, kIvfSampleThresh, kIvfSampleHead, ix->sample, ix->sample_start, ix->sample_count, st);
+    build_ivf_sample(ix, ids, kIvfCoarseThresh, kIvfCoarseHead, ix->coarse, ix->coarse_start, ix->coarse_count, st);
 }
 
 void ivf_create(const uint8_t* host, int64_t n, int32_t dim, const float* centroids, int32_t nlist,
@@ -709,13 +729,14 @@ void ivf_create(const uint8_t* host, int64_t n, int32_t dim, const float* centro
         MDH_CUDA(cudaMemcpyAsync(ix->centroids, centroids, (size_t)nlist * dim * 4, cudaMemcpyHostToDevice, st));
         MDH_CUDA(cudaStreamSynchronize(st));
         make_tmap_rows(lv, dpad);
-        build_ivf_sample(ix.get(), st);
+        build_ivf_samples(ix.get(), st);
         build_ivf_plan_info(ix.get(), st);
     } catch (...) {
         cudaStreamSynchronize(st);
         release_tmp();
         free_level_buffers(ix->rows);
         free_level_buffers(ix->sample);
+        free_level_buffers(ix->coarse);
         if (ix->centroids) cudaFree(ix->centroids);
         for (void* p : {(void*)ix->plan_info, (void*)ix->plan_order, (void*)ix->plan_scratch, (void*)ix->plan_pairs})
             if (p) cudaFree(p);
@@ -777,11 +798,12 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         const int m = std::min(chunk, nq - c0);
         ivf_route_impl(ix, host_q + (size_t)c0 * ix->dim, m, nprobe, nullptr);
         s.kernel_launches += 3;
-        int64_t bound[2];
+        int64_t bound[kIvfPasses];
         int32_t* nunits = nullptr;
         plan_passes(ix, m, nprobe, st, bound, &nunits);
         const int total = m * nprobe;
         s.kernel_launches += 5;
+        const IvfPassBufs& qm = ix->pass[kIvfPasses - 1];  // the grouped query matrix
         grow_dev(&w.thr_key, &w.thr_key_bytes, (size_t)m * 4);
         grow_dev(&w.thr_id, &w.thr_id_bytes, (size_t)m * 4);
         grow_dev(&w.counts, &w.counts_bytes, (size_t)m * 4);
@@ -799,21 +821,29 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         }
         MDH_CUDA(cudaMemsetAsync(w.status, 0, 6 * sizeof(int32_t), st));
         unsigned long long* n_cand = reinterpret_cast<unsigned long long*>(w.status + 2);
-        // Pass 1: samples of the probed cells, infinite thresholds -> k-th entry thresholds.
+        // Pass 0: coarse samples of the probed cells, infinite thresholds; the
+        // k-th (key, id) is a threshold for the union (the sample is part of it).
         launch_fill_threshold(w.thr_key, w.thr_id, m, kKeyInf, kIdInf, st);
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
-        launch_filter_tc_u8_l2_units(ix->sample, ix->dpad, ix->pass[1].g, total, ix->pass[1].gmap, w.qn,
-                                     ix->pass[0].units, (int)bound[0], nunits, w.thr_key, w.thr_id, w.counts, w.cand,
-                                     kIvfCap1, w.status, st);
-        launch_select(w.counts, w.cand, kIvfCap1, ix->sample.ids, m, k, 0, w.thr_key, w.thr_id, w.out_key, w.out_id, w.qlist,
-                      w.status + 1, nullptr, nullptr, st);
-        s.kernel_launches += 3;
-        // Pass 2: every probed cell with those thresholds.
+        launch_filter_tc_u8_l2_units(ix->coarse, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[0].units,
+                                     (int)bound[0], nunits, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap0,
+                                     w.status, st);
+        launch_select(w.counts, w.cand, kIvfCap0, ix->coarse.ids, m, k, 0, w.thr_key, w.thr_id, w.out_key, w.out_id,
+                      w.qlist, w.status + 1, nullptr, nullptr, st);
+        // Pass 1: the samples with that threshold tighten it (a list that
+        // overflows keeps the k-th of what it stored: still a valid bound).
+        MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
+        launch_filter_tc_u8_l2_units(ix->sample, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[1].units,
+                                     (int)bound[1], nunits + 1, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap1,
+                                     w.status, st);
+        launch_select(w.counts, w.cand, kIvfCap1, ix->sample.ids, m, k, 0, w.thr_key, w.thr_id, w.out_key, w.out_id,
+                      w.qlist, w.status + 1, nullptr, nullptr, st);
+        s.kernel_launches += 6;
+        // Pass 2: every probed cell with that threshold.
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
         MDH_CUDA(cudaEventRecord(w.ev0, st));
-        launch_filter_tc_u8_l2_units(lv, ix->dpad, ix->pass[1].g, total, ix->pass[1].gmap, w.qn,
-                                     ix->pass[1].units, (int)bound[1], nunits + 1, w.thr_key, w.thr_id, w.counts,
-                                     w.cand, kIvfCap2, w.status, st);
+        launch_filter_tc_u8_l2_units(lv, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[2].units, (int)bound[2],
+                                     nunits + 2, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap2, w.status, st);
         MDH_CUDA(cudaEventRecord(w.ev1, st));
         launch_select(w.counts, w.cand, kIvfCap2, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id, w.qlist,
                       w.status + 1, nullptr, n_cand, st);
@@ -822,14 +852,14 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         // (the results are copied again after an overflow round).
         hkey.resize((size_t)m * k);
         hid.resize((size_t)m * k);
-        unsigned long long pairs[2] = {0, 0};
+        unsigned long long pairs[kIvfPasses] = {};
         MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 6 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
         MDH_CUDA(cudaMemcpyAsync(pairs, ix->plan_pairs, sizeof(pairs), cudaMemcpyDeviceToHost, st));
         MDH_CUDA(cudaMemcpyAsync(hkey.data(), w.out_key, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
         MDH_CUDA(cudaMemcpyAsync(hid.data(), w.out_id, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
         MDH_CUDA(cudaStreamSynchronize(st));
-        s.pairs_scored += (int64_t)(pairs[0] + pairs[1]);
-        s.full_scan_pairs += (int64_t)pairs[1];
+        s.pairs_scored += (int64_t)(pairs[0] + pairs[1] + pairs[2]);
+        s.full_scan_pairs += (int64_t)pairs[2];
         if (w.h_status[0] != kDevOk)
             throw Error(MDH_ERR_TIMEOUT, "IVF scan reported device status " + std::to_string(w.h_status[0]));
         {
@@ -844,13 +874,13 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
             MDH_REQUIRE(++rounds < 64, MDH_ERR_INTERNAL, "candidate overflow did not converge");
             MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
             MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
-            launch_filter_tc_u8_l2_units(lv, ix->dpad, ix->pass[1].g, total, ix->pass[1].gmap, w.qn,
-                                         ix->pass[1].units, (int)bound[1], nunits + 1, w.thr_key, w.thr_id,
-                                         w.counts, w.cand, kIvfCap2, w.status, st);
+            launch_filter_tc_u8_l2_units(lv, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[2].units,
+                                         (int)bound[2], nunits + 2, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap2,
+                                         w.status, st);
             launch_select(w.counts, w.cand, kIvfCap2, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id,
                           w.qlist, w.status + 1, nullptr, n_cand, st);
             s.kernel_launches += 2;
-            s.pairs_scored += (int64_t)pairs[1];
+            s.pairs_scored += (int64_t)pairs[2];
             MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 6 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
             MDH_CUDA(cudaMemcpyAsync(hkey.data(), w.out_key, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
             MDH_CUDA(cudaMemcpyAsync(hid.data(), w.out_id, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
@@ -868,7 +898,7 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
             if (out_dist) out_dist[(size_t)c0 * k + i] = hid[i] >= 0 ? (int32_t)hkey[i] : -1;
         }
     }
-    s.levels = 2;
+    s.levels = kIvfPasses;
     s.tensor_core_path = 1;
     s.latency_ms = std::chrono::duration<double, std::milli>(std::chrono::high_resolution_clock::now() - t_start).count();
     if (stats) *stats = s;
@@ -947,8 +977,10 @@ mdh_status mdh_ivf_destroy(mdh_ivf* index) {
         if (ix->stream) cudaStreamSynchronize(ix->stream);
         ix->pass[0].free_all();
         ix->pass[1].free_all();
+        ix->pass[2].free_all();
         free_level_buffers(ix->rows);
         free_level_buffers(ix->sample);
+        free_level_buffers(ix->coarse);
         if (ix->centroids) cudaFree(ix->centroids);
         for (void* p : {(void*)ix->plan_info, (void*)ix->plan_order, (void*)ix->plan_scratch, (void*)ix->plan_pairs})
             if (p) cudaFree(p);
