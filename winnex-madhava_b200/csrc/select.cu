@@ -346,15 +346,17 @@ __global__ void k_merge_topk(const uint32_t* __restrict__ key_all, const int32_t
     }
 }
 
+// One thread per 16-byte piece of a gathered row (dpad is a multiple of 16).
 __global__ void k_gather_queries_u8(const uint8_t* __restrict__ src, const int32_t* __restrict__ qn_src,
                                     const int32_t* __restrict__ list, int m, int dpad, uint8_t* __restrict__ dst,
                                     int32_t* __restrict__ qn_dst) {
-    int i = blockIdx.x;
-    if (i >= m) return;
-    int s = list[i];
-    for (int b = threadIdx.x * 16; b < dpad; b += blockDim.x * 16)
-        *reinterpret_cast<uint4*>(dst + (size_t)i * dpad + b) = *reinterpret_cast<const uint4*>(src + (size_t)s * dpad + b);
-    if (threadIdx.x == 0) qn_dst[i] = qn_src[s];
+    const int per_row = dpad >> 4;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (int64_t)m * per_row) return;
+    const int i = (int)(t / per_row), b = (int)(t - (int64_t)i * per_row) * 16;
+    const int s = list[i];
+    *reinterpret_cast<uint4*>(dst + (size_t)i * dpad + b) = *reinterpret_cast<const uint4*>(src + (size_t)s * dpad + b);
+    if (b == 0) qn_dst[i] = qn_src[s];
 }
 
 size_t select_smem(int P) { return (size_t)P * sizeof(unsigned long long); }
@@ -424,7 +426,9 @@ void launch_merge_topk(const uint32_t* key_all, const int32_t* id_all, int nshar
 void launch_gather_queries_u8(const uint8_t* src, const int32_t* qn_src, const int32_t* list, int m, int dpad,
                               uint8_t* dst, int32_t* qn_dst, cudaStream_t st) {
     if (m <= 0) return;
-    k_gather_queries_u8<<<m, 64, 0, st>>>(src, qn_src, list, m, dpad, dst, qn_dst);
+    MDH_REQUIRE(dpad % 16 == 0, MDH_ERR_INTERNAL, "query rows must be 16-byte multiples");
+    const int64_t pieces = (int64_t)m * (dpad / 16);
+    k_gather_queries_u8<<<(unsigned)((pieces + 255) / 256), 256, 0, st>>>(src, qn_src, list, m, dpad, dst, qn_dst);
     MDH_CUDA(cudaGetLastError());
 }
 
