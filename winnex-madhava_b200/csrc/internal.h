@@ -138,7 +138,10 @@ void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const i
 // qmap[i]; thresholds, norms and candidate lists are indexed by that query)
 // against corpus tiles [t0, t1) of 256 rows, rows at or past row_end masked.
 // n_units bounds the table (it sizes the grid); when n_units_dev is given the
-// kernel reads the table's length from it (tables built on the device).
+// kernel reads the table's length from it (tables built on the device).  When
+// unit_counter is given (one int of device memory, reset by the launch), the
+// CTAs take units in table order as each finishes its previous one, instead
+// of fixed shares.
 struct ScanUnit {
     int32_t q_row;
     int32_t q_count;   // <= 128
@@ -148,8 +151,8 @@ struct ScanUnit {
 };
 void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat, int qmat_rows, const int32_t* qmap,
                                   const int32_t* qn, const ScanUnit* units, int n_units, const int32_t* n_units_dev,
-                                  const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts, uint2* cand,
-                                  int cap, int32_t* status, cudaStream_t st);
+                                  int32_t* unit_counter, const uint32_t* thr_key, const int32_t* thr_id,
+                                  uint32_t* counts, uint2* cand, int cap, int32_t* status, cudaStream_t st);
 // ---- tensor-core scan on SM pairs (scan_tc2.cu) ----
 bool tc2_supported(const mdh_index* ix, const Level& lv);
 void make_tmap_rows_pair(Level& lv, int dpad);

@@ -84,7 +84,7 @@ struct mdh_ivf {
     // offsets of each pass, table lengths) and pair counts.
     int32_t* plan_info = nullptr;        // [nlist][3 passes][3]
     int32_t* plan_order = nullptr;       // [nlist]
-    int32_t* plan_scratch = nullptr;     // [6 * nlist + 3]
+    int32_t* plan_scratch = nullptr;     // [6 * nlist + 3 + 1]
     unsigned long long* plan_pairs = nullptr;  // [3]
     int64_t unit_max_runs[3] = {0, 0, 0};  // per pass: max over cells of ceil(tiles / 64)
     int64_t unit_sum_runs[3] = {0, 0, 0};  // per pass: sum over cells of ceil(tiles / 64)
@@ -533,7 +533,7 @@ void build_ivf_plan_info(mdh_ivf* ix, cudaStream_t st) {
     });
     ix->plan_info = dalloc<int32_t>(info.size());
     ix->plan_order = dalloc<int32_t>(order.size());
-    ix->plan_scratch = dalloc<int32_t>((size_t)6 * nl + kIvfPasses);
+    ix->plan_scratch = dalloc<int32_t>((size_t)6 * nl + kIvfPasses + 1);  // + the scans' unit counter
     ix->plan_pairs = dalloc<unsigned long long>(kIvfPasses);
     MDH_CUDA(cudaMemcpyAsync(ix->plan_info, info.data(), info.size() * 4, cudaMemcpyHostToDevice, st));
     MDH_CUDA(cudaMemcpyAsync(ix->plan_order, order.data(), order.size() * 4, cudaMemcpyHostToDevice, st));
@@ -801,6 +801,7 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         int64_t bound[kIvfPasses];
         int32_t* nunits = nullptr;
         plan_passes(ix, m, nprobe, st, bound, &nunits);
+        int32_t* ucounter = nunits + kIvfPasses;  // the scans hand out units at run time, longest cells first
         const int total = m * nprobe;
         s.kernel_launches += 5;
         const IvfPassBufs& qm = ix->pass[kIvfPasses - 1];  // the grouped query matrix
@@ -826,7 +827,7 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         launch_fill_threshold(w.thr_key, w.thr_id, m, kKeyInf, kIdInf, st);
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
         launch_filter_tc_u8_l2_units(ix->coarse, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[0].units,
-                                     (int)bound[0], nunits, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap0,
+                                     (int)bound[0], nunits, ucounter, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap0,
                                      w.status, st);
         launch_select(w.counts, w.cand, kIvfCap0, ix->coarse.ids, m, k, 0, w.thr_key, w.thr_id, w.out_key, w.out_id,
                       w.qlist, w.status + 1, nullptr, nullptr, st);
@@ -834,7 +835,7 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         // overflows keeps the k-th of what it stored: still a valid bound).
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
         launch_filter_tc_u8_l2_units(ix->sample, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[1].units,
-                                     (int)bound[1], nunits + 1, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap1,
+                                     (int)bound[1], nunits + 1, ucounter, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap1,
                                      w.status, st);
         launch_select(w.counts, w.cand, kIvfCap1, ix->sample.ids, m, k, 0, w.thr_key, w.thr_id, w.out_key, w.out_id,
                       w.qlist, w.status + 1, nullptr, nullptr, st);
@@ -843,7 +844,8 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
         MDH_CUDA(cudaEventRecord(w.ev0, st));
         launch_filter_tc_u8_l2_units(lv, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[2].units, (int)bound[2],
-                                     nunits + 2, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap2, w.status, st);
+                                     nunits + 2, ucounter, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap2,
+                                     w.status, st);
         MDH_CUDA(cudaEventRecord(w.ev1, st));
         launch_select(w.counts, w.cand, kIvfCap2, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id, w.qlist,
                       w.status + 1, nullptr, n_cand, st);
@@ -875,7 +877,7 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
             MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
             MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
             launch_filter_tc_u8_l2_units(lv, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[2].units,
-                                         (int)bound[2], nunits + 2, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap2,
+                                         (int)bound[2], nunits + 2, ucounter, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap2,
                                          w.status, st);
             launch_select(w.counts, w.cand, kIvfCap2, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id,
                           w.qlist, w.status + 1, nullptr, n_cand, st);

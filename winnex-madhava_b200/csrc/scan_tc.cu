@@ -38,7 +38,9 @@
 //
 // Work units: (query group, corpus chunk), ordered chunk-major so the CTAs
 // running at the same time share corpus chunks through L2; each CTA takes
-// units blockIdx.x, blockIdx.x + gridDim.x, ...
+// units blockIdx.x, blockIdx.x + gridDim.x, ...  Unit tables (IVF) have
+// units of unequal length; given a counter, their units are handed out at
+// run time instead (feed_publish).
 //
 // Every mbarrier wait is bounded.  On expiry the kernel writes kDevTimeout to
 // *status, raises a shared abort flag so every role leaves its loop, drains
@@ -91,8 +93,11 @@ struct TcCfg {
     static constexpr uint32_t OFF_BAR = OFF_BUF + BUFN * EPI_THREADS * 8;
     static constexpr uint32_t BAR_FULL = 0, BAR_EMPTY = STAGES, BAR_ACC_FULL = 2 * STAGES,
                               BAR_ACC_EMPTY = 2 * STAGES + ACC_STAGES, BAR_A_FULL = 2 * STAGES + 2 * ACC_STAGES,
-                              BAR_A_EMPTY = BAR_A_FULL + 1, BAR_DRAIN = BAR_A_FULL + 2, NUM_BARS = BAR_A_FULL + 3;
-    static constexpr uint32_t OFF_TMEM_SLOT = OFF_BAR + NUM_BARS * 8;
+                              BAR_A_EMPTY = BAR_A_FULL + 1, BAR_DRAIN = BAR_A_FULL + 2,
+                              BAR_UNIT_FULL = BAR_A_FULL + 3, BAR_UNIT_EMPTY = BAR_UNIT_FULL + 2,
+                              NUM_BARS = BAR_UNIT_EMPTY + 2;
+    static constexpr uint32_t OFF_USLOT = OFF_BAR + NUM_BARS * 8;  // two unit indices handed out at run time
+    static constexpr uint32_t OFF_TMEM_SLOT = OFF_USLOT + 8;
     static constexpr uint32_t OFF_ABORT = OFF_TMEM_SLOT + 4;
     static constexpr uint32_t SMEM_BYTES = OFF_ABORT + 4 + 1024;  // + alignment slack
     static_assert(ACC_COLS == 4 * COLS_PER_WARP && ACC_STAGES >= 2, "four 64-column parts per accumulator stage");
@@ -171,6 +176,42 @@ __device__ __forceinline__ void chunk_filter(const uint32_t (&v)[32], int32_t ne
     }
 }
 
+// Run-time hand-out of a unit table (its units differ in length, so fixed
+// shares leave some SMs idle at the end).  The producer takes the next index
+// from a global counter and publishes it in one of two shared-memory slots
+// (UNIT_FULL); the MMA issuer and the 16 epilogue warps read it and release
+// the slot (UNIT_EMPTY, 17 arrivals).  An index past the table ends the CTA's
+// work.  Both return 1 with a unit, 0 when there are no more, -1 on abort.
+__device__ __forceinline__ int feed_publish(int32_t* counter, long long n_units, volatile int32_t* slots,
+                                            uint32_t bar_full, uint32_t bar_empty, int& s, uint32_t& ph,
+                                            long long& u, volatile int32_t* abort_flag, int32_t* status) {
+    if (!mbar_wait<false>(bar_empty + 8 * s, ph ^ 1, abort_flag, status)) return -1;
+    const int got = atomicAdd(counter, 1);
+    u = got < n_units ? got : -1;
+    slots[s] = (int32_t)u;
+    mbar_arrive(bar_full + 8 * s);  // release: the slot is visible to the readers
+    if (++s == 2) {
+        s = 0;
+        ph ^= 1;
+    }
+    return u >= 0 ? 1 : 0;
+}
+// whole_warp: every lane of an epilogue warp calls it; else the single
+// MMA-issuing thread.
+__device__ __forceinline__ int feed_take(bool whole_warp, volatile int32_t* slots, uint32_t bar_full,
+                                         uint32_t bar_empty, int& s, uint32_t& ph, long long& u,
+                                         volatile int32_t* abort_flag, int32_t* status) {
+    if (!mbar_wait_inl<false>(bar_full + 8 * s, ph, abort_flag, status)) return -1;
+    u = slots[s];
+    if (whole_warp) __syncwarp();
+    if (!whole_warp || (threadIdx.x & 31) == 0) mbar_arrive(bar_empty + 8 * s);
+    if (++s == 2) {
+        s = 0;
+        ph ^= 1;
+    }
+    return u >= 0 ? 1 : 0;
+}
+
 // UNITS: the unit-table form.  Its query rows are different queries probing
 // one cell, whose passing columns rarely coincide, so its slow path walks
 // each lane's own columns (reading the row norm from memory); the schedule
@@ -184,7 +225,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                       const int32_t* __restrict__ thr_id, uint32_t* __restrict__ counts, uint2* __restrict__ cand,
                       int cap, int dense, Sched sched, int32_t* __restrict__ status,
                       const ScanUnit* __restrict__ units, const int32_t* __restrict__ qmap,
-                      const int32_t* __restrict__ n_units_dev) {
+                      const int32_t* __restrict__ n_units_dev, int32_t* __restrict__ unit_counter) {
     constexpr int BN = C::BN, QT = C::QT, STAGES = C::STAGES, ACC_STAGES = C::ACC_STAGES;
     // A unit table built on the device carries its own length.
     const long long n_units = n_units_dev ? (long long)*n_units_dev : sched.n_units;
@@ -209,6 +250,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mbar_init(bars + 8 * C::BAR_A_FULL, 1);
         mbar_init(bars + 8 * C::BAR_A_EMPTY, 1);
         mbar_init(bars + 8 * C::BAR_DRAIN, 1);
+        for (int s = 0; s < 2; s++) {
+            mbar_init(bars + 8 * (C::BAR_UNIT_FULL + s), 1);
+            mbar_init(bars + 8 * (C::BAR_UNIT_EMPTY + s), EPI_WARPS + 1);
+        }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -218,6 +263,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Unit hand-out (unit tables with a counter only); see feed_publish.
+    const bool dyn = UNITS && unit_counter != nullptr;
+    volatile int32_t* uslots = reinterpret_cast<volatile int32_t*>(smem + C::OFF_USLOT);
+    const uint32_t ubar_full = bars + 8 * C::BAR_UNIT_FULL, ubar_empty = bars + 8 * C::BAR_UNIT_EMPTY;
+    int us = 0;
+    uint32_t uph = 0;
 
     if (warp == PRODUCER_WARP) {
         // ------------------------------------------------------------ TMA producer
@@ -229,7 +280,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t issued_mask = 0, last_parity = 0;
             bool a_issued = false;
             bool ok = true;
-            for (long long u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+            for (long long u = blockIdx.x;; u += gridDim.x) {
+                if (!ok) break;
+                if (dyn) {
+                    const int r = feed_publish(unit_counter, n_units, uslots, ubar_full, ubar_empty, us, uph, u, abort_flag, status);
+                    if (r < 0) ok = false;
+                    if (r <= 0) break;
+                } else if (u >= n_units) {
+                    break;
+                }
                 const UnitView uv = unit_view<C, UNITS>(sched, units, u, n_rows, nq);
                 const int t0 = uv.t0, t1 = uv.t1;
                 ok = mbar_wait<false>(bars + 8 * C::BAR_A_EMPTY, (a_iter & 1) ^ 1, abort_flag, status);
@@ -276,7 +335,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0, a_iter = 0;
             bool ok = true, issued = false;
-            for (long long u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+            for (long long u = blockIdx.x;; u += gridDim.x) {
+                if (!ok) break;
+                if (dyn) {
+                    const int r = feed_take(false, uslots, ubar_full, ubar_empty, us, uph, u, abort_flag, status);
+                    if (r < 0) ok = false;
+                    if (r <= 0) break;
+                } else if (u >= n_units) {
+                    break;
+                }
                 const UnitView uv = unit_view<C, UNITS>(sched, units, u, n_rows, nq);
                 const int t0 = uv.t0, t1 = uv.t1;
                 ok = mbar_wait<false>(bars + 8 * C::BAR_A_FULL, a_iter & 1, abort_flag, status);
@@ -350,7 +417,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int acc = 0;  // accumulator stage of the CTA's next tile
         uint32_t ph0 = 0, ph1 = 0;
         bool ok = true;
-        for (long long u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        for (long long u = blockIdx.x;; u += gridDim.x) {
+            if (!ok) break;
+            if (dyn) {
+                const int r = feed_take(true, uslots, ubar_full, ubar_empty, us, uph, u, abort_flag, status);
+                if (r < 0) ok = false;
+                if (r <= 0) break;
+            } else if (u >= n_units) {
+                break;
+            }
             const UnitView uv = unit_view<C, UNITS>(sched, units, u, n_rows, nq);
             const int t0 = uv.t0, t1 = uv.t1, row_end = uv.row_end;
             const int qlocal = quarter * 32 + lane;
@@ -440,7 +515,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t acc_phase = 0;
         bool ok = true;
         const int32_t* nrm = norms + rowoff;
-        for (long long u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        for (long long u = blockIdx.x;; u += gridDim.x) {
+            if (!ok) break;
+            if (dyn) {
+                const int r = feed_take(true, uslots, ubar_full, ubar_empty, us, uph, u, abort_flag, status);
+                if (r < 0) ok = false;
+                if (r <= 0) break;
+            } else if (u >= n_units) {
+                break;
+            }
             const UnitView uv = unit_view<C, UNITS>(sched, units, u, n_rows, nq);
             const int t0 = uv.t0, t1 = uv.t1, row_end = uv.row_end;
             const int qlocal = qt * BM + quarter * 32 + lane;
@@ -623,7 +706,7 @@ void launch_tc(const Level& lv, const CUtensorMap& tq, const int32_t* qn, int nq
                                   (int)C::SMEM_BYTES));
     k_filter_tc_u8_l2<C, false><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
                                                                    qn, nq, thr_key, thr_id, counts, cand, cap, dense,
-                                                                   s, status, nullptr, nullptr, nullptr);
+                                                                   s, status, nullptr, nullptr, nullptr, nullptr);
     MDH_CUDA(cudaGetLastError());
 }
 
@@ -640,8 +723,8 @@ void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const i
 
 void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat, int qmat_rows, const int32_t* qmap,
                                   const int32_t* qn, const ScanUnit* units, int n_units, const int32_t* n_units_dev,
-                                  const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts, uint2* cand,
-                                  int cap, int32_t* status, cudaStream_t st) {
+                                  int32_t* unit_counter, const uint32_t* thr_key, const int32_t* thr_id,
+                                  uint32_t* counts, uint2* cand, int cap, int32_t* status, cudaStream_t st) {
     using C = CfgNarrow;
     if (n_units <= 0 || qmat_rows <= 0 || lv.n == 0) return;
     MDH_REQUIRE(dpad == BK && lv.has_tmap, MDH_ERR_INTERNAL, "tensor-core scan needs 128-byte rows and a TMA map");
@@ -652,11 +735,13 @@ void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat
     Sched s{};
     s.n_units = n_units;
     const int ctas = std::min(device_sm_count(dev), n_units);
+    if (unit_counter) MDH_CUDA(cudaMemsetAsync(unit_counter, 0, sizeof(int32_t), st));
     MDH_CUDA(cudaFuncSetAttribute(k_filter_tc_u8_l2<C, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)C::SMEM_BYTES));
     k_filter_tc_u8_l2<C, true><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
                                                                    qn, qmat_rows, thr_key, thr_id, counts, cand, cap,
-                                                                   0, s, status, units, qmap, n_units_dev);
+                                                                   0, s, status, units, qmap, n_units_dev,
+                                                                   unit_counter);
     MDH_CUDA(cudaGetLastError());
 }
 
