@@ -293,6 +293,164 @@ __global__ void __launch_bounds__(32 * kWarpSelectWarps)
     }
 }
 
+// The same contract for kWarpSelectK < k <= kWarpSelectBigK, one warp per
+// query.  A lane's 8 smallest keys (keys only, no ids) form, over the warp,
+// a set U of min(c, 256) entries of the list; its k-th smallest key tau is at
+// least the list's k-th smallest key, so every entry of the top k has a key
+// <= tau.  The entries with key <= tau (usually little more than k) are
+// collected with their ids into shared memory and sorted there (bitonic).
+// If more than kBigBuf of them exist (many equal keys), the k smallest are
+// instead taken one at a time by warp minima over the list.
+constexpr int kWarpSelectBigK = 128;
+constexpr int kBigT = 8;                // keys kept per lane in the first pass
+constexpr int kBigWarps = 4;            // queries per 128-thread block
+constexpr int kBigBuf = 1024;           // collected entries per warp (8 KB)
+static_assert(kWarpSelectBigK <= 32 * kBigT, "the first pass keeps at least k keys");
+
+__global__ void __launch_bounds__(32 * kBigWarps)
+    k_select_warp_big(const uint32_t* __restrict__ counts, const uint2* __restrict__ cand, int cap,
+                      const int32_t* __restrict__ ids, int nq, int k, int final_, uint32_t* __restrict__ thr_key,
+                      int32_t* __restrict__ thr_id, uint32_t* __restrict__ out_key, int32_t* __restrict__ out_id,
+                      int32_t* __restrict__ flags, int32_t* __restrict__ n_flagged, const int32_t* __restrict__ qmap,
+                      unsigned long long* __restrict__ n_cand) {
+    __shared__ unsigned long long bufs[kBigWarps][kBigBuf];
+    const int wq = (int)(threadIdx.x >> 5);
+    const int q = blockIdx.x * kBigWarps + wq;
+    const int lane = threadIdx.x & 31;
+    if (q >= nq) return;  // whole warps leave together
+    unsigned long long* buf = bufs[wq];
+    const int qo = qmap ? qmap[q] : q;
+    const uint32_t c_all = counts[q];
+    const int c = (int)(c_all < (uint32_t)cap ? c_all : (uint32_t)cap);
+    const uint2* src = cand + (size_t)q * cap;
+    // Pass 1: this lane's kBigT smallest keys, ascending (empty slots hold 2^32).
+    unsigned long long t[kBigT];
+#pragma unroll
+    for (int j = 0; j < kBigT; j++) t[j] = 1ull << 32;
+    for (int i = lane; i < c; i += 32) {
+        const unsigned long long v = src[i].x;
+        if (v >= t[kBigT - 1]) continue;
+#pragma unroll
+        for (int j = kBigT - 1; j > 0; j--) t[j] = t[j - 1] > v ? t[j - 1] : (t[j] > v ? v : t[j]);
+        t[0] = t[0] > v ? v : t[0];
+    }
+    // tau: the k-th smallest of the warp's kept keys (all keys when c < k).
+    unsigned long long tau = 1ull << 32;
+    if (c >= k) {
+        for (int r = 0; r < k; r++) {
+            unsigned long long m = t[0];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xffffffffu, m, o);
+                m = other < m ? other : m;
+            }
+            const unsigned own = __ballot_sync(0xffffffffu, t[0] == m);
+            if (lane == __ffs(own) - 1) {
+#pragma unroll
+                for (int j = 0; j < kBigT - 1; j++) t[j] = t[j + 1];
+                t[kBigT - 1] = 1ull << 32;
+            }
+            tau = m;
+        }
+    }
+    // Pass 2: collect the entries with key <= tau, with their ids.
+    int n = 0;  // entries found (may exceed kBigBuf)
+    for (int i0 = 0; i0 < c; i0 += 32) {
+        const int i = i0 + lane;
+        bool take = false;
+        uint2 e = make_uint2(0u, 0u);
+        if (i < c) {
+            e = src[i];
+            take = (unsigned long long)e.x <= tau;
+        }
+        const unsigned b = __ballot_sync(0xffffffffu, take);
+        const int pos = n + __popc(b & ((1u << lane) - 1u));
+        if (take && pos < kBigBuf) buf[pos] = ((unsigned long long)e.x << 32) | (uint32_t)__ldg(ids + e.y);
+        n += __popc(b);
+    }
+    __syncwarp();
+    const int kk = c < k ? c : k;  // entries of the result
+    if (n <= kBigBuf) {
+        // Bitonic sort of buf[0, P), P = next power of two >= n, padded with the largest key.
+        int P = 1;
+        while (P < n) P <<= 1;
+        for (int i = n + lane; i < P; i += 32) buf[i] = ~0ull;
+        __syncwarp();
+        for (int size = 2; size <= P; size <<= 1)
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                for (int i = lane; i < (P >> 1); i += 32) {
+                    const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+                    const bool asc = (lo & size) == 0;
+                    const unsigned long long a = buf[lo], b = buf[hi];
+                    if ((a > b) == asc) {
+                        buf[lo] = b;
+                        buf[hi] = a;
+                    }
+                }
+                __syncwarp();
+            }
+    } else {
+        // Many entries share keys <= tau: take the k smallest (key, id) one at a
+        // time; round r finds the smallest entry above round r-1's.
+        unsigned long long prev = 0;
+        for (int r = 0; r < kk; r++) {
+            unsigned long long best = ~0ull;
+            for (int i = lane; i < c; i += 32) {
+                const uint2 e = src[i];
+                if ((unsigned long long)e.x > tau || ((unsigned long long)e.x << 32) > best) continue;
+                const unsigned long long v = ((unsigned long long)e.x << 32) | (uint32_t)__ldg(ids + e.y);
+                if ((r == 0 || v > prev) && v < best) best = v;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+                best = other < best ? other : best;
+            }
+            if (lane == 0) buf[r] = best;
+            prev = best;
+        }
+        __syncwarp();
+    }
+    if (!final_) {
+        if (lane == 0) {
+            if (c >= k) {
+                thr_key[qo] = (uint32_t)(buf[k - 1] >> 32);
+                thr_id[qo] = (int32_t)(buf[k - 1] & 0xffffffffu);
+            } else {
+                // Fewer than k rows in this level: every row of the next
+                // level stays a candidate.
+                thr_key[qo] = kKeyInf;
+                thr_id[qo] = kIdInf;
+            }
+        }
+        return;
+    }
+    if (c_all > (uint32_t)cap) {
+        // Overflow: the stored lists are a subset; their k-th key is a valid
+        // (tighter) threshold for a rerun.  c == cap >= k here.
+        if (lane == 0) {
+            flags[qo] = 1;
+            thr_key[qo] = (uint32_t)(buf[k - 1] >> 32);
+            thr_id[qo] = (int32_t)(buf[k - 1] & 0xffffffffu);
+            atomicAdd(n_flagged, 1);
+        }
+        return;
+    }
+    for (int j = lane; j < k; j += 32) {
+        if (j < kk) {
+            out_key[(size_t)qo * k + j] = (uint32_t)(buf[j] >> 32);
+            out_id[(size_t)qo * k + j] = (int32_t)(buf[j] & 0xffffffffu);
+        } else {
+            out_key[(size_t)qo * k + j] = kKeyInf;
+            out_id[(size_t)qo * k + j] = -1;
+        }
+    }
+    if (lane == 0) {
+        if (flags) flags[qo] = 0;
+        if (n_cand) atomicAdd(n_cand, (unsigned long long)c);
+    }
+}
+
 // Verification: query i of a compact list gets the threshold (key, id) of the
 // kk-th entry of its result (an empty entry, id -1, means no threshold).
 __global__ void k_verify_thresholds(const int32_t* __restrict__ list, int m, const uint32_t* __restrict__ out_key,
@@ -382,6 +540,12 @@ void launch_select(const uint32_t* counts, const uint2* cand, int cap, const int
     if (nq <= 0) return;
     if (k >= 1 && k <= kWarpSelectK) {
         k_select_warp<<<(nq + kWarpSelectWarps - 1) / kWarpSelectWarps, 32 * kWarpSelectWarps, 0, st>>>(
+            counts, cand, cap, ids, nq, k, final_, thr_key, thr_id, out_key, out_id, flags, n_flagged, qmap, n_cand);
+        MDH_CUDA(cudaGetLastError());
+        return;
+    }
+    if (k <= kWarpSelectBigK) {
+        k_select_warp_big<<<(nq + kBigWarps - 1) / kBigWarps, 32 * kBigWarps, 0, st>>>(
             counts, cand, cap, ids, nq, k, final_, thr_key, thr_id, out_key, out_id, flags, n_flagged, qmap, n_cand);
         MDH_CUDA(cudaGetLastError());
         return;
