@@ -88,6 +88,24 @@ def test_ivf_edge_cells_and_batches():
     assert L.mdh_ivf_destroy(h) == 0
 
 
+def test_ivf_all_keys_tied_large_k():
+    """40,000 equal rows in one cell: the last pass's candidate lists hold
+    ~2,000 entries with the same key, more than the large-k selection keeps in
+    shared memory, so it takes the k smallest (key, id) one at a time."""
+    L = capi()
+    C = np.full((40_000, 128), 7, np.uint8)
+    # Routing takes the largest inner product: the query goes to cell 0.
+    cen = np.stack([np.full(128, 200.0), np.full(128, 7.0)]).astype(np.float32)
+    labels = np.zeros(len(C), np.int32)  # cell 1 stays empty
+    h = _ivf(L, C, cen, labels)
+    Q = np.full((3, 128), 7, np.uint8)
+    for k in (64, 128):
+        ids, dist, _ = _search(L, h, Q, k, 1)
+        np.testing.assert_array_equal(ids, np.tile(np.arange(k, dtype=np.int32), (3, 1)))
+        np.testing.assert_array_equal(dist, 0)
+    assert L.mdh_ivf_destroy(h) == 0
+
+
 def test_ivf_rejects_bad_input():
     L = capi()
     C = np.zeros((100, 16), np.uint8)

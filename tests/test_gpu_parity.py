@@ -165,6 +165,11 @@ def test_all_equal_rows_and_edge_shapes():
     C = np.full((3000, 32), 7, np.uint8)
     ids = _run_exact(C, np.full((2, 32), 7, np.float32), 16, wm.Metric.L2)
     np.testing.assert_array_equal(ids, [list(range(16))] * 2)
+    # k in (16, 128] with every key tied: more than 1,024 entries share the
+    # bound, so the selection takes the k smallest (key, id) one at a time.
+    for k in (64, 128):
+        ids = _run_exact(C, np.full((2, 32), 7, np.float32), k, wm.Metric.L2)
+        np.testing.assert_array_equal(ids, [list(range(k))] * 2)
     # k > n and k == n
     C = np.random.default_rng(0).integers(0, 256, (6, 16), dtype=np.uint8)
     Q = C[:2].astype(np.float32)
