@@ -99,6 +99,8 @@ def load_lib():
     L.mdh_ivf_create_u8.argtypes = [P, i64, i32, P, i32, P, i32, ctypes.POINTER(P)]
     L.mdh_ivf_search_u8.argtypes = [P, P, i32, i32, i32, P, P, ctypes.POINTER(Stats)]
     L.mdh_ivf_destroy.argtypes = [P]
+    L.mdh_index_save.argtypes = [P, ctypes.c_char_p]
+    L.mdh_index_load.argtypes = [ctypes.c_char_p, P, i32, ctypes.POINTER(P)]
     L.mdh_index_create_f32.argtypes = [P, i64, i32, i32, P, i32, i64, ctypes.POINTER(P)]
     L.mdh_index_create_f32.restype = ctypes.c_int
     L.mdh_search_f32.argtypes = [P, P, i32, i32, i32, P, P, ctypes.POINTER(Stats)]
@@ -315,6 +317,121 @@ def run_ivf(args, torch, device, L, warmup):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- index files
+def run_persist(args, torch, device, L):
+    """Index files: build a 10M x 128 u8 index from host rows, save it, load it
+    back twice (from the disk after dropping the file's cached pages, then from
+    the page cache) and check that the loaded index answers 1,000 queries
+    exactly as the built one."""
+    import shutil
+    import tempfile
+
+    n = args.n if args.n != N_DEFAULT else 10_000_000
+    rows = make_rows_gpu(torch, 0, n, device, args.comps)
+    host = rows.cpu().numpy()
+    del rows
+    torch.cuda.empty_cache()
+    h = ctypes.c_void_p()
+    t0 = time.perf_counter()
+    check(L, L.mdh_index_create_u8(ctypes.c_void_p(host.ctypes.data), n, DIM, 1, None, 0, 0, ctypes.byref(h)), "build")
+    build_s = time.perf_counter() - t0
+    tmp = tempfile.mkdtemp(prefix="mdh_index_")
+    path = os.path.join(tmp, "index.mdh")
+    try:
+        t0 = time.perf_counter()
+        check(L, L.mdh_index_save(h, path.encode()), "save")
+        save_s = time.perf_counter() - t0
+        size = os.path.getsize(path)
+        # The storage ceiling: the same file read by 8 threads in 8 MB pieces
+        # (the library's own I/O shape) into host memory, after dropping its
+        # cached pages, then again from the page cache.
+        raw = [plain_read_seconds(path, size), plain_read_seconds(path, size, drop=False)]
+        loads = []
+        for i in range(2):
+            if i == 0:
+                drop_cached_pages(path)
+            h2 = ctypes.c_void_p()
+            t0 = time.perf_counter()
+            check(L, L.mdh_index_load(path.encode(), None, 0, ctypes.byref(h2)), "load")
+            loads.append(time.perf_counter() - t0)
+            if len(loads) < 2:
+                check(L, L.mdh_index_destroy(h2), "destroy")
+        m = 1000
+        queries = make_queries(m, args.comps)
+        out = []
+        for hx in (h, h2):
+            ids = np.empty((m, args.k), np.int32)
+            dd = np.empty((m, args.k), np.int32)
+            check(L, L.mdh_search_u8(hx, ctypes.c_void_p(queries.ctypes.data), m, args.k,
+                                     ctypes.c_void_p(ids.ctypes.data), ctypes.c_void_p(dd.ctypes.data), None), "search")
+            out.append((ids, dd))
+        same = bool(np.array_equal(out[0][0], out[1][0]) and np.array_equal(out[0][1], out[1][1]))
+        check(L, L.mdh_index_destroy(h2), "destroy")
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    check(L, L.mdh_index_destroy(h), "destroy")
+    line = {
+        "metric": f"index file load throughput, {n // 1_000_000}M x {DIM} u8 (file bytes / load time)",
+        "value": size / loads[0] / 1e9, "unit": "GB/s", "n_gpus": 1, "steps": 1, "warmup": 0,
+        "higher_is_better": True, "dtype": "u8", "data": "synthetic",
+        "config": {"workload": f"{n} x {DIM} u8 clipped-GMM ({args.comps} comps) index: build from host rows, "
+                               f"save, load", "file_bytes": size, "build_from_host_s": round(build_s, 3),
+                   "save_s": round(save_s, 3), "save_GBps": round(size / save_s / 1e9, 2),
+                   "load_after_page_drop_s": round(loads[0], 3), "load_page_cache_s": round(loads[1], 3),
+                   "load_page_cache_GBps": round(size / loads[1] / 1e9, 2),
+                   "plain_read_after_page_drop_GBps": round(size / raw[0] / 1e9, 2),
+                   "plain_read_page_cache_GBps": round(size / raw[1] / 1e9, 2),
+                   "loaded_index_equals_built": same,
+                   "timing": "wall clock around each C-ABI call; save includes fsync; the first load follows "
+                             "POSIX_FADV_DONTNEED on the file"},
+    }
+    line["roofline"] = {"bound": "storage read", "achieved": size / loads[0] / 1e9,
+                        "peak": size / raw[0] / 1e9, "unit": "GB/s", "frac": raw[0] / loads[0], "traffic": size,
+                        "peak_source": "plain 8-thread read of the same file after dropping its cached pages"}
+    print(json.dumps(line), flush=True)
+    if not same:
+        raise SystemExit("loaded index answered differently from the built index")
+
+
+def drop_cached_pages(path):
+    fd = os.open(path, os.O_RDONLY)
+    try:
+        os.posix_fadvise(fd, 0, 0, os.POSIX_FADV_DONTNEED)
+    finally:
+        os.close(fd)
+
+
+def plain_read_seconds(path, size, drop=True, lanes=8, piece=8 << 20):
+    """Seconds to read a file into host memory with `lanes` threads taking
+    `piece`-byte pieces in turn (no GPU work)."""
+    if drop:
+        drop_cached_pages(path)
+    bufs = [bytearray(piece) for _ in range(lanes)]
+    fd = os.open(path, os.O_RDONLY)
+
+    def lane(t):
+        mv = memoryview(bufs[t])
+        for off in range(t * piece, size, lanes * piece):
+            got = 0
+            want = min(piece, size - off)
+            while got < want:
+                r = os.preadv(fd, [mv[got:want]], off + got)
+                if r <= 0:
+                    raise OSError("short read")
+                got += r
+
+    try:
+        t0 = time.perf_counter()
+        th = [threading.Thread(target=lane, args=(t,)) for t in range(lanes)]
+        for x in th:
+            x.start()
+        for x in th:
+            x.join()
+        return time.perf_counter() - t0
+    finally:
+        os.close(fd)
+
+
 # --------------------------------------------------------------------------- float cosine workload
 COS_DIM, COS_COMPS = 768, 1024
 
@@ -418,9 +535,10 @@ def main():
     ap.add_argument("--cpu-slice", type=int, default=4_000_000)
     ap.add_argument("--cpu-queries", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="flat", choices=["flat", "ivf", "cos"],
+    ap.add_argument("--workload", default="flat", choices=["flat", "ivf", "cos", "persist"],
                     help="flat: exact u8 L2 scan (the headline); ivf: clustered search (nlist 1024, nprobe 16); "
-                         "cos: float32 cosine scan (10M x 768, 4,096 queries)")
+                         "cos: float32 cosine scan (10M x 768, 4,096 queries); persist: index file save/load "
+                         "(10M x 128)")
     args = ap.parse_args()
     warmup = max(3, args.warmup)
 
@@ -484,6 +602,9 @@ def main():
         return
     if args.workload == "cos":
         run_cos(args, torch, device, L, warmup)
+        return
+    if args.workload == "persist":
+        run_persist(args, torch, device, L)
         return
     sys.path.insert(0, os.path.join(ROOT, "winnex-madhava_b200"))
     from winnex_madhava.sharding import gather_topk, merge_topk_device, row_range

@@ -35,7 +35,9 @@ typedef enum {
     MDH_ERR_TIMEOUT = 5,       /* a bounded device-side wait expired */
     MDH_ERR_NOT_INTEGRAL = 6,  /* an integer-only entry point got non-integral data */
     MDH_ERR_UNSUPPORTED = 7,   /* valid request outside what this build implements */
-    MDH_ERR_INTERNAL = 8
+    MDH_ERR_INTERNAL = 8,
+    MDH_ERR_IO = 9             /* index file: cannot open / read / write, bad header, truncated,
+                                  or rows that fail the load-time integrity check */
 } mdh_status;
 
 /* Metric values match the reference enum (include/winnex_madhava/winnex_madhava.hpp:38-41). */
@@ -105,6 +107,37 @@ mdh_status mdh_index_destroy(mdh_index* index);
 /* Shape of an index. */
 mdh_status mdh_index_info(const mdh_index* index, int64_t* n, int32_t* dim, int32_t* metric,
                           int32_t* ndev);
+
+/* Index files.  A file holds, per shard, the norm-sorted rows with their
+ * padded stride, the integer |v|^2 and the global row ids (float corpora:
+ * float rows, float norms, ids), behind a fixed little-endian header:
+ *   0  char[8] "MDHB200I"   8  u32 version (1)   12 u32 kind (0 u8, 1 float32)
+ *   16 i64 n   24 i32 dim   28 i32 row stride (u8: dim rounded up to 128
+ *   bytes; float32: dim)   32 i32 metric   36 i32 shards   40 u64 data offset
+ *   48 u64 file size   56 u64 0;  64: shards x {i64 rows, i64 id_base,
+ *   u64 offset, u64 bytes};  each shard's data at its 4096-aligned offset:
+ *   rows [rows][stride], norms [rows] (4 bytes), ids [rows] (int32).
+ * Loading skips the sort: it streams each shard to its GPU, checks every row
+ * against its stored norm, order and id range on the device, and rebuilds
+ * the sample levels (they are chosen by a hash of the row id, so they come
+ * out the same).  Search results after a load equal those before the save.
+ *
+ * mdh_index_save writes `path` through a temporary file renamed into place.
+ * Replaces MadhavaL2::save_index (src/winnex_madhava.cpp:1120-1149, bound at
+ * bindings/py_module.cpp:227-230); the reference file holds the bound
+ * engine's projections and leaves the corpus out, this one holds the corpus
+ * in the order the scan reads it. */
+mdh_status mdh_index_save(mdh_index* index, const char* path);
+
+/* devices/ndev: one GPU per shard of the file, in file order; NULL/0 = every
+ * shard on the current device.  Replaces MadhavaL2::load_index
+ * (src/winnex_madhava.cpp:1151-1217, bound at bindings/py_module.cpp:232-235). */
+mdh_status mdh_index_load(const char* path, const int32_t* devices, int32_t ndev, mdh_index** out);
+
+/* Header of an index file (host only; no GPU needed).  Any output may be NULL.
+ * is_float: 1 for a float32 corpus. */
+mdh_status mdh_index_file_info(const char* path, int64_t* n, int32_t* dim, int32_t* metric, int32_t* shards,
+                               int32_t* is_float);
 
 /* Search with float32 host queries [nq][dim]; results to host buffers.
  * A query whose values are all integers in [0,255] runs the integer u8 path

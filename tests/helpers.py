@@ -53,6 +53,9 @@ def capi():
     L.mdh_ivf_search_u8.argtypes = [P, P, i32, i32, i32, P, P, ctypes.POINTER(Stats)]
     L.mdh_ivf_info.argtypes = [P, P, P, P, P]
     L.mdh_ivf_destroy.argtypes = [P]
+    L.mdh_index_save.argtypes = [P, ctypes.c_char_p]
+    L.mdh_index_load.argtypes = [ctypes.c_char_p, P, i32, ctypes.POINTER(P)]
+    L.mdh_index_file_info.argtypes = [ctypes.c_char_p, P, P, P, P, P]
     L.mdh_set_scan_path.argtypes = [i32]
     L.mdh_set_verify.argtypes = [i32]
     L.mdh_set_candidate_cap_limit.argtypes = [i32]
@@ -62,7 +65,7 @@ def capi():
     for fn in ("mdh_index_create_u8", "mdh_index_create_u8_device", "mdh_index_create_f32", "mdh_index_destroy", "mdh_index_info", "mdh_search_f32",
                "mdh_search_u8", "mdh_search_u8_device", "mdh_search_u8_device_noalloc", "mdh_merge_topk_device", "mdh_set_scan_path",
                "mdh_set_verify", "mdh_ivf_create_u8", "mdh_ivf_route_u8", "mdh_ivf_search_u8", "mdh_ivf_info",
-               "mdh_ivf_destroy",
+               "mdh_ivf_destroy", "mdh_index_save", "mdh_index_load", "mdh_index_file_info",
                "mdh_set_candidate_cap_limit"):
         getattr(L, fn).restype = ctypes.c_int
     return L

@@ -88,8 +88,10 @@ def test_engines_refuse_to_run_without_gpu():
 
 def test_bound_engine_only_features_raise():
     e = wm.MadhavaL2(wm.Config())
-    with pytest.raises(NotImplementedError):
-        e.save_index("/tmp/x")
+    # Like the reference, an unbuilt engine saves nothing and a missing file
+    # does not load.
+    assert e.save_index("/nonexistent-dir/x.idx") is False
+    assert e.load_index("/nonexistent-dir/x.idx") is False and e.built() is False
     with pytest.raises(NotImplementedError):
         e.search_audited(np.zeros(128, np.float32))
     # An unbuilt engine returns an empty result like the reference.

@@ -61,21 +61,6 @@ int next_pow2(int64_t x) {
     return (int)p;
 }
 
-void check_device_usable(int dev) {
-    int count = 0;
-    cudaError_t e = cudaGetDeviceCount(&count);
-    if (e != cudaSuccess || count == 0) {
-        cudaGetLastError();
-        throw Error(MDH_ERR_CUDA, "no CUDA device is available (this library has no CPU fallback)");
-    }
-    MDH_REQUIRE(dev >= 0 && dev < count, MDH_ERR_INVALID_ARG, "device ordinal out of range");
-    cudaDeviceProp p;
-    MDH_CUDA(cudaGetDeviceProperties(&p, dev));
-    if (p.major != 10 || p.minor != 0)
-        throw Error(MDH_ERR_CUDA, "this library is built for sm_100a (B200); device " + std::to_string(dev) +
-                                      " is sm_" + std::to_string(p.major) + std::to_string(p.minor));
-}
-
 // What the queries of one call are and which arithmetic ranks them.
 struct QueryPlan {
     bool integer = false;   // u8 integer path
@@ -701,6 +686,21 @@ void create_impl(const void* host, bool f32, int64_t n, int32_t dim, int32_t met
     mdh_status code = (e == cudaErrorMemoryAllocation) ? MDH_ERR_OOM : MDH_ERR_CUDA;
     throw Error(code, std::string("CUDA error ") + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ") in " + what +
                           " at " + file + ":" + std::to_string(line));
+}
+
+void check_device_usable(int dev) {
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0) {
+        cudaGetLastError();
+        throw Error(MDH_ERR_CUDA, "no CUDA device is available (this library has no CPU fallback)");
+    }
+    MDH_REQUIRE(dev >= 0 && dev < count, MDH_ERR_INVALID_ARG, "device ordinal out of range");
+    cudaDeviceProp p;
+    MDH_CUDA(cudaGetDeviceProperties(&p, dev));
+    if (p.major != 10 || p.minor != 0)
+        throw Error(MDH_ERR_CUDA, "this library is built for sm_100a (B200); device " + std::to_string(dev) +
+                                      " is sm_" + std::to_string(p.major) + std::to_string(p.minor));
 }
 
 int device_sm_count(int dev) {

@@ -145,27 +145,6 @@ T* dalloc(size_t count) {
     return static_cast<T*>(p);
 }
 
-void alloc_level(Level& lv, int64_t n, int dpad, int dim, bool u8, bool f32, cudaStream_t st) {
-    lv.n = n;
-    lv.n_pad = round_up(n > 0 ? n : 1, kTileRows);
-    lv.ids = dalloc<int32_t>(lv.n_pad);
-    if (u8) {
-        lv.rows = dalloc<uint8_t>((size_t)lv.n_pad * dpad);
-        lv.norms = dalloc<int32_t>(lv.n_pad);
-        if (lv.n_pad > n) {
-            MDH_CUDA(cudaMemsetAsync(lv.rows + (size_t)n * dpad, 0, (size_t)(lv.n_pad - n) * dpad, st));
-            k_fill_i32<<<(unsigned)((lv.n_pad - n + 255) / 256), 256, 0, st>>>(lv.norms + n, lv.n_pad - n, kNormPad);
-        }
-    }
-    if (f32) {
-        lv.rows_f32 = dalloc<float>((size_t)lv.n_pad * dim);
-        lv.norms_f32 = dalloc<float>(lv.n_pad);
-    }
-    if (lv.n_pad > n)
-        k_fill_i32<<<(unsigned)((lv.n_pad - n + 255) / 256), 256, 0, st>>>(lv.ids + n, lv.n_pad - n, -1);
-    MDH_CUDA(cudaGetLastError());
-}
-
 // Nested sample sizes: 1024 * 32^j while the sample stays <= n / 8.
 std::vector<int64_t> plan_samples(int64_t n) {
     std::vector<int64_t> s;
@@ -217,6 +196,37 @@ void build_samples(mdh_index* ix, Shard& sh, bool u8, bool f32) {
 
 }  // namespace
 
+void alloc_level(Level& lv, int64_t n, int dpad, int dim, bool u8, bool f32, cudaStream_t st) {
+    lv.n = n;
+    lv.n_pad = round_up(n > 0 ? n : 1, kTileRows);
+    lv.ids = dalloc<int32_t>(lv.n_pad);
+    if (u8) {
+        lv.rows = dalloc<uint8_t>((size_t)lv.n_pad * dpad);
+        lv.norms = dalloc<int32_t>(lv.n_pad);
+        if (lv.n_pad > n) {
+            MDH_CUDA(cudaMemsetAsync(lv.rows + (size_t)n * dpad, 0, (size_t)(lv.n_pad - n) * dpad, st));
+            k_fill_i32<<<(unsigned)((lv.n_pad - n + 255) / 256), 256, 0, st>>>(lv.norms + n, lv.n_pad - n, kNormPad);
+        }
+    }
+    if (f32) {
+        lv.rows_f32 = dalloc<float>((size_t)lv.n_pad * dim);
+        lv.norms_f32 = dalloc<float>(lv.n_pad);
+    }
+    if (lv.n_pad > n)
+        k_fill_i32<<<(unsigned)((lv.n_pad - n + 255) / 256), 256, 0, st>>>(lv.ids + n, lv.n_pad - n, -1);
+    MDH_CUDA(cudaGetLastError());
+}
+
+void finish_shard(mdh_index* ix, Shard& sh, bool u8, bool f32) {
+    build_samples(ix, sh, u8, f32);
+    if (u8)
+        for (Level& lv : sh.levels) {
+            if (tc_supported(ix, lv)) make_tmap_rows(lv, ix->dpad);
+            if (tc2_supported(ix, lv)) make_tmap_rows_pair(lv, ix->dpad);
+        }
+    MDH_CUDA(cudaStreamSynchronize(sh.stream));
+}
+
 void build_shard_u8(mdh_index* ix, Shard& sh, const uint8_t* host_rows, int64_t n) {
     MDH_CUDA(cudaSetDevice(sh.device));
     cudaStream_t st = sh.stream;
@@ -249,12 +259,7 @@ void build_shard_u8(mdh_index* ix, Shard& sh, const uint8_t* host_rows, int64_t 
     }
     sh.levels.clear();
     sh.levels.push_back(full);
-    build_samples(ix, sh, true, false);
-    for (Level& lv : sh.levels) {
-        if (tc_supported(ix, lv)) make_tmap_rows(lv, dpad);
-        if (tc2_supported(ix, lv)) make_tmap_rows_pair(lv, dpad);
-    }
-    MDH_CUDA(cudaStreamSynchronize(st));
+    finish_shard(ix, sh, true, false);
 }
 
 void build_shard_f32(mdh_index* ix, Shard& sh, const float* host_rows, int64_t n) {
@@ -280,8 +285,7 @@ void build_shard_f32(mdh_index* ix, Shard& sh, const float* host_rows, int64_t n
     }
     sh.levels.clear();
     sh.levels.push_back(full);
-    build_samples(ix, sh, false, true);
-    MDH_CUDA(cudaStreamSynchronize(st));
+    finish_shard(ix, sh, false, true);
 }
 
 // Float rows for SpeedEngine cosine over a u8 corpus (normalized copy),

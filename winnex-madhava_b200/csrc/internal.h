@@ -80,6 +80,12 @@ namespace mdh {
 // ---- index build (index.cu) ----
 void build_shard_u8(mdh_index* ix, Shard& sh, const uint8_t* host_rows, int64_t n);
 void build_shard_f32(mdh_index* ix, Shard& sh, const float* host_rows, int64_t n);
+// Device buffers of a level of n rows padded to kTileRows (pad rows: zero
+// bytes, kNormPad, id -1); u8 = rows + norms, f32 = float rows + float norms.
+void alloc_level(Level& lv, int64_t n, int dpad, int dim, bool u8, bool f32, cudaStream_t st);
+// Given sh.levels = {the full level}: adds the nested sample levels and the
+// TMA maps, then waits for the shard's stream.
+void finish_shard(mdh_index* ix, Shard& sh, bool u8, bool f32);
 void free_shard(Shard& sh);
 void free_level_buffers(Level& lv);   // frees owned buffers, resets lv
 void free_workspace(Workspace& w);    // frees every buffer, resets w
@@ -195,6 +201,8 @@ void launch_gather_queries_u8(const uint8_t* src, const int32_t* qn_src, const i
                               int dpad, uint8_t* dst, int32_t* qn_dst, cudaStream_t st);
 
 int device_sm_count(int dev);
+// Throws unless `dev` is a visible sm_100 device.
+void check_device_usable(int dev);
 
 // Runs fn(ctx) under the C ABI's error convention (status code, and the
 // message for mdh_last_error) without allocating on success.

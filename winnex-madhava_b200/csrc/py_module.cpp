@@ -10,8 +10,10 @@
 //     bound_violations = 0 (no pair is pruned without an exact comparison);
 //   * SpeedEngine always runs on the GPU (has_gpu() is True); n_anchors is
 //     accepted, and the scan stays exact;
-//   * bound-engine-only features (audit certificates, commitments, index
-//     persistence, projection bases) raise NotImplementedError.
+//   * save_index / load_index write and read this library's index file (the
+//     norm-sorted corpus, norms and ids; no re-attached base is needed);
+//   * bound-engine-only features (audit certificates, commitments,
+//     projection bases) raise NotImplementedError.
 #include <pybind11/numpy.h>
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
@@ -196,6 +198,47 @@ public:
         check(s);
         all.assign(ids.begin(), ids.end());
         return all;
+    }
+
+    // MadhavaL2::save_index (src/winnex_madhava.cpp:1120-1149): false when the
+    // engine is not built or the file cannot be written.  The file holds the
+    // norm-sorted corpus itself, so a loaded engine needs no re-attached base.
+    bool save_index(const std::string& path) const {
+        if (!built_) return false;
+        mdh_status s;
+        {
+            py::gil_scoped_release nogil;
+            s = mdh_index_save(h_.ix, path.c_str());
+        }
+        if (s == MDH_ERR_IO) return false;
+        check(s);
+        return true;
+    }
+
+    // MadhavaL2::load_index (src/winnex_madhava.cpp:1151-1217): drops the
+    // current state first, then returns false when the file cannot be read or
+    // fails its header or integrity checks.  dim and metric come from the file.
+    bool load_index(const std::string& path) {
+        h_.reset(nullptr);
+        built_ = false;
+        n_ = 0;
+        mdh_index* p = nullptr;
+        mdh_status s;
+        {
+            py::gil_scoped_release nogil;
+            s = mdh_index_load(path.c_str(), devices_.empty() ? nullptr : devices_.data(), (int32_t)devices_.size(), &p);
+        }
+        if (s == MDH_ERR_IO) return false;
+        check(s);
+        h_.reset(p);
+        int64_t n = 0;
+        int32_t dim = 0, metric = 0;
+        check(mdh_index_info(p, &n, &dim, &metric, nullptr));
+        n_ = (int)n;
+        cfg_.dim = dim;
+        cfg_.metric = (Metric)metric;
+        built_ = true;
+        return true;
     }
 
     int num_vectors() const { return n_; }
@@ -539,12 +582,8 @@ PYBIND11_MODULE(_winnex_madhava, m) {
             },
             py::arg("query"), py::arg("k") = 10, py::arg("max_sample") = 50)
         .def("search_batch", &MadhavaL2::search_batch, py::arg("queries"), py::arg("nq"), py::arg("k"))
-        .def(
-            "save_index", [](const MadhavaL2&, const std::string&) -> bool { not_implemented("MadhavaL2.save_index is not implemented in this build"); },
-            py::arg("path"))
-        .def(
-            "load_index", [](MadhavaL2&, const std::string&) -> bool { not_implemented("MadhavaL2.load_index is not implemented in this build"); },
-            py::arg("path"))
+        .def("save_index", &MadhavaL2::save_index, py::arg("path"))
+        .def("load_index", &MadhavaL2::load_index, py::arg("path"))
         .def("num_vectors", &MadhavaL2::num_vectors)
         .def("dim", &MadhavaL2::dim)
         .def("config", &MadhavaL2::config)
