@@ -585,19 +585,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 const int32_t m0 = max32(v[0]), m1 = max32(v[1]);
                 const bool pass0 = 2 * m0 >= need0, pass1 = 2 * m1 >= need1;
-                if (!pass0 && !pass1) continue;
+                if (!__any_sync(0xffffffffu, pass0 || pass1)) continue;
                 // The queries of a unit probe one cell but rarely keep the same
-                // columns: each passing lane walks its own columns.
+                // columns: each passing lane walks its own columns.  The whole
+                // warp runs the walk (as many steps as the busiest lane needs),
+                // so a column's norm comes by shuffle from the lane that holds
+                // it (nr0 / nr1) instead of a dependent load per column.
                 const int32_t row0 = t * BN + rowoff;  // rows < 2^31 (ids are int32)
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
                     uint32_t mask = (c ? pass1 : pass0) ? pass_mask32(v[c], c ? need1 : need0) : 0u;
-                    while (mask) {
-                        const int j = __ffs(mask) - 1;
-                        mask &= mask - 1;
+                    const int32_t valid = row_end - (row0 + 32 * c);  // pad rows trail the cell
+                    if (valid < 32) mask &= valid > 0 ? (1u << valid) - 1u : 0u;
+                    const int32_t nrc = c ? nr1 : nr0;
+                    while (__any_sync(0xffffffffu, mask != 0u)) {
+                        const bool have = mask != 0u;
+                        const int j = have ? __ffs(mask) - 1 : 0;
+                        mask &= mask - 1u;
+                        const int32_t nj = __shfl_sync(0xffffffffu, nrc, j);
+                        if (!have) continue;
                         const int32_t r = row0 + 32 * c + j;
-                        if (r >= row_end) break;  // pad rows trail the cell
-                        const uint32_t key = (uint32_t)(qnv + __ldg(norms + r) - 2 * (int32_t)pick32(v[c], j));
+                        const uint32_t key = (uint32_t)(qnv + nj - 2 * (int32_t)pick32(v[c], j));
                         if (key < tkey || (key == tkey && __ldg(ids + r) <= tid))
                             buf.push(key, (uint32_t)r, counts, cand, cap, qi);
                     }
