@@ -512,13 +512,26 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
     std::vector<int32_t> hid((size_t)chunk * kk);
     for (int c0 = 0; c0 < nq; c0 += chunk) {
         const int m = std::min(chunk, nq - c0);
-        // Stage this chunk's queries on the host.
+        // This chunk's u8 queries with the padded row stride: the caller's
+        // rows themselves when dim is already a multiple of the stride unit,
+        // else a zero-padded host copy.
+        const uint8_t* qsrc = nullptr;
         if (qp.integer) {
-            qbuf_u8.assign((size_t)m * dpad, 0);
-            for (int i = 0; i < m; i++)
-                for (int j = 0; j < dim; j++)
-                    qbuf_u8[(size_t)i * dpad + j] = host_u8 ? host_u8[(size_t)(c0 + i) * dim + j]
-                                                            : (uint8_t)host_f32[(size_t)(c0 + i) * dim + j];
+            if (host_u8 && dim == dpad) {
+                qsrc = host_u8 + (size_t)c0 * dim;
+            } else {
+                qbuf_u8.assign((size_t)m * dpad, 0);
+                for (int i = 0; i < m; i++) {
+                    uint8_t* dst = qbuf_u8.data() + (size_t)i * dpad;
+                    if (host_u8) {
+                        std::memcpy(dst, host_u8 + (size_t)(c0 + i) * dim, (size_t)dim);
+                    } else {
+                        const float* src = host_f32 + (size_t)(c0 + i) * dim;
+                        for (int j = 0; j < dim; j++) dst[j] = (uint8_t)src[j];
+                    }
+                }
+                qsrc = qbuf_u8.data();
+            }
         } else {
             prepare_float_queries(ix, qp, host_f32 + (size_t)c0 * dim, m, mode, qbuf_f32);
         }
@@ -534,7 +547,7 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
                 if (qp.integer) {
                     growT(&w.q_u8, &w.q_u8_bytes, (size_t)m * dpad);
                     growT(&w.qn, &w.qn_bytes, (size_t)m * 4);
-                    MDH_CUDA(cudaMemcpyAsync(w.q_u8, qbuf_u8.data(), (size_t)m * dpad, cudaMemcpyHostToDevice, sh.stream));
+                    MDH_CUDA(cudaMemcpyAsync(w.q_u8, qsrc, (size_t)m * dpad, cudaMemcpyHostToDevice, sh.stream));
                     launch_query_norms_u8(w.q_u8, m, dpad, w.qn, sh.stream);
                     st_launch[(size_t)si] = 1;
                 } else {
@@ -546,7 +559,7 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
                         launch_convert_bf16(w.q_f32, (int64_t)m * dim, w.q_bf16, sh.stream);
                     }
                 }
-                sres[(size_t)si] = search_shard(ix, sh, qp, m, kk, qbuf_u8.data(), qbuf_f32.data(), (size_t)dim);
+                sres[(size_t)si] = search_shard(ix, sh, qp, m, kk, qsrc, qbuf_f32.data(), (size_t)dim);
             } catch (const Error& e) {
                 codes[(size_t)si] = e.code;
                 errs[(size_t)si] = e.what();
