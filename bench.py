@@ -554,8 +554,10 @@ def main():
 
         import torch.distributed as dist
 
-        # Rank 0 prints exactly one JSON line: keep NCCL's version banner off stdout.
+        # Rank 0 prints exactly one JSON line on stdout: NCCL's own messages
+        # (its version banner, and whatever NCCL_DEBUG asks for) go to stderr.
         os.environ.setdefault("NCCL_DEBUG", "WARN")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
