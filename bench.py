@@ -314,7 +314,7 @@ def run_ivf(args, torch, device, L, warmup):
                      "algorithmic": "2 * (query, row) pairs of the probed cells * D",
                      "peak_source": f"2 x {peak_src} bf16 dense ({peaks['bf16_tflops']} TF/s)", "kernel_ms": ms},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # --------------------------------------------------------------------------- index files
@@ -388,7 +388,7 @@ def run_persist(args, torch, device, L):
     line["roofline"] = {"bound": "storage read", "achieved": size / loads[0] / 1e9,
                         "peak": size / raw[0] / 1e9, "unit": "GB/s", "frac": raw[0] / loads[0], "traffic": size,
                         "peak_source": "plain 8-thread read of the same file after dropping its cached pages"}
-    print(json.dumps(line), flush=True)
+    emit(line)
     if not same:
         raise SystemExit("loaded index answered differently from the built index")
 
@@ -517,11 +517,35 @@ def run_cos(args, torch, device, L, warmup):
                      "algorithmic": "2*N*Q*D flop per launch", "peak_source": f"{peak_src} bf16 dense",
                      "kernel_ms": ms},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+# --------------------------------------------------------------------------- output
+_RESULT_OUT = None  # the process's original stdout, kept for the result line
+
+
+def keep_stdout_for_result():
+    """From here on the result line is the only output on stdout: file
+    descriptor 1 is pointed at stderr, so NCCL's banner, library messages and
+    prints all go there, and emit() writes to a duplicate of the original."""
+    global _RESULT_OUT
+    try:
+        sys.stdout.flush()
+        _RESULT_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+    except OSError:
+        _RESULT_OUT = None
+
+
+def emit(line):
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
 
 
 # --------------------------------------------------------------------------- main
 def main():
+    keep_stdout_for_result()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -553,11 +577,6 @@ def main():
         import datetime
 
         import torch.distributed as dist
-
-        # Rank 0 prints exactly one JSON line on stdout: NCCL's own messages
-        # (its version banner, and whatever NCCL_DEBUG asks for) go to stderr.
-        os.environ.setdefault("NCCL_DEBUG", "WARN")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
@@ -593,7 +612,7 @@ def main():
                 "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
                 "impl": "reference", "cpu_baseline": cb,
                 "e2e": {"value": qps, "unit": "queries/sec", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
+        emit(line)
         if dist is not None:
             dist.destroy_process_group()
         return
@@ -780,7 +799,7 @@ def main():
             line["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
     check(L, L.mdh_index_destroy(h), "destroy")
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if dist is not None:
         dist.destroy_process_group()
 
