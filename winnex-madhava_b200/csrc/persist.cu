@@ -178,7 +178,9 @@ FileHeader read_header(int fd, const std::string& path) {
 // Pinned staging for the file <-> device pipelines: two halves of kIoLanes
 // chunk buffers each, and one copy event per half.  A group of up to kIoLanes
 // chunks is read (or written) by parallel host threads in one half while the
-// other half's copies run on the stream.
+// other half's copies run on the stream.  The buffers are portable (pinned
+// for every device); the events belong to one device, so use_device() makes
+// them anew on the current device before each shard's copies.
 struct Staging {
     static constexpr int kSlots = 2 * kIoLanes;
     uint8_t* buf[kSlots] = {};
@@ -186,7 +188,7 @@ struct Staging {
     Staging() {
         for (int i = 0; i < kSlots; i++) {
             void* p = nullptr;
-            cudaError_t e = cudaHostAlloc(&p, kStageBytes, cudaHostAllocDefault);
+            cudaError_t e = cudaHostAlloc(&p, kStageBytes, cudaHostAllocPortable);
             if (e != cudaSuccess) {
                 cudaGetLastError();
                 release();
@@ -194,23 +196,28 @@ struct Staging {
             }
             buf[i] = static_cast<uint8_t*>(p);
         }
-        for (int i = 0; i < 2; i++) {
-            cudaError_t e = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming);
-            if (e != cudaSuccess) {
-                cudaGetLastError();
-                release();
-                throw_cuda(e, "cudaEventCreateWithFlags", __FILE__, __LINE__);
-            }
-        }
     }
     // Waits for the last copies of each half (an error can leave some in
-    // flight) before the buffers are freed.
-    void release() {
+    // flight), then drops the events.
+    void drop_events() {
         for (int i = 0; i < 2; i++) {
             if (ev[i]) cudaEventSynchronize(ev[i]);
             if (ev[i]) cudaEventDestroy(ev[i]);
             ev[i] = nullptr;
         }
+    }
+    void use_device() {
+        drop_events();
+        for (int i = 0; i < 2; i++) {
+            cudaError_t e = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                throw_cuda(e, "cudaEventCreateWithFlags", __FILE__, __LINE__);
+            }
+        }
+    }
+    void release() {
+        drop_events();
         for (int i = 0; i < kSlots; i++) {
             if (buf[i]) cudaFreeHost(buf[i]);
             buf[i] = nullptr;
@@ -422,6 +429,7 @@ void save_impl(mdh_index* ix, const char* cpath) {
             Shard& sh = ix->shards[(size_t)i];
             const Level& lv = sh.levels.back();
             MDH_CUDA(cudaSetDevice(sh.device));
+            sg.use_device();
             const uint64_t n = (uint64_t)sh.n;
             const uint64_t rows_bytes = n * (kind == 0 ? (uint64_t)stride : (uint64_t)stride * 4);
             uint64_t off = table[(size_t)i].offset;
@@ -490,6 +498,7 @@ void load_impl(const char* cpath, const int32_t* devices, int32_t ndev, mdh_inde
             const FileShard& fs = h.shards[(size_t)i];
             sh.device = devs[(size_t)i];
             MDH_CUDA(cudaSetDevice(sh.device));
+            sg.use_device();
             MDH_CUDA(cudaStreamCreateWithFlags(&sh.stream, cudaStreamNonBlocking));
             sh.n = fs.rows;
             sh.id_base = fs.id_base;
