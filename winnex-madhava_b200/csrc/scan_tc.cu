@@ -34,7 +34,10 @@
 // (neighbouring rows of a sorted level have nearly equal norms); the unit
 // table form (IVF cells, whose tiles span a wider norm range) bounds each
 // 32-row chunk with its own first norm.  Blocks that pass are expanded per
-// lane: each passing lane walks its own passing columns.
+// lane: each passing lane walks its own passing columns.  In the unit table
+// form the whole warp runs that walk and takes each row's norm by shuffle
+// from the lane that loaded it (lane l holds rows l and 32 + l of the warp's
+// columns).
 //
 // Work units: (query group, corpus chunk), ordered chunk-major so the CTAs
 // running at the same time share corpus chunks through L2; each CTA takes
