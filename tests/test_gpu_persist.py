@@ -234,3 +234,25 @@ def test_facade_save_and_load_index(tmp_path):
     bad = str(tmp_path / "bad.idx")
     open(bad, "wb").write(bytes(raw))
     assert fresh.load_index(bad) is False and fresh.built() is False
+
+
+def test_roundtrip_across_devices(tmp_path):
+    """Shards on two GPUs are saved and loaded back onto two GPUs (each shard's
+    copies run on its own device), and onto one."""
+    L = capi()
+    if L.mdh_device_count() < 2:
+        pytest.skip("needs two GPUs")
+    C = cases.gmm_u8(80_000, 128, 64, seed=99)
+    Q = cases.gmm_u8_queries(100, 128, 64, seed_means=99, seed_q=100)
+    h = _create(L, C, devices=[0, 1])
+    ids0, d0, _ = _search_u8(L, h, Q, 10)
+    path = str(tmp_path / "two_gpus.idx")
+    _save(L, h, path)
+    for devs in ([1, 0], None):
+        st, h2 = _load(L, path, devices=devs)
+        assert st == 0, L.mdh_last_error()
+        ids1, d1, _ = _search_u8(L, h2, Q, 10)
+        np.testing.assert_array_equal(ids1, ids0)
+        np.testing.assert_array_equal(d1, d0)
+        assert L.mdh_index_destroy(h2) == 0
+    assert L.mdh_index_destroy(h) == 0
