@@ -321,6 +321,81 @@ void oracle_l2_exact_u8_int(const uint8_t* corpus, int64_t n, int d, const uint8
     free(dist);
 }
 
+/* The same integer ranking as oracle_l2_exact_u8_int (ascending (distance,
+ * index), MadhavaL2::search_exact, src/winnex_madhava.cpp:1224-1246), folded
+ * into a running top-k so a corpus can be checked one slice at a time:
+ * rows [0, n) of `corpus` carry the global ids id_base .. id_base + n - 1, and
+ * ids_io / dist_io ([nq][k]) hold the best k seen so far on entry (id -1 for
+ * an empty slot) and the best k including this slice on return.  Every
+ * thread scans a contiguous row range against all queries (each row is read
+ * once per call) into private lists, which are then merged; the result does
+ * not depend on the thread count.  Distances are exact: d * 255^2 < 2^31 for
+ * d <= 33025. */
+typedef struct { int64_t dist; int32_t id; } dk_t;
+
+static int dk_before(dk_t a, dk_t b) { return a.dist < b.dist || (a.dist == b.dist && a.id < b.id); }
+
+/* Insert x into the sorted list l of size *m (capacity k). */
+static void dk_insert(dk_t* l, int* m, int k, dk_t x) {
+    if (*m == k && !dk_before(x, l[k - 1])) return;
+    int i = *m < k ? (*m)++ : k - 1;
+    while (i > 0 && dk_before(x, l[i - 1])) { l[i] = l[i - 1]; i--; }
+    l[i] = x;
+}
+
+__attribute__((optimize("O3"))) void oracle_l2_topk_u8_update(const uint8_t* corpus, int64_t n, int d,
+                                                               int64_t id_base, const uint8_t* queries, int nq,
+                                                               int k, int32_t* ids_io, int64_t* dist_io) {
+    if (k <= 0 || nq <= 0) return;
+    int nt = 1;
+#ifdef _OPENMP
+    nt = omp_get_max_threads();
+#endif
+    dk_t* lists = (dk_t*)malloc(sizeof(dk_t) * (size_t)nt * nq * k);
+    int* sizes = (int*)calloc((size_t)nt * nq, sizeof(int));
+#pragma omp parallel num_threads(nt)
+    {
+        int t = 0;
+#ifdef _OPENMP
+        t = omp_get_thread_num();
+#endif
+        const int64_t r0 = n * t / nt, r1 = n * (t + 1) / nt;
+        dk_t* my = lists + (size_t)t * nq * k;
+        int* msz = sizes + (size_t)t * nq;
+        for (int64_t i = r0; i < r1; i++) {
+            const uint8_t* v = corpus + (size_t)i * d;
+            for (int qi = 0; qi < nq; qi++) {
+                const uint8_t* q = queries + (size_t)qi * d;
+                int32_t s = 0;
+                for (int j = 0; j < d; j++) { int32_t e = (int32_t)v[j] - (int32_t)q[j]; s += e * e; }
+                dk_t x = {s, (int32_t)(id_base + i)};
+                dk_insert(my + (size_t)qi * k, msz + qi, k, x);
+            }
+        }
+    }
+    dk_t* merged = (dk_t*)malloc(sizeof(dk_t) * (size_t)k);
+    for (int qi = 0; qi < nq; qi++) {
+        int m = 0;
+        for (int j = 0; j < k; j++) {
+            int32_t id = ids_io[(size_t)qi * k + j];
+            if (id < 0) break;
+            dk_t x = {dist_io[(size_t)qi * k + j], id};
+            dk_insert(merged, &m, k, x);
+        }
+        for (int t = 0; t < nt; t++) {
+            const dk_t* l = lists + ((size_t)t * nq + qi) * k;
+            for (int j = 0; j < sizes[(size_t)t * nq + qi]; j++) dk_insert(merged, &m, k, l[j]);
+        }
+        for (int j = 0; j < k; j++) {
+            ids_io[(size_t)qi * k + j] = j < m ? merged[j].id : -1;
+            dist_io[(size_t)qi * k + j] = j < m ? merged[j].dist : -1;
+        }
+    }
+    free(merged);
+    free(sizes);
+    free(lists);
+}
+
 /* Score given row ids of one query with the reference arithmetic.
  * kind 0: l2_sq_avx over u8 rows (MadhavaL2 L2);
  * kind 1: exact_score cosine over u8 rows (MadhavaL2 cosine);

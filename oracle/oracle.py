@@ -50,6 +50,7 @@ def lib() -> ctypes.CDLL:
         i64, i32, f32 = ctypes.c_int64, ctypes.c_int, ctypes.c_float
         L.oracle_l2_exact_u8.argtypes = [P, i64, i32, P, i32, i32, P, P]
         L.oracle_l2_exact_u8_int.argtypes = [P, i64, i32, P, i32, i32, P, P]
+        L.oracle_l2_topk_u8_update.argtypes = [P, i64, i32, i64, P, i32, i32, P, P]
         L.oracle_cosine_exact_u8.argtypes = [P, i64, i32, P, i32, i32, P, P]
         L.oracle_speed_exact.argtypes = [P, P, i64, i32, i32, P, i32, i32, P, P]
         L.oracle_speed_prepare_u8.argtypes = [P, i64, i32, i32, P, P]
@@ -60,7 +61,7 @@ def lib() -> ctypes.CDLL:
         L.oracle_score_ids.argtypes = [i32, i32, P, P, P, i32, P, P, i32, P]
         L.oracle_ivf_route.argtypes = [P, i32, i32, P, i32, i32, P]
         L.oracle_score_ids.restype = None
-        for fn in ("oracle_l2_exact_u8", "oracle_l2_exact_u8_int", "oracle_cosine_exact_u8",
+        for fn in ("oracle_l2_exact_u8", "oracle_l2_exact_u8_int", "oracle_l2_topk_u8_update", "oracle_cosine_exact_u8",
                    "oracle_speed_exact", "oracle_speed_prepare_u8", "oracle_speed_prepare_f32"):
             getattr(L, fn).restype = None
         _lib = L
@@ -102,6 +103,39 @@ def l2_exact_u8_int(corpus, queries_u8, k):
     dist = np.empty((nq, k), np.int64)
     lib().oracle_l2_exact_u8_int(_p(C), C.shape[0], C.shape[1], _p(Q), nq, k, _p(ids), _p(dist))
     return ids, dist
+
+
+class L2TopK:
+    """Exact L2 top-k of u8 queries over a corpus fed one row slice at a time
+    (``oracle_l2_topk_u8_update``): the same (distance, id) ranking as
+    :func:`l2_exact_u8_int`, for corpora too large to hold on the host at once.
+    ``update(rows, id_base)`` folds in rows with global ids starting at
+    ``id_base``; ``ids`` / ``dist`` ([nq, k]) hold the result (-1 past the rows
+    seen)."""
+
+    def __init__(self, queries_u8, k):
+        self.Q = np.ascontiguousarray(queries_u8, dtype=np.uint8)
+        if self.Q.ndim == 1:
+            self.Q = self.Q[None, :]
+        self.k = k
+        self.ids = np.full((self.Q.shape[0], k), -1, np.int32)
+        self.dist = np.full((self.Q.shape[0], k), -1, np.int64)
+
+    def update(self, rows_u8, id_base=0):
+        C = np.ascontiguousarray(rows_u8, dtype=np.uint8)
+        assert C.ndim == 2 and C.shape[1] == self.Q.shape[1]
+        lib().oracle_l2_topk_u8_update(_p(C), C.shape[0], C.shape[1], int(id_base), _p(self.Q), self.Q.shape[0],
+                                       self.k, _p(self.ids), _p(self.dist))
+        return self
+
+
+def l2_topk_u8(corpus, queries_u8, k, slice_rows=1 << 22):
+    """(ids, dist) like :func:`l2_exact_u8_int`, scanning the corpus once for
+    all queries (row slices of ``slice_rows``)."""
+    t = L2TopK(queries_u8, k)
+    for s in range(0, corpus.shape[0], slice_rows):
+        t.update(corpus[s:s + slice_rows], s)
+    return t.ids, t.dist
 
 
 def cosine_exact_u8(corpus, queries, k):

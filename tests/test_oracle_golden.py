@@ -156,3 +156,17 @@ def test_ivf_exact_oracle_full_probe_is_brute_force():
     want_ids, want_d = oracle.l2_exact_u8_int(C, Q[:12], 10)
     np.testing.assert_array_equal(ids, want_ids)
     np.testing.assert_array_equal(dist, want_d)
+
+
+def test_sliced_topk_oracle_matches_int_oracle():
+    """oracle.L2TopK (one pass over the rows for all queries, fed in slices)
+    ranks exactly like the per-query int64 oracle, ties and short corpora
+    included."""
+    C = cases.gmm_u8(60_000, 128, 64, seed=21)
+    Q = cases.gmm_u8_queries(40, 128, 64, seed_means=21, seed_q=22)
+    for corpus, q, k, sl in ((C, Q, 10, 7_001), (np.repeat(C[:500], 5, axis=0), Q[:9], 37, 777),
+                             (C[:20], Q[:3], 30, 7)):
+        a = oracle.l2_exact_u8_int(corpus, q, k)
+        b = oracle.l2_topk_u8(corpus, q, k, slice_rows=sl)
+        np.testing.assert_array_equal(a[0], b[0])
+        np.testing.assert_array_equal(a[1], b[1])
