@@ -79,7 +79,9 @@ class Stats(ctypes.Structure):
                 ("pairs_pruned_by_bound", ctypes.c_int64), ("bound_violations", ctypes.c_int64),
                 ("candidates", ctypes.c_int64), ("tensor_core_path", ctypes.c_int32), ("levels", ctypes.c_int32),
                 ("full_scan_ms", ctypes.c_double), ("full_scan_pairs", ctypes.c_int64),
-                ("kernel_launches", ctypes.c_int64), ("verified_queries", ctypes.c_int64)]
+                ("kernel_launches", ctypes.c_int64), ("verified_queries", ctypes.c_int64),
+                ("sample_ms", ctypes.c_double), ("select_ms", ctypes.c_double), ("rescore_ms", ctypes.c_double),
+                ("prep_ms", ctypes.c_double), ("blocks_tested", ctypes.c_int64), ("blocks_passed", ctypes.c_int64)]
 
 
 def load_lib():

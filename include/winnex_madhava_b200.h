@@ -60,8 +60,13 @@ typedef struct mdh_index mdh_index;
  * (include/winnex_madhava/winnex_madhava.hpp:118-164, speed_engine.hpp:36-41). */
 typedef struct {
     double latency_ms;            /* host wall time of the call (SearchResult::latency_ms) */
-    int64_t pairs_scored;         /* (query, row) pairs evaluated (bound_pairs / exact_evals) */
-    int64_t pairs_pruned_by_bound;/* pairs skipped by the norm lower bound */
+    int64_t pairs_scored;         /* (query, row) pairs scanned, every level (bound_pairs) */
+    int64_t pairs_pruned_by_bound;/* scanned pairs the tensor scan's block bound excluded without forming their
+                                     distance: the block's smallest |v|^2 and largest q.v prove every key in it
+                                     above the query's threshold (SearchResult::pruned_by_bound); the rest,
+                                     pairs_scored - pairs_pruned_by_bound, had their exact distance formed
+                                     (SearchResult::exact_evals).  0 on the CUDA-core and bf16 paths, which
+                                     form every distance */
     int64_t bound_violations;     /* rows misplaced relative to the returned top-K, counted for the
                                      verified queries by an exact unpruned scan (mdh_set_verify); 0 */
     int64_t candidates;           /* pairs that passed the threshold filter into the final selection */
@@ -72,6 +77,15 @@ typedef struct {
     int64_t full_scan_pairs;      /* (query, row) pairs that kernel scored */
     int64_t kernel_launches;      /* this library's kernels launched by the call */
     int64_t verified_queries;     /* queries re-checked by the verification scan (mdh_set_verify) */
+    /* Stage times, CUDA events on the search's stream (slowest shard per query chunk, summed over chunks): */
+    double sample_ms;             /* sample levels: their scans and threshold selections */
+    double select_ms;             /* final selection of the full level, overflow reruns included */
+    double rescore_ms;            /* exact fp32 rescore of the bf16 pass's candidates (float cosine); also
+                                     inside full_scan_ms */
+    double prep_ms;               /* query staging: host conversion and padding (wall time) plus the upload
+                                     and |q|^2 on the stream (events) */
+    int64_t blocks_tested;        /* (query, row block) bound tests of the 1-SM tensor scan, every level */
+    int64_t blocks_passed;        /* tests the bound did not settle; their rows' distances were formed */
 } mdh_stats;
 
 /* Build an index over a row-major u8 corpus [n][dim] held in host memory.
@@ -108,6 +122,11 @@ mdh_status mdh_index_destroy(mdh_index* index);
 mdh_status mdh_index_info(const mdh_index* index, int64_t* n, int32_t* dim, int32_t* metric,
                           int32_t* ndev);
 
+/* First global row id of an index: its rows carry ids [first_id, first_id + n)
+ * (the id_offset it was built with, or the first id of the file it was loaded
+ * from).  No counterpart in the reference (its ids always start at 0). */
+mdh_status mdh_index_id_base(const mdh_index* index, int64_t* first_id);
+
 /* Index files.  A file holds, per shard, the norm-sorted rows with their
  * padded stride, the integer |v|^2 and the global row ids (float corpora:
  * float rows, float norms, ids), behind a fixed little-endian header:
@@ -117,8 +136,10 @@ mdh_status mdh_index_info(const mdh_index* index, int64_t* n, int32_t* dim, int3
  *   48 u64 file size   56 u64 0;  64: shards x {i64 rows, i64 id_base,
  *   u64 offset, u64 bytes};  each shard's data at its 4096-aligned offset:
  *   rows [rows][stride], norms [rows] (4 bytes), ids [rows] (int32).
+ * The shards' id ranges tile one run [first id, first id + n) in file order.
  * Loading skips the sort: it streams each shard to its GPU, checks every row
- * against its stored norm, order and id range on the device, and rebuilds
+ * against its stored norm and order, and that the shard's ids are a
+ * permutation of its id range, on the device, and rebuilds
  * the sample levels (they are chosen by a hash of the row id, so they come
  * out the same).  Search results after a load equal those before the save.
  *
@@ -233,6 +254,21 @@ mdh_status mdh_set_verify(int32_t max_queries);
  * rerun with a strictly tighter threshold, so results stay exact; small
  * limits trade speed for scratch memory and exercise that rerun path. */
 mdh_status mdh_set_candidate_cap_limit(int32_t cap);
+
+/* Options (process-wide): sample plan.  An index shard of n rows keeps
+ * nested random samples of 1024 * 32^j rows up to about n / ratio rows (plus
+ * one of n / ratio rows when that ladder stops more than 4x short of it);
+ * a search scans them smallest first to set each query's distance threshold,
+ * and about k * ratio rows per query pass the full scan's threshold.  Larger
+ * ratios scan less sample and form more candidate distances.  0 restores the
+ * default (64).  Read when samples are built (index create and load). */
+mdh_status mdh_set_sample_ratio(int32_t ratio);
+
+/* Levels (samples, then the whole shard) a top-k search scans on one shard
+ * of shard_rows rows with the current sample plan, from the nominal sample
+ * sizes (host only; no GPU needed).  0 for an empty request, -1 when k is
+ * beyond what the selector supports for that shard. */
+int32_t mdh_plan_level_count(int64_t shard_rows, int32_t k);
 
 /* Number of CUDA devices visible (0 when none). */
 int32_t mdh_device_count(void);

@@ -32,7 +32,9 @@ class Stats(ctypes.Structure):
                 ("pairs_pruned_by_bound", ctypes.c_int64), ("bound_violations", ctypes.c_int64),
                 ("candidates", ctypes.c_int64), ("tensor_core_path", ctypes.c_int32), ("levels", ctypes.c_int32),
                 ("full_scan_ms", ctypes.c_double), ("full_scan_pairs", ctypes.c_int64),
-                ("kernel_launches", ctypes.c_int64), ("verified_queries", ctypes.c_int64)]
+                ("kernel_launches", ctypes.c_int64), ("verified_queries", ctypes.c_int64),
+                ("sample_ms", ctypes.c_double), ("select_ms", ctypes.c_double), ("rescore_ms", ctypes.c_double),
+                ("prep_ms", ctypes.c_double), ("blocks_tested", ctypes.c_int64), ("blocks_passed", ctypes.c_int64)]
 
 
 def capi():
@@ -59,6 +61,10 @@ def capi():
     L.mdh_set_scan_path.argtypes = [i32]
     L.mdh_set_verify.argtypes = [i32]
     L.mdh_set_candidate_cap_limit.argtypes = [i32]
+    L.mdh_set_sample_ratio.argtypes = [i32]
+    L.mdh_plan_level_count.argtypes = [i64, i32]
+    L.mdh_plan_level_count.restype = i32
+    L.mdh_index_id_base.argtypes = [P, P]
     L.mdh_last_error.restype = ctypes.c_char_p
     L.mdh_version.restype = ctypes.c_char_p
     L.mdh_device_count.restype = i32
@@ -66,7 +72,7 @@ def capi():
                "mdh_search_u8", "mdh_search_u8_device", "mdh_search_u8_device_noalloc", "mdh_merge_topk_device", "mdh_set_scan_path",
                "mdh_set_verify", "mdh_ivf_create_u8", "mdh_ivf_route_u8", "mdh_ivf_search_u8", "mdh_ivf_info",
                "mdh_ivf_destroy", "mdh_index_save", "mdh_index_load", "mdh_index_file_info",
-               "mdh_set_candidate_cap_limit"):
+               "mdh_set_candidate_cap_limit", "mdh_set_sample_ratio", "mdh_index_id_base"):
         getattr(L, fn).restype = ctypes.c_int
     return L
 

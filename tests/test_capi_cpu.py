@@ -59,3 +59,44 @@ def test_header_is_plain_c():
     assert 'extern "C"' in src
     for banned in ("torch", "std::", "class ", "template"):
         assert banned not in src
+
+
+def test_stats_struct_matches_header(tmp_path):
+    """The ctypes mirror of mdh_stats (tests, bench.py) has the header's size and field offsets."""
+    import shutil
+    import subprocess
+
+    from helpers import Stats
+
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "s.c"
+    names = [f[0] for f in Stats._fields_]
+    body = "".join(f'printf("%zu ", offsetof(mdh_stats, {n}));' for n in names)
+    src.write_text('#include <stddef.h>\n#include <stdio.h>\n#include "winnex_madhava_b200.h"\n'
+                   f'int main(void) {{ {body} printf("%zu\\n", sizeof(mdh_stats)); return 0; }}\n')
+    exe = tmp_path / "s"
+    subprocess.run(["gcc", "-I", HEADER.rsplit("/", 1)[0], str(src), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    want = [getattr(Stats, n).offset for n in names] + [ctypes.sizeof(Stats)]
+    assert got == want
+
+
+def test_sample_plan_shrinks_with_the_shard():
+    """Sample levels follow the shard size (the largest sample is about 1/64 of
+    the shard), so a rank of a G-way row split scans ~1/G of the sample rows."""
+    L = capi()
+    assert L.mdh_plan_level_count(100_000_000, 10) == 4    # 1,024 / 32,768 / 1,048,576 / full
+    assert L.mdh_plan_level_count(12_500_000, 10) == 3     # one of 8 ranks: 1,024 / 195,312 / full
+    assert L.mdh_plan_level_count(12_500_000, 100) == 4    # k = 100 steps by at most 20x: every sample
+    assert L.mdh_plan_level_count(1_000_000, 10) == 3      # 1,024 / 15,625 / full
+    assert L.mdh_plan_level_count(100_000, 10) == 2        # 1,024 / full
+    assert L.mdh_plan_level_count(5_000, 10) == 1          # dense scan of the shard
+    assert L.mdh_plan_level_count(0, 10) == 0
+    assert L.mdh_set_sample_ratio(8) == 0
+    try:
+        # The 100M ladder on a 10M shard: 1,024 / 32,768 / 1,048,576 / full.
+        assert L.mdh_plan_level_count(10_000_000, 10) == 4
+    finally:
+        assert L.mdh_set_sample_ratio(0) == 0
+    assert L.mdh_set_sample_ratio(1) == 1

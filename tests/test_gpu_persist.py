@@ -152,8 +152,9 @@ def test_roundtrip_f32_l2_speed(tmp_path):
 
 
 def test_load_rejects_damaged_rows(tmp_path):
-    """A changed row byte, a changed id and two swapped rows each fail the
-    load-time integrity check; the library stays usable afterwards."""
+    """A changed row byte, an id moved out of range, an id duplicated inside
+    the range and two swapped rows each fail the load-time integrity check;
+    the library stays usable afterwards."""
     L = capi()
     C = cases.gmm_u8(5_000, 128, 16, seed=95)
     h = _create(L, C)
@@ -178,6 +179,15 @@ def test_load_rejects_damaged_rows(tmp_path):
     raw = bytearray(good)
     raw[ids_at + 4 * 10:ids_at + 4 * 11] = (n + 3).to_bytes(4, "little")
     expect_rejected(raw, "id_range")
+    # An in-range id made equal to another row's id, at a row whose norm is
+    # strictly between its neighbours' (so the (norm, id) order still holds):
+    # a duplicate, caught by the permutation check.
+    raw = bytearray(good)
+    ids = np.frombuffer(bytes(raw[ids_at:ids_at + 4 * n]), np.int32)
+    norms = np.frombuffer(bytes(raw[norms_at:norms_at + 4 * n]), np.int32)
+    j = next(i for i in range(1, n - 201) if norms[i - 1] < norms[i] < norms[i + 1])
+    raw[ids_at + 4 * j:ids_at + 4 * j + 4] = int(ids[j + 200]).to_bytes(4, "little")
+    expect_rejected(raw, "id_duplicate")
     raw = bytearray(good)
     a, b = 100, 4000  # different norms: the order breaks
     ra, rb = bytes(raw[off + a * 128:off + (a + 1) * 128]), bytes(raw[off + b * 128:off + (b + 1) * 128])

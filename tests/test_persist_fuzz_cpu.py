@@ -28,11 +28,14 @@ def _accepted_layout_is_valid(raw: bytes) -> bool:
     if not (1 <= dim <= 4096) or stride != index_file.stride_of(kind, dim) or size != len(raw):
         return False
     per_row = (stride if kind == 0 else 4 * stride) + 8
-    end, total = data_off, 0
+    end, total, next_base = data_off, 0, None
     for i in range(nsh):
         rows, base, off, nbytes = index_file.ENTRY.unpack_from(raw, 64 + 32 * i)
         if rows < 0 or base < 0 or base + rows > 2**31 - 1 or nbytes != rows * per_row:
             return False
+        if next_base is not None and base != next_base:  # id ranges tile one run in file order
+            return False
+        next_base = base + rows
         if off % 4096 or off < end or off + nbytes > len(raw):
             return False
         end, total = off + nbytes, total + rows
@@ -67,3 +70,20 @@ def test_header_fuzz(tmp_path):
             rejected += 1
             assert L.mdh_last_error().startswith(b"index file ")
     assert rejected > 300 and accepted >= 1  # unchanged bytes (same value written back) are accepted
+
+
+def test_shard_id_ranges_must_tile(tmp_path):
+    """Shards whose id ranges overlap, leave a gap, or run out of order are
+    refused; ranges that tile [first, first + n) are accepted, whatever the
+    first id (a rank's slice of a larger corpus)."""
+    L = capi()
+    layouts = {"tiled": ([(7, 0), (0, 7), (5, 7)], 0), "offset_run": ([(4, 100), (6, 104)], 0),
+               "overlap": ([(7, 0), (5, 3)], MDH_ERR_IO), "gap": ([(7, 0), (5, 9)], MDH_ERR_IO),
+               "reversed": ([(5, 7), (7, 0)], MDH_ERR_IO)}
+    for name, (shards, want) in layouts.items():
+        p = str(tmp_path / (name + ".idx"))
+        index_file.write(p, 0, 64, 1, shards)
+        st, _ = _info(L, p)
+        assert st == want, (name, st, L.mdh_last_error())
+        if want:
+            assert b"id range" in L.mdh_last_error()

@@ -77,43 +77,50 @@ struct LevelStep {
     bool dense;  // infinite threshold (first level)
 };
 
-std::vector<LevelStep> plan_levels(const Shard& sh, int k) {
-    const int L = (int)sh.levels.size();
+// sizes: the level row counts, ascending (the last is the whole shard).
+std::vector<LevelStep> plan_levels(const std::vector<int64_t>& sizes, int64_t shard_rows, int k) {
+    const int L = (int)sizes.size();
     std::vector<LevelStep> steps;
     // First level: the smallest with at least k rows whose dense candidate
     // list fits the selector.
     int i0 = -1;
     for (int i = 0; i < L; i++) {
-        if (sh.levels[i].n >= k || i == L - 1) {
-            if (sh.levels[i].n <= kCapMax) i0 = i;
+        if (sizes[i] >= k || i == L - 1) {
+            if (sizes[i] <= kCapMax) i0 = i;
             break;
         }
     }
     if (i0 < 0)
         throw Error(MDH_ERR_UNSUPPORTED, "k = " + std::to_string(k) +
                                              " is larger than this build's exact selector supports for a corpus of " +
-                                             std::to_string(sh.n) + " rows");
+                                             std::to_string(shard_rows) + " rows");
     // A list must hold more than k entries: the rerun threshold (k-th
     // smallest stored key) is then strictly below the largest stored key,
     // so every overflow round makes progress even when distances tie.
     const int cap_floor = next_pow2(std::max(k + 1, 64));
     auto limit = [&](int cap) { return g_cap_limit > 0 ? std::max(cap_floor, std::min(cap, g_cap_limit)) : cap; };
-    steps.push_back({i0, limit(next_pow2(std::max<int64_t>(sh.levels[i0].n, k))), true});
+    steps.push_back({i0, limit(next_pow2(std::max<int64_t>(sizes[i0], k))), true});
     const double rmax = std::max(4.0, 2048.0 / (double)k);
     int cur = i0;
     while (cur != L - 1) {
         int nxt = cur + 1;
         for (int j = cur + 1; j < L; j++)
-            if ((double)sh.levels[j].n <= (double)sh.levels[cur].n * rmax) nxt = j;
-        double ratio = (double)sh.levels[nxt].n / (double)std::max<int64_t>(sh.levels[cur].n, 1);
+            if ((double)sizes[j] <= (double)sizes[cur] * rmax) nxt = j;
+        double ratio = (double)sizes[nxt] / (double)std::max<int64_t>(sizes[cur], 1);
         int cap = next_pow2((int64_t)(3.0 * k * ratio) + 256);
         cap = std::max(4096, std::min(kCapMax, cap));
-        if (nxt == L - 1 && sh.levels[nxt].n <= kCapMax) cap = std::max(cap, next_pow2(std::max<int64_t>(sh.levels[nxt].n, k)));
+        if (nxt == L - 1 && sizes[nxt] <= kCapMax) cap = std::max(cap, next_pow2(std::max<int64_t>(sizes[nxt], k)));
         cap = std::min(cap, kCapMax);
         steps.push_back({nxt, limit(cap), false});
         cur = nxt;
     }
     return steps;
+}
+
+std::vector<LevelStep> plan_levels(const Shard& sh, int k) {
+    std::vector<int64_t> sizes;
+    for (const Level& lv : sh.levels) sizes.push_back(lv.n);
+    return plan_levels(sizes, sh.n, k);
 }
 
 void grow(void** p, size_t* have, size_t need) {
@@ -139,9 +146,17 @@ void growT(T** p, size_t* have, size_t need_bytes) {
 
 void ensure_status(Workspace& w) {
     if (!w.status) {
-        MDH_CUDA(cudaMalloc(&w.status, 8 * sizeof(int32_t)));
-        MDH_CUDA(cudaHostAlloc(&w.h_status, 8 * sizeof(int32_t), cudaHostAllocDefault));
+        MDH_CUDA(cudaMalloc(&w.status, kStatusWords * sizeof(int32_t)));
+        MDH_CUDA(cudaHostAlloc(&w.h_status, kStatusWords * sizeof(int32_t), cudaHostAllocDefault));
     }
+    for (cudaEvent_t* e : {&w.ev0, &w.ev1, &w.ev_start, &w.ev_sel, &w.ev_rescore, &w.ev_prep})
+        if (!*e) MDH_CUDA(cudaEventCreate(e));
+}
+
+float event_ms(cudaEvent_t a, cudaEvent_t b) {
+    float ms = 0.0f;
+    MDH_CUDA(cudaEventElapsedTime(&ms, a, b));
+    return ms;
 }
 
 // Run one level's filter for `nq` queries already staged in the workspace.
@@ -166,6 +181,7 @@ int run_filter(mdh_index* ix, Shard& sh, const Level& lv, const QueryPlan& qp, c
                const int32_t* qn, const float* q_f32, int nq, const uint32_t* tk, const int32_t* ti, int cap,
                bool dense, const uint16_t* q_bf16 = nullptr, bool exact_only = false) {
     Workspace& w = sh.ws;
+    unsigned long long* bstats = reinterpret_cast<unsigned long long*>(w.status + kStatusBlockStats);
     const int d = dense ? 1 : 0;
     int used = 1;
     if (!qp.integer && qp.kind == kScoreSpeedCos && q_bf16 && !exact_only && g_scan_path != 1 &&
@@ -176,6 +192,7 @@ int run_filter(mdh_index* ix, Shard& sh, const Level& lv, const QueryPlan& qp, c
         launch_filter_tc_bf16_cos(lv, ix->dim, q_bf16, nq, tk, w.counts, w.cand, cap, d, bf16_cos_eps(ix->dim),
                                   w.status, sh.stream);
         if (dense) launch_fill_u32(w.counts, nq, (uint32_t)lv.n, sh.stream);
+        MDH_CUDA(cudaEventRecord(w.ev_rescore, sh.stream));
         launch_rescore_speed_cos(w.counts, w.cand, cap, lv.rows_f32, ix->dim, q_f32, nq, sh.stream);
         return 4;
     }
@@ -193,7 +210,8 @@ int run_filter(mdh_index* ix, Shard& sh, const Level& lv, const QueryPlan& qp, c
                 launch_filter_tc2_u8_l2(lv, ix->dpad, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, d, w.status,
                                         sh.stream);
             else if (used == 2)
-                launch_filter_tc_u8_l2(lv, ix->dpad, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, d, w.status, sh.stream);
+                launch_filter_tc_u8_l2(lv, ix->dpad, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, d, w.status, bstats,
+                                       sh.stream);
             else if (stream_supported(ix->dpad, lv))
                 launch_scan_stream_u8(lv, ix->dpad, 0, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, d, w.status,
                                       sh.stream);
@@ -222,6 +240,13 @@ struct ShardResult {
     int64_t candidates = 0;   // entries of the final candidate lists
     int64_t violations = 0;   // verification: rows misplaced relative to the results
     int64_t verified = 0;     // verification: queries re-checked
+    double sample_ms = 0.0;   // event time of the sample levels (scans and selections)
+    double select_ms = 0.0;   // final selection, overflow reruns included
+    double rescore_ms = 0.0;  // exact rescore inside the full-level scan (bf16 path)
+    int64_t tc_pairs = 0;     // pairs scanned by the 1-SM tensor scan (its block bound applies)
+    int64_t blocks_tested = 0;
+    int64_t blocks_passed = 0;
+    int64_t pruned = 0;       // tc_pairs whose distance the block bound made unnecessary
 };
 
 // Exact top-k for nq staged queries on one shard.  Results: ws.out_key /
@@ -244,11 +269,18 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
     growT(&w.out_id, &w.out_id_bytes, (size_t)nq * k * 4);
     growT(&w.flags, &w.flags_bytes, (size_t)nq * 4);
     ensure_status(w);
-    MDH_CUDA(cudaMemsetAsync(w.status, 0, 6 * sizeof(int32_t), st));
+    MDH_CUDA(cudaMemsetAsync(w.status, 0, 12 * sizeof(int32_t), st));
     unsigned long long* n_cand = reinterpret_cast<unsigned long long*>(w.status + 2);
     unsigned long long* n_viol = reinterpret_cast<unsigned long long*>(w.status + 4);
+    // Tests of the 1-SM tensor scan's schedule form: every (query, 64-row block).
+    auto count_tc = [&](const Level& lv, int used, int m) {
+        if (used != 2) return;
+        res.tc_pairs += lv.n * (int64_t)m;
+        res.blocks_tested += lv.n_pad / 64 * (int64_t)m;
+    };
 
     res.levels = (int)steps.size();
+    MDH_CUDA(cudaEventRecord(w.ev_start, st));
     for (size_t si = 0; si < steps.size(); si++) {
         const LevelStep& s = steps[si];
         const Level& lv = sh.levels[s.level];
@@ -259,15 +291,12 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)nq * 4, st));
         const bool last_level = si + 1 == steps.size();
         if (last_level) {
-            if (!w.ev0) {
-                MDH_CUDA(cudaEventCreate(&w.ev0));
-                MDH_CUDA(cudaEventCreate(&w.ev1));
-            }
             MDH_CUDA(cudaEventRecord(w.ev0, st));
         }
         const bool dense = s.dense && s.cap >= lv.n;
         const int used = run_filter(ix, sh, lv, qp, w.q_u8, w.qn, w.q_f32, nq, w.thr_key, w.thr_id, s.cap, dense,
                                     w.q_bf16);
+        count_tc(lv, used, nq);
         res.launches += (dense ? 2 : 1) + (used == 4 ? 1 : 0);
         if (last_level) {
             MDH_CUDA(cudaEventRecord(w.ev1, st));
@@ -281,6 +310,7 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
         launch_select(w.counts, w.cand, s.cap, lv.ids, nq, k, final_ ? 1 : 0, w.thr_key, w.thr_id, w.out_key,
                       w.out_id, w.flags, w.status + 1, nullptr, final_ ? n_cand : nullptr, st);
         res.launches++;
+        if (final_) MDH_CUDA(cudaEventRecord(w.ev_sel, st));
     }
     // Status words: [0] device error of the tensor-core scan, [1] overflowed queries.
     MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
@@ -288,12 +318,12 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
     if (w.h_status[0] != kDevOk)
         throw Error(w.h_status[0] == kDevTimeout ? MDH_ERR_TIMEOUT : MDH_ERR_INTERNAL,
                     "tensor-core scan reported device status " + std::to_string(w.h_status[0]));
-    {
-        float ms = 0.0f;
-        MDH_CUDA(cudaEventElapsedTime(&ms, w.ev0, w.ev1));
-        res.scan_ms = ms;
-    }
+    res.scan_ms = event_ms(w.ev0, w.ev1);
+    res.sample_ms = steps.size() > 1 ? event_ms(w.ev_start, w.ev0) : 0.0;
+    res.select_ms = event_ms(w.ev1, w.ev_sel);
+    if (qp.kind == kScoreSpeedCos && res.scan_path == 4) res.rescore_ms = event_ms(w.ev_rescore, w.ev1);
     int flagged = w.h_status[1];
+    const auto t_rerun = std::chrono::high_resolution_clock::now();
     const LevelStep last = steps.back();
     const Level& lv = sh.levels[last.level];
     int rounds = 0;
@@ -350,7 +380,7 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
             MDH_CUDA(cudaStreamSynchronize(st));
         }
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
-        run_filter(ix, sh, lv, qp, cq_u8, cqn, cq_f32, m, d_tk, d_ti, last.cap, false, nullptr, true);
+        count_tc(lv, run_filter(ix, sh, lv, qp, cq_u8, cqn, cq_f32, m, d_tk, d_ti, last.cap, false, nullptr, true), m);
         MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
         launch_select(w.counts, w.cand, last.cap, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id, w.flags,
                       w.status + 1, d_list, n_cand, st);
@@ -362,6 +392,9 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
         flagged = w.h_status[1];
         res.pairs += lv.n * (int64_t)m;
     }
+    if (rounds > 0)
+        res.select_ms += std::chrono::duration<double, std::milli>(std::chrono::high_resolution_clock::now() - t_rerun)
+                             .count();
     // Verification (opt-in): for up to g_verify queries, an exact scan with no
     // pruning (the CUDA-core kernels compare every row) counts the rows at or
     // before each query's k-th result by (key, id).  An exact result has
@@ -392,16 +425,19 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
         res.launches += 4;
         res.verified = m;
     }
-    MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 6 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 12 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
     MDH_CUDA(cudaStreamSynchronize(st));
     if (w.h_status[0] != kDevOk)
         throw Error(MDH_ERR_TIMEOUT, "scan reported device status " + std::to_string(w.h_status[0]));
     {
-        unsigned long long cand_n = 0, viol_n = 0;
+        unsigned long long cand_n = 0, viol_n = 0, bs[3] = {};
         std::memcpy(&cand_n, w.h_status + 2, 8);
         std::memcpy(&viol_n, w.h_status + 4, 8);
+        std::memcpy(bs, w.h_status + kStatusBlockStats, sizeof(bs));
         res.candidates = (int64_t)cand_n;
         res.violations = (int64_t)viol_n;
+        res.blocks_passed = (int64_t)bs[1];
+        res.pruned = res.tc_pairs - (int64_t)bs[2];
     }
     (void)host_q_u8;
     return res;
@@ -511,6 +547,7 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
     std::vector<uint32_t> hkey((size_t)chunk * kk);
     std::vector<int32_t> hid((size_t)chunk * kk);
     for (int c0 = 0; c0 < nq; c0 += chunk) {
+        const auto t_chunk = std::chrono::high_resolution_clock::now();
         const int m = std::min(chunk, nq - c0);
         // This chunk's u8 queries with the padded row stride: the caller's
         // rows themselves when dim is already a multiple of the stride unit,
@@ -535,15 +572,19 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
         } else {
             prepare_float_queries(ix, qp, host_f32 + (size_t)c0 * dim, m, mode, qbuf_f32);
         }
+        const auto t_staged = std::chrono::high_resolution_clock::now();  // host part of the query staging
         std::vector<ShardResult> sres((size_t)nshard);
         std::vector<std::string> errs((size_t)nshard);
         std::vector<mdh_status> codes((size_t)nshard, MDH_OK);
         std::vector<int64_t> st_launch((size_t)nshard, 0);
+        std::vector<double> st_prep((size_t)nshard, 0.0);
         auto run = [&](int si) {
             try {
                 Shard& sh = ix->shards[(size_t)si];
                 MDH_CUDA(cudaSetDevice(sh.device));
                 Workspace& w = sh.ws;
+                ensure_status(w);
+                MDH_CUDA(cudaEventRecord(w.ev_prep, sh.stream));
                 if (qp.integer) {
                     growT(&w.q_u8, &w.q_u8_bytes, (size_t)m * dpad);
                     growT(&w.qn, &w.qn_bytes, (size_t)m * 4);
@@ -560,6 +601,7 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
                     }
                 }
                 sres[(size_t)si] = search_shard(ix, sh, qp, m, kk, qsrc, qbuf_f32.data(), (size_t)dim);
+                st_prep[(size_t)si] = event_ms(w.ev_prep, w.ev_start);
             } catch (const Error& e) {
                 codes[(size_t)si] = e.code;
                 errs[(size_t)si] = e.what();
@@ -577,8 +619,16 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
         }
         for (int si = 0; si < nshard; si++)
             if (codes[(size_t)si] != MDH_OK) throw Error(codes[(size_t)si], errs[(size_t)si]);
-        double chunk_scan_ms = 0.0;
+        double chunk_scan_ms = 0.0, chunk_sample_ms = 0.0, chunk_select_ms = 0.0, chunk_rescore_ms = 0.0,
+               chunk_prep_ms = 0.0;
+        for (double p : st_prep) chunk_prep_ms = std::max(chunk_prep_ms, p);
         for (auto& r : sres) {
+            chunk_sample_ms = std::max(chunk_sample_ms, r.sample_ms);
+            chunk_select_ms = std::max(chunk_select_ms, r.select_ms);
+            chunk_rescore_ms = std::max(chunk_rescore_ms, r.rescore_ms);
+            st.blocks_tested += r.blocks_tested;
+            st.blocks_passed += r.blocks_passed;
+            st.pairs_pruned_by_bound += r.pruned;
             st.pairs_scored += r.pairs;
             st.levels = std::max(st.levels, r.levels);
             st.tensor_core_path = std::max(st.tensor_core_path, r.scan_path - 1);
@@ -590,6 +640,11 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
             chunk_scan_ms = std::max(chunk_scan_ms, r.scan_ms);  // shards run concurrently
         }
         st.full_scan_ms += chunk_scan_ms;
+        st.sample_ms += chunk_sample_ms;
+        st.select_ms += chunk_select_ms;
+        st.rescore_ms += chunk_rescore_ms;
+        st.prep_ms += chunk_prep_ms +
+                      std::chrono::duration<double, std::milli>(t_staged - t_chunk).count();
         for (int64_t l : st_launch) st.kernel_launches += l;
         // Gather / merge to the first shard's device.
         Shard& s0 = ix->shards[0];
@@ -780,6 +835,13 @@ mdh_status mdh_index_info(const mdh_index* index, int64_t* n, int32_t* dim, int3
     });
 }
 
+mdh_status mdh_index_id_base(const mdh_index* index, int64_t* first_id) {
+    return guard([&] {
+        MDH_REQUIRE(index && first_id, MDH_ERR_INVALID_ARG, "null argument");
+        *first_id = index->shards.empty() ? 0 : index->shards[0].id_base;
+    });
+}
+
 mdh_status mdh_search_f32(mdh_index* index, const float* host_queries, int32_t nq, int32_t k, int32_t mode,
                           int32_t* out_ids, float* out_dist, mdh_stats* stats) {
     return guard([&] {
@@ -818,6 +880,8 @@ mdh_status mdh_search_u8_device(mdh_index* index, const uint8_t* dev_queries, in
             if (nq > 0 && k > 0) {
                 Workspace& w = sh.ws;
                 const int dpad = index->dpad;
+                ensure_status(w);
+                MDH_CUDA(cudaEventRecord(w.ev_prep, sh.stream));
                 growT(&w.q_u8, &w.q_u8_bytes, (size_t)nq * dpad);
                 growT(&w.qn, &w.qn_bytes, (size_t)nq * 4);
                 if (dpad != index->dim) MDH_CUDA(cudaMemsetAsync(w.q_u8, 0, (size_t)nq * dpad, sh.stream));
@@ -838,6 +902,12 @@ mdh_status mdh_search_u8_device(mdh_index* index, const uint8_t* dev_queries, in
                 st.candidates = r.candidates;
                 st.bound_violations = r.violations;
                 st.verified_queries = r.verified;
+                st.sample_ms = r.sample_ms;
+                st.select_ms = r.select_ms;
+                st.blocks_tested = r.blocks_tested;
+                st.blocks_passed = r.blocks_passed;
+                st.pairs_pruned_by_bound = r.pruned;
+                if (kk > 0) st.prep_ms = event_ms(w.ev_prep, w.ev_start);
                 if (kk == k) {
                     MDH_CUDA(cudaMemcpyAsync(dev_ids, w.out_id, (size_t)nq * k * 4, cudaMemcpyDeviceToDevice, sh.stream));
                     if (dev_dist)
@@ -890,6 +960,25 @@ mdh_status mdh_set_verify(int32_t max_queries) {
         MDH_REQUIRE(max_queries >= 0 && max_queries <= 65536, MDH_ERR_INVALID_ARG, "max_queries must be in [0, 65536]");
         g_verify = max_queries;
     });
+}
+
+mdh_status mdh_set_sample_ratio(int32_t ratio) {
+    return guard([&] {
+        MDH_REQUIRE(ratio == 0 || (ratio >= 2 && ratio <= 65536), MDH_ERR_INVALID_ARG,
+                    "ratio must be 0 or in [2, 65536]");
+        g_sample_top_ratio = ratio == 0 ? kSampleTopRatioDefault : ratio;
+    });
+}
+
+int32_t mdh_plan_level_count(int64_t shard_rows, int32_t k) {
+    if (shard_rows <= 0 || k <= 0) return 0;
+    try {
+        std::vector<int64_t> sizes = plan_samples(shard_rows);
+        sizes.push_back(shard_rows);
+        return (int32_t)plan_levels(sizes, shard_rows, (int)std::min<int64_t>(k, shard_rows)).size();
+    } catch (...) {
+        return -1;
+    }
 }
 
 mdh_status mdh_set_candidate_cap_limit(int32_t cap) {

@@ -145,12 +145,26 @@ T* dalloc(size_t count) {
     return static_cast<T*>(p);
 }
 
-// Nested sample sizes: 1024 * 32^j while the sample stays <= n / 8.
+}  // namespace
+
+int g_sample_top_ratio = kSampleTopRatioDefault;
+
+// Nested sample sizes for a shard of n rows: 1024 * 32^j while the sample
+// stays <= n / R (R = g_sample_top_ratio), then n / R itself when that ladder
+// stops more than 4x below it.  The largest sample sets the full level's
+// threshold: about k * n / (its size) rows of the shard pass it, so its size
+// tracks the shard (a fixed size would cost a fixed scan per rank however
+// many ranks share the corpus).  Shards under 8,192 rows get no sample.
 std::vector<int64_t> plan_samples(int64_t n) {
     std::vector<int64_t> s;
-    for (int64_t m = 1024; m * 8 <= n; m *= 32) s.push_back(m);
+    if (n < 8 * 1024) return s;
+    const int64_t top = std::max<int64_t>(1024, n / std::max(2, g_sample_top_ratio));
+    for (int64_t m = 1024; m <= top; m *= 32) s.push_back(m);
+    if (top > 4 * s.back()) s.push_back(top);
     return s;
 }
+
+namespace {
 
 void build_samples(mdh_index* ix, Shard& sh, bool u8, bool f32) {
     cudaStream_t st = sh.stream;
@@ -322,8 +336,8 @@ void free_workspace(Workspace& w) {
                     w.qlist, w.status, w.tmp};
     for (void* p : ptrs) cudaFree(p);
     if (w.h_status) cudaFreeHost(w.h_status);
-    if (w.ev0) cudaEventDestroy(w.ev0);
-    if (w.ev1) cudaEventDestroy(w.ev1);
+    for (cudaEvent_t e : {w.ev0, w.ev1, w.ev_start, w.ev_sel, w.ev_rescore, w.ev_prep})
+        if (e) cudaEventDestroy(e);
     w = Workspace();
 }
 

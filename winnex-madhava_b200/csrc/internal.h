@@ -47,12 +47,17 @@ struct Workspace {
     int32_t* out_id = nullptr;   size_t out_id_bytes = 0;   // [nq][k]
     int32_t* flags = nullptr;    size_t flags_bytes = 0;    // [nq] overflow flags
     int32_t* qlist = nullptr;    size_t qlist_bytes = 0;    // [nq] query index list
-    int32_t* status = nullptr;   // [8] device status words: [0] scan error, [1] overflowed
-                                 // queries, [2..3] u64 final candidates, [4..5] u64 violations
+    int32_t* status = nullptr;   // [kStatusWords] device status words: [0] scan error, [1] overflowed
+                                 // queries, [2..3] u64 final candidates, [4..5] u64 violations,
+                                 // [6..11] u64 block-bound counts (tests, unsettled, rows formed)
     int32_t* h_status = nullptr;                             // pinned mirror
     void* tmp = nullptr;         size_t tmp_bytes = 0;      // CUB / misc scratch
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;               // brackets the full-shard scan
+    cudaEvent_t ev_start = nullptr, ev_sel = nullptr;       // first level's start; end of the final selection
+    cudaEvent_t ev_rescore = nullptr, ev_prep = nullptr;    // start of the rescore; start of query staging
 };
+constexpr int kStatusWords = 16;
+constexpr int kStatusBlockStats = 6;   // first word of the three u64 block-bound counters
 
 struct Shard {
     int device = 0;
@@ -78,6 +83,11 @@ struct mdh_index {
 namespace mdh {
 
 // ---- index build (index.cu) ----
+// Largest sample of a shard of n rows is about n / g_sample_top_ratio rows
+// (process-wide; read when samples are built: index create and load).
+constexpr int kSampleTopRatioDefault = 64;
+extern int g_sample_top_ratio;
+std::vector<int64_t> plan_samples(int64_t n);   // nested sample sizes, ascending
 void build_shard_u8(mdh_index* ix, Shard& sh, const uint8_t* host_rows, int64_t n);
 void build_shard_f32(mdh_index* ix, Shard& sh, const float* host_rows, int64_t n);
 // Device buffers of a level of n rows padded to kTileRows (pad rows: zero
@@ -136,9 +146,14 @@ void encode_u8_rows_tmap(CUtensorMap* map, const void* base, int64_t rows, int d
 int choose_scan_chunks(int groups, int n_tiles, int workers);
 bool tc_supported(const mdh_index* ix, const Level& lv);
 void make_tmap_rows(Level& lv, int dpad);
+// block_stats (may be null): [0] += bound tests counted by the kernel (unit
+// tables only; the schedule form tests every (query, 64-row block)), [1] +=
+// tests the bound did not settle, [2] += real rows of those blocks (pairs whose
+// exact distance was formed).
 void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
                             const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts,
-                            uint2* cand, int cap, int dense, int32_t* status, cudaStream_t st);
+                            uint2* cand, int cap, int dense, int32_t* status, unsigned long long* block_stats,
+                            cudaStream_t st);
 // Unit-table form of the tensor-core scan (used by the IVF search, ivf.cu):
 // unit u scans query rows [q_row, q_row + q_count) of `qmat` (row i is query
 // qmap[i]; thresholds, norms and candidate lists are indexed by that query)
@@ -158,7 +173,8 @@ struct ScanUnit {
 void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat, int qmat_rows, const int32_t* qmap,
                                   const int32_t* qn, const ScanUnit* units, int n_units, const int32_t* n_units_dev,
                                   int32_t* unit_counter, const uint32_t* thr_key, const int32_t* thr_id,
-                                  uint32_t* counts, uint2* cand, int cap, int32_t* status, cudaStream_t st);
+                                  uint32_t* counts, uint2* cand, int cap, int32_t* status,
+                                  unsigned long long* block_stats, cudaStream_t st);
 // ---- tensor-core scan on SM pairs (scan_tc2.cu) ----
 bool tc2_supported(const mdh_index* ix, const Level& lv);
 void make_tmap_rows_pair(Level& lv, int dpad);

@@ -813,22 +813,23 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         grow_dev(&w.out_id, &w.out_id_bytes, (size_t)m * k * 4);
         grow_dev(&w.qlist, &w.qlist_bytes, (size_t)m * 4);  // overflow flags
         if (!w.status) {
-            MDH_CUDA(cudaMalloc(&w.status, 8 * sizeof(int32_t)));
-            MDH_CUDA(cudaHostAlloc(&w.h_status, 8 * sizeof(int32_t), cudaHostAllocDefault));
+            MDH_CUDA(cudaMalloc(&w.status, kStatusWords * sizeof(int32_t)));
+            MDH_CUDA(cudaHostAlloc(&w.h_status, kStatusWords * sizeof(int32_t), cudaHostAllocDefault));
         }
         if (!w.ev0) {
             MDH_CUDA(cudaEventCreate(&w.ev0));
             MDH_CUDA(cudaEventCreate(&w.ev1));
         }
-        MDH_CUDA(cudaMemsetAsync(w.status, 0, 6 * sizeof(int32_t), st));
+        MDH_CUDA(cudaMemsetAsync(w.status, 0, 12 * sizeof(int32_t), st));
         unsigned long long* n_cand = reinterpret_cast<unsigned long long*>(w.status + 2);
+        unsigned long long* bstats = reinterpret_cast<unsigned long long*>(w.status + kStatusBlockStats);
         // Pass 0: coarse samples of the probed cells, infinite thresholds; the
         // k-th (key, id) is a threshold for the union (the sample is part of it).
         launch_fill_threshold(w.thr_key, w.thr_id, m, kKeyInf, kIdInf, st);
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
         launch_filter_tc_u8_l2_units(ix->coarse, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[0].units,
                                      (int)bound[0], nunits, ucounter, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap0,
-                                     w.status, st);
+                                     w.status, bstats, st);
         launch_select(w.counts, w.cand, kIvfCap0, ix->coarse.ids, m, k, 0, w.thr_key, w.thr_id, w.out_key, w.out_id,
                       w.qlist, w.status + 1, nullptr, nullptr, st);
         // Pass 1: the samples with that threshold tighten it (a list that
@@ -836,7 +837,7 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
         launch_filter_tc_u8_l2_units(ix->sample, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[1].units,
                                      (int)bound[1], nunits + 1, ucounter, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap1,
-                                     w.status, st);
+                                     w.status, bstats, st);
         launch_select(w.counts, w.cand, kIvfCap1, ix->sample.ids, m, k, 0, w.thr_key, w.thr_id, w.out_key, w.out_id,
                       w.qlist, w.status + 1, nullptr, nullptr, st);
         s.kernel_launches += 6;
@@ -845,7 +846,7 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         MDH_CUDA(cudaEventRecord(w.ev0, st));
         launch_filter_tc_u8_l2_units(lv, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[2].units, (int)bound[2],
                                      nunits + 2, ucounter, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap2,
-                                     w.status, st);
+                                     w.status, bstats, st);
         MDH_CUDA(cudaEventRecord(w.ev1, st));
         launch_select(w.counts, w.cand, kIvfCap2, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id, w.qlist,
                       w.status + 1, nullptr, n_cand, st);
@@ -855,12 +856,13 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         hkey.resize((size_t)m * k);
         hid.resize((size_t)m * k);
         unsigned long long pairs[kIvfPasses] = {};
-        MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 6 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+        MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 12 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
         MDH_CUDA(cudaMemcpyAsync(pairs, ix->plan_pairs, sizeof(pairs), cudaMemcpyDeviceToHost, st));
         MDH_CUDA(cudaMemcpyAsync(hkey.data(), w.out_key, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
         MDH_CUDA(cudaMemcpyAsync(hid.data(), w.out_id, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
         MDH_CUDA(cudaStreamSynchronize(st));
-        s.pairs_scored += (int64_t)(pairs[0] + pairs[1] + pairs[2]);
+        int64_t chunk_pairs = (int64_t)(pairs[0] + pairs[1] + pairs[2]);
+        s.pairs_scored += chunk_pairs;
         s.full_scan_pairs += (int64_t)pairs[2];
         if (w.h_status[0] != kDevOk)
             throw Error(MDH_ERR_TIMEOUT, "IVF scan reported device status " + std::to_string(w.h_status[0]));
@@ -878,12 +880,13 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
             MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
             launch_filter_tc_u8_l2_units(lv, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[2].units,
                                          (int)bound[2], nunits + 2, ucounter, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap2,
-                                         w.status, st);
+                                         w.status, bstats, st);
             launch_select(w.counts, w.cand, kIvfCap2, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id,
                           w.qlist, w.status + 1, nullptr, n_cand, st);
             s.kernel_launches += 2;
             s.pairs_scored += (int64_t)pairs[2];
-            MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 6 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+            chunk_pairs += (int64_t)pairs[2];
+            MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 12 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
             MDH_CUDA(cudaMemcpyAsync(hkey.data(), w.out_key, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
             MDH_CUDA(cudaMemcpyAsync(hid.data(), w.out_id, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
             MDH_CUDA(cudaStreamSynchronize(st));
@@ -891,9 +894,15 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
                 throw Error(MDH_ERR_TIMEOUT, "IVF scan reported device status " + std::to_string(w.h_status[0]));
         }
         {
-            unsigned long long cand_n = 0;
+            unsigned long long cand_n = 0, bs[3] = {};
             std::memcpy(&cand_n, w.h_status + 2, 8);
+            std::memcpy(bs, w.h_status + kStatusBlockStats, sizeof(bs));
             s.candidates += (int64_t)cand_n;
+            // Every pass and rerun ran the unit-table scan: each pair of a
+            // probed cell was either settled by its chunk's bound or formed.
+            s.blocks_tested += (int64_t)bs[0];
+            s.blocks_passed += (int64_t)bs[1];
+            s.pairs_pruned_by_bound += chunk_pairs - (int64_t)bs[2];
         }
         for (size_t i = 0; i < (size_t)m * k; i++) {
             out_ids[(size_t)c0 * k + i] = hid[i];

@@ -118,7 +118,7 @@ void filter(mdh_index* ix, const Level& lv, const uint8_t* q, const int32_t* qn,
             int* path) {
     const int d = dense ? 1 : 0;
     if (lv.has_tmap && tc_supported(ix, lv)) {
-        launch_filter_tc_u8_l2(lv, ix->dpad, q, qn, nq, tk, ti, counts, cand, cap, d, status, st);
+        launch_filter_tc_u8_l2(lv, ix->dpad, q, qn, nq, tk, ti, counts, cand, cap, d, status, nullptr, st);
         *path = 1;
     } else if (stream_supported(ix->dpad, lv)) {
         launch_scan_stream_u8(lv, ix->dpad, 0, q, qn, nq, tk, ti, counts, cand, cap, d, status, st);

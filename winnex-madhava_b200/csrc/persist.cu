@@ -164,6 +164,10 @@ FileHeader read_header(int fd, const std::string& path) {
         const std::string which = "shard " + std::to_string(i) + ": ";
         if (s.rows < 0 || s.rows > f.n) io_fail(path, which + "row count out of range");
         if (s.id_base < 0 || s.id_base + s.rows > 0x7FFFFFFF) io_fail(path, which + "row ids out of int32 range");
+        // The shards' id ranges tile one run [first id, first id + n) in file
+        // order, so no two shards can hand out the same id.
+        if (i > 0 && s.id_base != f.shards.back().id_base + f.shards.back().rows)
+            io_fail(path, which + "id range does not follow the previous shard's");
         if (s.bytes != (uint64_t)s.rows * per_row) io_fail(path, which + "size does not match its row count");
         if (s.offset % kAlign != 0 || s.offset < prev_end) io_fail(path, which + "bad offset");
         if (s.offset > actual || s.bytes > actual - s.offset) io_fail(path, which + "runs past the end of the file");
@@ -305,9 +309,12 @@ void file_to_device(int fd, uint64_t off, void* dev, uint64_t bytes, cudaStream_
 // u8 level check, 8 lanes per row (16 bytes each per step): the row's |v|^2
 // over its padded stride equals the stored norm, its id lies in [id_lo,
 // id_hi), and (norm, id) ascends strictly from the previous position.
+// seen: a zeroed bitmap of id_hi - id_lo bits; each id sets its bit, and an
+// id whose bit was already set is a duplicate.  n ids in range with no
+// duplicate are a permutation of [id_lo, id_hi).
 __global__ void k_check_level_u8(const uint8_t* __restrict__ rows, const int32_t* __restrict__ norms,
                                  const int32_t* __restrict__ ids, int64_t n, int dpad, int64_t id_lo, int64_t id_hi,
-                                 unsigned long long* __restrict__ bad) {
+                                 uint32_t* __restrict__ seen, unsigned long long* __restrict__ bad) {
     const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
     const int l8 = threadIdx.x & 7;
     uint32_t s = 0;
@@ -327,6 +334,11 @@ __global__ void k_check_level_u8(const uint8_t* __restrict__ rows, const int32_t
     if (r < n && l8 == 0) {
         const int32_t nr = norms[r], id = ids[r];
         bool ok = (int32_t)s == nr && id >= id_lo && id < id_hi;
+        if (id >= id_lo && id < id_hi) {
+            const int64_t b = id - id_lo;
+            const uint32_t bit = 1u << (b & 31);
+            if (atomicOr(seen + (b >> 5), bit) & bit) ok = false;
+        }
         if (r > 0) {
             const int32_t np = norms[r - 1], ip = ids[r - 1];
             ok = ok && (np < nr || (np == nr && ip < id));
@@ -357,16 +369,18 @@ __global__ void k_check_level_f32(const float* __restrict__ rows, const float* _
 uint64_t check_level(const mdh_index* ix, const Shard& sh, const Level& lv) {
     if (lv.n == 0) return 0;
     unsigned long long* bad = nullptr;
-    MDH_CUDA(cudaMalloc(&bad, sizeof(unsigned long long)));
+    const size_t seen_bytes = ix->is_f32 ? 0 : (size_t)((sh.n + 31) / 32) * 4;
+    MDH_CUDA(cudaMalloc(&bad, sizeof(unsigned long long) + seen_bytes));
+    uint32_t* seen = reinterpret_cast<uint32_t*>(bad + 1);
     unsigned long long h = 0;
     try {
-        MDH_CUDA(cudaMemsetAsync(bad, 0, sizeof(unsigned long long), sh.stream));
+        MDH_CUDA(cudaMemsetAsync(bad, 0, sizeof(unsigned long long) + seen_bytes, sh.stream));
         if (ix->is_f32)
             k_check_level_f32<<<(unsigned)((lv.n + 255) / 256), 256, 0, sh.stream>>>(
                 lv.rows_f32, lv.norms_f32, lv.ids, lv.n, ix->dim, ix->metric == MDH_METRIC_COSINE, sh.id_base, bad);
         else
             k_check_level_u8<<<(unsigned)((lv.n * 8 + 255) / 256), 256, 0, sh.stream>>>(
-                lv.rows, lv.norms, lv.ids, lv.n, ix->dpad, sh.id_base, sh.id_base + sh.n, bad);
+                lv.rows, lv.norms, lv.ids, lv.n, ix->dpad, sh.id_base, sh.id_base + sh.n, seen, bad);
         MDH_CUDA(cudaGetLastError());
         MDH_CUDA(cudaMemcpyAsync(&h, bad, sizeof(h), cudaMemcpyDeviceToHost, sh.stream));
         MDH_CUDA(cudaStreamSynchronize(sh.stream));

@@ -6,8 +6,12 @@
 // Search runs on the GPU through libwinnex_madhava_b200.so with the GIL
 // released.  What changes by design:
 //   * MadhavaL2.search / search_batch return the exact top-K (the same list
-//     as search_exact); k1 = k2 = N, k3 = exact_evals = pairs scored,
-//     bound_violations = 0 (no pair is pruned without an exact comparison);
+//     as search_exact); k1 = k2 = N; pruned_by_bound = pairs the tensor
+//     scan's block bound proved outside the top-K without forming their
+//     distance (a Cauchy-Schwarz-style certificate on norm-sorted rows);
+//     k3 = exact_evals = the pairs whose exact distance was formed;
+//     bound_violations is measured when verification is on (set_verify) and
+//     is 0 otherwise;
 //   * SpeedEngine always runs on the GPU (has_gpu() is True); n_anchors is
 //     accepted, and the scan stays exact;
 //   * save_index / load_index write and read this library's index file (the
@@ -174,9 +178,10 @@ public:
             if (id >= 0) out.indices.push_back(id);
         out.k1 = n_;
         out.k2 = n_;
-        out.k3 = (int)std::min<int64_t>(st.pairs_scored, 0x7fffffff);
+        const int64_t formed = st.pairs_scored - st.pairs_pruned_by_bound;
+        out.k3 = (int)std::min<int64_t>(formed, 0x7fffffff);
         out.bound_pairs = n_;
-        out.exact_evals = st.pairs_scored;
+        out.exact_evals = formed;
         out.bound_violations = st.bound_violations;
         out.pruned_by_bound = st.pairs_pruned_by_bound;
         out.latency_ms = st.latency_ms;
@@ -231,6 +236,14 @@ public:
         if (s == MDH_ERR_IO) return false;
         check(s);
         h_.reset(p);
+        // Engine results index the corpus from row 0; a file holding another
+        // id range (one rank's rows of a larger corpus) cannot back it.
+        int64_t first = 0;
+        check(mdh_index_id_base(p, &first));
+        if (first != 0) {
+            h_.reset(nullptr);
+            return false;
+        }
         int64_t n = 0;
         int32_t dim = 0, metric = 0;
         check(mdh_index_info(p, &n, &dim, &metric, nullptr));
@@ -305,6 +318,10 @@ public:
         py::dict d;
         d["latency_ms"] = st.latency_ms;
         d["pairs_scored"] = (long long)st.pairs_scored;
+        d["pruned_by_bound"] = (long long)st.pairs_pruned_by_bound;
+        d["blocks_tested"] = (long long)st.blocks_tested;
+        d["blocks_passed"] = (long long)st.blocks_passed;
+        d["bound_violations"] = (long long)st.bound_violations;
         d["full_scan_ms"] = st.full_scan_ms;
         d["kernel_launches"] = (long long)st.kernel_launches;
         return py::make_tuple(ids, dist, d);
@@ -371,6 +388,8 @@ public:
         d["latency_ms"] = st.latency_ms;
         d["bound_pairs"] = (long long)n_;
         d["bound_violations"] = (long long)st.bound_violations;
+        d["pruned_by_bound"] = (long long)st.pairs_pruned_by_bound;
+        d["verified_queries"] = (long long)st.verified_queries;
         return d;
     }
 
@@ -392,9 +411,15 @@ public:
         out.reserve((size_t)nq * kk);
         for (int i = 0; i < nq; i++)
             for (int j = 0; j < kk; j++) out.push_back(ids[(size_t)i * k + j]);
+        // The reference returns indices and latency_ms here; the counters
+        // below are this library's additions (bound_pairs as in search()).
         py::dict d;
         d["indices"] = out;
         d["latency_ms"] = st.latency_ms;
+        d["bound_pairs"] = (long long)n_ * nq;
+        d["bound_violations"] = (long long)st.bound_violations;
+        d["pruned_by_bound"] = (long long)st.pairs_pruned_by_bound;
+        d["verified_queries"] = (long long)st.verified_queries;
         return d;
     }
 

@@ -102,7 +102,8 @@ struct TcCfg {
     static constexpr uint32_t OFF_USLOT = OFF_BAR + NUM_BARS * 8;  // two unit indices handed out at run time
     static constexpr uint32_t OFF_TMEM_SLOT = OFF_USLOT + 8;
     static constexpr uint32_t OFF_ABORT = OFF_TMEM_SLOT + 4;
-    static constexpr uint32_t SMEM_BYTES = OFF_ABORT + 4 + 1024;  // + alignment slack
+    static constexpr uint32_t OFF_STATS = OFF_ABORT + 4;        // u32 block-bound counts: tests, unsettled, rows
+    static constexpr uint32_t SMEM_BYTES = OFF_STATS + 12 + 1024;  // + alignment slack
     static_assert(ACC_COLS == 4 * COLS_PER_WARP && ACC_STAGES >= 2, "four 64-column parts per accumulator stage");
     static_assert(BN % BOX_ROWS == 0 && BN <= 256 && (COLS_PER_WARP % BN == 0 || BN % COLS_PER_WARP == 0),
                   "tile shape");
@@ -179,6 +180,12 @@ __device__ __forceinline__ void chunk_filter(const uint32_t (&v)[32], int32_t ne
     }
 }
 
+// Block-bound counts live in shared memory (three u32: tests, unsettled
+// blocks, real rows of those blocks) and are added on the rare unsettled path
+// only, so the common path keeps no counter in registers; the CTA adds them to
+// the global u64 counters once, at exit.
+__device__ __forceinline__ void stat_add(uint32_t* s, uint32_t v) { atomicAdd(s, v); }
+
 // Run-time hand-out of a unit table (its units differ in length, so fixed
 // shares leave some SMs idle at the end).  The producer takes the next index
 // from a global counter and publishes it in one of two shared-memory slots
@@ -228,7 +235,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                       const int32_t* __restrict__ thr_id, uint32_t* __restrict__ counts, uint2* __restrict__ cand,
                       int cap, int dense, Sched sched, int32_t* __restrict__ status,
                       const ScanUnit* __restrict__ units, const int32_t* __restrict__ qmap,
-                      const int32_t* __restrict__ n_units_dev, int32_t* __restrict__ unit_counter) {
+                      const int32_t* __restrict__ n_units_dev, int32_t* __restrict__ unit_counter,
+                      unsigned long long* __restrict__ block_stats) {
     constexpr int BN = C::BN, QT = C::QT, STAGES = C::STAGES, ACC_STAGES = C::ACC_STAGES;
     // A unit table built on the device carries its own length.
     const long long n_units = n_units_dev ? (long long)*n_units_dev : sched.n_units;
@@ -237,6 +245,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bars = sbase + C::OFF_BAR;
     volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + C::OFF_ABORT);
+    uint32_t* stats = reinterpret_cast<uint32_t*>(smem + C::OFF_STATS);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_TMEM_SLOT);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -258,6 +267,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(bars + 8 * (C::BAR_UNIT_EMPTY + s), EPI_WARPS + 1);
         }
         *abort_flag = 0;
+        stats[0] = stats[1] = stats[2] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -474,6 +484,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     fmaxf(__uint_as_float((uint32_t)max32(v[0])), __uint_as_float((uint32_t)max32(v[1]))));
                 if (2 * m >= need) {
                     const int32_t row0 = t * BN + rowoff;  // rows < 2^31 (ids are int32)
+                    if (block_stats) {
+                        stat_add(stats + 1, 1u);
+                        stat_add(stats + 2, (uint32_t)min(max(row_end - row0, 0), COLS_PER_WARP));
+                    }
                     chunk_filter(v[0], need, row0, row_end, tkey, tid, qnv, qi, norms, ids, dense, buf, counts, cand,
                                  cap);
                     chunk_filter(v[1], need, row0 + 32, row_end, tkey, tid, qnv, qi, norms, ids, dense, buf, counts,
@@ -599,6 +613,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int c = 0; c < 2; c++) {
                     uint32_t mask = (c ? pass1 : pass0) ? pass_mask32(v[c], c ? need1 : need0) : 0u;
                     const int32_t valid = row_end - (row0 + 32 * c);  // pad rows trail the cell
+                    if (block_stats && (c ? pass1 : pass0)) {
+                        stat_add(stats + 1, 1u);
+                        stat_add(stats + 2, (uint32_t)min(max(valid, 0), 32));
+                    }
                     if (valid < 32) mask &= valid > 0 ? (1u << valid) - 1u : 0u;
                     const int32_t nrc = c ? nr1 : nr0;
                     while (__any_sync(0xffffffffu, mask != 0u)) {
@@ -615,6 +633,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
             }
             if (qvalid) buf.flush(counts, cand, cap, qi);
+            // Two chunk tests per tile for each of the unit's queries.
+            if (block_stats && qvalid) stat_add(stats, 2u * (uint32_t)(t1 - t0));
         }
     }
 
@@ -624,6 +644,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         tmem_dealloc<1>(tmem_base, TMEM_COLS);
     }
+    if (block_stats && threadIdx.x == 0)
+        for (int i = 0; i < 3; i++)
+            if (stats[i]) atomicAdd(block_stats + i, (unsigned long long)stats[i]);
 }
 
 using CfgNarrow = TcCfg<256, 1>;  // 128 queries per CTA
@@ -701,7 +724,7 @@ void make_tmap_rows(Level& lv, int dpad) {
 template <class C>
 void launch_tc(const Level& lv, const CUtensorMap& tq, const int32_t* qn, int nq, const uint32_t* thr_key,
                const int32_t* thr_id, uint32_t* counts, uint2* cand, int cap, int dense, int32_t* status,
-               cudaStream_t st) {
+               unsigned long long* block_stats, cudaStream_t st) {
     int dev;
     MDH_CUDA(cudaGetDevice(&dev));
     const int sms = device_sm_count(dev);
@@ -717,25 +740,27 @@ void launch_tc(const Level& lv, const CUtensorMap& tq, const int32_t* qn, int nq
                                   (int)C::SMEM_BYTES));
     k_filter_tc_u8_l2<C, false><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
                                                                    qn, nq, thr_key, thr_id, counts, cand, cap, dense,
-                                                                   s, status, nullptr, nullptr, nullptr, nullptr);
+                                                                   s, status, nullptr, nullptr, nullptr, nullptr,
+                                                                   block_stats);
     MDH_CUDA(cudaGetLastError());
 }
 
 void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
                             const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts, uint2* cand, int cap,
-                            int dense, int32_t* status, cudaStream_t st) {
+                            int dense, int32_t* status, unsigned long long* block_stats, cudaStream_t st) {
     if (nq <= 0 || lv.n == 0) return;
     MDH_REQUIRE(dpad == BK && lv.has_tmap, MDH_ERR_INTERNAL, "tensor-core scan needs 128-byte rows and a TMA map");
     MDH_REQUIRE(!dense || cap >= lv.n, MDH_ERR_INTERNAL, "dense scan needs cap >= rows");
     CUtensorMap tq;
     encode_u8_rows_tmap(&tq, q, nq, dpad, BM);
-    launch_tc<CfgNarrow>(lv, tq, qn, nq, thr_key, thr_id, counts, cand, cap, dense, status, st);
+    launch_tc<CfgNarrow>(lv, tq, qn, nq, thr_key, thr_id, counts, cand, cap, dense, status, block_stats, st);
 }
 
 void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat, int qmat_rows, const int32_t* qmap,
                                   const int32_t* qn, const ScanUnit* units, int n_units, const int32_t* n_units_dev,
                                   int32_t* unit_counter, const uint32_t* thr_key, const int32_t* thr_id,
-                                  uint32_t* counts, uint2* cand, int cap, int32_t* status, cudaStream_t st) {
+                                  uint32_t* counts, uint2* cand, int cap, int32_t* status,
+                                  unsigned long long* block_stats, cudaStream_t st) {
     using C = CfgNarrow;
     if (n_units <= 0 || qmat_rows <= 0 || lv.n == 0) return;
     MDH_REQUIRE(dpad == BK && lv.has_tmap, MDH_ERR_INTERNAL, "tensor-core scan needs 128-byte rows and a TMA map");
@@ -752,7 +777,7 @@ void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat
     k_filter_tc_u8_l2<C, true><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
                                                                    qn, qmat_rows, thr_key, thr_id, counts, cand, cap,
                                                                    0, s, status, units, qmap, n_units_dev,
-                                                                   unit_counter);
+                                                                   unit_counter, block_stats);
     MDH_CUDA(cudaGetLastError());
 }
 

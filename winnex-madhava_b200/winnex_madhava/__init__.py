@@ -252,6 +252,19 @@ class _SimpleResult:
         self.latency_ms = 0.0
         self.bound_pairs = 0
         self.modulation_gain = 0.0
+        self.pruned_by_bound = 0
+        self.verified_queries = 0
+
+
+def _speed_result(res):
+    """_SimpleResult from a native SpeedEngine dict, keeping its measured
+    counters (bound_violations is measured when set_verify is on)."""
+    out = _SimpleResult(res["indices"], int(res.get("bound_violations", 0)))
+    out.latency_ms = res["latency_ms"]
+    out.bound_pairs = int(res.get("bound_pairs", 0))
+    out.pruned_by_bound = int(res.get("pruned_by_bound", 0))
+    out.verified_queries = int(res.get("verified_queries", 0))
+    return out
 
 
 class MadhavaSpeed:
@@ -283,21 +296,14 @@ class MadhavaSpeed:
     def search(self, query, k: int | None = None):
         kk = k or self._k
         q = np.ascontiguousarray(query, dtype=np.float32).reshape(-1)
-        res = self._native.search(q, kk)
-        out = _SimpleResult(res["indices"], 0)
-        out.latency_ms = res["latency_ms"]
-        out.bound_pairs = res["bound_pairs"]
-        return out
+        return _speed_result(self._native.search(q, kk))
 
     def search_batch(self, queries, k: int | None = None, chunk: int = 128):
         kk = k or self._k
         Q = np.ascontiguousarray(queries, dtype=np.float32)
         if Q.ndim == 1:
             Q = Q.reshape(1, -1)
-        res = self._native.search_batch(Q, len(Q), kk)
-        out = _SimpleResult(res["indices"], 0)
-        out.latency_ms = res["latency_ms"]
-        return out
+        return _speed_result(self._native.search_batch(Q, len(Q), kk))
 
     def search_exact(self, query, k: int | None = None):
         return self.search(query, k=k)
@@ -390,6 +396,14 @@ class MadHybrid:
                 self._cells[cid] = MadhavaSpeed(cell, k=self._k, metric="cosine" if self._metric == "cosine" else "l2",
                                                 devices=devices)
 
+    @staticmethod
+    def _ivf_result(indices, st):
+        r = _SimpleResult(indices, int(st.get("bound_violations", 0)))
+        r.latency_ms = float(st["latency_ms"])
+        r.bound_pairs = int(st.get("pairs_scored", 0))
+        r.pruned_by_bound = int(st.get("pruned_by_bound", 0))
+        return r
+
     def _probe(self, q, nprobe):
         sims = self._centroids @ q
         return np.argsort(-sims, kind="stable")[:nprobe]
@@ -400,9 +414,7 @@ class MadHybrid:
         q = np.ascontiguousarray(query, dtype=np.float32).reshape(-1)
         if self._ivf is not None and np.all((q >= 0) & (q <= 255) & (q == np.round(q))):
             ids, _, st = self._ivf.search(q.astype(np.uint8)[None, :], kk, np_)
-            r = _SimpleResult([int(i) for i in ids[0] if i >= 0], 0)
-            r.latency_ms = float(st["latency_ms"])
-            return r
+            return self._ivf_result([int(i) for i in ids[0] if i >= 0], st)
         if not self._cells:
             self._build_cells()
         cands = []
@@ -440,9 +452,7 @@ class MadHybrid:
         Q = np.ascontiguousarray(queries, dtype=np.float32).reshape(-1, self._dim)
         if self._ivf is not None and np.all((Q >= 0) & (Q <= 255) & (Q == np.round(Q))):
             ids, _, st = self._ivf.search(Q.astype(np.uint8), kk, np_)
-            r = _SimpleResult([int(i) for i in ids.reshape(-1)], 0)
-            r.latency_ms = float(st["latency_ms"])
-            return r
+            return self._ivf_result([int(i) for i in ids.reshape(-1)], st)
         out = []
         for q in Q:
             got = self.search(q, k=kk, nprobe=np_).indices

@@ -29,8 +29,9 @@ def gather_topk(dist, ids, group=None):
     """All-gather this rank's ``[Q][k]`` int32 (distance, id) tensors.
 
     Returns ``(all_dist, all_ids)`` shaped ``[world][Q][k]``, rank-major,
-    on the inputs' device.  Works with any backend that implements
-    ``all_gather`` (NCCL on GPUs, gloo on CPU).
+    on the inputs' device.  The pair travels as one ``[Q][k][2]`` tensor, so
+    the exchange is a single collective (8*Q*k bytes per rank).  Works with
+    any backend that implements ``all_gather`` (NCCL on GPUs, gloo on CPU).
     """
     import torch
     import torch.distributed as tdist
@@ -38,11 +39,13 @@ def gather_topk(dist, ids, group=None):
     if dist.shape != ids.shape or dist.dtype != torch.int32 or ids.dtype != torch.int32:
         raise ValueError("dist and ids must be int32 tensors of the same shape")
     world = tdist.get_world_size(group)
-    out_d = torch.empty((world,) + tuple(dist.shape), dtype=torch.int32, device=dist.device)
-    out_i = torch.empty_like(out_d)
-    tdist.all_gather(list(out_d.unbind(0)), dist.contiguous(), group=group)
-    tdist.all_gather(list(out_i.unbind(0)), ids.contiguous(), group=group)
-    return out_d, out_i
+    pair = torch.stack((dist, ids), dim=-1).contiguous()
+    out = torch.empty((world,) + tuple(pair.shape), dtype=torch.int32, device=dist.device)
+    if tdist.get_backend(group) == "nccl":
+        tdist.all_gather_into_tensor(out, pair, group=group)
+    else:
+        tdist.all_gather(list(out.unbind(0)), pair, group=group)
+    return out[..., 0].contiguous(), out[..., 1].contiguous()
 
 
 def merge_topk_device(lib, all_dist, all_ids, stream=None):
@@ -56,7 +59,11 @@ def merge_topk_device(lib, all_dist, all_ids, stream=None):
     world, nq, k = all_dist.shape
     out_d = torch.empty((nq, k), dtype=torch.int32, device=all_dist.device)
     out_i = torch.empty_like(out_d)
-    sp = ctypes.c_void_p(stream.cuda_stream if stream is not None else 0)
+    # Default: torch's current stream on the inputs' device, the stream that
+    # produced the gathered lists and the output buffers.
+    if stream is None:
+        stream = torch.cuda.current_stream(all_dist.device)
+    sp = ctypes.c_void_p(stream.cuda_stream)
     st = lib.mdh_merge_topk_device(ctypes.c_void_p(all_dist.data_ptr()), ctypes.c_void_p(all_ids.data_ptr()),
                                    world, nq, k, ctypes.c_void_p(out_d.data_ptr()), ctypes.c_void_p(out_i.data_ptr()),
                                    sp)
