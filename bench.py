@@ -98,6 +98,7 @@ def load_lib():
     L.mdh_search_u8_device.argtypes = [P, P, i32, i32, P, P, P, ctypes.POINTER(Stats)]
     L.mdh_merge_topk_device.argtypes = [P, P, i32, i32, i32, P, P, P]
     L.mdh_set_scan_path.argtypes = [i32]
+    L.mdh_set_sample_ratio.argtypes = [i32]
     L.mdh_ivf_create_u8.argtypes = [P, i64, i32, P, i32, P, i32, ctypes.POINTER(P)]
     L.mdh_ivf_search_u8.argtypes = [P, P, i32, i32, i32, P, P, ctypes.POINTER(Stats)]
     L.mdh_ivf_destroy.argtypes = [P]
@@ -110,7 +111,8 @@ def load_lib():
     L.mdh_search_u8.restype = ctypes.c_int
     L.mdh_last_error.restype = ctypes.c_char_p
     for f in ("mdh_index_create_u8_device", "mdh_index_destroy", "mdh_search_u8", "mdh_search_u8_device",
-              "mdh_merge_topk_device", "mdh_set_scan_path", "mdh_ivf_create_u8", "mdh_ivf_search_u8",
+              "mdh_merge_topk_device", "mdh_set_scan_path", "mdh_set_sample_ratio", "mdh_ivf_create_u8",
+              "mdh_ivf_search_u8",
               "mdh_ivf_destroy"):
         getattr(L, f).restype = ctypes.c_int
     return L
@@ -522,6 +524,44 @@ def run_cos(args, torch, device, L, warmup):
     emit(line)
 
 
+# --------------------------------------------------------------------------- result checks
+def result_digest(dist_arr, ids_arr):
+    """sha256 (first 16 hex digits) of the [Q][k] int32 distances then ids."""
+    import hashlib
+
+    h = hashlib.sha256()
+    h.update(np.ascontiguousarray(dist_arr, dtype=np.int32).tobytes())
+    h.update(np.ascontiguousarray(ids_arr, dtype=np.int32).tobytes())
+    return h.hexdigest()[:16]
+
+
+def check_parity(torch, device, args, queries, res_d, res_i):
+    """Check `--parity-queries` of the timed queries (spread over the batch)
+    against the oracle's exact int64 top-k over the whole corpus.  The corpus
+    is regenerated slice by slice on this GPU (the same rows the index was
+    built from) and folded into the oracle's running top-k on the host."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # test infrastructure: the checker, outside the timed region
+
+    m = max(1, min(args.parity_queries, args.nq))
+    pick = np.unique(np.linspace(0, args.nq - 1, m).astype(np.int64))
+    t0 = time.perf_counter()
+    ref = oracle.L2TopK(queries[pick], args.k)
+    step = 4 * CHUNK
+    for s0 in range(0, args.n, step):
+        e0 = min(args.n, s0 + step)
+        rows = make_rows_gpu(torch, s0, e0, device, args.comps).cpu().numpy()
+        ref.update(rows, s0)
+        del rows
+    torch.cuda.empty_cache()
+    got_i, got_d = res_i[pick], res_d[pick]
+    bad = [int(q) for j, q in enumerate(pick)
+           if not (np.array_equal(got_i[j], ref.ids[j]) and np.array_equal(got_d[j], ref.dist[j]))]
+    return {"queries": int(len(pick)), "match": not bad, "mismatched_queries": bad[:8],
+            "oracle": "oracle.L2TopK: int64 (distance, id) ranking of MadhavaL2::search_exact over every row",
+            "seconds": round(time.perf_counter() - t0, 1)}
+
+
 # --------------------------------------------------------------------------- output
 _RESULT_OUT = None  # the process's original stdout, kept for the result line
 
@@ -561,6 +601,11 @@ def main():
     ap.add_argument("--cpu-slice", type=int, default=4_000_000)
     ap.add_argument("--cpu-queries", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the oracle check of the timed results (flat workload)")
+    ap.add_argument("--parity-queries", type=int, default=16)
+    ap.add_argument("--sample-ratio", type=int, default=0,
+                    help="largest sample = shard / ratio (0 = the library default)")
     ap.add_argument("--workload", default="flat", choices=["flat", "ivf", "cos", "persist"],
                     help="flat: exact u8 L2 scan (the headline); ivf: clustered search (nlist 1024, nprobe 16); "
                          "cos: float32 cosine scan (10M x 768, 4,096 queries); persist: index file save/load "
@@ -633,6 +678,7 @@ def main():
     from winnex_madhava.sharding import gather_topk, merge_topk_device, row_range
 
     check(L, L.mdh_set_scan_path(args.scan_path), "set_scan_path")
+    check(L, L.mdh_set_sample_ratio(args.sample_ratio), "set_sample_ratio")
     start, end = row_range(args.n, rank, world)
     flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device) if small_corpus else None
     rows = make_rows_gpu(torch, start, end, device, args.comps)
@@ -652,7 +698,7 @@ def main():
     stream = torch.cuda.current_stream(device)
     sp = ctypes.c_void_p(stream.cuda_stream)
     st = Stats()
-    scan_ms, scan_pairs, launches = [], [], []
+    scan_ms, scan_pairs, launches, stages, blocks = [], [], [], [], []
 
     def step(record):
         check(L, L.mdh_search_u8_device(h, ctypes.c_void_p(dq.data_ptr()), nq, k, ctypes.c_void_p(ids.data_ptr()),
@@ -661,9 +707,14 @@ def main():
             scan_ms.append(st.full_scan_ms)
             scan_pairs.append(st.full_scan_pairs)
             launches.append(st.kernel_launches + (1 if world > 1 else 0))  # + the merge kernel
+            stages.append({"prep": st.prep_ms, "samples": st.sample_ms, "full_scan": st.full_scan_ms,
+                           "select": st.select_ms})
+            blocks.append((st.blocks_tested, st.blocks_passed, st.pairs_pruned_by_bound, st.pairs_scored,
+                           st.candidates))
         if world > 1:
             all_d, all_i = gather_topk(dd, ids)
-            merge_topk_device(L, all_d, all_i, stream)
+            return merge_topk_device(L, all_d, all_i, stream)
+        return dd, ids
 
     for _ in range(warmup):
         step(False)
@@ -673,11 +724,12 @@ def main():
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
     sampler.start()
+    result = None
     if flush_buf is None:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(args.steps):
-            step(True)
+            result = step(True)
         e1.record(stream)
         torch.cuda.synchronize()
         elapsed = e0.elapsed_time(e1) / 1e3
@@ -687,7 +739,7 @@ def main():
             flush_buf.fill_(i & 255)
             a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a_ev.record(stream)
-            step(True)
+            result = step(True)
             b_ev.record(stream)
             evs.append((a_ev, b_ev))
         torch.cuda.synchronize()
@@ -700,6 +752,11 @@ def main():
         dist.barrier()
     tensor_path = bool(st.tensor_core_path)
     levels = int(st.levels)
+    # The timed steps' merged result, identical for every GPU count: its digest
+    # goes into the line so runs at different N can be compared.
+    res_d = result[0].cpu().numpy()
+    res_i = result[1].cpu().numpy()
+    digest = result_digest(res_d, res_i)
 
     # End to end through the C ABI with host buffers (pinned queries in, ids out).
     hq = torch.from_numpy(queries).pin_memory()
@@ -791,19 +848,39 @@ def main():
         "clocks": clocks,
         "roofline": roofline,
     }
+    st_med = {key: statistics.median(x[key] for x in stages) for key in stages[0]} if stages else {}
+    line["stages_ms"] = dict({key: round(v, 3) for key, v in st_med.items()},
+                             step=round(elapsed / args.steps * 1e3, 3),
+                             note="CUDA events per stage inside the library, median over the timed steps "
+                                  "(rank 0); step = the device-timed step")
+    if blocks:
+        bt, bp, pruned, scored, cand = blocks[-1]
+        line["block_bound"] = {"blocks_tested": int(bt), "blocks_passed": int(bp),
+                               "pass_rate": (bp / bt) if bt else None, "pairs_pruned_by_bound": int(pruned),
+                               "pairs_scanned": int(scored), "final_candidates": int(cand),
+                               "block": "(query, 64-row block) of a norm-sorted level, every level"}
+    line["result_digest"] = digest
+    check(L, L.mdh_index_destroy(h), "destroy")
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             n_slice = min(args.cpu_slice, args.n)
             rows = make_rows_gpu(torch, 0, n_slice, device, args.comps).cpu().numpy()
-            _, cb = cpu_reference_qps(rows, args.n, queries[:args.cpu_queries], k, steps=1, warmup=0)
+            _, cb = cpu_reference_qps(rows, args.n, queries[:args.cpu_queries], k, steps=args.steps,
+                                      warmup=min(warmup, 1))
             line["cpu_baseline"] = cb
         except Exception as exc:  # the baseline must not hide the GPU number
             line["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
-    check(L, L.mdh_index_destroy(h), "destroy")
+    ok = True
+    if rank == 0 and not args.no_parity:
+        line["parity"] = check_parity(torch, device, args, queries, res_d, res_i)
+        ok = line["parity"]["match"]
     if rank == 0:
         emit(line)
     if dist is not None:
+        dist.barrier()
         dist.destroy_process_group()
+    if not ok:
+        raise SystemExit("parity check failed: the timed results differ from the oracle")
 
 
 if __name__ == "__main__":

@@ -122,6 +122,13 @@ mdh_status mdh_index_destroy(mdh_index* index);
 mdh_status mdh_index_info(const mdh_index* index, int64_t* n, int32_t* dim, int32_t* metric,
                           int32_t* ndev);
 
+/* Device memory an index holds (host only; no GPU work): level_bytes for its
+ * rows, norms and ids (samples included), workspace_bytes for the per-device
+ * scratch that searches grow on demand and keep (query staging, thresholds,
+ * candidate lists, results).  Either output may be NULL.  No counterpart in
+ * the reference. */
+mdh_status mdh_index_memory(const mdh_index* index, int64_t* level_bytes, int64_t* workspace_bytes);
+
 /* First global row id of an index: its rows carry ids [first_id, first_id + n)
  * (the id_offset it was built with, or the first id of the file it was loaded
  * from).  No counterpart in the reference (its ids always start at 0). */

@@ -65,6 +65,7 @@ def capi():
     L.mdh_plan_level_count.argtypes = [i64, i32]
     L.mdh_plan_level_count.restype = i32
     L.mdh_index_id_base.argtypes = [P, P]
+    L.mdh_index_memory.argtypes = [P, P, P]
     L.mdh_last_error.restype = ctypes.c_char_p
     L.mdh_version.restype = ctypes.c_char_p
     L.mdh_device_count.restype = i32
@@ -72,7 +73,8 @@ def capi():
                "mdh_search_u8", "mdh_search_u8_device", "mdh_search_u8_device_noalloc", "mdh_merge_topk_device", "mdh_set_scan_path",
                "mdh_set_verify", "mdh_ivf_create_u8", "mdh_ivf_route_u8", "mdh_ivf_search_u8", "mdh_ivf_info",
                "mdh_ivf_destroy", "mdh_index_save", "mdh_index_load", "mdh_index_file_info",
-               "mdh_set_candidate_cap_limit", "mdh_set_sample_ratio", "mdh_index_id_base"):
+               "mdh_set_candidate_cap_limit", "mdh_set_sample_ratio", "mdh_index_id_base",
+               "mdh_index_memory"):
         getattr(L, fn).restype = ctypes.c_int
     return L
 

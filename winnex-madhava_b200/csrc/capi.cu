@@ -835,6 +835,30 @@ mdh_status mdh_index_info(const mdh_index* index, int64_t* n, int32_t* dim, int3
     });
 }
 
+mdh_status mdh_index_memory(const mdh_index* index, int64_t* level_bytes, int64_t* workspace_bytes) {
+    return guard([&] {
+        MDH_REQUIRE(index, MDH_ERR_INVALID_ARG, "null index");
+        int64_t lv_b = 0, ws_b = 0;
+        for (const Shard& sh : index->shards) {
+            for (const Level& lv : sh.levels) {
+                if (!lv.owns) continue;
+                if (lv.rows) lv_b += lv.n_pad * index->dpad + lv.n_pad * 4;
+                if (lv.ids) lv_b += lv.n_pad * 4;
+                if (lv.rows_f32) lv_b += lv.n_pad * (int64_t)index->dim * 4 + lv.n_pad * 4;
+                if (lv.rows_bf16) lv_b += lv.n_pad * (int64_t)index->dim * 2;
+            }
+            const Workspace& w = sh.ws;
+            for (size_t b : {w.q_u8_bytes, w.q_f32_bytes, w.q_bf16_bytes, w.qn_bytes, w.thr_key_bytes, w.thr_id_bytes,
+                             w.counts_bytes, w.cand_bytes, w.out_key_bytes, w.out_id_bytes, w.flags_bytes,
+                             w.qlist_bytes, w.tmp_bytes})
+                ws_b += (int64_t)b;
+            if (w.status) ws_b += kStatusWords * 4;
+        }
+        if (level_bytes) *level_bytes = lv_b;
+        if (workspace_bytes) *workspace_bytes = ws_b;
+    });
+}
+
 mdh_status mdh_index_id_base(const mdh_index* index, int64_t* first_id) {
     return guard([&] {
         MDH_REQUIRE(index && first_id, MDH_ERR_INVALID_ARG, "null argument");
