@@ -28,6 +28,10 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
+# Where the reference's sources lie (the one setting for every script that
+# reads them: this module, oracle/Makefile, tests/golden/make_golden.py and
+# __graft_entry__.build); override with MDH_REFERENCE_DIR.
+REFERENCE_DIR = os.environ.get("MDH_REFERENCE_DIR", "/root/reference")
 REF_DIR = os.path.join(HERE, "_ref")
 
 _lib = None
@@ -36,7 +40,7 @@ _lib = None
 def build() -> None:
     """Compile liboracle.so (and the reference module when its sources exist)."""
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
-    if os.path.isdir("/root/reference/src"):
+    if os.path.isdir(os.path.join(REFERENCE_DIR, "src")):
         subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
 
 

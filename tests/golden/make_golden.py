@@ -63,7 +63,7 @@ def reference_hybrid(C, Q):
     import shutil
     import tempfile
 
-    ref_py = "/root/reference/python/winnex_madhava/__init__.py"
+    ref_py = os.path.join(oracle.REFERENCE_DIR, "python", "winnex_madhava", "__init__.py")
     so = [f for f in os.listdir(oracle.REF_DIR) if f.startswith("_winnex_madhava") and f.endswith(".so")][0]
     tmp = tempfile.mkdtemp()
     try:

@@ -80,7 +80,14 @@ def capi():
 
 
 def ptr(a):
-    return ctypes.c_void_p(a.ctypes.data) if a is not None else None
+    """Data address of `a` for a C call.  The returned object keeps `a`
+    alive, so ``ptr(np.ascontiguousarray(x))`` stays valid through the call
+    even when that makes a temporary copy."""
+    if a is None:
+        return None
+    p = ctypes.c_void_p(a.ctypes.data)
+    p._keep = a
+    return p
 
 
 def sorted_by_key(ids, key, asc=True):

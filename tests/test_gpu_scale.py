@@ -81,7 +81,7 @@ def test_headline_plan_10m_rows(big, plan, k):
 def config2():
     L = capi()
     C = cases.gmm_u8(1_000_000, 128, 256, seed=63)
-    Q = cases.gmm_u8_queries(10_000, 128, 256, seed_means=63, seed_q=64)[::10]
+    Q = np.ascontiguousarray(cases.gmm_u8_queries(10_000, 128, 256, seed_means=63, seed_q=64)[::10])
     h = _build(L, C)
     yield L, h, C, Q
     assert L.mdh_index_destroy(h) == 0
