@@ -223,18 +223,30 @@ mdh_status mdh_merge_topk_device(const int32_t* dev_dist_all, const int32_t* dev
  * computes them with MiniBatchKMeans, __init__.py:577-593).  A query goes to
  * the nprobe cells with the largest centroid inner product (the reference's
  * `centroids @ q`, :631-632; here in fp64, ties to the lower cell id) and the
- * result is the exact top-k over the union of those cells by (squared L2
- * distance, row id).  dim <= 128, nlist <= 8192, nprobe <= 1024, k <= 4096. */
+ * result is the exact top-k over the union of those cells: by (squared L2
+ * distance, row id) for metric L2, or by (inner product q.v descending, row
+ * id) for metric COSINE -- the ranking MadHybrid's merge uses for a u8 corpus
+ * under metric "cosine", `corpus[ids].astype(float32) @ q` (:640-646), which
+ * is exact in integers for u8 rows and integral queries.  dim <= 128,
+ * nlist <= 8192, nprobe <= 1024, k <= 4096. */
 typedef struct mdh_ivf mdh_ivf;
 
-/* device: GPU ordinal, -1 = the current device.  Row ids are 0..n-1. */
+/* device: GPU ordinal, -1 = the current device.  Row ids are 0..n-1.
+ * metric: MDH_METRIC_L2 or MDH_METRIC_COSINE (inner-product ranking, above).
+ * Replaces MadHybrid.__init__'s per-cell engines (__init__.py:600-608). */
+mdh_status mdh_ivf_create_u8_metric(const uint8_t* host_corpus, int64_t n, int32_t dim, const float* centroids,
+                                    int32_t nlist, const int32_t* labels, int32_t metric, int32_t device,
+                                    mdh_ivf** out);
+/* mdh_ivf_create_u8_metric with MDH_METRIC_L2. */
 mdh_status mdh_ivf_create_u8(const uint8_t* host_corpus, int64_t n, int32_t dim, const float* centroids,
                              int32_t nlist, const int32_t* labels, int32_t device, mdh_ivf** out);
 /* out_cells [nq][nprobe]: the cells each query probes, best first. */
 mdh_status mdh_ivf_route_u8(mdh_ivf* index, const uint8_t* host_queries, int32_t nq, int32_t nprobe,
                             int32_t* out_cells);
-/* u8 host queries [nq][dim]; out_ids / out_dist (exact squared L2, NULL
- * allowed) [nq][k], -1 past the rows of the probed cells. */
+/* u8 host queries [nq][dim]; out_ids / out_dist [nq][k] (NULL allowed; the
+ * exact squared L2 distance, or the exact inner product for metric COSINE),
+ * -1 past the rows of the probed cells.  Replaces MadHybrid.search
+ * (__init__.py:625-654). */
 mdh_status mdh_ivf_search_u8(mdh_ivf* index, const uint8_t* host_queries, int32_t nq, int32_t k, int32_t nprobe,
                              int32_t* out_ids, int32_t* out_dist, mdh_stats* stats);
 /* cell_rows (NULL allowed): [nlist] rows per cell. */

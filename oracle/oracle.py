@@ -242,9 +242,11 @@ def ivf_route(centroids, queries_u8, nprobe):
     return out
 
 
-def ivf_exact(corpus, labels, centroids, queries_u8, k, nprobe):
-    """(ids, dist) [nq, k]: exact top-k by (squared L2, row id) over the union
-    of each query's probed cells; -1 past the rows available."""
+def ivf_exact(corpus, labels, centroids, queries_u8, k, nprobe, metric="l2"):
+    """(ids, dist) [nq, k]: exact top-k over the union of each query's probed
+    cells; -1 past the rows available.  metric "l2": by (squared L2, row id);
+    "ip": by (inner product descending, row id), dist = the inner product
+    (MadHybrid's merge for metric "cosine", python/winnex_madhava/__init__.py:640-646)."""
     C = np.ascontiguousarray(corpus, dtype=np.uint8)
     Q = np.ascontiguousarray(queries_u8, dtype=np.uint8)
     probe = ivf_route(centroids, Q, nprobe)
@@ -254,8 +256,12 @@ def ivf_exact(corpus, labels, centroids, queries_u8, k, nprobe):
     C64 = C.astype(np.int64)
     for i in range(Q.shape[0]):
         rows = np.flatnonzero(np.isin(labels, probe[i]))
-        d = ((C64[rows] - Q[i].astype(np.int64)) ** 2).sum(axis=1)
-        order = np.lexsort((rows, d))[:k]
+        if metric == "ip":
+            d = C64[rows] @ Q[i].astype(np.int64)
+            order = np.lexsort((rows, -d))[:k]
+        else:
+            d = ((C64[rows] - Q[i].astype(np.int64)) ** 2).sum(axis=1)
+            order = np.lexsort((rows, d))[:k]
         ids[i, :len(order)] = rows[order]
         dist[i, :len(order)] = d[order]
     return ids, dist

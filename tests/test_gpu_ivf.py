@@ -151,3 +151,52 @@ def test_hybrid_facade_uint8_l2():
     assert len(r.indices) == 10
     default = wm.build_engine(Xu, dim=Xu.shape[1], k=10, metric="l2")
     assert type(default).__name__ == "MadhavaL2" and default.search(Xu[0].astype(np.float32)).bound_violations == 0
+
+
+def test_ivf_inner_product_on_reference_cells():
+    """Metric COSINE (MadHybrid's default): ranking by the inner product, the
+    reference's merge `corpus[ids].astype(float32) @ q` (python/winnex_madhava/
+    __init__.py:640-646), exact in integers for u8 rows and u8 queries.  The
+    reference's own cells (tests/golden/hybrid.npz); ids and inner products
+    equal the oracle's exact top-k over the probed cells, and probing every
+    cell gives the exact inner-product top-k of the corpus."""
+    L = capi()
+    _, res = load_fixture("hybrid")
+    C, Q = cases.case_hybrid()
+    cen, labels, nprobe = res["centroids"], res["labels"], cases.HYBRID["nprobe"]
+    Cc, cenc, labc = (np.ascontiguousarray(C, dtype=np.uint8), np.ascontiguousarray(cen, dtype=np.float32),
+                      np.ascontiguousarray(labels, dtype=np.int32))
+    h = ctypes.c_void_p()
+    st = L.mdh_ivf_create_u8_metric(ptr(Cc), Cc.shape[0], Cc.shape[1], ptr(cenc), cenc.shape[0], ptr(labc), 0, -1,
+                                    ctypes.byref(h))
+    assert st == 0, L.mdh_last_error()
+    for k in (1, 10, 100):
+        ids, dots, s = _search(L, h, Q, k, nprobe)
+        want_ids, want_d = oracle.ivf_exact(C, labels, cen, Q, k, nprobe, metric="ip")
+        np.testing.assert_array_equal(ids, want_ids)
+        np.testing.assert_array_equal(dots[want_ids >= 0], want_d[want_ids >= 0])
+        assert 0 < s.pairs_pruned_by_bound < s.pairs_scored
+    ids, dots, _ = _search(L, h, Q, 10, cases.HYBRID["nlist"])
+    full = C.astype(np.int64) @ Q.astype(np.int64).T  # [n][nq]
+    for i in range(len(Q)):
+        order = np.lexsort((np.arange(len(C)), -full[:, i]))[:10]
+        np.testing.assert_array_equal(ids[i], order)
+        np.testing.assert_array_equal(dots[i], full[order, i])
+    assert L.mdh_ivf_destroy(h) == 0
+
+
+def test_hybrid_facade_default_metric_on_gpu():
+    """build_engine(hybrid=True) with the default metric ("cosine") on a u8
+    corpus runs one batched call on the GPU IVF index; results are the exact
+    inner-product top-k over the probed cells of its own clustering."""
+    pytest.importorskip("sklearn")
+    import winnex_madhava as wm
+    _, Xu = _structured()
+    eng = wm.build_engine(Xu, dim=Xu.shape[1], k=10, hybrid=True, nlist=16, nprobe=5)
+    assert type(eng).__name__ == "MadHybrid" and eng._ivf is not None and eng._metric == "cosine"
+    Q = Xu[:40]
+    got = np.array(eng.search_batch(Q.astype(np.float32), k=10).indices).reshape(40, 10)
+    want, _ = oracle.ivf_exact(Xu, eng._labels, eng._centroids, Q, 10, 5, metric="ip")
+    np.testing.assert_array_equal(got, want)
+    assert eng.search(Q[3].astype(np.float32), k=10).indices == [int(v) for v in want[3] if v >= 0]
+    assert not eng._cells  # no per-cell engines were built

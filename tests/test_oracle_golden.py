@@ -170,3 +170,19 @@ def test_sliced_topk_oracle_matches_int_oracle():
         b = oracle.l2_topk_u8(corpus, q, k, slice_rows=sl)
         np.testing.assert_array_equal(a[0], b[0])
         np.testing.assert_array_equal(a[1], b[1])
+
+
+def test_ivf_inner_product_oracle_full_probe_is_brute_force():
+    """ivf_exact(metric="ip") probing every cell is the exact inner-product
+    top-k by (q.v descending, id)."""
+    C = cases.gmm_u8(3_000, 32, 8, seed=81)
+    Q = cases.gmm_u8_queries(12, 32, 8, seed_means=81, seed_q=82)
+    rng = np.random.default_rng(83)
+    cen = rng.uniform(0, 60, (6, 32)).astype(np.float32)
+    labels = rng.integers(0, 6, len(C))
+    ids, dots = oracle.ivf_exact(C, labels, cen, Q, 7, 6, metric="ip")
+    full = C.astype(np.int64) @ Q.astype(np.int64).T
+    for i in range(len(Q)):
+        order = np.lexsort((np.arange(len(C)), -full[:, i]))[:7]
+        np.testing.assert_array_equal(ids[i], order)
+        np.testing.assert_array_equal(dots[i], full[order, i])

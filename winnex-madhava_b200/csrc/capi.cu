@@ -211,7 +211,7 @@ int run_filter(mdh_index* ix, Shard& sh, const Level& lv, const QueryPlan& qp, c
                                         sh.stream);
             else if (used == 2)
                 launch_filter_tc_u8_l2(lv, ix->dpad, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, d, w.status, bstats,
-                                       sh.stream);
+                                       exact_only ? 1 : 0, sh.stream);
             else if (stream_supported(ix->dpad, lv))
                 launch_scan_stream_u8(lv, ix->dpad, 0, q_u8, qn, nq, tk, ti, w.counts, w.cand, cap, d, w.status,
                                       sh.stream);

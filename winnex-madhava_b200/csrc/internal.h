@@ -150,10 +150,14 @@ void make_tmap_rows(Level& lv, int dpad);
 // tables only; the schedule form tests every (query, 64-row block)), [1] +=
 // tests the bound did not settle, [2] += real rows of those blocks (pairs whose
 // exact distance was formed).
+// The lists come back holding exact keys.  exact = 0: they hold every row the
+// block bound could not exclude (a superset of the rows at or under the
+// threshold; keys are formed by a pass after the scan).  exact = 1 (overflow
+// reruns): only the rows at or under the threshold.
 void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
                             const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts,
                             uint2* cand, int cap, int dense, int32_t* status, unsigned long long* block_stats,
-                            cudaStream_t st);
+                            int exact, cudaStream_t st);
 // Unit-table form of the tensor-core scan (used by the IVF search, ivf.cu):
 // unit u scans query rows [q_row, q_row + q_count) of `qmat` (row i is query
 // qmap[i]; thresholds, norms and candidate lists are indexed by that query)

@@ -66,6 +66,7 @@ struct mdh_ivf {
     int32_t dim = 0;
     int32_t dpad = 0;
     int32_t nlist = 0;
+    int32_t metric = MDH_METRIC_L2;      // L2, or COSINE: rank by the inner product q.v
     mdh::Level rows;                     // all cells, padded
     std::vector<int64_t> cell_start;     // first row of cell c
     std::vector<int64_t> cell_count;     // real rows of cell c
@@ -107,6 +108,11 @@ constexpr int kIvfSampleHead = 8;     // lowest-norm rows of every cell always i
 constexpr uint32_t kIvfCoarseThresh = 0x01000000u;  // ... in the coarse sample (1/256)
 constexpr int kIvfCoarseHead = 2;
 constexpr int kIvfCap2 = 16384;       // pass 2 candidate lists
+// Inner-product ranking (metric COSINE) runs the L2 scan with every row norm
+// set to 0 and every query norm to this offset: the key offset - 2 q.v is then
+// positive (2 q.v <= 2 * 128 * 255^2 < 2^24 for dim <= 128) and ascends as
+// q.v descends; the chunk bound (first norm 0) stays exact.
+constexpr int32_t kIvfIpOffset = 1 << 24;
 
 template <class T>
 T* dalloc(size_t count) {
@@ -149,7 +155,8 @@ __global__ void k_ivf_keys(const uint8_t* __restrict__ rows, const int32_t* __re
 __global__ void k_ivf_gather(const uint8_t* __restrict__ src, const unsigned long long* __restrict__ keys,
                              const int32_t* __restrict__ vals, int64_t n, int dpad,
                              const int64_t* __restrict__ cell_start, const int64_t* __restrict__ cell_first,
-                             uint8_t* __restrict__ rows, int32_t* __restrict__ norms, int32_t* __restrict__ ids) {
+                             uint8_t* __restrict__ rows, int32_t* __restrict__ norms, int32_t* __restrict__ ids,
+                             int zero_norms) {
     const int64_t p = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
     const int l8 = threadIdx.x & 7;
     if (p >= n) return;
@@ -161,7 +168,7 @@ __global__ void k_ivf_gather(const uint8_t* __restrict__ src, const unsigned lon
         *reinterpret_cast<uint4*>(rows + (size_t)dst * dpad + off) =
             *reinterpret_cast<const uint4*>(src + (size_t)s * dpad + off);
     if (l8 == 0) {
-        norms[dst] = (int32_t)(key & 0xffffffffull);
+        norms[dst] = zero_norms ? 0 : (int32_t)(key & 0xffffffffull);
         ids[dst] = (int32_t)s;
     }
 }
@@ -638,13 +645,14 @@ void build_ivf_samples(mdh_ivf* ix, cudaStream_t st) {
 }
 
 void ivf_create(const uint8_t* host, int64_t n, int32_t dim, const float* centroids, int32_t nlist,
-                const int32_t* labels, int32_t device, mdh_ivf** out) {
+                const int32_t* labels, int32_t metric, int32_t device, mdh_ivf** out) {
     MDH_REQUIRE(out, MDH_ERR_INVALID_ARG, "null output pointer");
     *out = nullptr;
     MDH_REQUIRE(n >= 1 && host && labels && centroids, MDH_ERR_INVALID_ARG, "null or empty corpus");
     MDH_REQUIRE(n <= 0x7FFFFFFF - 256 * (int64_t)kIvfMaxNlist, MDH_ERR_INVALID_ARG, "too many rows");
     MDH_REQUIRE(dim >= 1 && dim <= 128, MDH_ERR_UNSUPPORTED, "the IVF scan supports dim <= 128");
     MDH_REQUIRE(nlist >= 1 && nlist <= kIvfMaxNlist, MDH_ERR_UNSUPPORTED, "nlist must be in [1, 8192]");
+    MDH_REQUIRE(metric == MDH_METRIC_L2 || metric == MDH_METRIC_COSINE, MDH_ERR_INVALID_ARG, "metric must be 0 or 1");
     int dev = device;
     if (dev < 0) {
         if (cudaGetDevice(&dev) != cudaSuccess) {
@@ -666,6 +674,7 @@ void ivf_create(const uint8_t* host, int64_t n, int32_t dim, const float* centro
     ix->n = n;
     ix->dim = dim;
     ix->dpad = 128;
+    ix->metric = metric;
     ix->nlist = nlist;
     ix->cell_count = count;
     ix->cell_start.resize((size_t)nlist);
@@ -723,7 +732,8 @@ void ivf_create(const uint8_t* host, int64_t n, int32_t dim, const float* centro
         MDH_CUDA(cudaMemcpyAsync(dstart, ix->cell_start.data(), (size_t)nlist * 8, cudaMemcpyHostToDevice, st));
         MDH_CUDA(cudaMemcpyAsync(dfirst, first.data(), (size_t)nlist * 8, cudaMemcpyHostToDevice, st));
         k_ivf_gather<<<(unsigned)((n * 8 + 255) / 256), 256, 0, st>>>(stage, keys2, vals2, n, dpad, dstart, dfirst,
-                                                                       lv.rows, lv.norms, lv.ids);
+                                                                       lv.rows, lv.norms, lv.ids,
+                                                                       metric == MDH_METRIC_COSINE ? 1 : 0);
         MDH_CUDA(cudaGetLastError());
         ix->centroids = dalloc<float>((size_t)nlist * dim);
         MDH_CUDA(cudaMemcpyAsync(ix->centroids, centroids, (size_t)nlist * dim * 4, cudaMemcpyHostToDevice, st));
@@ -757,7 +767,10 @@ void ivf_route_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int nprobe, std:
     grow_dev(&w.flags, &w.flags_bytes, (size_t)nq * nprobe * 4);  // probe matrix
     MDH_CUDA(cudaMemsetAsync(w.q_u8, 0, (size_t)nq * ix->dpad, st));
     MDH_CUDA(cudaMemcpy2DAsync(w.q_u8, ix->dpad, host_q, ix->dim, ix->dim, nq, cudaMemcpyHostToDevice, st));
-    launch_query_norms_u8(w.q_u8, nq, ix->dpad, w.qn, st);
+    if (ix->metric == MDH_METRIC_COSINE)
+        launch_fill_u32(reinterpret_cast<uint32_t*>(w.qn), nq, (uint32_t)kIvfIpOffset, st);
+    else
+        launch_query_norms_u8(w.q_u8, nq, ix->dpad, w.qn, st);
     grow_dev(&w.tmp, &w.tmp_bytes, (size_t)nq * ix->nlist * sizeof(double));  // similarities
     launch_route(w.q_u8, nq, ix->dpad, ix->dim, ix->centroids, ix->nlist, nprobe, static_cast<double*>(w.tmp), w.flags,
                  st);
@@ -906,7 +919,10 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         }
         for (size_t i = 0; i < (size_t)m * k; i++) {
             out_ids[(size_t)c0 * k + i] = hid[i];
-            if (out_dist) out_dist[(size_t)c0 * k + i] = hid[i] >= 0 ? (int32_t)hkey[i] : -1;
+            if (out_dist)
+                out_dist[(size_t)c0 * k + i] = hid[i] < 0                        ? -1
+                                               : ix->metric == MDH_METRIC_COSINE ? (kIvfIpOffset - (int32_t)hkey[i]) / 2
+                                                                                 : (int32_t)hkey[i];
         }
     }
     s.levels = kIvfPasses;
@@ -923,16 +939,22 @@ using namespace mdh;
 
 extern "C" {
 
-mdh_status mdh_ivf_create_u8(const uint8_t* host_corpus, int64_t n, int32_t dim, const float* centroids,
-                             int32_t nlist, const int32_t* labels, int32_t device, mdh_ivf** out) {
+mdh_status mdh_ivf_create_u8_metric(const uint8_t* host_corpus, int64_t n, int32_t dim, const float* centroids,
+                                    int32_t nlist, const int32_t* labels, int32_t metric, int32_t device,
+                                    mdh_ivf** out) {
     struct A {
-        const uint8_t* c; int64_t n; int32_t dim; const float* cen; int32_t nl; const int32_t* lab; int32_t dev;
-        mdh_ivf** out;
-    } a{host_corpus, n, dim, centroids, nlist, labels, device, out};
+        const uint8_t* c; int64_t n; int32_t dim; const float* cen; int32_t nl; const int32_t* lab; int32_t metric;
+        int32_t dev; mdh_ivf** out;
+    } a{host_corpus, n, dim, centroids, nlist, labels, metric, device, out};
     return run_guarded([](void* p) {
         A& x = *static_cast<A*>(p);
-        ivf_create(x.c, x.n, x.dim, x.cen, x.nl, x.lab, x.dev, x.out);
+        ivf_create(x.c, x.n, x.dim, x.cen, x.nl, x.lab, x.metric, x.dev, x.out);
     }, &a);
+}
+
+mdh_status mdh_ivf_create_u8(const uint8_t* host_corpus, int64_t n, int32_t dim, const float* centroids,
+                             int32_t nlist, const int32_t* labels, int32_t device, mdh_ivf** out) {
+    return mdh_ivf_create_u8_metric(host_corpus, n, dim, centroids, nlist, labels, MDH_METRIC_L2, device, out);
 }
 
 mdh_status mdh_ivf_route_u8(mdh_ivf* index, const uint8_t* host_queries, int32_t nq, int32_t nprobe,

@@ -113,12 +113,15 @@ int plan(const Shard& sh, int k, NaStep* steps) {
     return ns;
 }
 
+// rerun: an overflow rerun (the tensor scan then keeps only rows at or under
+// the threshold, so each rerun tightens it).
 void filter(mdh_index* ix, const Level& lv, const uint8_t* q, const int32_t* qn, int nq, const uint32_t* tk,
             const int32_t* ti, uint32_t* counts, uint2* cand, int cap, bool dense, int32_t* status, cudaStream_t st,
-            int* path) {
+            int* path, bool rerun = false) {
     const int d = dense ? 1 : 0;
     if (lv.has_tmap && tc_supported(ix, lv)) {
-        launch_filter_tc_u8_l2(lv, ix->dpad, q, qn, nq, tk, ti, counts, cand, cap, d, status, nullptr, st);
+        launch_filter_tc_u8_l2(lv, ix->dpad, q, qn, nq, tk, ti, counts, cand, cap, d, status, nullptr, rerun ? 1 : 0,
+                               st);
         *path = 1;
     } else if (stream_supported(ix->dpad, lv)) {
         launch_scan_stream_u8(lv, ix->dpad, 0, q, qn, nq, tk, ti, counts, cand, cap, d, status, st);
@@ -211,7 +214,7 @@ void search_noalloc(mdh_index* ix, const uint8_t* dev_q, int nq, int k, int32_t*
                 MDH_REQUIRE(++rounds < 64, MDH_ERR_INTERNAL, "candidate overflow did not converge");
                 MDH_CUDA(cudaMemsetAsync(counts, 0, (size_t)nq * 4, st));
                 MDH_CUDA(cudaMemsetAsync(status + 1, 0, sizeof(int32_t), st));
-                filter(ix, lv, q, qn, nq, thr_key, thr_id, counts, cand, last.cap, false, status, st, &path);
+                filter(ix, lv, q, qn, nq, thr_key, thr_id, counts, cand, last.cap, false, status, st, &path, true);
                 launch_select(counts, cand, last.cap, lv.ids, nq, kk, 1, thr_key, thr_id, out_key, out_id, flags,
                               status + 1, nullptr, nullptr, st);
                 s.kernel_launches += 2;

@@ -277,7 +277,7 @@ class IvfIndex {
 public:
     IvfIndex(const U8Array& corpus, const F32Array& centroids, py::array_t<int32_t, py::array::c_style |
                                                                              py::array::forcecast> labels,
-             int device) {
+             int device, int metric) {
         auto ic = corpus.request(), ie = centroids.request(), il = labels.request();
         if (ic.ndim != 2) throw std::runtime_error("corpus must be a 2-D uint8 array");
         if (ie.ndim != 2 || ie.shape[1] != ic.shape[1]) throw std::runtime_error("centroids must be [nlist][dim]");
@@ -289,8 +289,8 @@ public:
         mdh_status s;
         {
             py::gil_scoped_release nogil;
-            s = mdh_ivf_create_u8((const uint8_t*)ic.ptr, n_, dim_, (const float*)ie.ptr, nlist_,
-                                  (const int32_t*)il.ptr, device, &p);
+            s = mdh_ivf_create_u8_metric((const uint8_t*)ic.ptr, n_, dim_, (const float*)ie.ptr, nlist_,
+                                         (const int32_t*)il.ptr, metric, device, &p);
         }
         check(s);
         ix_ = p;
@@ -622,8 +622,9 @@ PYBIND11_MODULE(_winnex_madhava, m) {
 
     py::class_<IvfIndex>(m, "IvfIndex")
         .def(py::init<const U8Array&, const F32Array&, py::array_t<int32_t, py::array::c_style | py::array::forcecast>,
-                      int>(),
-             py::arg("corpus"), py::arg("centroids"), py::arg("labels"), py::arg("device") = -1)
+                      int, int>(),
+             py::arg("corpus"), py::arg("centroids"), py::arg("labels"), py::arg("device") = -1,
+             py::arg("metric") = 1)
         .def("search", &IvfIndex::search, py::arg("queries"), py::arg("k"), py::arg("nprobe"))
         .def("route", &IvfIndex::route, py::arg("queries"), py::arg("nprobe"))
         .def("num_vectors", &IvfIndex::num_vectors)

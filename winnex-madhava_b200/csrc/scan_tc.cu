@@ -64,6 +64,10 @@ namespace {
 
 using namespace tc;
 
+#ifndef MDH_EPI_V2
+#define MDH_EPI_V2 0
+#endif
+
 constexpr int BM = 128;           // queries per query tile (TMEM lanes)
 constexpr int BK = 128;           // bytes per row (K)
 constexpr int BOX_ROWS = 128;     // corpus rows per TMA box (BN / BOX_ROWS boxes per stage)
@@ -156,27 +160,57 @@ __device__ __forceinline__ UnitView unit_view(const Sched& s, const ScanUnit* un
 }
 
 // The rows [row0, row0 + 32) of one 32-column chunk against this thread's
-// query: v[j] = q.v of row row0 + j.  Nothing passes unless 2 max(v) >= need
-// (need = n_min + |q|^2 - threshold for an n_min no larger than any of the
-// rows' norms); a passing lane walks its own passing columns, reads their
-// norms and appends the rows whose exact (key, id) reaches the threshold.
-__device__ __forceinline__ void chunk_filter(const uint32_t (&v)[32], int32_t need, int32_t row0, int row_end,
-                                             uint32_t tkey, int32_t tid, int32_t qnv, int qi,
-                                             const int32_t* __restrict__ norms, const int32_t* __restrict__ ids,
-                                             int dense, CandBuf<EPI_THREADS, BUFN>& buf, uint32_t* __restrict__ counts,
-                                             uint2* __restrict__ cand, int cap) {
+// query: v[j] = q.v of row row0 + j.  need = n_min + |q|^2 - threshold, with
+// n_min no larger than any of the rows' norms, so a row can reach the
+// threshold only if 2 v[j] >= need.  Every such row goes to the candidate
+// list as {q.v, row}: the exact key |q|^2 + |v|^2 - 2 q.v is formed after the
+// scan (k_rekey_l2), so the epilogue reads no norm and no id.  The list is a
+// superset of the rows at or under the threshold, which is all the selection
+// needs.  Dense levels (every row a candidate) write row r at slot r.
+// exact: overflow reruns instead form each key here (the row's norm and, on
+// a tie, its id) and keep only rows at or under (tkey, tid), so every rerun's
+// list holds rows under its threshold alone and the next threshold is
+// strictly tighter.
+template <bool EXACT>
+__device__ __forceinline__ void chunk_emit(const uint32_t (&v)[32], int32_t need, int32_t row0, int row_end, int qi,
+                                           int dense, uint32_t tkey, int32_t tid, int32_t qnv,
+                                           const int32_t* __restrict__ norms, const int32_t* __restrict__ ids,
+                                           CandBuf<EPI_THREADS, BUFN>& buf, uint32_t* __restrict__ counts,
+                                           uint2* __restrict__ cand, int cap) {
     if (2 * max32(v) < need) return;
     uint32_t mask = pass_mask32(v, need);
+    const int32_t valid = row_end - row0;  // pad rows trail the level
+    if (valid < 32) mask &= valid > 0 ? (1u << valid) - 1u : 0u;
     while (mask) {
         const int j = __ffs(mask) - 1;
         mask &= mask - 1;
-        const int32_t r = row0 + j;
-        if (r >= row_end) break;  // pad rows trail the level
-        const uint32_t key = (uint32_t)(qnv + __ldg(norms + r) - 2 * (int32_t)pick32(v, j));
-        if (dense)
-            cand[(size_t)qi * cap + r] = make_uint2(key, (uint32_t)r);
-        else if (key < tkey || (key == tkey && __ldg(ids + r) <= tid))
-            buf.push(key, (uint32_t)r, counts, cand, cap, qi);
+        const uint32_t x = pick32(v, j), r = (uint32_t)(row0 + j);
+        if (dense) {
+            cand[(size_t)qi * cap + r] = make_uint2(x, r);
+        } else if (EXACT) {
+            const uint32_t key = (uint32_t)(qnv + __ldg(norms + r) - 2 * (int32_t)x);
+            if (key < tkey || (key == tkey && __ldg(ids + r) <= tid)) buf.push(key, r, counts, cand, cap, qi);
+        } else {
+            buf.push(x, r, counts, cand, cap, qi);
+        }
+    }
+}
+
+// Candidates written by the schedule-form scan hold {q.v, row}; this turns
+// each into {|q|^2 + |v|^2 - 2 q.v, row}, the exact L2 key the selection
+// ranks by.  One block per query; dense_rows > 0: every one of the first
+// dense_rows slots is filled (dense level), else counts[q] (capped) are.
+__global__ void k_rekey_l2(const uint32_t* __restrict__ counts, uint2* __restrict__ cand, int cap,
+                           const int32_t* __restrict__ norms, const int32_t* __restrict__ qn, int dense_rows) {
+    const int q = blockIdx.x;
+    const uint32_t c_all = dense_rows > 0 ? (uint32_t)dense_rows : counts[q];
+    const int c = (int)(c_all < (uint32_t)cap ? c_all : (uint32_t)cap);
+    const int32_t qv = qn[q];
+    uint2* list = cand + (size_t)q * cap;
+    for (int i = threadIdx.x; i < c; i += blockDim.x) {
+        uint2 e = list[i];
+        e.x = (uint32_t)(qv + __ldg(norms + e.y) - 2 * (int32_t)e.x);
+        list[i] = e;
     }
 }
 
@@ -227,7 +261,7 @@ __device__ __forceinline__ int feed_take(bool whole_warp, volatile int32_t* slot
 // each lane's own columns (reading the row norm from memory); the schedule
 // form walks the columns any lane keeps, warp-uniformly, with the norms
 // already in registers.
-template <class C, bool UNITS>
+template <class C, bool UNITS, bool EXACT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_filter_tc_u8_l2(const __grid_constant__ CUtensorMap tmap_rows, const __grid_constant__ CUtensorMap tmap_q,
                       const int32_t* __restrict__ norms, const int32_t* __restrict__ ids, int32_t n_rows,
@@ -472,26 +506,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tc_fence_after();
                 uint32_t v[2][32];
                 __syncwarp();
+#if MDH_EPI_V2
+                tmem_ld64(tcol0 + A * C::ACC_COLS, v[0], v[1]);
+#else
                 tmem_ld32_issue(tcol0 + A * C::ACC_COLS, v[0]);
                 tmem_ld32_issue(tcol0 + A * C::ACC_COLS + 32, v[1]);
                 tmem_ld_wait(v[0]);  // waits for both loads
                 tmem_ld_wait(v[1]);
+#endif
                 // The chunks are in registers: hand the accumulator back to the MMA.
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bars + 8 * (C::BAR_ACC_EMPTY + A));
                 const int32_t m = (int32_t)__float_as_uint(
                     fmaxf(__uint_as_float((uint32_t)max32(v[0])), __uint_as_float((uint32_t)max32(v[1]))));
-                if (2 * m >= need) {
+                const bool pass = 2 * m >= need;
+#if MDH_EPI_V2
+                // One vote settles the tile for the whole warp (the usual case);
+                // the buffer can only have grown when some lane passed.
+                if (!__any_sync(0xffffffffu, pass)) return true;
+#endif
+                if (pass) {
                     const int32_t row0 = t * BN + rowoff;  // rows < 2^31 (ids are int32)
                     if (block_stats) {
                         stat_add(stats + 1, 1u);
                         stat_add(stats + 2, (uint32_t)min(max(row_end - row0, 0), COLS_PER_WARP));
                     }
-                    chunk_filter(v[0], need, row0, row_end, tkey, tid, qnv, qi, norms, ids, dense, buf, counts, cand,
-                                 cap);
-                    chunk_filter(v[1], need, row0 + 32, row_end, tkey, tid, qnv, qi, norms, ids, dense, buf, counts,
-                                 cand, cap);
+                    chunk_emit<EXACT>(v[0], need, row0, row_end, qi, dense, tkey, tid, qnv, norms, ids, buf,
+                                      counts, cand, cap);
+                    chunk_emit<EXACT>(v[1], need, row0 + 32, row_end, qi, dense, tkey, tid, qnv, norms, ids, buf,
+                                      counts, cand, cap);
                 }
                 buf.warp_flush_at(BUF_FLUSH_AT, counts, cand, cap, qi);
                 return true;
@@ -724,7 +768,7 @@ void make_tmap_rows(Level& lv, int dpad) {
 template <class C>
 void launch_tc(const Level& lv, const CUtensorMap& tq, const int32_t* qn, int nq, const uint32_t* thr_key,
                const int32_t* thr_id, uint32_t* counts, uint2* cand, int cap, int dense, int32_t* status,
-               unsigned long long* block_stats, cudaStream_t st) {
+               unsigned long long* block_stats, int exact, cudaStream_t st) {
     int dev;
     MDH_CUDA(cudaGetDevice(&dev));
     const int sms = device_sm_count(dev);
@@ -736,24 +780,27 @@ void launch_tc(const Level& lv, const CUtensorMap& tq, const int32_t* qn, int nq
     s.n_units = (long long)s.n_groups * s.n_chunks;
     if (s.n_units < ctas) ctas = (int)s.n_units;
     // A function attribute belongs to the current device: set it on every launch.
-    MDH_CUDA(cudaFuncSetAttribute(k_filter_tc_u8_l2<C, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)C::SMEM_BYTES));
-    k_filter_tc_u8_l2<C, false><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
-                                                                   qn, nq, thr_key, thr_id, counts, cand, cap, dense,
-                                                                   s, status, nullptr, nullptr, nullptr, nullptr,
-                                                                   block_stats);
+    auto kern = exact ? k_filter_tc_u8_l2<C, false, true> : k_filter_tc_u8_l2<C, false, false>;
+    MDH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM_BYTES));
+    kern<<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n, qn, nq, thr_key,
+                                                   thr_id, counts, cand, cap, dense, s, status, nullptr, nullptr,
+                                                   nullptr, nullptr, block_stats);
     MDH_CUDA(cudaGetLastError());
 }
 
 void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const int32_t* qn, int nq,
                             const uint32_t* thr_key, const int32_t* thr_id, uint32_t* counts, uint2* cand, int cap,
-                            int dense, int32_t* status, unsigned long long* block_stats, cudaStream_t st) {
+                            int dense, int32_t* status, unsigned long long* block_stats, int exact, cudaStream_t st) {
     if (nq <= 0 || lv.n == 0) return;
     MDH_REQUIRE(dpad == BK && lv.has_tmap, MDH_ERR_INTERNAL, "tensor-core scan needs 128-byte rows and a TMA map");
     MDH_REQUIRE(!dense || cap >= lv.n, MDH_ERR_INTERNAL, "dense scan needs cap >= rows");
     CUtensorMap tq;
     encode_u8_rows_tmap(&tq, q, nq, dpad, BM);
-    launch_tc<CfgNarrow>(lv, tq, qn, nq, thr_key, thr_id, counts, cand, cap, dense, status, block_stats, st);
+    launch_tc<CfgNarrow>(lv, tq, qn, nq, thr_key, thr_id, counts, cand, cap, dense, status, block_stats, exact, st);
+    if (!exact) {
+        k_rekey_l2<<<nq, 128, 0, st>>>(counts, cand, cap, lv.norms, qn, dense ? (int)lv.n : 0);
+        MDH_CUDA(cudaGetLastError());
+    }
 }
 
 void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat, int qmat_rows, const int32_t* qmap,
@@ -772,9 +819,9 @@ void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat
     s.n_units = n_units;
     const int ctas = std::min(device_sm_count(dev), n_units);
     if (unit_counter) MDH_CUDA(cudaMemsetAsync(unit_counter, 0, sizeof(int32_t), st));
-    MDH_CUDA(cudaFuncSetAttribute(k_filter_tc_u8_l2<C, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    MDH_CUDA(cudaFuncSetAttribute(k_filter_tc_u8_l2<C, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)C::SMEM_BYTES));
-    k_filter_tc_u8_l2<C, true><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
+    k_filter_tc_u8_l2<C, true, true><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
                                                                    qn, qmat_rows, thr_key, thr_id, counts, cand, cap,
                                                                    0, s, status, units, qmap, n_units_dev,
                                                                    unit_counter, block_stats);

@@ -36,6 +36,20 @@ __device__ __forceinline__ int next_pow2(int x) {
     return p;
 }
 
+// Lowers a query's threshold (key, id) to `v` (key << 32 | id) when that is
+// smaller.  Every threshold a selection computes is a valid upper bound on
+// the query's k-th (key, id), and so is the one it replaces, so keeping the
+// smaller of the two is valid too.  A candidate list may hold rows above the
+// threshold that produced it (the scan keeps every row its block bound cannot
+// exclude); the minimum keeps an overflow rerun from loosening the bound.
+__device__ __forceinline__ void tighten_threshold(uint32_t* thr_key, int32_t* thr_id, int qo, unsigned long long v) {
+    const unsigned long long cur = ((unsigned long long)thr_key[qo] << 32) | (uint32_t)thr_id[qo];
+    if (v < cur) {
+        thr_key[qo] = (uint32_t)(v >> 32);
+        thr_id[qo] = (int32_t)(v & 0xffffffffu);
+    }
+}
+
 __global__ void k_fill_u32(uint32_t* p, int n, uint32_t v) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) p[i] = v;
@@ -135,8 +149,7 @@ __global__ void k_select(const uint32_t* __restrict__ counts, const uint2* __res
         __syncthreads();
         const unsigned long long kth = radix_select_kth(keys, c, k);
         if (threadIdx.x == 0) {
-            thr_key[qo] = (uint32_t)(kth >> 32);
-            thr_id[qo] = (int32_t)(kth & 0xffffffffu);
+            tighten_threshold(thr_key, thr_id, qo, kth);
         }
         return;
     }
@@ -145,8 +158,7 @@ __global__ void k_select(const uint32_t* __restrict__ counts, const uint2* __res
         if (threadIdx.x == 0) {
             int idx = (c < k ? c : k) - 1;
             if (idx >= 0 && c >= k) {
-                thr_key[qo] = (uint32_t)(keys[idx] >> 32);
-                thr_id[qo] = (int32_t)(keys[idx] & 0xffffffffu);
+                tighten_threshold(thr_key, thr_id, qo, keys[idx]);
             } else {
                 // Fewer than k rows in this level: every row of the next
                 // level stays a candidate.
@@ -161,8 +173,7 @@ __global__ void k_select(const uint32_t* __restrict__ counts, const uint2* __res
         // (tighter) threshold for a rerun.  c == cap >= k here.
         if (threadIdx.x == 0) {
             flags[qo] = 1;
-            thr_key[qo] = (uint32_t)(keys[k - 1] >> 32);
-            thr_id[qo] = (int32_t)(keys[k - 1] & 0xffffffffu);
+            tighten_threshold(thr_key, thr_id, qo, keys[k - 1]);
             atomicAdd(n_flagged, 1);
         }
         return;
@@ -256,8 +267,7 @@ __global__ void __launch_bounds__(32 * kWarpSelectWarps)
     if (!final_) {
         if (lane == 0) {
             if (c >= k) {
-                thr_key[qo] = (uint32_t)(kth >> 32);
-                thr_id[qo] = (int32_t)(kth & 0xffffffffu);
+                tighten_threshold(thr_key, thr_id, qo, kth);
             } else {
                 // Fewer than k rows in this level: every row of the next
                 // level stays a candidate.
@@ -272,8 +282,7 @@ __global__ void __launch_bounds__(32 * kWarpSelectWarps)
         // (tighter) threshold for a rerun.  c == cap >= k here.
         if (lane == 0) {
             flags[qo] = 1;
-            thr_key[qo] = (uint32_t)(kth >> 32);
-            thr_id[qo] = (int32_t)(kth & 0xffffffffu);
+            tighten_threshold(thr_key, thr_id, qo, kth);
             atomicAdd(n_flagged, 1);
         }
         return;
@@ -414,8 +423,7 @@ __global__ void __launch_bounds__(32 * kBigWarps)
     if (!final_) {
         if (lane == 0) {
             if (c >= k) {
-                thr_key[qo] = (uint32_t)(buf[k - 1] >> 32);
-                thr_id[qo] = (int32_t)(buf[k - 1] & 0xffffffffu);
+                tighten_threshold(thr_key, thr_id, qo, buf[k - 1]);
             } else {
                 // Fewer than k rows in this level: every row of the next
                 // level stays a candidate.
@@ -430,8 +438,7 @@ __global__ void __launch_bounds__(32 * kBigWarps)
         // (tighter) threshold for a rerun.  c == cap >= k here.
         if (lane == 0) {
             flags[qo] = 1;
-            thr_key[qo] = (uint32_t)(buf[k - 1] >> 32);
-            thr_id[qo] = (int32_t)(buf[k - 1] & 0xffffffffu);
+            tighten_threshold(thr_key, thr_id, qo, buf[k - 1]);
             atomicAdd(n_flagged, 1);
         }
         return;

@@ -332,10 +332,13 @@ class MadHybrid:
     (python/winnex_madhava/__init__.py:577-593); a query is routed to the
     ``nprobe`` cells whose centroids have the largest inner product with it
     (:631-632), and the result is the exact top-k over the union of those
-    cells.  For a uint8 corpus under L2 (dim <= 128) with integral queries
-    that runs entirely on the GPU index ``IvfIndex`` (routing in fp64, ties to
-    the lower cell id; ranking by (squared distance, row id)); other corpora
-    and float queries use one exact GPU engine per cell.
+    cells.  For a uint8 corpus (dim <= 128) with integral queries that runs
+    entirely on the GPU index ``IvfIndex`` in one batched call (routing in
+    fp64, ties to the lower cell id): under L2 ranked by (squared distance,
+    row id), under the default metric "cosine" by (inner product, row id) --
+    the reference merges a u8 corpus by ``corpus[ids] @ q`` (:640-646), exact
+    in integers here.  Float corpora and non-integral queries use one exact
+    GPU engine per cell.
     """
 
     def __init__(self, corpus, *, nlist: int = 64, nprobe: int = 5, dtype: str | None = None,
@@ -367,10 +370,14 @@ class MadHybrid:
         self._devices = devices
         self._ivf = None
         t0 = time.time()
-        if self._dtype == "uint8" and self._metric != "cosine" and self._dim <= 128:
+        if self._dtype == "uint8" and self._dim <= 128:
+            # metric "cosine" merges by the raw inner product corpus @ q
+            # (python/winnex_madhava/__init__.py:640-646): the index's
+            # inner-product form (metric 0); otherwise L2 (metric 1).
             dev = int(devices[0]) if devices else -1
             self._ivf = _native.IvfIndex(np.ascontiguousarray(arr, dtype=np.uint8), self._centroids,
-                                         np.ascontiguousarray(labels, dtype=np.int32), dev)
+                                         np.ascontiguousarray(labels, dtype=np.int32), dev,
+                                         0 if self._metric == "cosine" else 1)
             for cid in range(self._nlist):
                 idxs = np.where(labels == cid)[0]
                 if len(idxs):
