@@ -96,6 +96,10 @@ def load_lib():
     L.mdh_index_create_u8.argtypes = [P, i64, i32, i32, P, i32, i64, ctypes.POINTER(P)]
     L.mdh_index_create_u8.restype = ctypes.c_int
     L.mdh_search_u8_device.argtypes = [P, P, i32, i32, P, P, P, ctypes.POINTER(Stats)]
+    L.mdh_search_u8_device_sample.argtypes = [P, P, i32, i32, P, P, P, ctypes.POINTER(Stats)]
+    L.mdh_search_u8_device_bounded.argtypes = [P, P, i32, i32, P, P, P, P, P, ctypes.POINTER(Stats)]
+    L.mdh_search_u8_device_sample.restype = ctypes.c_int
+    L.mdh_search_u8_device_bounded.restype = ctypes.c_int
     L.mdh_merge_topk_device.argtypes = [P, P, i32, i32, i32, P, P, P]
     L.mdh_set_scan_path.argtypes = [i32]
     L.mdh_set_sample_ratio.argtypes = [i32]
@@ -279,6 +283,10 @@ def run_ivf(args, torch, device, L, warmup):
     elapsed = time.perf_counter() - t0
     clocks = sampler.stop()
     launches = int(st.kernel_launches) * args.steps
+    ivf_block = {"blocks_tested": int(st.blocks_tested), "blocks_passed": int(st.blocks_passed),
+                 "pass_rate": (st.blocks_passed / st.blocks_tested) if st.blocks_tested else None,
+                 "pairs_pruned_by_bound": int(st.pairs_pruned_by_bound), "pairs_scanned": int(st.pairs_scored),
+                 "final_candidates": int(st.candidates), "block": "(query, 32-row chunk) of a probed cell, all passes"}
     # Recall of the clustered search against the exact scan, on 1,000 queries.
     m = min(nq, 1000)
     flat = ctypes.c_void_p()
@@ -311,6 +319,7 @@ def run_ivf(args, torch, device, L, warmup):
         "e2e": {"value": qps, "unit": "queries/sec", "h2d_bytes_per_step": int(nq * DIM),
                 "d2h_bytes_per_step": int(nq * k * 8)},
         "gpu_launches": launches,
+        "block_bound": ivf_block,
         "clocks": clocks,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",
                      "frac": (achieved / int8_peak) if achieved else None, "traffic": None,
@@ -499,6 +508,10 @@ def run_cos(args, torch, device, L, warmup):
     ms = statistics.median(scan_ms)
     achieved = 2.0 * pairs[0] * COS_DIM / (ms / 1e3) / 1e12 if ms > 0 else None
     qps = nq * args.steps / elapsed
+    cos_stages = {"prep": round(st.prep_ms, 3), "samples": round(st.sample_ms, 3),
+                  "full_scan": round(st.full_scan_ms, 3), "rescore_in_full_scan": round(st.rescore_ms, 3),
+                  "select": round(st.select_ms, 3), "call_wall": round(st.latency_ms, 3),
+                  "note": "last timed step; CUDA events per stage, prep includes the host query normalization"}
     path = {0: "CUDA cores (fp32 replica)", 3: "bf16 tcgen05 pass + exact fp32 rescore"}.get(int(st.tensor_core_path),
                                                                                            str(st.tensor_core_path))
     line = {
@@ -514,6 +527,7 @@ def run_cos(args, torch, device, L, warmup):
         "e2e": {"value": qps, "unit": "queries/sec", "h2d_bytes_per_step": int(nq * COS_DIM * 4),
                 "d2h_bytes_per_step": int(nq * k * 8)},
         "gpu_launches": int(st.kernel_launches) * args.steps,
+        "stages_ms": cos_stages,
         "clocks": clocks,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": (achieved / peaks["bf16_tflops"]) if achieved else None, "traffic": None,
@@ -604,6 +618,8 @@ def main():
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the oracle check of the timed results (flat workload)")
     ap.add_argument("--parity-queries", type=int, default=16)
+    ap.add_argument("--no-coop", action="store_true",
+                    help="N > 1: each rank uses its own sample thresholds (no exchange of sample results)")
     ap.add_argument("--sample-ratio", type=int, default=0,
                     help="largest sample = shard / ratio (0 = the library default)")
     ap.add_argument("--workload", default="flat", choices=["flat", "ivf", "cos", "persist"],
@@ -675,10 +691,18 @@ def main():
         run_persist(args, torch, device, L)
         return
     sys.path.insert(0, os.path.join(ROOT, "winnex-madhava_b200"))
-    from winnex_madhava.sharding import gather_topk, merge_topk_device, row_range
+    from winnex_madhava.sharding import cooperative_topk, device_phases, gather_topk, merge_topk_device, row_range
 
     check(L, L.mdh_set_scan_path(args.scan_path), "set_scan_path")
-    check(L, L.mdh_set_sample_ratio(args.sample_ratio), "set_sample_ratio")
+    # With G ranks sharing their sample results, each rank samples 1/G of what
+    # it would alone for the same threshold: its largest sample is shard/(16 G).
+    coop = world > 1 and not args.no_coop
+    ratio = args.sample_ratio or (16 * world if coop else 0)
+    check(L, L.mdh_set_sample_ratio(ratio), "set_sample_ratio")
+    config["threshold_exchange"] = ("each rank scans its samples, the ranks all_gather and merge their sample top-k "
+                                    "lists, every rank scans its shard under the merged k-th distance, then the "
+                                    "final lists are all_gathered and merged" if coop else "none")
+    config["sample_ratio"] = ratio or 64
     start, end = row_range(args.n, rank, world)
     flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device) if small_corpus else None
     rows = make_rows_gpu(torch, start, end, device, args.comps)
@@ -698,23 +722,36 @@ def main():
     stream = torch.cuda.current_stream(device)
     sp = ctypes.c_void_p(stream.cuda_stream)
     st = Stats()
+    st1 = Stats()  # the sample phase of a cooperative search
     scan_ms, scan_pairs, launches, stages, blocks = [], [], [], [], []
+    merge = lambda d, i: merge_topk_device(L, d, i, stream)  # noqa: E731
+    if coop:
+        sample_phase = device_phases(L, h, dq, stream, ctypes.byref(st1))[0]
+        bounded_phase = device_phases(L, h, dq, stream, ctypes.byref(st))[1]
+
+    def search(q):
+        if coop:
+            return cooperative_topk(sample_phase, bounded_phase, merge, q, k)
+        check(L, L.mdh_search_u8_device(h, ctypes.c_void_p(q.data_ptr()), nq, k, ctypes.c_void_p(ids.data_ptr()),
+                                        ctypes.c_void_p(dd.data_ptr()), sp, ctypes.byref(st)), "search")
+        if world > 1:
+            return merge(*gather_topk(dd, ids))
+        return dd, ids
 
     def step(record):
-        check(L, L.mdh_search_u8_device(h, ctypes.c_void_p(dq.data_ptr()), nq, k, ctypes.c_void_p(ids.data_ptr()),
-                                        ctypes.c_void_p(dd.data_ptr()), sp, ctypes.byref(st)), "search")
+        out = search(dq)
         if record:
             scan_ms.append(st.full_scan_ms)
             scan_pairs.append(st.full_scan_pairs)
-            launches.append(st.kernel_launches + (1 if world > 1 else 0))  # + the merge kernel
-            stages.append({"prep": st.prep_ms, "samples": st.sample_ms, "full_scan": st.full_scan_ms,
-                           "select": st.select_ms})
-            blocks.append((st.blocks_tested, st.blocks_passed, st.pairs_pruned_by_bound, st.pairs_scored,
+            # + the merge kernels (two with shared thresholds)
+            launches.append(st.kernel_launches + st1.kernel_launches + (0 if world == 1 else (2 if coop else 1)))
+            stages.append({"prep": st.prep_ms + st1.prep_ms,
+                           "samples": (st1.sample_ms + st1.full_scan_ms + st1.select_ms) if coop else st.sample_ms,
+                           "full_scan": st.full_scan_ms, "select": st.select_ms})
+            blocks.append((st.blocks_tested + st1.blocks_tested, st.blocks_passed + st1.blocks_passed,
+                           st.pairs_pruned_by_bound + st1.pairs_pruned_by_bound, st.pairs_scored + st1.pairs_scored,
                            st.candidates))
-        if world > 1:
-            all_d, all_i = gather_topk(dd, ids)
-            return merge_topk_device(L, all_d, all_i, stream)
-        return dd, ids
+        return out
 
     for _ in range(warmup):
         step(False)
@@ -751,7 +788,7 @@ def main():
         elapsed = float(t.item())
         dist.barrier()
     tensor_path = bool(st.tensor_core_path)
-    levels = int(st.levels)
+    levels = int(st.levels + st1.levels)
     # The timed steps' merged result, identical for every GPU count: its digest
     # goes into the line so runs at different N can be compared.
     res_d = result[0].cpu().numpy()
@@ -765,15 +802,16 @@ def main():
     e2e_steps = max(1, min(args.steps, 3))
 
     def e2e_step():
-        check(L, L.mdh_search_u8(h, ctypes.c_void_p(hq.data_ptr()), nq, k, ctypes.c_void_p(hid.data_ptr()),
-                                 ctypes.c_void_p(hdist.data_ptr()), None), "e2e search")
-        if world > 1:
-            ids.copy_(hid, non_blocking=True)
-            dd.copy_(hdist, non_blocking=True)
-            all_d, all_i = gather_topk(dd, ids)
-            out_d, out_i = merge_topk_device(L, all_d, all_i, stream)
-            hid.copy_(out_i)
-            hdist.copy_(out_d)
+        if world == 1:
+            check(L, L.mdh_search_u8(h, ctypes.c_void_p(hq.data_ptr()), nq, k, ctypes.c_void_p(hid.data_ptr()),
+                                     ctypes.c_void_p(hdist.data_ptr()), None), "e2e search")
+            return
+        # The sharded public path: queries from pinned host memory to this
+        # rank's GPU, the search with its exchanges, the merged result back.
+        q = hq.to(device, non_blocking=True)
+        out_d, out_i = search(q)
+        hid.copy_(out_i)
+        hdist.copy_(out_d)
 
     e2e_step()
     torch.cuda.synchronize()

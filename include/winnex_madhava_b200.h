@@ -195,6 +195,28 @@ mdh_status mdh_search_u8(mdh_index* index, const uint8_t* host_queries, int32_t 
 mdh_status mdh_search_u8_device(mdh_index* index, const uint8_t* dev_queries, int32_t nq, int32_t k,
                                 int32_t* dev_ids, int32_t* dev_dist, void* stream, mdh_stats* stats);
 
+/* Cooperative thresholds for a corpus sharded over ranks (one index per rank,
+ * global row ids).  Phase 1, mdh_search_u8_device_sample, scans only this
+ * shard's sample levels and writes each query's exact top-k (distance, id) of
+ * the largest sample scanned ([nq][k], id -1 past its rows).  The ranks
+ * exchange these lists (all_gather) and merge them (mdh_merge_topk_device):
+ * the merged list's k-th entry is the k-th best of the union of every rank's
+ * sample, a valid distance threshold for the whole corpus and tighter than
+ * any one rank's own.  Phase 2, mdh_search_u8_device_bounded, takes the merged
+ * lists (dev_thr_dist / dev_thr_ids, [nq][k]) and scans the full shard under
+ * that threshold: its results are the exact top-k among this shard's rows at
+ * or under it (-1 past them).  Merging the ranks' phase-2 lists gives the
+ * exact global top-k.  A rank's sample then only needs 1/G of the rows that
+ * one rank alone would need for the same threshold, G = the number of ranks.
+ * Single-device indexes; device pointers and stream as mdh_search_u8_device.
+ * No counterpart in the reference (it has no multi-GPU path,
+ * src/speed_gpu.cu:113-117). */
+mdh_status mdh_search_u8_device_sample(mdh_index* index, const uint8_t* dev_queries, int32_t nq, int32_t k,
+                                       int32_t* dev_ids, int32_t* dev_dist, void* stream, mdh_stats* stats);
+mdh_status mdh_search_u8_device_bounded(mdh_index* index, const uint8_t* dev_queries, int32_t nq, int32_t k,
+                                        const int32_t* dev_thr_dist, const int32_t* dev_thr_ids, int32_t* dev_ids,
+                                        int32_t* dev_dist, void* stream, mdh_stats* stats);
+
 /* mdh_search_u8_device without any allocation: no cudaMalloc / cudaFree
  * or allocating library call; scratch is a fixed 9 MiB __device__ array per
  * device.  For callers that must not allocate (a serving loop beside a

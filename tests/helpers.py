@@ -49,6 +49,8 @@ def capi():
     L.mdh_search_u8.argtypes = [P, P, i32, i32, P, P, ctypes.POINTER(Stats)]
     L.mdh_search_u8_device.argtypes = [P, P, i32, i32, P, P, P, ctypes.POINTER(Stats)]
     L.mdh_search_u8_device_noalloc.argtypes = [P, P, i32, i32, P, P, P, ctypes.POINTER(Stats)]
+    L.mdh_search_u8_device_sample.argtypes = [P, P, i32, i32, P, P, P, ctypes.POINTER(Stats)]
+    L.mdh_search_u8_device_bounded.argtypes = [P, P, i32, i32, P, P, P, P, P, ctypes.POINTER(Stats)]
     L.mdh_merge_topk_device.argtypes = [P, P, i32, i32, i32, P, P, P]
     L.mdh_ivf_create_u8.argtypes = [P, i64, i32, P, i32, P, i32, ctypes.POINTER(P)]
     L.mdh_ivf_create_u8_metric.argtypes = [P, i64, i32, P, i32, P, i32, i32, ctypes.POINTER(P)]
@@ -75,7 +77,8 @@ def capi():
                "mdh_set_verify", "mdh_ivf_create_u8", "mdh_ivf_route_u8", "mdh_ivf_search_u8", "mdh_ivf_info",
                "mdh_ivf_destroy", "mdh_index_save", "mdh_index_load", "mdh_index_file_info",
                "mdh_set_candidate_cap_limit", "mdh_set_sample_ratio", "mdh_index_id_base",
-               "mdh_index_memory", "mdh_ivf_create_u8_metric"):
+               "mdh_index_memory", "mdh_ivf_create_u8_metric", "mdh_search_u8_device_sample",
+               "mdh_search_u8_device_bounded"):
         getattr(L, fn).restype = ctypes.c_int
     return L
 

@@ -176,3 +176,64 @@ def test_float_queries_through_capi():
     np.testing.assert_array_equal(ids, want_ids)
     np.testing.assert_array_equal(dist, want_d)  # bit-identical float distances
     L.mdh_index_destroy(h)
+
+
+@pytest.mark.parametrize("k", [10, 100])
+def test_cooperative_thresholds_two_shards(k):
+    """Two row shards (global ids) searched with shared thresholds:
+    mdh_search_u8_device_sample on each, the lists merged on the device, then
+    mdh_search_u8_device_bounded on each with the merged lists; merging the
+    bounded results gives the oracle's exact top-k.  The shards are built with
+    the larger sample ratio a rank of a 2-way split uses (32), so each rank's
+    sample is half what it would need alone."""
+    torch = pytest.importorskip("torch")
+    L = capi()
+    C = cases.gmm_u8(400_000, 128, 256, seed=33)
+    Q = np.ascontiguousarray(cases.gmm_u8_queries(300, 128, 256, seed_means=33, seed_q=34))
+    want_ids, want_d = oracle.l2_topk_u8(C, Q, k)
+    half = C.shape[0] // 2
+    assert L.mdh_set_sample_ratio(32) == 0
+    try:
+        hs = [_create_u8(L, C[:half], id_offset=0), _create_u8(L, C[half:], id_offset=half)]
+    finally:
+        assert L.mdh_set_sample_ratio(0) == 0
+    dq = torch.from_numpy(Q).cuda()
+    nq = len(Q)
+
+    def merged(lists):
+        all_d = torch.stack([d for d, _ in lists]).contiguous()
+        all_i = torch.stack([i for _, i in lists]).contiguous()
+        out_d = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+        out_i = torch.empty_like(out_d)
+        assert L.mdh_merge_topk_device(ctypes.c_void_p(all_d.data_ptr()), ctypes.c_void_p(all_i.data_ptr()), 2, nq,
+                                       k, ctypes.c_void_p(out_d.data_ptr()), ctypes.c_void_p(out_i.data_ptr()),
+                                       None) == 0, L.mdh_last_error()
+        return out_d, out_i
+
+    phase1 = []
+    for h in hs:
+        d = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+        i = torch.empty_like(d)
+        s = Stats()
+        assert L.mdh_search_u8_device_sample(h, ctypes.c_void_p(dq.data_ptr()), nq, k, ctypes.c_void_p(i.data_ptr()),
+                                             ctypes.c_void_p(d.data_ptr()), None, ctypes.byref(s)) == 0, \
+            L.mdh_last_error()
+        assert s.full_scan_pairs < half * nq  # only sample rows were scanned
+        phase1.append((d, i))
+    thr_d, thr_i = merged(phase1)
+    phase2 = []
+    for h in hs:
+        d = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+        i = torch.empty_like(d)
+        s = Stats()
+        assert L.mdh_search_u8_device_bounded(h, ctypes.c_void_p(dq.data_ptr()), nq, k,
+                                              ctypes.c_void_p(thr_d.data_ptr()), ctypes.c_void_p(thr_i.data_ptr()),
+                                              ctypes.c_void_p(i.data_ptr()), ctypes.c_void_p(d.data_ptr()), None,
+                                              ctypes.byref(s)) == 0, L.mdh_last_error()
+        assert s.levels == 1 and s.full_scan_pairs == half * nq
+        phase2.append((d, i))
+    out_d, out_i = merged(phase2)
+    np.testing.assert_array_equal(out_i.cpu().numpy(), want_ids)
+    np.testing.assert_array_equal(out_d.cpu().numpy(), want_d)
+    for h in hs:
+        assert L.mdh_index_destroy(h) == 0

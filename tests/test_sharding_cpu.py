@@ -94,3 +94,67 @@ def test_row_range_partitions():
             assert max(e - s for s, e in spans) - min(e - s for s, e in spans) <= 1
     with pytest.raises(ValueError):
         row_range(10, 2, 2)
+
+
+def _coop_worker(rank, world, port, n, nq, k, frac, out):
+    import torch
+    import torch.distributed as dist
+
+    from winnex_madhava.sharding import cooperative_topk, row_range
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        C = cases.gmm_u8(n, 32, 8, seed=65)
+        Q = cases.gmm_u8_queries(nq, 32, 8, seed_means=65, seed_q=66)
+        s, e = row_range(n, rank, world)
+        gid = np.arange(s, e)
+        D = ((C[s:e].astype(np.int64)[None, :, :] - Q.astype(np.int64)[:, None, :]) ** 2).sum(-1)  # [nq][rows]
+        in_sample = (gid * 2654435761 % 1000) < frac * 1000  # a fixed subset of this shard
+
+        def topk(mask_rows):
+            di = np.full((nq, k), -1, np.int32)
+            ii = np.full((nq, k), -1, np.int32)
+            for q in range(nq):
+                rows = np.flatnonzero(mask_rows[q])
+                o = np.lexsort((gid[rows], D[q, rows]))[:k]
+                di[q, :len(o)], ii[q, :len(o)] = D[q, rows[o]], gid[rows[o]]
+            return torch.from_numpy(di), torch.from_numpy(ii)
+
+        def sample(_q, _k):
+            return topk(np.broadcast_to(in_sample, D.shape))
+
+        def bounded(_q, _k, thr_d, thr_i):
+            td, ti = thr_d[:, k - 1].numpy().astype(np.int64), thr_i[:, k - 1].numpy()
+            inf = ti < 0
+            ok = (D < td[:, None]) | ((D == td[:, None]) & (gid[None, :] <= ti[:, None])) | inf[:, None]
+            return topk(ok)
+
+        def merge(all_d, all_i):
+            md, mi = _merge(all_d.numpy(), all_i.numpy(), k)
+            return torch.from_numpy(md.astype(np.int32)), torch.from_numpy(mi)
+
+        d, i = cooperative_topk(sample, bounded, merge, None, k)
+        np.savez(out + f".{rank}.npz", d=d.numpy(), i=i.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("frac", [0.05, 0.0])
+def test_two_rank_cooperative_thresholds(frac):
+    """Thresholds from the merged sample lists of both ranks keep the result
+    exact: every rank returns the single-shard oracle's top-k (an empty sample
+    gives no threshold, and the bounded phase then keeps every row)."""
+    mp = pytest.importorskip("torch.multiprocessing")
+    n, nq, k, world = 4001, 12, 10, 2
+    with tempfile.TemporaryDirectory() as tmp:
+        out = os.path.join(tmp, "coop")
+        mp.spawn(_coop_worker, args=(world, _free_port(), n, nq, k, frac, out), nprocs=world, join=True)
+        got = [np.load(out + f".{r}.npz") for r in range(world)]
+    C = cases.gmm_u8(n, 32, 8, seed=65)
+    Q = cases.gmm_u8_queries(nq, 32, 8, seed_means=65, seed_q=66)
+    want_i, want_d = oracle.l2_exact_u8_int(C, Q, k)
+    for g in got:
+        np.testing.assert_array_equal(g["i"], want_i)
+        np.testing.assert_array_equal(g["d"], want_d)

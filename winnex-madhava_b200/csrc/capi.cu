@@ -249,16 +249,28 @@ struct ShardResult {
     int64_t pruned = 0;       // tc_pairs whose distance the block bound made unnecessary
 };
 
+// Phases of a search that ranks share their sample results in between
+// (cooperative thresholds, mdh_search_u8_device_sample / _bounded).
+enum SearchPhase { kPhaseAll = 0, kPhaseSample = 1, kPhaseBounded = 2 };
+
 // Exact top-k for nq staged queries on one shard.  Results: ws.out_key /
 // ws.out_id ([nq][k], device).  host_q_u8 / host_q_f32 hold the staged
 // queries on the host for overflow reruns.
+// phase kPhaseSample: the plan without its full level; the results are the
+// exact top-k of the largest sample scanned (the whole shard when it has no
+// sample).  kPhaseBounded: the full level alone, with each query's threshold
+// the k-th entry of thr_lists ([nq][k] (distance, id) on the device, id -1 =
+// empty); the results are the exact top-k among the rows at or under it.
 ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, int k, const uint8_t* host_q_u8,
-                         const float* host_q_f32, size_t f32_stride_floats) {
+                         const float* host_q_f32, size_t f32_stride_floats, int phase = kPhaseAll,
+                         const int32_t* thr_dist = nullptr, const int32_t* thr_ids = nullptr) {
     MDH_CUDA(cudaSetDevice(sh.device));
     Workspace& w = sh.ws;
     cudaStream_t st = sh.stream;
     ShardResult res;
     std::vector<LevelStep> steps = plan_levels(sh, k);
+    if (phase == kPhaseSample && steps.size() > 1) steps.pop_back();
+    if (phase == kPhaseBounded) steps = {LevelStep{(int)sh.levels.size() - 1, steps.back().cap, false}};
     int capmax = 0;
     for (auto& s : steps) capmax = std::max(capmax, s.cap);
     growT(&w.thr_key, &w.thr_key_bytes, (size_t)nq * 4);
@@ -281,6 +293,11 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
 
     res.levels = (int)steps.size();
     MDH_CUDA(cudaEventRecord(w.ev_start, st));
+    if (phase == kPhaseBounded) {
+        launch_thresholds_from_lists(reinterpret_cast<const uint32_t*>(thr_dist), thr_ids, nq, k, w.thr_key, w.thr_id,
+                                     st);
+        res.launches++;
+    }
     for (size_t si = 0; si < steps.size(); si++) {
         const LevelStep& s = steps[si];
         const Level& lv = sh.levels[s.level];
@@ -399,7 +416,7 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
     // pruning (the CUDA-core kernels compare every row) counts the rows at or
     // before each query's k-th result by (key, id).  An exact result has
     // exactly k of them; any other count is reported as violations.
-    if (g_verify > 0 && qp.integer && nq > 0) {
+    if (g_verify > 0 && qp.integer && nq > 0 && phase == kPhaseAll) {
         const int m = std::min(nq, g_verify);
         std::vector<int32_t> list((size_t)m);
         for (int i = 0; i < m; i++) list[(size_t)i] = (int32_t)((int64_t)i * nq / m);
@@ -883,9 +900,17 @@ mdh_status mdh_search_u8(mdh_index* index, const uint8_t* host_queries, int32_t 
     });
 }
 
-mdh_status mdh_search_u8_device(mdh_index* index, const uint8_t* dev_queries, int32_t nq, int32_t k,
-                                int32_t* dev_ids, int32_t* dev_dist, void* stream, mdh_stats* stats) {
-    return guard([&] {
+}  // extern "C"
+
+namespace mdh {
+namespace {
+
+// The device-resident u8 search (mdh_search_u8_device) and its cooperative
+// phases (mdh_search_u8_device_sample / _bounded): queries, results and the
+// threshold lists are device pointers on the index's device.
+void device_search(mdh_index* index, const uint8_t* dev_queries, int32_t nq, int32_t k, int phase,
+                   const int32_t* thr_dist, const int32_t* thr_ids, int32_t* dev_ids, int32_t* dev_dist, void* stream,
+                   mdh_stats* stats) {
         auto t0 = std::chrono::high_resolution_clock::now();
         MDH_REQUIRE(index && !index->is_f32, MDH_ERR_INVALID_ARG, "u8 queries need a u8 index");
         MDH_REQUIRE(index->shards.size() == 1, MDH_ERR_UNSUPPORTED, "device search needs a single-device index");
@@ -916,7 +941,7 @@ mdh_status mdh_search_u8_device(mdh_index* index, const uint8_t* dev_queries, in
                 qp.integer = true;
                 qp.int_dist = index->metric == MDH_METRIC_L2;
                 ShardResult r;
-                if (kk > 0) r = search_shard(index, sh, qp, nq, kk, nullptr, nullptr, 0);
+                if (kk > 0) r = search_shard(index, sh, qp, nq, kk, nullptr, nullptr, 0, phase, thr_dist, thr_ids);
                 st.pairs_scored = r.pairs;
                 st.levels = r.levels;
                 st.tensor_core_path = std::max(0, r.scan_path - 1);
@@ -956,6 +981,35 @@ mdh_status mdh_search_u8_device(mdh_index* index, const uint8_t* dev_queries, in
         sh.stream = saved;
         st.latency_ms = std::chrono::duration<double, std::milli>(std::chrono::high_resolution_clock::now() - t0).count();
         if (stats) *stats = st;
+}
+
+}  // namespace
+}  // namespace mdh
+
+extern "C" {
+
+mdh_status mdh_search_u8_device(mdh_index* index, const uint8_t* dev_queries, int32_t nq, int32_t k,
+                                int32_t* dev_ids, int32_t* dev_dist, void* stream, mdh_stats* stats) {
+    return guard([&] {
+        device_search(index, dev_queries, nq, k, kPhaseAll, nullptr, nullptr, dev_ids, dev_dist, stream, stats);
+    });
+}
+
+mdh_status mdh_search_u8_device_sample(mdh_index* index, const uint8_t* dev_queries, int32_t nq, int32_t k,
+                                       int32_t* dev_ids, int32_t* dev_dist, void* stream, mdh_stats* stats) {
+    return guard([&] {
+        device_search(index, dev_queries, nq, k, kPhaseSample, nullptr, nullptr, dev_ids, dev_dist, stream, stats);
+    });
+}
+
+mdh_status mdh_search_u8_device_bounded(mdh_index* index, const uint8_t* dev_queries, int32_t nq, int32_t k,
+                                        const int32_t* dev_thr_dist, const int32_t* dev_thr_ids, int32_t* dev_ids,
+                                        int32_t* dev_dist, void* stream, mdh_stats* stats) {
+    return guard([&] {
+        MDH_REQUIRE(nq == 0 || k == 0 || (dev_thr_dist && dev_thr_ids), MDH_ERR_INVALID_ARG,
+                    "null threshold lists");
+        device_search(index, dev_queries, nq, k, kPhaseBounded, dev_thr_dist, dev_thr_ids, dev_ids, dev_dist,
+                      stream, stats);
     });
 }
 

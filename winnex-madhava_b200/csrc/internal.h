@@ -211,6 +211,10 @@ void launch_select(const uint32_t* counts, const uint2* cand, int cap, const int
                    uint32_t* thr_key, int32_t* thr_id, uint32_t* out_key, int32_t* out_id,
                    int32_t* flags, int32_t* n_flagged, const int32_t* qmap, unsigned long long* n_cand,
                    cudaStream_t st);
+// thr[q] = the k-th entry (key, id) of list q of [nq][k] (key, id) lists,
+// or infinity when that entry is empty (id -1).
+void launch_thresholds_from_lists(const uint32_t* keys, const int32_t* ids, int nq, int k, uint32_t* thr_key,
+                                  int32_t* thr_id, cudaStream_t st);
 // Verification of results (capi.cu, search with verification on).
 void launch_verify_thresholds(const int32_t* list, int m, const uint32_t* out_key, const int32_t* out_id, int k, int kk,
                               uint32_t* thr_key, int32_t* thr_id, cudaStream_t st);

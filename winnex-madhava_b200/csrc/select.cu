@@ -568,6 +568,27 @@ void launch_select(const uint32_t* counts, const uint2* cand, int cap, const int
     MDH_CUDA(cudaGetLastError());
 }
 
+namespace {
+
+__global__ void k_thresholds_from_lists(const uint32_t* __restrict__ keys, const int32_t* __restrict__ ids, int nq,
+                                        int k, uint32_t* __restrict__ thr_key, int32_t* __restrict__ thr_id) {
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= nq) return;
+    const size_t e = (size_t)q * k + (k - 1);
+    const int32_t id = ids[e];
+    thr_key[q] = id >= 0 ? keys[e] : kKeyInf;
+    thr_id[q] = id >= 0 ? id : kIdInf;
+}
+
+}  // namespace
+
+void launch_thresholds_from_lists(const uint32_t* keys, const int32_t* ids, int nq, int k, uint32_t* thr_key,
+                                  int32_t* thr_id, cudaStream_t st) {
+    if (nq <= 0 || k <= 0) return;
+    k_thresholds_from_lists<<<(nq + 255) / 256, 256, 0, st>>>(keys, ids, nq, k, thr_key, thr_id);
+    MDH_CUDA(cudaGetLastError());
+}
+
 void launch_verify_thresholds(const int32_t* list, int m, const uint32_t* out_key, const int32_t* out_id, int k, int kk,
                               uint32_t* thr_key, int32_t* thr_id, cudaStream_t st) {
     if (m <= 0) return;

@@ -70,3 +70,56 @@ def merge_topk_device(lib, all_dist, all_ids, stream=None):
     if st != 0:
         raise RuntimeError(lib.mdh_last_error().decode() if lib.mdh_last_error() else f"merge failed ({st})")
     return out_d, out_i
+
+
+def cooperative_topk(sample, bounded, merge, queries, k, group=None):
+    """Row-sharded exact top-k with thresholds shared across the ranks.
+
+    ``sample(queries, k)`` -> this rank's ``(dist, ids)`` top-k over its sample
+    rows; ``bounded(queries, k, thr_dist, thr_ids)`` -> its exact top-k among
+    its rows at or under each query's threshold, the k-th entry of the merged
+    ``[Q][k]`` lists given; ``merge(all_dist, all_ids)`` -> the k smallest
+    ``(dist, global id)`` of ``[world][Q][k]`` lists.  Two exchanges
+    (``gather_topk``): the sample lists, whose merged k-th entry is the k-th
+    best of the union of every rank's sample and so a threshold valid for the
+    whole corpus, then the final lists.  Returns the merged ``(dist, ids)``,
+    the same on every rank and for every rank count.
+    """
+    d1, i1 = sample(queries, k)
+    thr_d, thr_i = merge(*gather_topk(d1, i1, group))
+    d2, i2 = bounded(queries, k, thr_d, thr_i)
+    return merge(*gather_topk(d2, i2, group))
+
+
+def device_phases(lib, index, dev_queries, stream=None, stats=None):
+    """The (sample, bounded) callables of :func:`cooperative_topk` for one
+    rank's index through the C ABI (``mdh_search_u8_device_sample`` /
+    ``mdh_search_u8_device_bounded``), on CUDA tensors."""
+    import torch
+
+    def _stream(t):
+        s = stream if stream is not None else torch.cuda.current_stream(t.device)
+        return ctypes.c_void_p(s.cuda_stream)
+
+    def _check(st):
+        if st != 0:
+            raise RuntimeError(lib.mdh_last_error().decode())
+
+    def sample(q, k):
+        ids = torch.empty((q.shape[0], k), dtype=torch.int32, device=q.device)
+        dist = torch.empty_like(ids)
+        _check(lib.mdh_search_u8_device_sample(index, ctypes.c_void_p(q.data_ptr()), q.shape[0], k,
+                                               ctypes.c_void_p(ids.data_ptr()), ctypes.c_void_p(dist.data_ptr()),
+                                               _stream(q), stats))
+        return dist, ids
+
+    def bounded(q, k, thr_d, thr_i):
+        ids = torch.empty((q.shape[0], k), dtype=torch.int32, device=q.device)
+        dist = torch.empty_like(ids)
+        _check(lib.mdh_search_u8_device_bounded(index, ctypes.c_void_p(q.data_ptr()), q.shape[0], k,
+                                                ctypes.c_void_p(thr_d.data_ptr()), ctypes.c_void_p(thr_i.data_ptr()),
+                                                ctypes.c_void_p(ids.data_ptr()), ctypes.c_void_p(dist.data_ptr()),
+                                                _stream(q), stats))
+        return dist, ids
+
+    return sample, bounded
