@@ -37,7 +37,7 @@ SEED = 20261201
 CHUNK = 3_125_000
 L2_BYTES = 126 << 20        # B200 L2
 L2_FLUSH_BYTES = 512 << 20
-TRAFFIC_BYTES_PER_ROW = (1.322692e9 + 12.821248e6) / 10_000_000
+TRAFFIC_BYTES_PER_ROW = (1.288509e9 + 34.518272e6) / 10_000_000
 METRIC = "queries/sec, 100M×128 u8 exact top-10, 10K-query batch at 1/2/4/8 B200; % roofline"
 
 
@@ -103,6 +103,7 @@ def load_lib():
     L.mdh_merge_topk_device.argtypes = [P, P, i32, i32, i32, P, P, P]
     L.mdh_set_scan_path.argtypes = [i32]
     L.mdh_set_sample_ratio.argtypes = [i32]
+    L.mdh_set_threshold_sharing.argtypes = [i32]
     L.mdh_ivf_create_u8.argtypes = [P, i64, i32, P, i32, P, i32, ctypes.POINTER(P)]
     L.mdh_ivf_search_u8.argtypes = [P, P, i32, i32, i32, P, P, ctypes.POINTER(Stats)]
     L.mdh_ivf_destroy.argtypes = [P]
@@ -115,7 +116,8 @@ def load_lib():
     L.mdh_search_u8.restype = ctypes.c_int
     L.mdh_last_error.restype = ctypes.c_char_p
     for f in ("mdh_index_create_u8_device", "mdh_index_destroy", "mdh_search_u8", "mdh_search_u8_device",
-              "mdh_merge_topk_device", "mdh_set_scan_path", "mdh_set_sample_ratio", "mdh_ivf_create_u8",
+              "mdh_merge_topk_device", "mdh_set_scan_path", "mdh_set_sample_ratio", "mdh_set_threshold_sharing",
+              "mdh_ivf_create_u8",
               "mdh_ivf_search_u8",
               "mdh_ivf_destroy"):
         getattr(L, f).restype = ctypes.c_int
@@ -477,6 +479,7 @@ def run_cos(args, torch, device, L, warmup):
     queries = make_cos_rows_gpu(torch, nq, device, SEED + 13).cpu().numpy()
     torch.cuda.empty_cache()
     check(L, L.mdh_set_scan_path(args.scan_path), "set_scan_path")
+    check(L, L.mdh_set_sample_ratio(args.sample_ratio), "set_sample_ratio")
     h = ctypes.c_void_p()
     t0 = time.time()
     check(L, L.mdh_index_create_f32(ctypes.c_void_p(rows.ctypes.data), n, COS_DIM, 0, None, 0, 0, ctypes.byref(h)),
@@ -511,6 +514,7 @@ def run_cos(args, torch, device, L, warmup):
     cos_stages = {"prep": round(st.prep_ms, 3), "samples": round(st.sample_ms, 3),
                   "full_scan": round(st.full_scan_ms, 3), "rescore_in_full_scan": round(st.rescore_ms, 3),
                   "select": round(st.select_ms, 3), "call_wall": round(st.latency_ms, 3),
+                  "final_candidates": int(st.candidates), "sample_ratio": args.sample_ratio or 8,
                   "note": "last timed step; CUDA events per stage, prep includes the host query normalization"}
     path = {0: "CUDA cores (fp32 replica)", 3: "bf16 tcgen05 pass + exact fp32 rescore"}.get(int(st.tensor_core_path),
                                                                                            str(st.tensor_core_path))
@@ -697,12 +701,13 @@ def main():
     # With G ranks sharing their sample results, each rank samples 1/G of what
     # it would alone for the same threshold: its largest sample is shard/(16 G).
     coop = world > 1 and not args.no_coop
-    ratio = args.sample_ratio or (16 * world if coop else 0)
+    ratio = args.sample_ratio
     check(L, L.mdh_set_sample_ratio(ratio), "set_sample_ratio")
+    check(L, L.mdh_set_threshold_sharing(world if coop else 1), "set_threshold_sharing")
     config["threshold_exchange"] = ("each rank scans its samples, the ranks all_gather and merge their sample top-k "
                                     "lists, every rank scans its shard under the merged k-th distance, then the "
                                     "final lists are all_gathered and merged" if coop else "none")
-    config["sample_ratio"] = ratio or 64
+    config["sample_ratio"] = ratio or 8
     start, end = row_range(args.n, rank, world)
     flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device) if small_corpus else None
     rows = make_rows_gpu(torch, start, end, device, args.comps)
@@ -841,7 +846,7 @@ def main():
         achieved = 2.0 * pairs * DIM / (ms_scan / 1e3) / 1e12 if ms_scan > 0 else None
         # DRAM traffic of the scan: ncu capture of the same kernel on a
         # 10M-row case (dram__bytes_read.sum + dram__bytes_write.sum =
-        # 1.3381e9 B per launch for 10,000 queries); the corpus and norms cross
+        # 1.3230e9 B per launch for 10,000 queries); the corpus and norms cross
         # HBM once per launch, so traffic scales with the rows scanned.
         traffic = TRAFFIC_BYTES_PER_ROW * rows_scanned if pairs else None
         roofline = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",

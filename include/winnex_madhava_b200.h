@@ -296,13 +296,34 @@ mdh_status mdh_set_verify(int32_t max_queries);
  * limits trade speed for scratch memory and exercise that rerun path. */
 mdh_status mdh_set_candidate_cap_limit(int32_t cap);
 
+/* Failure handling, exercised without a device fault.
+ * mdh_set_fault(site): a one-shot host-side fault for tests.  site 1: the
+ * next growth of a search workspace fails as out of memory (MDH_ERR_OOM);
+ * site 2: the next shard search thread fails before it scans
+ * (MDH_ERR_INTERNAL).  0 clears it.  The index stays usable afterwards.
+ * mdh_check_wait_timeout(device, budget_cycles): runs the scans' bounded
+ * mbarrier wait on a barrier that nothing arrives on, with a budget of
+ * budget_cycles (1,000 .. 2^32 clock cycles; the scans use ~4e9): it must
+ * give up and record the timeout, and the call returns MDH_ERR_TIMEOUT; any
+ * other status means the timeout path is broken.  device -1 = current.
+ * No counterpart in the reference. */
+mdh_status mdh_set_fault(int32_t site);
+mdh_status mdh_check_wait_timeout(int32_t device, int64_t budget_cycles);
+
 /* Options (process-wide): sample plan.  An index shard of n rows keeps
- * nested random samples of 1024 * 32^j rows up to about n / ratio rows (plus
- * one of n / ratio rows when that ladder stops more than 4x short of it);
- * a search scans them smallest first to set each query's distance threshold,
- * and about k * ratio rows per query pass the full scan's threshold.  Larger
- * ratios scan less sample and form more candidate distances.  0 restores the
- * default (64).  Read when samples are built (index create and load). */
+ * nested random samples of 1024 * 4^j rows up to n / ratio rows (default
+ * ratio 8; 0 restores it).  Read when samples are built (index create and
+ * load).  A search scans a chain of them, smallest first, to set each
+ * query's distance threshold: the chain is the cheapest under a measured
+ * cost model (a level costs its rows plus a fixed overhead, and a level
+ * keeps about k * (its rows / the previous level's) candidates per query,
+ * each costing ~4,500 row scans), so its largest sample is about
+ * sqrt(4,500 k n) rows.
+ * mdh_set_threshold_sharing(ranks): the full level's threshold comes from the
+ * union of `ranks` ranks' samples (mdh_search_u8_device_sample), so the
+ * chain's last step expects `ranks` times fewer candidates and stops at a
+ * smaller sample.  1 (default) for a shard searched alone.  Read at search. */
+mdh_status mdh_set_threshold_sharing(int32_t ranks);
 mdh_status mdh_set_sample_ratio(int32_t ratio);
 
 /* Levels (samples, then the whole shard) a top-k search scans on one shard

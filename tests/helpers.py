@@ -65,6 +65,9 @@ def capi():
     L.mdh_set_verify.argtypes = [i32]
     L.mdh_set_candidate_cap_limit.argtypes = [i32]
     L.mdh_set_sample_ratio.argtypes = [i32]
+    L.mdh_set_fault.argtypes = [i32]
+    L.mdh_set_threshold_sharing.argtypes = [i32]
+    L.mdh_check_wait_timeout.argtypes = [i32, i64]
     L.mdh_plan_level_count.argtypes = [i64, i32]
     L.mdh_plan_level_count.restype = i32
     L.mdh_index_id_base.argtypes = [P, P]
@@ -78,7 +81,8 @@ def capi():
                "mdh_ivf_destroy", "mdh_index_save", "mdh_index_load", "mdh_index_file_info",
                "mdh_set_candidate_cap_limit", "mdh_set_sample_ratio", "mdh_index_id_base",
                "mdh_index_memory", "mdh_ivf_create_u8_metric", "mdh_search_u8_device_sample",
-               "mdh_search_u8_device_bounded"):
+               "mdh_search_u8_device_bounded", "mdh_set_fault", "mdh_check_wait_timeout",
+               "mdh_set_threshold_sharing"):
         getattr(L, fn).restype = ctypes.c_int
     return L
 

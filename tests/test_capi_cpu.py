@@ -82,21 +82,30 @@ def test_stats_struct_matches_header(tmp_path):
     assert got == want
 
 
-def test_sample_plan_shrinks_with_the_shard():
-    """Sample levels follow the shard size (the largest sample is about 1/64 of
-    the shard), so a rank of a G-way row split scans ~1/G of the sample rows."""
+def test_sample_plan_follows_the_cost_model():
+    """Sample ladders of 1024 * 4^j rows up to shard / 8; a search scans the
+    cheapest chain of them under the cost model (largest sample near
+    sqrt(4,500 k n)): longer chains for larger shards and larger k, a single
+    dense level for a tiny shard, and shorter chains when ranks share their
+    sample thresholds."""
     L = capi()
-    assert L.mdh_plan_level_count(100_000_000, 10) == 4    # 1,024 / 32,768 / 1,048,576 / full
-    assert L.mdh_plan_level_count(12_500_000, 10) == 3     # one of 8 ranks: 1,024 / 195,312 / full
-    assert L.mdh_plan_level_count(12_500_000, 100) == 4    # k = 100 steps by at most 20x: every sample
-    assert L.mdh_plan_level_count(1_000_000, 10) == 3      # 1,024 / 15,625 / full
-    assert L.mdh_plan_level_count(100_000, 10) == 2        # 1,024 / full
+    assert L.mdh_plan_level_count(100_000_000, 10) == 6
+    assert L.mdh_plan_level_count(100_000_000, 100) == 8
+    assert L.mdh_plan_level_count(12_500_000, 10) == 6
+    assert L.mdh_plan_level_count(1_000_000, 10) == 5
+    assert L.mdh_plan_level_count(100_000, 10) == 3
     assert L.mdh_plan_level_count(5_000, 10) == 1          # dense scan of the shard
     assert L.mdh_plan_level_count(0, 10) == 0
-    assert L.mdh_set_sample_ratio(8) == 0
+    assert L.mdh_set_threshold_sharing(8) == 0
     try:
-        # The 100M ladder on a 10M shard: 1,024 / 32,768 / 1,048,576 / full.
-        assert L.mdh_plan_level_count(10_000_000, 10) == 4
+        assert L.mdh_plan_level_count(12_500_000, 100) == 6  # one fewer than alone
+        assert L.mdh_plan_level_count(1_000_000, 10) == 4
+    finally:
+        assert L.mdh_set_threshold_sharing(1) == 0
+    assert L.mdh_set_sample_ratio(64) == 0
+    try:
+        assert L.mdh_plan_level_count(1_000_000, 10) == 3   # a shorter ladder (top <= n / 64)
     finally:
         assert L.mdh_set_sample_ratio(0) == 0
     assert L.mdh_set_sample_ratio(1) == 1
+    assert L.mdh_set_threshold_sharing(0) == 1

@@ -183,20 +183,17 @@ def test_cooperative_thresholds_two_shards(k):
     """Two row shards (global ids) searched with shared thresholds:
     mdh_search_u8_device_sample on each, the lists merged on the device, then
     mdh_search_u8_device_bounded on each with the merged lists; merging the
-    bounded results gives the oracle's exact top-k.  The shards are built with
-    the larger sample ratio a rank of a 2-way split uses (32), so each rank's
-    sample is half what it would need alone."""
+    bounded results gives the oracle's exact top-k.  The searches plan for
+    thresholds shared by 2 ranks (mdh_set_threshold_sharing), so each rank's
+    sample chain stops at a smaller sample than it would alone."""
     torch = pytest.importorskip("torch")
     L = capi()
     C = cases.gmm_u8(400_000, 128, 256, seed=33)
     Q = np.ascontiguousarray(cases.gmm_u8_queries(300, 128, 256, seed_means=33, seed_q=34))
     want_ids, want_d = oracle.l2_topk_u8(C, Q, k)
     half = C.shape[0] // 2
-    assert L.mdh_set_sample_ratio(32) == 0
-    try:
-        hs = [_create_u8(L, C[:half], id_offset=0), _create_u8(L, C[half:], id_offset=half)]
-    finally:
-        assert L.mdh_set_sample_ratio(0) == 0
+    hs = [_create_u8(L, C[:half], id_offset=0), _create_u8(L, C[half:], id_offset=half)]
+    assert L.mdh_set_threshold_sharing(2) == 0
     dq = torch.from_numpy(Q).cuda()
     nq = len(Q)
 
@@ -233,6 +230,7 @@ def test_cooperative_thresholds_two_shards(k):
         assert s.levels == 1 and s.full_scan_pairs == half * nq
         phase2.append((d, i))
     out_d, out_i = merged(phase2)
+    assert L.mdh_set_threshold_sharing(1) == 0
     np.testing.assert_array_equal(out_i.cpu().numpy(), want_ids)
     np.testing.assert_array_equal(out_d.cpu().numpy(), want_d)
     for h in hs:

@@ -62,7 +62,7 @@ def _load(L, path, devices=None):
 
 
 def test_roundtrip_u8_l2(tmp_path):
-    """300K GMM rows (three levels: two samples and the shard): the file holds
+    """300K GMM rows (a chain of samples and the shard): the file holds
     the norm-sorted shard, and the loaded index answers bit for bit."""
     L = capi()
     C = cases.gmm_u8(300_000, 128, 256, seed=91)
@@ -85,7 +85,9 @@ def test_roundtrip_u8_l2(tmp_path):
     ids1, d1, s1 = _search_u8(L, h2, Q, 10)
     np.testing.assert_array_equal(ids1, ids0)
     np.testing.assert_array_equal(d1, d0)
-    assert s1.levels == s0.levels == 3 and s1.tensor_core_path == s0.tensor_core_path == 1
+    # The loaded index rebuilt the same samples, so it runs the same chain.
+    assert s1.levels == s0.levels == L.mdh_plan_level_count(len(C), 10) >= 3
+    assert s1.tensor_core_path == s0.tensor_core_path == 1
     n, dim, metric, nd = ctypes.c_int64(), ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
     assert L.mdh_index_info(h2, ctypes.byref(n), ctypes.byref(dim), ctypes.byref(metric), ctypes.byref(nd)) == 0
     assert (n.value, dim.value, metric.value, nd.value) == (len(C), 128, 1, 1)

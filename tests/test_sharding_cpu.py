@@ -158,3 +158,51 @@ def test_two_rank_cooperative_thresholds(frac):
     for g in got:
         np.testing.assert_array_equal(g["i"], want_i)
         np.testing.assert_array_equal(g["d"], want_d)
+
+
+def _failing_rank_worker(rank, world, port, out):
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    from winnex_madhava.sharding import cooperative_topk
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    k, nq = 4, 3
+    lists = (torch.zeros((nq, k), dtype=torch.int32), torch.arange(nq * k, dtype=torch.int32).reshape(nq, k))
+
+    def sample(_q, _k):
+        if rank == 1:
+            raise RuntimeError("sample phase failed on this rank")
+        return lists
+
+    t0 = time.monotonic()
+    try:
+        cooperative_topk(sample, lambda *a: lists, lambda d, i: (d[0], i[0]), None, k)
+        outcome = "completed"
+    except Exception as exc:  # noqa: BLE001 - the outcome is what the test checks
+        outcome = f"{type(exc).__name__}: {exc}"
+    with open(f"{out}.{rank}", "w") as f:
+        f.write(f"{time.monotonic() - t0:.1f}\n{outcome}\n")
+    if rank == 0:
+        try:
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001 - the group may already be broken
+            pass
+
+
+def test_failing_rank_ends_the_exchange_with_an_error():
+    """A rank whose sample phase raises never joins the exchange; the other
+    rank's all_gather ends with an error once the group's timeout (5 s)
+    passes, instead of waiting forever, and no rank reports a result."""
+    mp = pytest.importorskip("torch.multiprocessing")
+    with tempfile.TemporaryDirectory() as tmp:
+        out = os.path.join(tmp, "outcome")
+        mp.spawn(_failing_rank_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+        r0 = open(out + ".0").read().split("\n", 1)
+        r1 = open(out + ".1").read().split("\n", 1)
+    assert "sample phase failed" in r1[1]
+    assert not r0[1].startswith("completed") and float(r0[0]) < 60

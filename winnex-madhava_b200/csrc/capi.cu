@@ -14,6 +14,7 @@
 //   If a query's candidate list overflows on the full shard, the k-th
 //   smallest stored entry is a strictly smaller valid threshold (ids make
 //   keys unique); that query reruns with it until its list fits.
+#include <atomic>
 #include <chrono>
 #include <cmath>
 #include <cstring>
@@ -33,8 +34,18 @@ thread_local std::string g_last_error;
 int g_scan_path = 0;  // 0 auto, 1 CUDA cores only, 2 tensor cores when possible
 int g_cap_limit = 0;  // 0 = default candidate capacities
 int g_verify = 0;     // queries per search re-checked by an exact unpruned scan (0 = off)
+// Fault injection (host side, one shot): the next workspace growth reports
+// OOM, or the next shard search thread fails before it scans.
+enum FaultSite : int { kFaultNone = 0, kFaultOom = 1, kFaultShard = 2 };
+std::atomic<int> g_fault{kFaultNone};
 
 constexpr int kCapMax = 16384;          // largest candidate list the selection kernel sorts
+// Level-plan cost model (row-scan units per query): a level's fixed cost and
+// one candidate's cost (epilogue expansion, re-key, selection), measured on
+// B200 (u8 L2, 10K queries; the bf16 cosine scan and its rescore scale alike).
+constexpr double kPlanLevelCost = 2.0e5;
+constexpr double kPlanCandidateCost = 4.5e3;
+int g_threshold_sharing = 1;  // ranks whose sample results set the full level's threshold
 constexpr size_t kCandBudget = size_t(2) << 30;  // bytes of candidate lists per query chunk
 
 template <class F>
@@ -100,13 +111,37 @@ std::vector<LevelStep> plan_levels(const std::vector<int64_t>& sizes, int64_t sh
     const int cap_floor = next_pow2(std::max(k + 1, 64));
     auto limit = [&](int cap) { return g_cap_limit > 0 ? std::max(cap_floor, std::min(cap, g_cap_limit)) : cap; };
     steps.push_back({i0, limit(next_pow2(std::max<int64_t>(sizes[i0], k))), true});
-    const double rmax = std::max(4.0, 2048.0 / (double)k);
+    // The levels after the first: the cheapest chain to the full shard under
+    // a cost model in row-scan units per query (measured on B200 with 10K
+    // queries): each level scanned costs its rows plus a fixed kPlanLevelCost
+    // (launches, selection), and each candidate it keeps costs
+    // kPlanCandidateCost -- about k * (its rows / the previous level's rows)
+    // candidates per query pass the previous level's threshold.  When the
+    // ranks of a row split share their sample results (g_threshold_sharing =
+    // G), the full level's threshold is the union's, G times tighter.  A step
+    // is allowed only while its expected list fits the selector.
+    const double rmax = std::max(4.0, (double)(kCapMax - 256) / (3.0 * k));
+    std::vector<double> cost((size_t)L, 1e300);
+    std::vector<int> prev((size_t)L, -1);
+    cost[(size_t)i0] = (double)sizes[i0] + kPlanLevelCost;
+    for (int j = i0 + 1; j < L; j++) {
+        const double share = j == L - 1 ? (double)std::max(1, g_threshold_sharing) : 1.0;
+        for (int i = i0; i < j; i++) {
+            const double ratio = (double)sizes[j] / (double)std::max<int64_t>(sizes[i], 1);
+            if (ratio > rmax && i != j - 1) continue;
+            const double c = cost[(size_t)i] + (double)sizes[j] + kPlanLevelCost + kPlanCandidateCost * k * ratio / share;
+            if (c < cost[(size_t)j]) {
+                cost[(size_t)j] = c;
+                prev[(size_t)j] = i;
+            }
+        }
+    }
+    std::vector<int> chain;
+    for (int j = L - 1; j != i0; j = prev[(size_t)j]) chain.push_back(j);
     int cur = i0;
-    while (cur != L - 1) {
-        int nxt = cur + 1;
-        for (int j = cur + 1; j < L; j++)
-            if ((double)sizes[j] <= (double)sizes[cur] * rmax) nxt = j;
-        double ratio = (double)sizes[nxt] / (double)std::max<int64_t>(sizes[cur], 1);
+    for (auto it = chain.rbegin(); it != chain.rend(); ++it) {
+        const int nxt = *it;
+        const double ratio = (double)sizes[nxt] / (double)std::max<int64_t>(sizes[cur], 1);
         int cap = next_pow2((int64_t)(3.0 * k * ratio) + 256);
         cap = std::max(4096, std::min(kCapMax, cap));
         if (nxt == L - 1 && sizes[nxt] <= kCapMax) cap = std::max(cap, next_pow2(std::max<int64_t>(sizes[nxt], k)));
@@ -125,6 +160,9 @@ std::vector<LevelStep> plan_levels(const Shard& sh, int k) {
 
 void grow(void** p, size_t* have, size_t need) {
     if (need <= *have) return;
+    int want_fault = kFaultOom;
+    if (g_fault.load() == kFaultOom && g_fault.compare_exchange_strong(want_fault, kFaultNone))
+        throw Error(MDH_ERR_OOM, "device scratch allocation failed: injected out-of-memory (mdh_set_fault)");
     if (*p) cudaFree(*p);
     *p = nullptr;
     *have = 0;
@@ -385,16 +423,10 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
             launch_gather_queries_u8(w.q_u8, w.qn, d_list, m, ix->dpad, cq_u8, cqn, st);
             res.launches++;
         } else {
-            // Host copy of the flagged float queries: [m][dim] then [m] aux.
-            std::vector<float> hq((size_t)m * ix->dim + (size_t)m);
-            for (int i = 0; i < m; i++) {
-                std::memcpy(&hq[(size_t)i * ix->dim], host_q_f32 + (size_t)list[(size_t)i] * ix->dim,
-                            (size_t)ix->dim * 4);
-                hq[(size_t)m * ix->dim + i] = host_q_f32[(size_t)nq * ix->dim + list[(size_t)i]];
-            }
+            // The flagged float queries, gathered from the staged batch: [m][dim] then [m] aux.
             cq_f32 = static_cast<float*>(tmpbuf);
-            MDH_CUDA(cudaMemcpyAsync(cq_f32, hq.data(), hq.size() * 4, cudaMemcpyHostToDevice, st));
-            MDH_CUDA(cudaStreamSynchronize(st));
+            launch_gather_queries_f32(w.q_f32, nq, ix->dim, d_list, m, cq_f32, st);
+            res.launches++;
         }
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
         count_tc(lv, run_filter(ix, sh, lv, qp, cq_u8, cqn, cq_f32, m, d_tk, d_ti, last.cap, false, nullptr, true), m);
@@ -586,7 +618,7 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
                 }
                 qsrc = qbuf_u8.data();
             }
-        } else {
+        } else if (qp.kind != kScoreSpeedCos) {
             prepare_float_queries(ix, qp, host_f32 + (size_t)c0 * dim, m, mode, qbuf_f32);
         }
         const auto t_staged = std::chrono::high_resolution_clock::now();  // host part of the query staging
@@ -598,6 +630,10 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
         auto run = [&](int si) {
             try {
                 Shard& sh = ix->shards[(size_t)si];
+                int want_fault = kFaultShard;
+                if (g_fault.load() == kFaultShard && g_fault.compare_exchange_strong(want_fault, kFaultNone))
+                    throw Error(MDH_ERR_INTERNAL, "shard " + std::to_string(si) +
+                                                      " search failed: injected fault (mdh_set_fault)");
                 MDH_CUDA(cudaSetDevice(sh.device));
                 Workspace& w = sh.ws;
                 ensure_status(w);
@@ -608,14 +644,24 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
                     MDH_CUDA(cudaMemcpyAsync(w.q_u8, qsrc, (size_t)m * dpad, cudaMemcpyHostToDevice, sh.stream));
                     launch_query_norms_u8(w.q_u8, m, dpad, w.qn, sh.stream);
                     st_launch[(size_t)si] = 1;
+                } else if (qp.kind == kScoreSpeedCos) {
+                    // Raw rows up, normalized on the device in the reference's
+                    // order (no aux term for this score).
+                    growT(&w.q_f32, &w.q_f32_bytes, ((size_t)m * dim + m) * 4);
+                    MDH_CUDA(cudaMemcpyAsync(w.q_f32, host_f32 + (size_t)c0 * dim, (size_t)m * dim * 4,
+                                             cudaMemcpyHostToDevice, sh.stream));
+                    MDH_CUDA(cudaMemsetAsync(w.q_f32 + (size_t)m * dim, 0, (size_t)m * 4, sh.stream));
+                    uint16_t* qb = nullptr;
+                    if (ix->dim % 8 == 0) {
+                        growT(&w.q_bf16, &w.q_bf16_bytes, (size_t)m * dim * 2);
+                        qb = w.q_bf16;
+                    }
+                    launch_normalize_speed_cos(w.q_f32, m, dim, mode == MDH_SCORE_SPEED_BATCH ? 1 : 0, qb, sh.stream);
+                    st_launch[(size_t)si] = 1;
                 } else {
                     growT(&w.q_f32, &w.q_f32_bytes, qbuf_f32.size() * 4);
                     MDH_CUDA(cudaMemcpyAsync(w.q_f32, qbuf_f32.data(), qbuf_f32.size() * 4, cudaMemcpyHostToDevice,
                                              sh.stream));
-                    if (qp.kind == kScoreSpeedCos && ix->dim % 8 == 0) {
-                        growT(&w.q_bf16, &w.q_bf16_bytes, (size_t)m * dim * 2);
-                        launch_convert_bf16(w.q_f32, (int64_t)m * dim, w.q_bf16, sh.stream);
-                    }
                 }
                 sres[(size_t)si] = search_shard(ix, sh, qp, m, kk, qsrc, qbuf_f32.data(), (size_t)dim);
                 st_prep[(size_t)si] = event_ms(w.ev_prep, w.ev_start);
@@ -1037,6 +1083,51 @@ mdh_status mdh_set_verify(int32_t max_queries) {
     return guard([&] {
         MDH_REQUIRE(max_queries >= 0 && max_queries <= 65536, MDH_ERR_INVALID_ARG, "max_queries must be in [0, 65536]");
         g_verify = max_queries;
+    });
+}
+
+mdh_status mdh_set_fault(int32_t site) {
+    return guard([&] {
+        MDH_REQUIRE(site >= kFaultNone && site <= kFaultShard, MDH_ERR_INVALID_ARG, "site must be 0, 1 or 2");
+        g_fault.store(site);
+    });
+}
+
+mdh_status mdh_check_wait_timeout(int32_t device, int64_t budget_cycles) {
+    return guard([&] {
+        MDH_REQUIRE(budget_cycles >= 1000 && budget_cycles <= (int64_t)1 << 32, MDH_ERR_INVALID_ARG,
+                    "budget_cycles must be in [1000, 2^32]");
+        int dev = device;
+        if (dev < 0) MDH_CUDA(cudaGetDevice(&dev));
+        check_device_usable(dev);
+        MDH_CUDA(cudaSetDevice(dev));
+        int32_t* d = nullptr;
+        MDH_CUDA(cudaMalloc(&d, 2 * sizeof(int32_t)));
+        int32_t h[2] = {-1, -1};
+        cudaError_t e = cudaMemset(d, 0, 2 * sizeof(int32_t));
+        if (e == cudaSuccess) {
+            try {
+                launch_wait_timeout_probe((long long)budget_cycles, d, nullptr);
+            } catch (...) {
+                cudaFree(d);
+                throw;
+            }
+            e = cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost);
+        }
+        cudaFree(d);
+        MDH_CUDA(e);
+        MDH_REQUIRE(h[1] == 0, MDH_ERR_INTERNAL, "the probe's barrier completed: nothing should arrive on it");
+        if (h[0] == kDevTimeout)
+            throw Error(MDH_ERR_TIMEOUT, "bounded device wait gave up after " + std::to_string(budget_cycles) +
+                                             " cycles (expected: nothing arrives on the probe's barrier)");
+        throw Error(MDH_ERR_INTERNAL, "bounded device wait returned without recording a timeout");
+    });
+}
+
+mdh_status mdh_set_threshold_sharing(int32_t ranks) {
+    return guard([&] {
+        MDH_REQUIRE(ranks >= 1 && ranks <= 4096, MDH_ERR_INVALID_ARG, "ranks must be in [1, 4096]");
+        g_threshold_sharing = ranks;
     });
 }
 

@@ -149,18 +149,18 @@ T* dalloc(size_t count) {
 
 int g_sample_top_ratio = kSampleTopRatioDefault;
 
-// Nested sample sizes for a shard of n rows: 1024 * 32^j while the sample
-// stays <= n / R (R = g_sample_top_ratio), then n / R itself when that ladder
-// stops more than 4x below it.  The largest sample sets the full level's
-// threshold: about k * n / (its size) rows of the shard pass it, so its size
-// tracks the shard (a fixed size would cost a fixed scan per rank however
-// many ranks share the corpus).  Shards under 8,192 rows get no sample.
+// Nested sample sizes for a shard of n rows: 1024 * 4^j up to n / R
+// (R = g_sample_top_ratio, 8 by default).  A search picks its chain of levels
+// from this ladder by cost (capi.cu, plan_levels): the best largest sample
+// is about sqrt(4,500 k n) rows (scan cost against candidate cost), which the
+// ladder brackets within a factor of 2 for every k up to 128 and n above
+// ~1M.  The samples hold at most n/6 rows (0.056 n at 100M rows).  Shards
+// under 8,192 rows get no sample.
 std::vector<int64_t> plan_samples(int64_t n) {
     std::vector<int64_t> s;
     if (n < 8 * 1024) return s;
     const int64_t top = std::max<int64_t>(1024, n / std::max(2, g_sample_top_ratio));
-    for (int64_t m = 1024; m <= top; m *= 32) s.push_back(m);
-    if (top > 4 * s.back()) s.push_back(top);
+    for (int64_t m = 1024; m <= top; m *= 4) s.push_back(m);
     return s;
 }
 

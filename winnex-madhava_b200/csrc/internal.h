@@ -85,7 +85,7 @@ namespace mdh {
 // ---- index build (index.cu) ----
 // Largest sample of a shard of n rows is about n / g_sample_top_ratio rows
 // (process-wide; read when samples are built: index create and load).
-constexpr int kSampleTopRatioDefault = 64;
+constexpr int kSampleTopRatioDefault = 8;
 extern int g_sample_top_ratio;
 std::vector<int64_t> plan_samples(int64_t n);   // nested sample sizes, ascending
 void build_shard_u8(mdh_index* ix, Shard& sh, const uint8_t* host_rows, int64_t n);
@@ -146,6 +146,9 @@ void encode_u8_rows_tmap(CUtensorMap* map, const void* base, int64_t rows, int d
 int choose_scan_chunks(int groups, int n_tiles, int workers);
 bool tc_supported(const mdh_index* ix, const Level& lv);
 void make_tmap_rows(Level& lv, int dpad);
+// One CTA runs the scans' bounded mbarrier wait on a barrier that never
+// completes, with `budget` cycles: status[0] gets kDevTimeout when it gives up.
+void launch_wait_timeout_probe(long long budget, int32_t* status, cudaStream_t st);
 // block_stats (may be null): [0] += bound tests counted by the kernel (unit
 // tables only; the schedule form tests every (query, 64-row block)), [1] +=
 // tests the bound did not settle, [2] += real rows of those blocks (pairs whose
@@ -196,6 +199,10 @@ void launch_convert_bf16(const float* src, int64_t count, uint16_t* dst, cudaStr
 void launch_filter_tc_bf16_cos(const Level& lv, int dim, const uint16_t* q_bf16, int nq, const uint32_t* thr_key,
                                uint32_t* counts, uint2* cand, int cap, int dense, float eps, int32_t* status,
                                cudaStream_t st);
+// SpeedEngine cosine query normalization in place ([nq][dim] fp32, the
+// reference's arithmetic; batch_guard: search_batch's |q|^2 > 1e-12 test),
+// plus the bf16 copy when q_bf16 is not null.
+void launch_normalize_speed_cos(float* q, int nq, int dim, int batch_guard, uint16_t* q_bf16, cudaStream_t st);
 void launch_rescore_speed_cos(const uint32_t* counts, uint2* cand, int cap, const float* rows_f32, int dim,
                               const float* q_f32, int nq, cudaStream_t st);
 
@@ -221,6 +228,9 @@ void launch_verify_thresholds(const int32_t* list, int m, const uint32_t* out_ke
 void launch_count_violations(const uint32_t* counts, int m, int kk, unsigned long long* violations, cudaStream_t st);
 void launch_merge_topk(const uint32_t* key_all, const int32_t* id_all, int nshard, int nq, int k,
                        uint32_t* key_out, int32_t* id_out, cudaStream_t st);
+// Float query rows [nq][dim] + [nq] aux -> the listed m rows, same layout.
+void launch_gather_queries_f32(const float* src, int nq, int dim, const int32_t* list, int m, float* dst,
+                               cudaStream_t st);
 void launch_gather_queries_u8(const uint8_t* src, const int32_t* qn_src, const int32_t* list, int m,
                               int dpad, uint8_t* dst, int32_t* qn_dst, cudaStream_t st);
 

@@ -64,10 +64,6 @@ namespace {
 
 using namespace tc;
 
-#ifndef MDH_EPI_V2
-#define MDH_EPI_V2 0
-#endif
-
 constexpr int BM = 128;           // queries per query tile (TMEM lanes)
 constexpr int BK = 128;           // bytes per row (K)
 constexpr int BOX_ROWS = 128;     // corpus rows per TMA box (BN / BOX_ROWS boxes per stage)
@@ -506,14 +502,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tc_fence_after();
                 uint32_t v[2][32];
                 __syncwarp();
-#if MDH_EPI_V2
-                tmem_ld64(tcol0 + A * C::ACC_COLS, v[0], v[1]);
-#else
-                tmem_ld32_issue(tcol0 + A * C::ACC_COLS, v[0]);
-                tmem_ld32_issue(tcol0 + A * C::ACC_COLS + 32, v[1]);
-                tmem_ld_wait(v[0]);  // waits for both loads
-                tmem_ld_wait(v[1]);
-#endif
+                tmem_ld64(tcol0 + A * C::ACC_COLS, v[0], v[1]);  // one load and one wait for both chunks
                 // The chunks are in registers: hand the accumulator back to the MMA.
                 tc_fence_before();
                 __syncwarp();
@@ -521,11 +510,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 const int32_t m = (int32_t)__float_as_uint(
                     fmaxf(__uint_as_float((uint32_t)max32(v[0])), __uint_as_float((uint32_t)max32(v[1]))));
                 const bool pass = 2 * m >= need;
-#if MDH_EPI_V2
                 // One vote settles the tile for the whole warp (the usual case);
                 // the buffer can only have grown when some lane passed.
                 if (!__any_sync(0xffffffffu, pass)) return true;
-#endif
                 if (pass) {
                     const int32_t row0 = t * BN + rowoff;  // rows < 2^31 (ids are int32)
                     if (block_stats) {
@@ -707,7 +694,30 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     return fn;
 }
 
+// The scans' bounded wait (mbar_wait) on a barrier nothing arrives on: it
+// gives up after `budget` cycles, raises the abort flag and records
+// kDevTimeout in status[0]; status[1] = 1 if the wait returned "ready".
+__global__ void k_wait_timeout_probe(long long budget, int32_t* __restrict__ status) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int32_t abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const bool ok = mbar_wait<false>(smem_u32(&bar), 0, &abort_flag, status, budget);
+        status[1] = ok ? 1 : 0;
+    }
+}
+
 }  // namespace
+
+void launch_wait_timeout_probe(long long budget, int32_t* status, cudaStream_t st) {
+    k_wait_timeout_probe<<<1, 32, 0, st>>>(budget, status);
+    MDH_CUDA(cudaGetLastError());
+}
 
 void encode_tmap_2d_sw128(CUtensorMap* map, int bf16, const void* base, uint64_t inner, uint64_t rows,
                          uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {

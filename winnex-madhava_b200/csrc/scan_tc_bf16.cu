@@ -395,6 +395,47 @@ void launch_filter_tc_bf16_cos(const Level& lv, int dim, const uint16_t* q_bf16,
     MDH_CUDA(cudaGetLastError());
 }
 
+namespace {
+
+// SpeedEngine query normalization (src/speed_cpu.cpp:278-287 single query,
+// :365-372 batch) on the device, in the reference's fp32 order: |q|^2 by a
+// sequential FMA chain, then the scale 1/sqrt, then one multiply per element.
+// One warp per query: lane 0 runs the chain, the warp scales and writes the
+// fp32 row in place and its bf16 copy (bf16 may be null).
+__global__ void k_normalize_speed_cos(float* __restrict__ q, int nq, int dim, int batch_guard,
+                                      __nv_bfloat16* __restrict__ q_bf16) {
+    const int qi = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (qi >= nq) return;
+    float* row = q + (size_t)qi * dim;
+    float inv = 0.0f;
+    if (lane == 0) {
+        float qn = 0.0f;
+        for (int j = 0; j < dim; j++) qn = __fmaf_rn(row[j], row[j], qn);
+        if (batch_guard) {
+            inv = qn > 1e-12f ? __fdiv_rn(1.0f, __fsqrt_rn(qn)) : 0.0f;
+        } else {
+            const float s = __fsqrt_rn(qn);
+            inv = s > 1e-12f ? __fdiv_rn(1.0f, s) : 0.0f;
+        }
+    }
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    for (int j = lane; j < dim; j += 32) {
+        const float x = __fmul_rn(row[j], inv);
+        row[j] = x;
+        if (q_bf16) q_bf16[(size_t)qi * dim + j] = __float2bfloat16_rn(x);
+    }
+}
+
+}  // namespace
+
+void launch_normalize_speed_cos(float* q, int nq, int dim, int batch_guard, uint16_t* q_bf16, cudaStream_t st) {
+    if (nq <= 0) return;
+    k_normalize_speed_cos<<<(nq + 7) / 8, 256, 0, st>>>(q, nq, dim, batch_guard,
+                                                        reinterpret_cast<__nv_bfloat16*>(q_bf16));
+    MDH_CUDA(cudaGetLastError());
+}
+
 void launch_rescore_speed_cos(const uint32_t* counts, uint2* cand, int cap, const float* rows_f32, int dim,
                               const float* q_f32, int nq, cudaStream_t st) {
     if (nq <= 0) return;

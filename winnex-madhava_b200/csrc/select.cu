@@ -615,6 +615,33 @@ void launch_merge_topk(const uint32_t* key_all, const int32_t* id_all, int nshar
     MDH_CUDA(cudaGetLastError());
 }
 
+namespace {
+
+// Float query rows of a compact list: src [nq][dim] then [nq] aux, dst
+// [m][dim] then [m] aux; one thread per element.
+__global__ void k_gather_queries_f32(const float* __restrict__ src, int nq, int dim, const int32_t* __restrict__ list,
+                                     int m, float* __restrict__ dst) {
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t per = (int64_t)dim + 1;
+    if (t >= (int64_t)m * per) return;
+    const int i = (int)(t / per), j = (int)(t - (int64_t)i * per);
+    const int s = list[i];
+    if (j < dim)
+        dst[(size_t)i * dim + j] = src[(size_t)s * dim + j];
+    else
+        dst[(size_t)m * dim + i] = src[(size_t)nq * dim + s];
+}
+
+}  // namespace
+
+void launch_gather_queries_f32(const float* src, int nq, int dim, const int32_t* list, int m, float* dst,
+                               cudaStream_t st) {
+    if (m <= 0) return;
+    const int64_t total = (int64_t)m * (dim + 1);
+    k_gather_queries_f32<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, nq, dim, list, m, dst);
+    MDH_CUDA(cudaGetLastError());
+}
+
 void launch_gather_queries_u8(const uint8_t* src, const int32_t* qn_src, const int32_t* list, int m, int dpad,
                               uint8_t* dst, int32_t* qn_dst, cudaStream_t st) {
     if (m <= 0) return;

@@ -68,13 +68,14 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
 // Bounded wait; false when the CTA is aborting (this wait timed out, or
 // another role's did).  On expiry the status word records kDevTimeout.
 template <bool CLUSTER>
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int32_t* abort_flag, int32_t* status) {
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int32_t* abort_flag, int32_t* status,
+                                       long long budget = kWaitBudget) {
     if (mbar_try_wait<CLUSTER>(bar, parity)) return true;
     const long long t0 = clock64();
     for (;;) {
         if (mbar_try_wait<CLUSTER>(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (clock64() - t0 > kWaitBudget) {
+        if (clock64() - t0 > budget) {
             *abort_flag = 1;
             atomicExch(status, (int32_t)kDevTimeout);
             return false;
