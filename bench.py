@@ -107,6 +107,8 @@ def load_lib():
     L.mdh_ivf_create_u8.argtypes = [P, i64, i32, P, i32, P, i32, ctypes.POINTER(P)]
     L.mdh_ivf_search_u8.argtypes = [P, P, i32, i32, i32, P, P, ctypes.POINTER(Stats)]
     L.mdh_ivf_destroy.argtypes = [P]
+    L.mdh_ivf_route_u8.argtypes = [P, P, i32, i32, P]
+    L.mdh_ivf_info.argtypes = [P, P, P, P, P]
     L.mdh_index_save.argtypes = [P, ctypes.c_char_p]
     L.mdh_index_load.argtypes = [ctypes.c_char_p, P, i32, ctypes.POINTER(P)]
     L.mdh_index_create_f32.argtypes = [P, i64, i32, i32, P, i32, i64, ctypes.POINTER(P)]
@@ -299,6 +301,16 @@ def run_ivf(args, torch, device, L, warmup):
                              None, None), "flat search")
     check(L, L.mdh_index_destroy(flat), "flat destroy")
     recall = float(np.mean([len(set(ids[i]) & set(fids[i])) / k for i in range(m)]))
+    # Bytes pass 2 must stream: each unit (one cell, up to 128 of the queries
+    # probing it) reads the cell's padded rows once.
+    cells = np.empty((nq, IVF_NPROBE), np.int32)
+    check(L, L.mdh_ivf_route_u8(h, ctypes.c_void_p(queries.ctypes.data), nq, IVF_NPROBE,
+                                ctypes.c_void_p(cells.ctypes.data)), "ivf route")
+    cell_rows = np.empty(IVF_NLIST, np.int64)
+    check(L, L.mdh_ivf_info(h, None, None, None, ctypes.c_void_p(cell_rows.ctypes.data)), "ivf info")
+    q_per_cell = np.bincount(cells.ravel(), minlength=IVF_NLIST)
+    unit_rows = int(np.sum(-(-q_per_cell // 128) * (-(-cell_rows // 256)) * 256))
+    pass2_bytes = unit_rows * DIM
     check(L, L.mdh_ivf_destroy(h), "ivf destroy")
     peaks, peak_src = measured_peaks()
     int8_peak = 2.0 * peaks["bf16_tflops"]
@@ -321,13 +333,25 @@ def run_ivf(args, torch, device, L, warmup):
         "e2e": {"value": qps, "unit": "queries/sec", "h2d_bytes_per_step": int(nq * DIM),
                 "d2h_bytes_per_step": int(nq * k * 8)},
         "gpu_launches": launches,
+        "stages_ms": {"route_and_plan": round(st.prep_ms, 3), "passes_0_1": round(st.sample_ms, 3),
+                      "pass_2_scan_and_rekey": round(st.full_scan_ms, 3), "select": round(st.select_ms, 3),
+                      "call_wall": round(st.latency_ms, 3),
+                      "note": "last timed step; CUDA events per stage inside the library; route_and_plan includes "
+                              "the query upload"},
         "block_bound": ivf_block,
         "clocks": clocks,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",
                      "frac": (achieved / int8_peak) if achieved else None, "traffic": None,
-                     "kernel": "pass-2 scan over the probed cells (k_filter_tc_u8_l2, unit table)",
+                     "kernel": "pass-2 scan over the probed cells (k_filter_tc_u8_l2, unit table) and its "
+                               "re-key pass (k_rekey_chunks)",
                      "algorithmic": "2 * (query, row) pairs of the probed cells * D",
-                     "peak_source": f"2 x {peak_src} bf16 dense ({peaks['bf16_tflops']} TF/s)", "kernel_ms": ms},
+                     "peak_source": f"2 x {peak_src} bf16 dense ({peaks['bf16_tflops']} TF/s)", "kernel_ms": ms,
+                     "hbm": {"achieved": pass2_bytes / (ms / 1e3) / 1e9 if ms > 0 else None,
+                             "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                             "frac": (pass2_bytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]) if ms > 0 else None,
+                             "bytes_per_launch": pass2_bytes,
+                             "algorithmic": "sum over units of the cell's padded rows x 128 B (each unit streams "
+                                            "its cell once)"}},
     }
     emit(line)
 

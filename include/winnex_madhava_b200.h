@@ -186,6 +186,46 @@ mdh_status mdh_search_f32(mdh_index* index, const float* host_queries, int32_t n
 mdh_status mdh_search_u8(mdh_index* index, const uint8_t* host_queries, int32_t nq, int32_t k,
                          int32_t* out_ids, int32_t* out_dist, mdh_stats* stats);
 
+/* Audited search: replaces MadhavaL2::search_audited / audit_json /
+ * search_with_commitment (src/winnex_madhava.cpp:1258-1591,
+ * include/winnex_madhava/winnex_madhava.hpp:172-234).  The reference
+ * certifies its Stage-1 projection bound; this engine is exact, so the audit
+ * certifies the exact top k against a second GPU pass over every row with
+ * the final threshold.  Per query:
+ *   threshold          the k-th result's distance (L2) or score (cosine);
+ *   within             rows whose (exact) key is at or within the threshold:
+ *                      the k results and rows tied with the k-th;
+ *   excluded           rows - within: rows strictly worse than the k-th
+ *                      result, i.e. provably outside the top k (the
+ *                      reference's audit_excluded / total_excluded_count);
+ *   excluded_by_bound  of those, the rows the 64-row block bound of the
+ *                      tensor-core scan settled without a key (-1 when the
+ *                      scan path has no block bound);
+ *   violations         max(0, k - within): 0 for a correct result;
+ *   n_records          the excluded rows nearest the threshold written to
+ *                      rec_ids / rec values (ascending key, then id; at most
+ *                      max_records), the deterministic sample of the
+ *                      commitment; fewer only when more than 2^18 rows tie
+ *                      with the k-th result.
+ * Queries run one at a time.  mdh_audit_f32 ranks by MDH_SCORE_EXACT. */
+typedef struct mdh_audit {
+    int64_t rows;
+    int64_t within;
+    int64_t excluded;
+    int64_t excluded_by_bound;
+    int64_t violations;
+    double threshold;
+    int32_t n_records;
+    int32_t reserved;
+} mdh_audit;
+
+mdh_status mdh_audit_f32(mdh_index* index, const float* host_queries, int32_t nq, int32_t k, int32_t max_records,
+                         int32_t* out_ids, float* out_values, int32_t* rec_ids, float* rec_values,
+                         mdh_audit* audit, mdh_stats* stats);
+mdh_status mdh_audit_u8(mdh_index* index, const uint8_t* host_queries, int32_t nq, int32_t k, int32_t max_records,
+                        int32_t* out_ids, int32_t* out_dist, int32_t* rec_ids, int32_t* rec_dist,
+                        mdh_audit* audit, mdh_stats* stats);
+
 /* Device-resident variant of mdh_search_u8 for a single-device index:
  * queries, ids and distances are device pointers on the index's device;
  * work is enqueued on `stream` (a cudaStream_t, NULL = the index's stream)
@@ -300,7 +340,10 @@ mdh_status mdh_set_candidate_cap_limit(int32_t cap);
  * mdh_set_fault(site): a one-shot host-side fault for tests.  site 1: the
  * next growth of a search workspace fails as out of memory (MDH_ERR_OOM);
  * site 2: the next shard search thread fails before it scans
- * (MDH_ERR_INTERNAL).  0 clears it.  The index stays usable afterwards.
+ * (MDH_ERR_INTERNAL); site 3: the next IVF search gets a one-block chunk
+ * buffer, so its deferred scans overflow it and pass 2 reruns with keys
+ * formed in the scan (the results stay exact).  0 clears it.  The index
+ * stays usable afterwards.
  * mdh_check_wait_timeout(device, budget_cycles): runs the scans' bounded
  * mbarrier wait on a barrier that nothing arrives on, with a budget of
  * budget_cycles (1,000 .. 2^32 clock cycles; the scans use ~4e9): it must

@@ -37,6 +37,12 @@ class Stats(ctypes.Structure):
                 ("prep_ms", ctypes.c_double), ("blocks_tested", ctypes.c_int64), ("blocks_passed", ctypes.c_int64)]
 
 
+class Audit(ctypes.Structure):
+    _fields_ = [("rows", ctypes.c_int64), ("within", ctypes.c_int64), ("excluded", ctypes.c_int64),
+                ("excluded_by_bound", ctypes.c_int64), ("violations", ctypes.c_int64), ("threshold", ctypes.c_double),
+                ("n_records", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
 def capi():
     L = ctypes.CDLL(LIB)
     P, i32, i64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
@@ -47,6 +53,8 @@ def capi():
     L.mdh_index_info.argtypes = [P, P, P, P, P]
     L.mdh_search_f32.argtypes = [P, P, i32, i32, i32, P, P, ctypes.POINTER(Stats)]
     L.mdh_search_u8.argtypes = [P, P, i32, i32, P, P, ctypes.POINTER(Stats)]
+    L.mdh_audit_f32.argtypes = [P, P, i32, i32, i32, P, P, P, P, P, ctypes.POINTER(Stats)]
+    L.mdh_audit_u8.argtypes = [P, P, i32, i32, i32, P, P, P, P, P, ctypes.POINTER(Stats)]
     L.mdh_search_u8_device.argtypes = [P, P, i32, i32, P, P, P, ctypes.POINTER(Stats)]
     L.mdh_search_u8_device_noalloc.argtypes = [P, P, i32, i32, P, P, P, ctypes.POINTER(Stats)]
     L.mdh_search_u8_device_sample.argtypes = [P, P, i32, i32, P, P, P, ctypes.POINTER(Stats)]

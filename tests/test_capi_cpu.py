@@ -40,6 +40,8 @@ def test_argument_validation_before_device_use():
     assert L.mdh_set_candidate_cap_limit(100) == 1
     assert L.mdh_set_candidate_cap_limit(0) == 0
     assert L.mdh_search_f32(None, None, 1, 10, 0, None, None, None) == 1
+    assert L.mdh_audit_u8(None, None, 1, 10, 5, None, None, None, None, None, None) == 1
+    assert L.mdh_audit_f32(None, None, 1, 0, 5, None, None, None, None, None, None) == 1
 
 
 def test_no_cpu_fallback_without_gpu():
@@ -61,39 +63,43 @@ def test_header_is_plain_c():
         assert banned not in src
 
 
-def test_stats_struct_matches_header(tmp_path):
-    """The ctypes mirror of mdh_stats (tests, bench.py) has the header's size and field offsets."""
+@pytest.mark.parametrize("struct", ["mdh_stats", "mdh_audit"])
+def test_structs_match_header(tmp_path, struct):
+    """The ctypes mirrors of mdh_stats and mdh_audit (tests, bench.py) have the
+    header's sizes and field offsets."""
     import shutil
     import subprocess
 
-    from helpers import Stats
+    from helpers import Audit, Stats
 
     if shutil.which("gcc") is None:
         pytest.skip("no C compiler")
+    mirror = {"mdh_stats": Stats, "mdh_audit": Audit}[struct]
     src = tmp_path / "s.c"
-    names = [f[0] for f in Stats._fields_]
-    body = "".join(f'printf("%zu ", offsetof(mdh_stats, {n}));' for n in names)
+    names = [f[0] for f in mirror._fields_]
+    body = "".join(f'printf("%zu ", offsetof({struct}, {n}));' for n in names)
     src.write_text('#include <stddef.h>\n#include <stdio.h>\n#include "winnex_madhava_b200.h"\n'
-                   f'int main(void) {{ {body} printf("%zu\\n", sizeof(mdh_stats)); return 0; }}\n')
+                   f'int main(void) {{ {body} printf("%zu\\n", sizeof({struct})); return 0; }}\n')
     exe = tmp_path / "s"
     subprocess.run(["gcc", "-I", HEADER.rsplit("/", 1)[0], str(src), "-o", str(exe)], check=True)
     got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
-    want = [getattr(Stats, n).offset for n in names] + [ctypes.sizeof(Stats)]
+    want = [getattr(mirror, n).offset for n in names] + [ctypes.sizeof(mirror)]
     assert got == want
 
 
 def test_sample_plan_follows_the_cost_model():
-    """Sample ladders of 1024 * 4^j rows up to shard / 8; a search scans the
-    cheapest chain of them under the cost model (largest sample near
-    sqrt(4,500 k n)): longer chains for larger shards and larger k, a single
-    dense level for a tiny shard, and shorter chains when ranks share their
-    sample thresholds."""
+    """Sample ladders of 1024 * 4^j rows up to shard / 8 (plus a 16,384-row
+    level when the ladder stops short of it); a search scans the cheapest
+    chain of them under the cost model (largest sample near sqrt(4,500 k n)):
+    longer chains for larger shards and larger k, a single dense level for a
+    tiny shard, and shorter chains when ranks share their sample thresholds."""
     L = capi()
     assert L.mdh_plan_level_count(100_000_000, 10) == 6
     assert L.mdh_plan_level_count(100_000_000, 100) == 8
     assert L.mdh_plan_level_count(12_500_000, 10) == 6
     assert L.mdh_plan_level_count(1_000_000, 10) == 5
-    assert L.mdh_plan_level_count(100_000, 10) == 3
+    assert L.mdh_plan_level_count(100_000, 10) == 4         # 1,024 -> 4,096 -> 16,384 -> 100,000
+    assert L.mdh_plan_level_count(20_000, 3_020) == 2       # a first level of >= k rows exists
     assert L.mdh_plan_level_count(5_000, 10) == 1          # dense scan of the shard
     assert L.mdh_plan_level_count(0, 10) == 0
     assert L.mdh_set_threshold_sharing(8) == 0
@@ -104,7 +110,7 @@ def test_sample_plan_follows_the_cost_model():
         assert L.mdh_set_threshold_sharing(1) == 0
     assert L.mdh_set_sample_ratio(64) == 0
     try:
-        assert L.mdh_plan_level_count(1_000_000, 10) == 3   # a shorter ladder (top <= n / 64)
+        assert L.mdh_plan_level_count(12_500_000, 10) == 5  # a shorter ladder (top <= n / 64)
     finally:
         assert L.mdh_set_sample_ratio(0) == 0
     assert L.mdh_set_sample_ratio(1) == 1

@@ -93,7 +93,11 @@ def test_bound_engine_only_features_raise():
     assert e.save_index("/nonexistent-dir/x.idx") is False
     assert e.load_index("/nonexistent-dir/x.idx") is False and e.built() is False
     with pytest.raises(NotImplementedError):
-        e.search_audited(np.zeros(128, np.float32))
+        e.basis1()
+    # An unbuilt engine audits nothing (src/winnex_madhava.cpp:1266).
+    r = e.search_audited(np.zeros(128, np.float32))
+    assert r["indices"] == [] and r["audit"] == [] and r["audit_excluded"] == 0
+    assert e.search_with_commitment(np.zeros(128, np.float32))["sampled_records"] == []
     # An unbuilt engine returns an empty result like the reference.
     assert e.search(np.zeros(128, np.float32)).indices == []
     with pytest.raises(RuntimeError, match="query must be float32 of length dim"):

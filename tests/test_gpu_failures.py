@@ -74,7 +74,8 @@ def test_injected_out_of_memory_then_recovery(data):
     np.testing.assert_array_equal(ids, want_i)
     np.testing.assert_array_equal(dist, want_d)
     assert L.mdh_index_destroy(h) == 0
-    assert L.mdh_set_fault(3) != 0
+    assert L.mdh_set_fault(4) != 0 and b"site" in L.mdh_last_error()
+    assert L.mdh_set_fault(0) == 0
 
 
 @pytest.mark.parametrize("devices", [None, [0, 0]])

@@ -88,6 +88,32 @@ def test_ivf_edge_cells_and_batches():
     assert L.mdh_ivf_destroy(h) == 0
 
 
+def test_ivf_chunk_buffer_overflow_reruns_exact():
+    """The passes write their unsettled (query, 32-row chunk) blocks to a
+    chunk buffer that a re-key kernel turns into candidates.  With a one-block
+    buffer (injected, mdh_set_fault(3)) every pass overflows it: passes 0 and
+    1 only get looser thresholds, and pass 2 reruns with keys formed in the
+    scan, so the results stay the oracle's."""
+    L = capi()
+    C = cases.gmm_u8(60_000, 128, 64, seed=77)
+    Q = cases.gmm_u8_queries(300, 128, 64, seed_means=77, seed_q=78)
+    rng = np.random.default_rng(79)
+    nlist = 24
+    cen = rng.uniform(0, 60, (nlist, 128)).astype(np.float32)
+    labels = rng.integers(0, nlist, len(C)).astype(np.int32)
+    h = _ivf(L, C, cen, labels)
+    want_ids, want_d = oracle.ivf_exact(C, labels, cen, Q, 10, 4)
+    for fault in (0, 3, 0):
+        assert L.mdh_set_fault(fault) == 0
+        ids, dist, s = _search(L, h, Q, 10, 4)
+        np.testing.assert_array_equal(ids, want_ids)
+        np.testing.assert_array_equal(dist[want_ids >= 0], want_d[want_ids >= 0])
+        # A rerun scans the probed cells a second time; the sample passes
+        # alone stay far below one scan of them.
+        assert (s.pairs_scored >= 2 * s.full_scan_pairs) == bool(fault)
+    assert L.mdh_ivf_destroy(h) == 0
+
+
 def test_ivf_all_keys_tied_large_k():
     """40,000 equal rows in one cell: the last pass's candidate lists hold
     ~2,000 entries with the same key, more than the large-k selection keeps in

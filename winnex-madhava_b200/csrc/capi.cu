@@ -34,9 +34,6 @@ thread_local std::string g_last_error;
 int g_scan_path = 0;  // 0 auto, 1 CUDA cores only, 2 tensor cores when possible
 int g_cap_limit = 0;  // 0 = default candidate capacities
 int g_verify = 0;     // queries per search re-checked by an exact unpruned scan (0 = off)
-// Fault injection (host side, one shot): the next workspace growth reports
-// OOM, or the next shard search thread fails before it scans.
-enum FaultSite : int { kFaultNone = 0, kFaultOom = 1, kFaultShard = 2 };
 std::atomic<int> g_fault{kFaultNone};
 
 constexpr int kCapMax = 16384;          // largest candidate list the selection kernel sorts
@@ -160,8 +157,7 @@ std::vector<LevelStep> plan_levels(const Shard& sh, int k) {
 
 void grow(void** p, size_t* have, size_t need) {
     if (need <= *have) return;
-    int want_fault = kFaultOom;
-    if (g_fault.load() == kFaultOom && g_fault.compare_exchange_strong(want_fault, kFaultNone))
+    if (take_fault(kFaultOom))
         throw Error(MDH_ERR_OOM, "device scratch allocation failed: injected out-of-memory (mdh_set_fault)");
     if (*p) cudaFree(*p);
     *p = nullptr;
@@ -557,14 +553,16 @@ bool all_integral_u8(const float* q, size_t count) {
 // Full search of a batch: chunk queries, run every shard, merge.
 // Exactly one of host_u8 / host_f32 is set.
 void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, int nq, int k, int mode,
-                 int32_t* out_ids, float* out_val_f, int32_t* out_val_i, mdh_stats* stats) {
+                 int32_t* out_ids, float* out_val_f, int32_t* out_val_i, mdh_stats* stats,
+                 uint32_t* out_keys = nullptr, bool locked = false) {
     auto t0 = std::chrono::high_resolution_clock::now();
     MDH_REQUIRE(ix, MDH_ERR_INVALID_ARG, "null index");
     MDH_REQUIRE(nq >= 0, MDH_ERR_INVALID_ARG, "nq must be >= 0");
     MDH_REQUIRE(k >= 0, MDH_ERR_INVALID_ARG, "k must be >= 0");
     MDH_REQUIRE(nq == 0 || host_u8 || host_f32, MDH_ERR_INVALID_ARG, "null queries");
     MDH_REQUIRE(nq == 0 || k == 0 || out_ids, MDH_ERR_INVALID_ARG, "null output ids");
-    std::lock_guard<std::mutex> lock(ix->mu);
+    std::unique_lock<std::mutex> lock(ix->mu, std::defer_lock);
+    if (!locked) lock.lock();
     mdh_stats st{};
     const int dim = ix->dim, dpad = ix->dpad;
     const int kk = (int)std::min<int64_t>(k, ix->n);
@@ -630,8 +628,7 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
         auto run = [&](int si) {
             try {
                 Shard& sh = ix->shards[(size_t)si];
-                int want_fault = kFaultShard;
-                if (g_fault.load() == kFaultShard && g_fault.compare_exchange_strong(want_fault, kFaultNone))
+                if (take_fault(kFaultShard))
                     throw Error(MDH_ERR_INTERNAL, "shard " + std::to_string(si) +
                                                       " search failed: injected fault (mdh_set_fault)");
                 MDH_CUDA(cudaSetDevice(sh.device));
@@ -741,6 +738,7 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
                 const size_t src = (size_t)i * kk + j, dst = (size_t)(c0 + i) * k + j;
                 const int32_t id = hid[src];
                 out_ids[dst] = id;
+                if (out_keys) out_keys[dst] = hkey[src];
                 if (id < 0) continue;
                 const uint32_t key = hkey[src];
                 if (out_val_i) out_val_i[dst] = qp.int_dist ? (int32_t)key : -1;
@@ -757,6 +755,161 @@ void search_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, i
     }
     st.latency_ms = std::chrono::duration<double, std::milli>(std::chrono::high_resolution_clock::now() - t0).count();
     if (stats) *stats = st;
+}
+
+// Audited search (MadhavaL2::search_audited / search_with_commitment,
+// src/winnex_madhava.cpp:1258-1591) on the exact engine, one query at a time:
+//   1. the exact top-(k + max_records): its first k are the result, its
+//      k-th key is the threshold T, and the rest are the excluded rows
+//      nearest the cut, in (key, id) order (the deterministic sample);
+//   2. the audit pass: every shard's whole level scanned once more with the
+//      threshold (T, any id) and no candidate storage, so the counters give
+//      the rows at or within T -- every other row is provably outside the
+//      top k -- and, on the tensor-core path, the real rows of the 64-row
+//      blocks whose bound could not settle them; the rest were excluded by
+//      the block bound alone.
+constexpr int64_t kAuditRecordSearchMax = int64_t(1) << 18;
+
+void audit_impl(mdh_index* ix, const uint8_t* host_u8, const float* host_f32, int nq, int k, int max_records,
+                int32_t* out_ids, float* out_val_f, int32_t* out_val_i, int32_t* rec_ids, float* rec_val_f,
+                int32_t* rec_val_i, mdh_audit* audit, mdh_stats* stats) {
+    auto t0 = std::chrono::high_resolution_clock::now();
+    MDH_REQUIRE(ix, MDH_ERR_INVALID_ARG, "null index");
+    MDH_REQUIRE(nq >= 0 && k >= 1 && max_records >= 0, MDH_ERR_INVALID_ARG,
+                "nq and max_records must be >= 0, k >= 1");
+    MDH_REQUIRE(nq == 0 || ((host_u8 || host_f32) && out_ids && audit), MDH_ERR_INVALID_ARG,
+                "null queries or outputs");
+    MDH_REQUIRE(nq == 0 || max_records == 0 || rec_ids, MDH_ERR_INVALID_ARG, "null record ids");
+    std::lock_guard<std::mutex> lock(ix->mu);
+    mdh_stats total{};
+    const int dim = ix->dim;
+    const int64_t n = ix->n;
+    const int kk = (int)std::min<int64_t>(k, n);
+    const int m = (int)std::max<int64_t>(0, std::min<int64_t>(max_records, n - kk));
+    const int k2 = kk + m;
+    std::vector<int32_t> ids2((size_t)std::max(k2, 1)), vi2((size_t)std::max(k2, 1));
+    std::vector<float> vf2((size_t)std::max(k2, 1));
+    std::vector<uint32_t> keys2((size_t)std::max(k2, 1));
+    for (int i = 0; i < nq; i++) {
+        mdh_audit& a = audit[i];
+        a = mdh_audit{};
+        a.rows = n;
+        for (int j = 0; j < k; j++) {
+            out_ids[(size_t)i * k + j] = -1;
+            if (out_val_f) out_val_f[(size_t)i * k + j] = NAN;
+            if (out_val_i) out_val_i[(size_t)i * k + j] = -1;
+        }
+        for (int j = 0; j < max_records; j++) {
+            rec_ids[(size_t)i * max_records + j] = -1;
+            if (rec_val_f) rec_val_f[(size_t)i * max_records + j] = NAN;
+            if (rec_val_i) rec_val_i[(size_t)i * max_records + j] = -1;
+        }
+        if (kk == 0) continue;
+        const uint8_t* qu = host_u8 ? host_u8 + (size_t)i * dim : nullptr;
+        const float* qf = host_f32 ? host_f32 + (size_t)i * dim : nullptr;
+        mdh_stats st{};
+        search_impl(ix, qu, qf, 1, k2, MDH_SCORE_EXACT, ids2.data(), vf2.data(), vi2.data(), &st, keys2.data(), true);
+        total.pairs_scored += st.pairs_scored;
+        total.pairs_pruned_by_bound += st.pairs_pruned_by_bound;
+        total.full_scan_pairs += st.full_scan_pairs;
+        total.kernel_launches += st.kernel_launches;
+        total.candidates += st.candidates;
+        total.blocks_tested += st.blocks_tested;
+        total.blocks_passed += st.blocks_passed;
+        total.full_scan_ms += st.full_scan_ms;
+        total.sample_ms += st.sample_ms;
+        total.select_ms += st.select_ms;
+        total.prep_ms += st.prep_ms;
+        total.levels = std::max(total.levels, st.levels);
+        total.tensor_core_path = std::max(total.tensor_core_path, st.tensor_core_path);
+        for (int j = 0; j < kk; j++) {
+            out_ids[(size_t)i * k + j] = ids2[(size_t)j];
+            if (out_val_f) out_val_f[(size_t)i * k + j] = vf2[(size_t)j];
+            if (out_val_i) out_val_i[(size_t)i * k + j] = vi2[(size_t)j];
+        }
+        const uint32_t T = keys2[(size_t)kk - 1];
+        // An integer distance where the path returns one, else the float score.
+        a.threshold = vi2[(size_t)kk - 1] >= 0 ? (double)vi2[(size_t)kk - 1] : (double)vf2[(size_t)kk - 1];
+        int r = 0;
+        for (int j = kk; j < k2; j++) {
+            if (ids2[(size_t)j] < 0 || keys2[(size_t)j] <= T) continue;  // ties with the k-th are not excluded
+            rec_ids[(size_t)i * max_records + r] = ids2[(size_t)j];
+            if (rec_val_f) rec_val_f[(size_t)i * max_records + r] = vf2[(size_t)j];
+            if (rec_val_i) rec_val_i[(size_t)i * max_records + r] = vi2[(size_t)j];
+            r++;
+        }
+        a.n_records = r;
+        // The audit pass over every shard's whole level, on the query the
+        // search just staged in each shard's workspace.
+        const bool integral = host_u8 != nullptr || (!ix->is_f32 && all_integral_u8(qf, (size_t)dim));
+        const QueryPlan qp = plan_query(ix, integral, MDH_SCORE_EXACT);
+        int64_t within = 0, unsettled_rows = 0;
+        bool bounded = true;
+        for (Shard& sh : ix->shards) {
+            MDH_CUDA(cudaSetDevice(sh.device));
+            Workspace& w = sh.ws;
+            const Level& lv = sh.levels.back();
+            const uint32_t tk = T;
+            const int32_t ti = 0x7fffffff;
+            MDH_CUDA(cudaMemcpyAsync(w.thr_key, &tk, 4, cudaMemcpyHostToDevice, sh.stream));
+            MDH_CUDA(cudaMemcpyAsync(w.thr_id, &ti, 4, cudaMemcpyHostToDevice, sh.stream));
+            MDH_CUDA(cudaMemsetAsync(w.counts, 0, 4, sh.stream));
+            MDH_CUDA(cudaMemsetAsync(w.status, 0, kStatusWords * sizeof(int32_t), sh.stream));
+            const int used = run_filter(ix, sh, lv, qp, w.q_u8, w.qn, w.q_f32, 1, w.thr_key, w.thr_id, 0, false,
+                                        nullptr, true);
+            uint32_t cnt = 0;
+            MDH_CUDA(cudaMemcpyAsync(&cnt, w.counts, 4, cudaMemcpyDeviceToHost, sh.stream));
+            MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, kStatusWords * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                     sh.stream));
+            MDH_CUDA(cudaStreamSynchronize(sh.stream));
+            if (w.h_status[0] != kDevOk)
+                throw Error(w.h_status[0] == kDevTimeout ? MDH_ERR_TIMEOUT : MDH_ERR_INTERNAL,
+                            "audit scan reported device status " + std::to_string(w.h_status[0]));
+            unsigned long long bs[3] = {};
+            std::memcpy(bs, w.h_status + kStatusBlockStats, sizeof(bs));
+            within += (int64_t)cnt;
+            if (used == 2)
+                unsettled_rows += (int64_t)bs[2];
+            else
+                bounded = false;
+            total.pairs_scored += lv.n;
+            total.kernel_launches += 1;
+        }
+        // Rows tied with the k-th result fill the list before any excluded
+        // row: then the records come from the top (within + max_records),
+        // past the ties (a bounded search; beyond the bound the records stop
+        // short).
+        if (r < m && within > (int64_t)kk && within + m <= std::min<int64_t>(n, kAuditRecordSearchMax)) {
+            const int k3 = (int)(within + m);
+            std::vector<int32_t> ids3((size_t)k3), vi3((size_t)k3);
+            std::vector<float> vf3((size_t)k3);
+            std::vector<uint32_t> keys3((size_t)k3);
+            mdh_stats st3{};
+            search_impl(ix, qu, qf, 1, k3, MDH_SCORE_EXACT, ids3.data(), vf3.data(), vi3.data(), &st3, keys3.data(),
+                        true);
+            total.pairs_scored += st3.pairs_scored;
+            total.kernel_launches += st3.kernel_launches;
+            r = 0;
+            for (int j = (int)within; j < k3 && r < m; j++) {
+                if (ids3[(size_t)j] < 0 || keys3[(size_t)j] <= T) continue;
+                rec_ids[(size_t)i * max_records + r] = ids3[(size_t)j];
+                if (rec_val_f) rec_val_f[(size_t)i * max_records + r] = vf3[(size_t)j];
+                if (rec_val_i) rec_val_i[(size_t)i * max_records + r] = vi3[(size_t)j];
+                r++;
+            }
+            a.n_records = r;
+        }
+        a.within = within;
+        a.excluded = n - within;
+        a.excluded_by_bound = bounded ? n - unsettled_rows : -1;
+        // Every returned row is at or within T, so fewer than k such rows
+        // would mean a row the search missed or mis-scored.
+        a.violations = within < kk ? kk - within : 0;
+        total.bound_violations += a.violations;
+        total.verified_queries += 1;
+    }
+    total.latency_ms = std::chrono::duration<double, std::milli>(std::chrono::high_resolution_clock::now() - t0).count();
+    if (stats) *stats = total;
 }
 
 void create_impl(const void* host, bool f32, int64_t n, int32_t dim, int32_t metric, const int32_t* devices,
@@ -811,6 +964,11 @@ void create_impl(const void* host, bool f32, int64_t n, int32_t dim, int32_t met
 }
 
 }  // namespace
+
+bool take_fault(int site) {
+    int want = site;
+    return g_fault.load() == site && g_fault.compare_exchange_strong(want, kFaultNone);
+}
 
 [[noreturn]] void throw_cuda(cudaError_t e, const char* what, const char* file, int line) {
     cudaGetLastError();
@@ -943,6 +1101,24 @@ mdh_status mdh_search_u8(mdh_index* index, const uint8_t* host_queries, int32_t 
     return guard([&] {
         MDH_REQUIRE(index && !index->is_f32, MDH_ERR_INVALID_ARG, "u8 queries need a u8 index");
         search_impl(index, host_queries, nullptr, nq, k, MDH_SCORE_EXACT, out_ids, nullptr, out_dist, stats);
+    });
+}
+
+mdh_status mdh_audit_f32(mdh_index* index, const float* host_queries, int32_t nq, int32_t k, int32_t max_records,
+                         int32_t* out_ids, float* out_values, int32_t* rec_ids, float* rec_values, mdh_audit* audit,
+                         mdh_stats* stats) {
+    return guard([&] {
+        audit_impl(index, nullptr, host_queries, nq, k, max_records, out_ids, out_values, nullptr, rec_ids,
+                   rec_values, nullptr, audit, stats);
+    });
+}
+
+mdh_status mdh_audit_u8(mdh_index* index, const uint8_t* host_queries, int32_t nq, int32_t k, int32_t max_records,
+                        int32_t* out_ids, int32_t* out_dist, int32_t* rec_ids, int32_t* rec_dist, mdh_audit* audit,
+                        mdh_stats* stats) {
+    return guard([&] {
+        audit_impl(index, host_queries, nullptr, nq, k, max_records, out_ids, nullptr, out_dist, rec_ids, nullptr,
+                   rec_dist, audit, stats);
     });
 }
 
@@ -1088,7 +1264,7 @@ mdh_status mdh_set_verify(int32_t max_queries) {
 
 mdh_status mdh_set_fault(int32_t site) {
     return guard([&] {
-        MDH_REQUIRE(site >= kFaultNone && site <= kFaultShard, MDH_ERR_INVALID_ARG, "site must be 0, 1 or 2");
+        MDH_REQUIRE(site >= kFaultNone && site <= kFaultIvfChunks, MDH_ERR_INVALID_ARG, "site must be 0 .. 3");
         g_fault.store(site);
     });
 }

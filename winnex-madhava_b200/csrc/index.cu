@@ -161,6 +161,12 @@ std::vector<int64_t> plan_samples(int64_t n) {
     if (n < 8 * 1024) return s;
     const int64_t top = std::max<int64_t>(1024, n / std::max(2, g_sample_top_ratio));
     for (int64_t m = 1024; m <= top; m *= 4) s.push_back(m);
+    // A search for k rows starts from a level of at least k rows whose dense
+    // list fits the selector (16,384 entries).  Shards above that size whose
+    // ladder stops short of it get a 16,384-row level too, so any k up to it
+    // has a first level; the planner skips it where it does not pay.
+    constexpr int64_t kSelectorRows = 16384;
+    if (n > kSelectorRows && s.back() < kSelectorRows) s.push_back(kSelectorRows);
     return s;
 }
 

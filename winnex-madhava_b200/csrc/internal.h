@@ -49,15 +49,27 @@ struct Workspace {
     int32_t* qlist = nullptr;    size_t qlist_bytes = 0;    // [nq] query index list
     int32_t* status = nullptr;   // [kStatusWords] device status words: [0] scan error, [1] overflowed
                                  // queries, [2..3] u64 final candidates, [4..5] u64 violations,
-                                 // [6..11] u64 block-bound counts (tests, unsettled, rows formed)
+                                 // [6..11] u64 block-bound counts (tests, unsettled, rows formed),
+                                 // [12] chunk-buffer overflow and [13] entry counter of a
+                                 // deferred unit scan
     int32_t* h_status = nullptr;                             // pinned mirror
     void* tmp = nullptr;         size_t tmp_bytes = 0;      // CUB / misc scratch
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;               // brackets the full-shard scan
     cudaEvent_t ev_start = nullptr, ev_sel = nullptr;       // first level's start; end of the final selection
     cudaEvent_t ev_rescore = nullptr, ev_prep = nullptr;    // start of the rescore; start of query staging
 };
+// Fault injection (host side, one shot, mdh_set_fault): the next workspace
+// growth reports OOM; the next shard search thread fails before it scans; the
+// next IVF search gets a chunk buffer of one block per pass (its deferred
+// passes overflow and pass 2 reruns with keys formed in the scan).
+enum FaultSite : int { kFaultNone = 0, kFaultOom = 1, kFaultShard = 2, kFaultIvfChunks = 3 };
+// True once for an armed site (and disarms it).
+bool take_fault(int site);
+
 constexpr int kStatusWords = 16;
 constexpr int kStatusBlockStats = 6;   // first word of the three u64 block-bound counters
+constexpr int kStatusChunkOverflow = 12;
+constexpr int kStatusChunkCounter = 13;  // u32 entry counter of a deferred unit scan
 
 struct Shard {
     int device = 0;
@@ -177,11 +189,30 @@ struct ScanUnit {
     int32_t row_end;
     int32_t pad;
 };
+// Passing chunks of a deferred unit scan: entry e holds the 32 dot products
+// of one (query, 32-row chunk) whose block bound could not settle it
+// (x[8e .. 8e+8) as u32 x 32) and hdr[e] = {query, first row position, valid
+// rows, 0}.  CTAs' warps take 64-entry blocks from *counter; capacity is a
+// multiple of 64, and a block past it is dropped and flags
+// status[kStatusChunkOverflow].  nq: the number of candidate lists (query
+// indices in the entries are below it).
+struct ChunkOut {
+    uint4* x = nullptr;
+    int4* hdr = nullptr;
+    uint32_t* counter = nullptr;
+    uint32_t capacity = 0;
+    int32_t nq = 0;
+};
+constexpr int kChunkBlock = 64;
+// With `defer` null the scan forms exact keys in its epilogue (the form the
+// overflow reruns use).  With it, the scan writes the passing chunks to
+// *defer and a re-key pass (k_rekey_chunks) forms the same candidates:
+// every row of those chunks with (key, id) <= the query's threshold.
 void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat, int qmat_rows, const int32_t* qmap,
                                   const int32_t* qn, const ScanUnit* units, int n_units, const int32_t* n_units_dev,
                                   int32_t* unit_counter, const uint32_t* thr_key, const int32_t* thr_id,
                                   uint32_t* counts, uint2* cand, int cap, int32_t* status,
-                                  unsigned long long* block_stats, cudaStream_t st);
+                                  unsigned long long* block_stats, const ChunkOut* defer, cudaStream_t st);
 // ---- tensor-core scan on SM pairs (scan_tc2.cu) ----
 bool tc2_supported(const mdh_index* ix, const Level& lv);
 void make_tmap_rows_pair(Level& lv, int dpad);

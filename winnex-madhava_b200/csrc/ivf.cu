@@ -89,6 +89,10 @@ struct mdh_ivf {
     unsigned long long* plan_pairs = nullptr;  // [3]
     int64_t unit_max_runs[3] = {0, 0, 0};  // per pass: max over cells of ceil(tiles / 64)
     int64_t unit_sum_runs[3] = {0, 0, 0};  // per pass: sum over cells of ceil(tiles / 64)
+    // Passing chunks of the deferred scans (mdh::ChunkOut): 32 dot products
+    // and a header per entry.
+    uint4* chunk_x = nullptr;  size_t chunk_x_bytes = 0;
+    int4* chunk_hdr = nullptr; size_t chunk_hdr_bytes = 0;
     std::mutex mu;
 };
 
@@ -108,6 +112,11 @@ constexpr int kIvfSampleHead = 8;     // lowest-norm rows of every cell always i
 constexpr uint32_t kIvfCoarseThresh = 0x01000000u;  // ... in the coarse sample (1/256)
 constexpr int kIvfCoarseHead = 2;
 constexpr int kIvfCap2 = 16384;       // pass 2 candidate lists
+// Chunk-buffer entries per query of a deferred pass, plus two partly used
+// 64-entry blocks per epilogue warp.  Config-5 queries (10M rows, nlist 1024,
+// nprobe 16) leave about 300 chunks each to pass 2.  A pass that needs more
+// reruns pass 2 with keys formed in the scan.
+constexpr int kIvfChunksPerQuery = 512;
 // Inner-product ranking (metric COSINE) runs the L2 scan with every row norm
 // set to 0 and every query norm to this offset: the key offset - 2 q.v is then
 // positive (2 q.v <= 2 * 128 * 255^2 < 2^24 for dim <= 128) and ascends as
@@ -748,7 +757,8 @@ void ivf_create(const uint8_t* host, int64_t n, int32_t dim, const float* centro
         free_level_buffers(ix->sample);
         free_level_buffers(ix->coarse);
         if (ix->centroids) cudaFree(ix->centroids);
-        for (void* p : {(void*)ix->plan_info, (void*)ix->plan_order, (void*)ix->plan_scratch, (void*)ix->plan_pairs})
+        for (void* p : {(void*)ix->plan_info, (void*)ix->plan_order, (void*)ix->plan_scratch, (void*)ix->plan_pairs,
+                        (void*)ix->chunk_x, (void*)ix->chunk_hdr})
             if (p) cudaFree(p);
         cudaStreamDestroy(ix->stream);
         throw;
@@ -807,8 +817,12 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
     const int chunk = (int)std::max<int64_t>(1, std::min<int64_t>(nq, (int64_t(2) << 30) / ((int64_t)kIvfCap2 * 8)));
     std::vector<uint32_t> hkey;
     std::vector<int32_t> hid;
+    if (!w.ev_prep)
+        for (cudaEvent_t* e : {&w.ev0, &w.ev1, &w.ev_start, &w.ev_sel, &w.ev_prep})
+            if (!*e) MDH_CUDA(cudaEventCreate(e));
     for (int c0 = 0; c0 < nq; c0 += chunk) {
         const int m = std::min(chunk, nq - c0);
+        MDH_CUDA(cudaEventRecord(w.ev_prep, st));
         ivf_route_impl(ix, host_q + (size_t)c0 * ix->dim, m, nprobe, nullptr);
         s.kernel_launches += 3;
         int64_t bound[kIvfPasses];
@@ -825,24 +839,37 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         grow_dev(&w.out_key, &w.out_key_bytes, (size_t)m * k * 4);
         grow_dev(&w.out_id, &w.out_id_bytes, (size_t)m * k * 4);
         grow_dev(&w.qlist, &w.qlist_bytes, (size_t)m * 4);  // overflow flags
+        ChunkOut defer;
+        {
+            int sms = 0;
+            MDH_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ix->device));
+            const uint64_t cap = (uint64_t)m * kIvfChunksPerQuery + (uint64_t)sms * 16 * 2 * kChunkBlock;
+            uint64_t cap64 = std::min<uint64_t>((cap + kChunkBlock - 1) / kChunkBlock * kChunkBlock,
+                                                (uint64_t)1 << 30);
+            if (take_fault(kFaultIvfChunks)) cap64 = kChunkBlock;
+            grow_dev(&ix->chunk_x, &ix->chunk_x_bytes, (size_t)cap64 * 128);
+            grow_dev(&ix->chunk_hdr, &ix->chunk_hdr_bytes, (size_t)cap64 * 16);
+            defer.x = ix->chunk_x;
+            defer.hdr = ix->chunk_hdr;
+            defer.capacity = (uint32_t)cap64;
+            defer.nq = m;
+        }
         if (!w.status) {
             MDH_CUDA(cudaMalloc(&w.status, kStatusWords * sizeof(int32_t)));
             MDH_CUDA(cudaHostAlloc(&w.h_status, kStatusWords * sizeof(int32_t), cudaHostAllocDefault));
         }
-        if (!w.ev0) {
-            MDH_CUDA(cudaEventCreate(&w.ev0));
-            MDH_CUDA(cudaEventCreate(&w.ev1));
-        }
-        MDH_CUDA(cudaMemsetAsync(w.status, 0, 12 * sizeof(int32_t), st));
+        MDH_CUDA(cudaMemsetAsync(w.status, 0, (kStatusChunkOverflow + 1) * sizeof(int32_t), st));
+        defer.counter = reinterpret_cast<uint32_t*>(w.status + kStatusChunkCounter);
         unsigned long long* n_cand = reinterpret_cast<unsigned long long*>(w.status + 2);
         unsigned long long* bstats = reinterpret_cast<unsigned long long*>(w.status + kStatusBlockStats);
         // Pass 0: coarse samples of the probed cells, infinite thresholds; the
         // k-th (key, id) is a threshold for the union (the sample is part of it).
+        MDH_CUDA(cudaEventRecord(w.ev_start, st));
         launch_fill_threshold(w.thr_key, w.thr_id, m, kKeyInf, kIdInf, st);
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
         launch_filter_tc_u8_l2_units(ix->coarse, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[0].units,
                                      (int)bound[0], nunits, ucounter, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap0,
-                                     w.status, bstats, st);
+                                     w.status, bstats, &defer, st);
         launch_select(w.counts, w.cand, kIvfCap0, ix->coarse.ids, m, k, 0, w.thr_key, w.thr_id, w.out_key, w.out_id,
                       w.qlist, w.status + 1, nullptr, nullptr, st);
         // Pass 1: the samples with that threshold tighten it (a list that
@@ -850,26 +877,31 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
         launch_filter_tc_u8_l2_units(ix->sample, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[1].units,
                                      (int)bound[1], nunits + 1, ucounter, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap1,
-                                     w.status, bstats, st);
+                                     w.status, bstats, &defer, st);
         launch_select(w.counts, w.cand, kIvfCap1, ix->sample.ids, m, k, 0, w.thr_key, w.thr_id, w.out_key, w.out_id,
                       w.qlist, w.status + 1, nullptr, nullptr, st);
         s.kernel_launches += 6;
-        // Pass 2: every probed cell with that threshold.
+        // Pass 2: every probed cell with that threshold.  A chunk buffer that
+        // overflowed in passes 0 and 1 only left their thresholds looser (a
+        // k-th over part of a sample still bounds the union); in pass 2 it
+        // means a rerun, so its flag starts clear.
         MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
+        MDH_CUDA(cudaMemsetAsync(w.status + kStatusChunkOverflow, 0, sizeof(int32_t), st));
         MDH_CUDA(cudaEventRecord(w.ev0, st));
         launch_filter_tc_u8_l2_units(lv, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[2].units, (int)bound[2],
                                      nunits + 2, ucounter, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap2,
-                                     w.status, bstats, st);
+                                     w.status, bstats, &defer, st);
         MDH_CUDA(cudaEventRecord(w.ev1, st));
         launch_select(w.counts, w.cand, kIvfCap2, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id, w.qlist,
                       w.status + 1, nullptr, n_cand, st);
-        s.kernel_launches += 2;
+        MDH_CUDA(cudaEventRecord(w.ev_sel, st));
+        s.kernel_launches += 5;  // three re-key passes, the selection and the pass-2 scan
         // Status, pair counts and the results come back with one synchronization
         // (the results are copied again after an overflow round).
         hkey.resize((size_t)m * k);
         hid.resize((size_t)m * k);
         unsigned long long pairs[kIvfPasses] = {};
-        MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 12 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+        MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, kStatusWords * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
         MDH_CUDA(cudaMemcpyAsync(pairs, ix->plan_pairs, sizeof(pairs), cudaMemcpyDeviceToHost, st));
         MDH_CUDA(cudaMemcpyAsync(hkey.data(), w.out_key, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
         MDH_CUDA(cudaMemcpyAsync(hid.data(), w.out_id, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
@@ -880,26 +912,38 @@ void ivf_search_impl(mdh_ivf* ix, const uint8_t* host_q, int nq, int k, int npro
         if (w.h_status[0] != kDevOk)
             throw Error(MDH_ERR_TIMEOUT, "IVF scan reported device status " + std::to_string(w.h_status[0]));
         {
-            float ms = 0.0f;
-            MDH_CUDA(cudaEventElapsedTime(&ms, w.ev0, w.ev1));
-            s.full_scan_ms += ms;
+            // Stages of this chunk: routing and planning (with the query
+            // upload), passes 0 and 1 with their re-key passes and
+            // selections, pass 2 with its re-key pass, the final selection.
+            auto ms = [](cudaEvent_t a, cudaEvent_t b) {
+                float v = 0.0f;
+                MDH_CUDA(cudaEventElapsedTime(&v, a, b));
+                return (double)v;
+            };
+            s.prep_ms += ms(w.ev_prep, w.ev_start);
+            s.sample_ms += ms(w.ev_start, w.ev0);
+            s.full_scan_ms += ms(w.ev0, w.ev1);
+            s.select_ms += ms(w.ev1, w.ev_sel);
         }
         int rounds = 0;
-        while (w.h_status[1] > 0) {
+        while (w.h_status[1] > 0 || w.h_status[kStatusChunkOverflow] != 0) {
             // Overflowed lists got a strictly tighter threshold; the others keep
-            // theirs and reproduce their result.
+            // theirs and reproduce their result.  After a chunk-buffer overflow
+            // every list reruns: its threshold is still a valid bound.  Reruns
+            // form keys in the scan (no chunk buffer).
             MDH_REQUIRE(++rounds < 64, MDH_ERR_INTERNAL, "candidate overflow did not converge");
+            w.h_status[kStatusChunkOverflow] = 0;
             MDH_CUDA(cudaMemsetAsync(w.counts, 0, (size_t)m * 4, st));
             MDH_CUDA(cudaMemsetAsync(w.status + 1, 0, sizeof(int32_t), st));
             launch_filter_tc_u8_l2_units(lv, ix->dpad, qm.g, total, qm.gmap, w.qn, ix->pass[2].units,
                                          (int)bound[2], nunits + 2, ucounter, w.thr_key, w.thr_id, w.counts, w.cand, kIvfCap2,
-                                         w.status, bstats, st);
+                                         w.status, bstats, nullptr, st);
             launch_select(w.counts, w.cand, kIvfCap2, lv.ids, m, k, 1, w.thr_key, w.thr_id, w.out_key, w.out_id,
                           w.qlist, w.status + 1, nullptr, n_cand, st);
             s.kernel_launches += 2;
             s.pairs_scored += (int64_t)pairs[2];
             chunk_pairs += (int64_t)pairs[2];
-            MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, 12 * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+            MDH_CUDA(cudaMemcpyAsync(w.h_status, w.status, kStatusChunkOverflow * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
             MDH_CUDA(cudaMemcpyAsync(hkey.data(), w.out_key, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
             MDH_CUDA(cudaMemcpyAsync(hid.data(), w.out_id, (size_t)m * k * 4, cudaMemcpyDeviceToHost, st));
             MDH_CUDA(cudaStreamSynchronize(st));
@@ -1015,7 +1059,8 @@ mdh_status mdh_ivf_destroy(mdh_ivf* index) {
         free_level_buffers(ix->sample);
         free_level_buffers(ix->coarse);
         if (ix->centroids) cudaFree(ix->centroids);
-        for (void* p : {(void*)ix->plan_info, (void*)ix->plan_order, (void*)ix->plan_scratch, (void*)ix->plan_pairs})
+        for (void* p : {(void*)ix->plan_info, (void*)ix->plan_order, (void*)ix->plan_scratch, (void*)ix->plan_pairs,
+                        (void*)ix->chunk_x, (void*)ix->chunk_hdr})
             if (p) cudaFree(p);
         free_workspace(ix->ws);
         if (ix->stream) cudaStreamDestroy(ix->stream);

@@ -16,8 +16,13 @@
 //     accepted, and the scan stays exact;
 //   * save_index / load_index write and read this library's index file (the
 //     norm-sorted corpus, norms and ids; no re-attached base is needed);
-//   * bound-engine-only features (audit certificates, commitments,
-//     projection bases) raise NotImplementedError.
+//   * audit certificates and commitments (search_audited, audit_json,
+//     search_with_commitment) certify the exact result against a second GPU
+//     pass over every row with the k-th result's value as the threshold;
+//     their sample is the excluded rows nearest that threshold, in
+//     (value, id) order;
+//   * projection bases and residuals (bound-engine internals) raise
+//     NotImplementedError.
 #include <pybind11/numpy.h>
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
@@ -186,6 +191,37 @@ public:
         out.pruned_by_bound = st.pairs_pruned_by_bound;
         out.latency_ms = st.latency_ms;
         return out;
+    }
+
+    // One audited query (mdh_audit_f32): the top min(k, config.k) and the
+    // excluded rows nearest the threshold, at most max_records of them.
+    struct Audit {
+        std::vector<int32_t> ids, rec_ids;
+        std::vector<float> vals, rec_vals;
+        mdh_audit a{};
+        mdh_stats st{};
+        int k = 0;
+    };
+    Audit audit_one(const F32Array& q, int64_t k, int64_t max_records) const {
+        auto info = q.request();
+        if (info.ndim != 1 || (int)info.shape[0] != cfg_.dim)
+            throw std::runtime_error("query must be float32 of length dim");
+        Audit r;
+        if (!built_) return r;
+        r.k = (int)std::max<int64_t>(1, std::min<int64_t>(k > 0 ? k : cfg_.k, cfg_.k));
+        const int mr = (int)std::max<int64_t>(0, std::min<int64_t>(max_records, 0x7fffffff));
+        r.ids.assign((size_t)r.k, -1);
+        r.vals.assign((size_t)r.k, 0.0f);
+        r.rec_ids.assign((size_t)std::max(mr, 1), -1);
+        r.rec_vals.assign((size_t)std::max(mr, 1), 0.0f);
+        mdh_status s;
+        {
+            py::gil_scoped_release nogil;
+            s = mdh_audit_f32(h_.ix, (const float*)info.ptr, 1, r.k, mr, r.ids.data(), r.vals.data(),
+                              r.rec_ids.data(), r.rec_vals.data(), &r.a, &r.st);
+        }
+        check(s);
+        return r;
     }
 
     std::vector<int> search_batch(const F32Array& q, int nq, int k) const {
@@ -588,22 +624,121 @@ PYBIND11_MODULE(_winnex_madhava, m) {
             py::arg("P1"), py::arg("P2") = py::none())
         .def("search", &MadhavaL2::search_one, py::arg("query"))
         .def("search_exact", &MadhavaL2::search_one, py::arg("query"))
+        // Audits on the exact engine (mdh_audit_f32): the certificate covers
+        // the returned top k (stage "in_topk") and the excluded rows nearest
+        // the threshold (stage "exact": their exact value is the bound that
+        // excludes them), at most max_audit_records of those; audit_excluded
+        // counts every row strictly worse than the k-th result, from a second
+        // GPU pass over all rows with that threshold.
         .def(
             "search_audited",
-            [](const MadhavaL2&, py::object, int64_t, int64_t) -> py::dict {
-                not_implemented("MadhavaL2.search_audited (bound-engine audit certificate) is not implemented in this build");
+            [](const MadhavaL2& self, const F32Array& q, int64_t k, int64_t max_audit_records) -> py::dict {
+                auto r = self.audit_one(q, k, max_audit_records);
+                py::dict d;
+                py::list audit;
+                std::vector<int> idx;
+                for (int j = 0; j < r.k; j++)
+                    if (r.ids[(size_t)j] >= 0) idx.push_back(r.ids[(size_t)j]);
+                for (int j = 0; j < r.a.n_records; j++) {
+                    py::dict rd;
+                    const double v = r.rec_vals[(size_t)j];
+                    rd["doc_id"] = (int64_t)r.rec_ids[(size_t)j];
+                    rd["true_cosine"] = v;
+                    rd["projected_cosine"] = v;
+                    rd["residual_norm"] = 0.0;
+                    rd["upper_bound"] = v;
+                    rd["threshold"] = r.a.threshold;
+                    rd["excluded"] = true;
+                    rd["stage"] = "exact";
+                    audit.append(rd);
+                }
+                for (int j = 0; j < (int)idx.size(); j++) {
+                    py::dict rd;
+                    rd["doc_id"] = (int64_t)idx[(size_t)j];
+                    rd["true_cosine"] = (double)r.vals[(size_t)j];
+                    rd["projected_cosine"] = 0.0;
+                    rd["residual_norm"] = 0.0;
+                    rd["upper_bound"] = 0.0;
+                    rd["threshold"] = r.a.threshold;
+                    rd["excluded"] = false;
+                    rd["stage"] = "in_topk";
+                    audit.append(rd);
+                }
+                d["indices"] = idx;
+                d["latency_ms"] = r.st.latency_ms;
+                d["bound_violations"] = r.a.violations;
+                d["bound_pairs"] = r.a.rows;
+                d["audit_candidates"] = r.a.rows;
+                d["audit_excluded"] = r.a.excluded;
+                d["audit_excluded_by_bound"] = r.a.excluded_by_bound;
+                d["audit_threshold"] = r.a.threshold;
+                d["audit"] = audit;
+                return d;
             },
             py::arg("query"), py::arg("k") = 10, py::arg("max_audit_records") = 500)
         .def(
             "audit_json",
-            [](const MadhavaL2&, py::object, int64_t, int64_t) -> std::string {
-                not_implemented("MadhavaL2.audit_json is not implemented in this build");
+            [](const MadhavaL2& self, const F32Array& q, int64_t k, int64_t max_audit_records) -> std::string {
+                auto r = self.audit_one(q, k, max_audit_records);
+                auto num = [](double x) {
+                    char b[64];
+                    std::snprintf(b, sizeof(b), "%f", x);
+                    return std::string(b);
+                };
+                std::string j = "{\n  \"query_id\": \"madhava_audit\",\n";
+                j += "  \"latency_ms\": " + num(r.st.latency_ms) + ",\n";
+                j += "  \"bound_violations\": " + std::to_string(r.a.violations) + ",\n";
+                j += "  \"audit_excluded\": " + std::to_string(r.a.excluded) + ",\n";
+                j += "  \"results\": [";
+                int rank = 0;
+                for (int i = 0; i < r.k; i++) {
+                    if (r.ids[(size_t)i] < 0) continue;
+                    if (rank > 0) j += ",";
+                    j += "\n    {\"rank\": " + std::to_string(rank + 1) +
+                         ", \"doc_id\": " + std::to_string(r.ids[(size_t)i]) + "}";
+                    rank++;
+                }
+                j += "\n  ],\n  \"audit_trail\": [\n";
+                int count = 0;
+                auto rec = [&](int64_t id, double v, double ub, bool excl, const char* stage) {
+                    if (count++ > 0) j += ",\n";
+                    j += "    {\"doc_id\": " + std::to_string(id) + ", \"true_cosine\": " + num(v) +
+                         ", \"upper_bound\": " + num(ub) + ", \"threshold\": " + num(r.a.threshold) +
+                         ", \"excluded\": " + (excl ? "true" : "false") + ", \"stage\": \"" + stage + "\"}";
+                };
+                for (int i = 0; i < r.a.n_records; i++)
+                    rec(r.rec_ids[(size_t)i], r.rec_vals[(size_t)i], r.rec_vals[(size_t)i], true, "exact");
+                for (int i = 0; i < r.k; i++)
+                    if (r.ids[(size_t)i] >= 0) rec(r.ids[(size_t)i], r.vals[(size_t)i], 0.0, false, "in_topk");
+                j += "\n  ]\n}\n";
+                return j;
             },
             py::arg("query"), py::arg("k") = 10, py::arg("max_audit_records") = 500)
         .def(
             "search_with_commitment",
-            [](const MadhavaL2&, py::object, int64_t, int64_t) -> py::dict {
-                not_implemented("MadhavaL2.search_with_commitment is not implemented in this build");
+            [](const MadhavaL2& self, const F32Array& q, int64_t k, int64_t max_sample) -> py::dict {
+                auto r = self.audit_one(q, k, max_sample);
+                py::dict d;
+                std::vector<int> idx;
+                for (int j = 0; j < r.k; j++)
+                    if (r.ids[(size_t)j] >= 0) idx.push_back(r.ids[(size_t)j]);
+                d["indices"] = idx;
+                d["bound_pairs"] = r.a.rows;
+                d["bound_violations"] = r.a.violations;
+                d["latency_ms"] = r.st.latency_ms;
+                d["total_excluded_count"] = r.a.excluded;
+                d["excluded_by_bound"] = r.a.excluded_by_bound;
+                d["global_threshold"] = r.a.threshold;
+                py::list samples;
+                for (int j = 0; j < r.a.n_records; j++) {
+                    py::dict sd;
+                    sd["doc_id"] = (int64_t)r.rec_ids[(size_t)j];
+                    sd["upper_bound"] = (double)r.rec_vals[(size_t)j];
+                    sd["excluded"] = true;
+                    samples.append(sd);
+                }
+                d["sampled_records"] = samples;
+                return d;
             },
             py::arg("query"), py::arg("k") = 10, py::arg("max_sample") = 50)
         .def("search_batch", &MadhavaL2::search_batch, py::arg("queries"), py::arg("nq"), py::arg("k"))

@@ -210,11 +210,104 @@ __global__ void k_rekey_l2(const uint32_t* __restrict__ counts, uint2* __restric
     }
 }
 
+// Keys of a deferred unit scan's entries (see ChunkOut), one thread per
+// entry: the thread reads the entry's 32 dot products and the 32 row norms
+// (16-byte loads of 128-byte aligned runs; chunks start at multiples of 32
+// rows), marks each row with (key, id) <= the query's threshold -- the
+// epilogue's exact test -- and appends the marked rows with one atomic on the
+// query's count (a few rows per entry in the IVF passes; the values are read
+// again, from cache, for them).  The keys and ids are those of the EXACT
+// epilogue, so a list gets the same rows in another order.  Headers are
+// bounds-checked, and nothing runs after a scan that did not finish.
+__global__ void __launch_bounds__(256) k_rekey_chunks(ChunkOut out, const int32_t* __restrict__ norms,
+                                                      const int32_t* __restrict__ ids, int32_t n_rows_pad,
+                                                      const int32_t* __restrict__ qn, int nq,
+                                                      const uint32_t* __restrict__ thr_key,
+                                                      const int32_t* __restrict__ thr_id,
+                                                      uint32_t* __restrict__ counts, uint2* __restrict__ cand, int cap,
+                                                      const int32_t* __restrict__ status) {
+    if (*reinterpret_cast<const volatile int32_t*>(status) != kDevOk) return;
+    const uint32_t n = min(*out.counter, out.capacity);
+    const uint32_t stride = gridDim.x * blockDim.x;
+    const uint32_t* xs = reinterpret_cast<const uint32_t*>(out.x);
+    for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += stride) {
+        const int4 h = out.hdr[e];
+        const int qi = h.x, row0 = h.y, valid = h.z;
+        if (qi < 0 || qi >= nq || valid <= 0 || valid > 32 || row0 < 0 || row0 > n_rows_pad - 32 || (row0 & 31))
+            continue;
+        const int32_t qv = __ldg(qn + qi);
+        const uint32_t tk = __ldg(thr_key + qi);
+        const uint4* xp = out.x + (size_t)e * 8;
+        const int4* np = reinterpret_cast<const int4*>(norms + row0);
+        uint32_t mask = 0;
+#pragma unroll
+        for (int c8 = 0; c8 < 4; c8++) {
+            const uint4 xa = xp[2 * c8], xb = xp[2 * c8 + 1];
+            const int4 na = __ldg(np + 2 * c8), nb = __ldg(np + 2 * c8 + 1);
+            const uint32_t xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+            const int32_t nv[8] = {na.x, na.y, na.z, na.w, nb.x, nb.y, nb.z, nb.w};
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                if ((uint32_t)(qv + nv[j] - 2 * (int32_t)xv[j]) <= tk) mask |= 1u << (8 * c8 + j);
+        }
+        mask &= valid == 32 ? 0xffffffffu : (1u << valid) - 1u;
+        if (mask == 0u) continue;
+        // Rows tied with the threshold key stay only up to its id.
+        for (uint32_t m = mask; m; m &= m - 1u) {
+            const int j = __ffs(m) - 1;
+            const uint32_t key = (uint32_t)(qv + __ldg(norms + row0 + j) - 2 * (int32_t)xs[(size_t)e * 32 + j]);
+            if (key == tk && __ldg(ids + row0 + j) > __ldg(thr_id + qi)) mask &= ~(1u << j);
+        }
+        if (mask == 0u) continue;
+        uint32_t at = atomicAdd(counts + qi, (uint32_t)__popc(mask));
+        for (; mask; mask &= mask - 1u, at++) {
+            const int j = __ffs(mask) - 1;
+            if (at >= (uint32_t)cap) break;
+            const uint32_t key = (uint32_t)(qv + __ldg(norms + row0 + j) - 2 * (int32_t)xs[(size_t)e * 32 + j]);
+            cand[(size_t)qi * cap + at] = make_uint2(key, (uint32_t)(row0 + j));
+        }
+    }
+}
+
 // Block-bound counts live in shared memory (three u32: tests, unsettled
 // blocks, real rows of those blocks) and are added on the rare unsettled path
 // only, so the common path keeps no counter in registers; the CTA adds them to
 // the global u64 counters once, at exit.
 __device__ __forceinline__ void stat_add(uint32_t* s, uint32_t v) { atomicAdd(s, v); }
+
+// Deferred unit scans: a warp's next 64-entry block of chunk_out (warp-wide
+// call), or kNoChunkBlock past the capacity, which flags the overflow.
+constexpr uint32_t kNoChunkBlock = 0xffffffffu;
+__device__ __forceinline__ uint32_t chunk_block_take(const ChunkOut& out, int32_t* status, int lane) {
+    uint32_t base = 0;
+    if (lane == 0) base = atomicAdd(out.counter, (uint32_t)kChunkBlock);
+    base = __shfl_sync(0xffffffffu, base, 0);
+    if (base > out.capacity - kChunkBlock) {
+        if (lane == 0) atomicExch(status + kStatusChunkOverflow, 1);
+        return kNoChunkBlock;
+    }
+    return base;
+}
+
+// Entry `idx` (< 128) of the warp's current block, continuing into the next
+// one: a lane's 32 dot products of one chunk and its header.
+__device__ __forceinline__ void chunk_put(const ChunkOut& out, uint32_t cur, uint32_t nxt, int idx,
+                                          const uint32_t (&v)[32], int qi, int32_t row0, int32_t valid) {
+    const uint32_t base = idx < kChunkBlock ? cur : nxt;
+    if (base == kNoChunkBlock) return;
+    const uint32_t slot = base + (uint32_t)(idx & (kChunkBlock - 1));
+    uint4* dst = out.x + (size_t)slot * 8;
+#pragma unroll
+    for (int i = 0; i < 8; i++) dst[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    out.hdr[slot] = make_int4(qi, row0, valid, 0);
+}
+
+// Marks the unused entries [used, 64) of a warp's block (query -1) so that
+// the re-key pass skips them.
+__device__ __forceinline__ void chunk_block_close(const ChunkOut& out, uint32_t base, int used, int lane) {
+    if (base == kNoChunkBlock) return;
+    for (int j = used + lane; j < kChunkBlock; j += 32) out.hdr[base + j] = make_int4(-1, 0, 0, 0);
+}
 
 // Run-time hand-out of a unit table (its units differ in length, so fixed
 // shares leave some SMs idle at the end).  The producer takes the next index
@@ -253,10 +346,12 @@ __device__ __forceinline__ int feed_take(bool whole_warp, volatile int32_t* slot
 }
 
 // UNITS: the unit-table form.  Its query rows are different queries probing
-// one cell, whose passing columns rarely coincide, so its slow path walks
-// each lane's own columns (reading the row norm from memory); the schedule
-// form walks the columns any lane keeps, warp-uniformly, with the norms
-// already in registers.
+// one cell, whose passing columns rarely coincide.  With EXACT its slow path
+// walks each lane's own columns (the row norm comes by shuffle); without it
+// a lane whose chunk passes writes the chunk's 32 dot products to chunk_out
+// and k_rekey_chunks forms the keys after the scan.  The schedule form walks
+// the columns any lane keeps, warp-uniformly, with the norms already in
+// registers.
 template <class C, bool UNITS, bool EXACT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_filter_tc_u8_l2(const __grid_constant__ CUtensorMap tmap_rows, const __grid_constant__ CUtensorMap tmap_q,
@@ -266,7 +361,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                       int cap, int dense, Sched sched, int32_t* __restrict__ status,
                       const ScanUnit* __restrict__ units, const int32_t* __restrict__ qmap,
                       const int32_t* __restrict__ n_units_dev, int32_t* __restrict__ unit_counter,
-                      unsigned long long* __restrict__ block_stats) {
+                      unsigned long long* __restrict__ block_stats, ChunkOut chunk_out) {
     constexpr int BN = C::BN, QT = C::QT, STAGES = C::STAGES, ACC_STAGES = C::ACC_STAGES;
     // A unit table built on the device carries its own length.
     const long long n_units = n_units_dev ? (long long)*n_units_dev : sched.n_units;
@@ -559,6 +654,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         CandBuf<EPI_THREADS, BUFN> buf;
         buf.base = reinterpret_cast<uint2*>(smem + C::OFF_BUF) + threadIdx.x;
         buf.n = 0;
+        // Deferred form: this warp's current block of chunk_out entries and
+        // the next one, taken ahead so that a tile's entries always fit (a
+        // tile makes at most 64) and no atomic is waited on while the
+        // accumulator values are live.
+        uint32_t blk_cur = 0, blk_nxt = 0;
+        int blk_used = 0;
+        if constexpr (!EXACT) {
+            blk_cur = chunk_block_take(chunk_out, status, lane);
+            blk_nxt = chunk_block_take(chunk_out, status, lane);
+        }
         int acc = 0;
         uint32_t acc_phase = 0;
         bool ok = true;
@@ -605,7 +710,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 nx1 = __ldg(nrm + (int64_t)t0 * BN + 32 + lane);
             }
             for (int t = t0; t < t1; t++) {
-                buf.warp_flush_at(BUF_FLUSH_AT, counts, cand, cap, qi);
+                if constexpr (EXACT) buf.warp_flush_at(BUF_FLUSH_AT, counts, cand, cap, qi);
                 const int32_t nr0 = nx0, nr1 = nx1;
                 const int32_t need0 = __shfl_sync(0xffffffffu, nr0, 0) + bias;
                 const int32_t need1 = __shfl_sync(0xffffffffu, nr1, 0) + bias;
@@ -632,6 +737,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     acc_phase ^= 1;
                 }
                 const int32_t m0 = max32(v[0]), m1 = max32(v[1]);
+                if constexpr (!EXACT) {
+                    // Chunks wholly past the cell's last row hold pad rows only.
+                    const int32_t row0 = t * BN + rowoff;  // rows < 2^31 (ids are int32)
+                    const int32_t valid0 = row_end - row0, valid1 = valid0 - 32;
+                    const bool pass0 = 2 * m0 >= need0 && valid0 > 0, pass1 = 2 * m1 >= need1 && valid1 > 0;
+                    const uint32_t b0 = __ballot_sync(0xffffffffu, pass0), b1 = __ballot_sync(0xffffffffu, pass1);
+                    if ((b0 | b1) == 0u) continue;
+                    const int n0 = __popc(b0), n = n0 + __popc(b1);
+                    if (block_stats && lane == 0) {
+                        stat_add(stats + 1, (uint32_t)n);
+                        stat_add(stats + 2, (uint32_t)(n0 * min(valid0, 32) + (n - n0) * min(max(valid1, 0), 32)));
+                    }
+                    const uint32_t lt = (1u << lane) - 1u;
+                    if (pass0)
+                        chunk_put(chunk_out, blk_cur, blk_nxt, blk_used + __popc(b0 & lt), v[0], qi, row0,
+                                  min(valid0, 32));
+                    if (pass1)
+                        chunk_put(chunk_out, blk_cur, blk_nxt, blk_used + n0 + __popc(b1 & lt), v[1], qi, row0 + 32,
+                                  min(valid1, 32));
+                    blk_used += n;
+                    if (blk_used >= kChunkBlock) {
+                        blk_used -= kChunkBlock;
+                        blk_cur = blk_nxt;
+                        blk_nxt = chunk_block_take(chunk_out, status, lane);
+                    }
+                    continue;
+                }
                 const bool pass0 = 2 * m0 >= need0, pass1 = 2 * m1 >= need1;
                 if (!__any_sync(0xffffffffu, pass0 || pass1)) continue;
                 // The queries of a unit probe one cell but rarely keep the same
@@ -663,9 +795,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     }
                 }
             }
-            if (qvalid) buf.flush(counts, cand, cap, qi);
+            if constexpr (EXACT) {
+                if (qvalid) buf.flush(counts, cand, cap, qi);
+            }
             // Two chunk tests per tile for each of the unit's queries.
             if (block_stats && qvalid) stat_add(stats, 2u * (uint32_t)(t1 - t0));
+        }
+        if constexpr (!EXACT) {
+            chunk_block_close(chunk_out, blk_cur, blk_used, lane);
+            chunk_block_close(chunk_out, blk_nxt, 0, lane);
         }
     }
 
@@ -794,7 +932,7 @@ void launch_tc(const Level& lv, const CUtensorMap& tq, const int32_t* qn, int nq
     MDH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM_BYTES));
     kern<<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n, qn, nq, thr_key,
                                                    thr_id, counts, cand, cap, dense, s, status, nullptr, nullptr,
-                                                   nullptr, nullptr, block_stats);
+                                                   nullptr, nullptr, block_stats, ChunkOut{});
     MDH_CUDA(cudaGetLastError());
 }
 
@@ -817,9 +955,12 @@ void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat
                                   const int32_t* qn, const ScanUnit* units, int n_units, const int32_t* n_units_dev,
                                   int32_t* unit_counter, const uint32_t* thr_key, const int32_t* thr_id,
                                   uint32_t* counts, uint2* cand, int cap, int32_t* status,
-                                  unsigned long long* block_stats, cudaStream_t st) {
+                                  unsigned long long* block_stats, const ChunkOut* defer, cudaStream_t st) {
     using C = CfgNarrow;
     if (n_units <= 0 || qmat_rows <= 0 || lv.n == 0) return;
+    MDH_REQUIRE(!defer || (defer->x && defer->hdr && defer->counter && defer->nq > 0 &&
+                           defer->capacity >= (uint32_t)kChunkBlock && defer->capacity % kChunkBlock == 0),
+                MDH_ERR_INTERNAL, "deferred unit scan needs a chunk buffer of whole 64-entry blocks");
     MDH_REQUIRE(dpad == BK && lv.has_tmap, MDH_ERR_INTERNAL, "tensor-core scan needs 128-byte rows and a TMA map");
     CUtensorMap tq;
     encode_u8_rows_tmap(&tq, qmat, qmat_rows, dpad, BM);
@@ -829,13 +970,20 @@ void launch_filter_tc_u8_l2_units(const Level& lv, int dpad, const uint8_t* qmat
     s.n_units = n_units;
     const int ctas = std::min(device_sm_count(dev), n_units);
     if (unit_counter) MDH_CUDA(cudaMemsetAsync(unit_counter, 0, sizeof(int32_t), st));
-    MDH_CUDA(cudaFuncSetAttribute(k_filter_tc_u8_l2<C, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)C::SMEM_BYTES));
-    k_filter_tc_u8_l2<C, true, true><<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n,
-                                                                   qn, qmat_rows, thr_key, thr_id, counts, cand, cap,
-                                                                   0, s, status, units, qmap, n_units_dev,
-                                                                   unit_counter, block_stats);
+    if (defer) MDH_CUDA(cudaMemsetAsync(defer->counter, 0, sizeof(uint32_t), st));
+    auto kern = defer ? k_filter_tc_u8_l2<C, true, false> : k_filter_tc_u8_l2<C, true, true>;
+    MDH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM_BYTES));
+    kern<<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n, qn, qmat_rows,
+                                                   thr_key, thr_id, counts, cand, cap, 0, s, status, units, qmap,
+                                                   n_units_dev, unit_counter, block_stats,
+                                                   defer ? *defer : ChunkOut{});
     MDH_CUDA(cudaGetLastError());
+    if (defer) {
+        k_rekey_chunks<<<device_sm_count(dev) * 8, 256, 0, st>>>(*defer, lv.norms, lv.ids, (int32_t)lv.n_pad, qn,
+                                                                 defer->nq, thr_key, thr_id, counts, cand, cap,
+                                                                 status);
+        MDH_CUDA(cudaGetLastError());
+    }
 }
 
 }  // namespace mdh

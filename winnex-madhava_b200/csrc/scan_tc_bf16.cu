@@ -298,37 +298,76 @@ __global__ void k_convert_bf16(const float* __restrict__ src, int64_t count, __n
 // normalized float query (dot_f32, src/speed_cpu.cpp:60-76): lane l of 8
 // accumulates fused multiply-adds of elements l, l + 8, l + 16, ...; the 8
 // lanes are summed left to right, then the scalar tail -- the operations and
-// order of k_filter_f32 (scan_simt.cu).  Here the 8 lanes of one candidate are
-// 8 threads (each lane's chain is sequential, as in the reference), so a warp
-// rescores 4 candidates with coalesced 32-byte reads.
-__global__ void __launch_bounds__(256) k_rescore_speed_cos(const uint32_t* __restrict__ counts, uint2* __restrict__ cand,
-                                                           int cap, const float* __restrict__ rows, int dim,
-                                                           const float* __restrict__ q, int nq) {
-    extern __shared__ float sq[];
+// order of k_filter_f32 (scan_simt.cu).  A warp rescores 4 candidates at a
+// time: threads 8c .. 8c + 7 run the 8 lane chains of candidate c.  The rows
+// are read in 128-float segments, one coalesced 512-byte float4 load per
+// candidate and thread, staged in the warp's shared buffer; each thread then
+// folds its chain's 16 elements of the segment in order.  One block per
+// query; the query row sits in shared memory.
+constexpr int RESCORE_WARPS = 8;
+constexpr int RESCORE_SEG = 128;  // floats per staged segment
+
+__global__ void __launch_bounds__(RESCORE_WARPS * 32) k_rescore_speed_cos(const uint32_t* __restrict__ counts,
+                                                                          uint2* __restrict__ cand, int cap,
+                                                                          const float* __restrict__ rows, int dim,
+                                                                          const float* __restrict__ q, int nq) {
+    extern __shared__ float4 smem4[];
+    float* sq = reinterpret_cast<float*>(smem4);                        // [dim rounded up to 4]
     const int qi = blockIdx.x;
     if (qi >= nq) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float4* wbuf = smem4 + (dim + 3) / 4 + warp * (4 * RESCORE_SEG / 4);  // [4][128] floats of this warp
+    const float* wf = reinterpret_cast<const float*>(wbuf);
     for (int j = threadIdx.x; j < dim; j += blockDim.x) sq[j] = q[(size_t)qi * dim + j];
     __syncthreads();
     const uint32_t c_all = counts[qi];
     const int c = (int)(c_all < (uint32_t)cap ? c_all : (uint32_t)cap);
     uint2* lst = cand + (size_t)qi * cap;
-    const int l = threadIdx.x & 7;
-    const int gbase = (threadIdx.x & 31) & ~7;  // first lane of this candidate's group in the warp
+    const int g = lane >> 3, l = lane & 7;  // this thread: chain l of candidate g
     const int jt_end = dim & ~7;
-    for (int i0 = 0; i0 < c; i0 += blockDim.x / 8) {
-        const int i = i0 + (threadIdx.x >> 3);
-        const bool valid = i < c;
-        const uint32_t r = valid ? lst[i].y : 0u;
-        const float* row = rows + (size_t)r * dim;
+    const bool vec = (dim & 3) == 0;         // rows are 16-byte aligned for float4 reads
+    for (int i0 = warp * 4; i0 < c; i0 += RESCORE_WARPS * 4) {
+        uint32_t r4[4];
+#pragma unroll
+        for (int h = 0; h < 4; h++) r4[h] = i0 + h < c ? lst[i0 + h].y : 0xffffffffu;
         float acc = 0.0f;
-        if (valid)
-            for (int jt = 0; jt < jt_end; jt += 8) acc = __fmaf_rn(__ldg(row + jt + l), sq[jt + l], acc);
+        for (int s0 = 0; s0 < jt_end; s0 += RESCORE_SEG) {
+            float4 x[4];
+#pragma unroll
+            for (int h = 0; h < 4; h++) {
+                const int e = s0 + 4 * lane;
+                x[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (r4[h] != 0xffffffffu && e < dim) {
+                    const float* src = rows + (size_t)r4[h] * dim + e;
+                    if (vec && e + 3 < dim) {
+                        x[h] = __ldg(reinterpret_cast<const float4*>(src));
+                    } else {
+                        x[h].x = __ldg(src);
+                        if (e + 1 < dim) x[h].y = __ldg(src + 1);
+                        if (e + 2 < dim) x[h].z = __ldg(src + 2);
+                        if (e + 3 < dim) x[h].w = __ldg(src + 3);
+                    }
+                }
+            }
+            __syncwarp();  // the previous segment's folds are done with the buffer
+#pragma unroll
+            for (int h = 0; h < 4; h++) wbuf[h * (RESCORE_SEG / 4) + lane] = x[h];
+            __syncwarp();
+            const float* seg = wf + g * RESCORE_SEG;
+#pragma unroll
+            for (int m = 0; m < RESCORE_SEG / 8; m++) {
+                const int jt = s0 + 8 * m;
+                if (jt < jt_end) acc = __fmaf_rn(seg[8 * m + l], sq[jt + l], acc);
+            }
+        }
+        const int gbase = g * 8;
         float sum = __shfl_sync(0xffffffffu, acc, gbase);
 #pragma unroll
-        for (int m = 1; m < 8; m++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, acc, gbase + m));
-        if (valid && l == 0) {
+        for (int mm = 1; mm < 8; mm++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, acc, gbase + mm));
+        if (l == 0 && r4[g] != 0xffffffffu) {
+            const float* row = rows + (size_t)r4[g] * dim;
             for (int t = jt_end; t < dim; t++) sum = __fmaf_rn(__ldg(row + t), sq[t], sum);
-            lst[i].x = ordered_key_desc(sum);
+            lst[i0 + g].x = ordered_key_desc(sum);
         }
     }
 }
@@ -439,9 +478,9 @@ void launch_normalize_speed_cos(float* q, int nq, int dim, int batch_guard, uint
 void launch_rescore_speed_cos(const uint32_t* counts, uint2* cand, int cap, const float* rows_f32, int dim,
                               const float* q_f32, int nq, cudaStream_t st) {
     if (nq <= 0) return;
-    const size_t smem = (size_t)dim * sizeof(float);
+    const size_t smem = (size_t)(dim + 3) / 4 * 16 + (size_t)RESCORE_WARPS * 4 * RESCORE_SEG * sizeof(float);
     MDH_REQUIRE(smem <= 48 * 1024, MDH_ERR_UNSUPPORTED, "dimension too large for the rescore kernel");
-    k_rescore_speed_cos<<<nq, 256, smem, st>>>(counts, cand, cap, rows_f32, dim, q_f32, nq);
+    k_rescore_speed_cos<<<nq, RESCORE_WARPS * 32, smem, st>>>(counts, cand, cap, rows_f32, dim, q_f32, nq);
     MDH_CUDA(cudaGetLastError());
 }
 
