@@ -142,6 +142,32 @@ def test_reference_test_semantics():
     assert e.search(corpus[0].astype(np.float32)).indices == [0]
 
 
+def test_speed_engine_counters_with_verification():
+    """build_engine(..., speed=True) with set_verify(n): the result reports
+    the verified queries and their measured violations (0), and on a
+    clustered u8 corpus the tensor scan's block bound settles pairs without
+    forming their distance (pruned_by_bound > 0).  The reference declares
+    these counters (include/winnex_madhava/speed_engine.hpp:36-41) but never
+    measures them."""
+    C = cases.gmm_u8(120_000, 128, 64, seed=111)
+    Q = cases.gmm_u8_queries(256, 128, 64, seed_means=111, seed_q=112)
+    eng = wm.build_engine(C, dim=128, k=10, metric="l2", speed=True)
+    wm.set_verify(32)
+    try:
+        r = eng.search_batch(Q.astype(np.float32), k=10)
+    finally:
+        wm.set_verify(0)
+    assert r.verified_queries == 32 and r.bound_violations == 0
+    # Pairs settled by the block bound, over every level scanned (the sample
+    # levels too), so it is compared with the pairs of all levels.
+    assert r.pruned_by_bound > len(C) * len(Q) // 2
+    assert r.bound_pairs == len(C) * len(Q)
+    want, _ = oracle.l2_exact_u8_int(C, Q, 10)
+    np.testing.assert_array_equal(np.asarray(r.indices).reshape(len(Q), 10), want)
+    one = eng.search(Q[0].astype(np.float32), k=10)
+    assert one.verified_queries == 0 and one.pruned_by_bound >= 0
+
+
 def test_overflow_rerun_keeps_results_exact():
     """Tiny candidate lists force the overflow / tighter-threshold reruns."""
     C, Q = cases.case_dups()

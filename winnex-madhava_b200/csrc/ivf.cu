@@ -215,10 +215,11 @@ __global__ void k_ivf_fill(int32_t* __restrict__ p, int64_t n, int32_t v) {
 
 // Routing, step 1: sims[q][c] = sum_j q[j] * centroid[c][j] in fp64, one
 // fused multiply-add per j in dimension order from 0.0 (deterministic, so the
-// cell order is reproducible).  Block tile: 32 queries x 64 centroids, both
-// converted to fp64 once in shared memory; each thread forms 2 x 4 of the
-// 2048 dot products, so a step of j is 6 shared loads for 8 multiply-adds.
-constexpr int kRouteQ = 32, kRouteC = 64, kRouteDim = 128;
+// cell order is reproducible).  Block tile: 64 queries x 64 centroids, both
+// converted to fp64 once in shared memory; each thread forms 4 x 4 of the
+// 4096 dot products, so a step of j is 8 shared loads for 16 multiply-adds
+// (one shared-memory wavefront per fp64 pipe slot of the SM).
+constexpr int kRouteQ = 64, kRouteC = 64, kRouteDim = 128;
 constexpr size_t kRouteSmem = (size_t)(kRouteQ * kRouteDim + kRouteC * (kRouteDim + 1)) * sizeof(double);
 __global__ void __launch_bounds__(256) k_route_sims(const uint8_t* __restrict__ q, int nq, int dpad, int dim,
                                                     const float* __restrict__ centroids, int nlist,
@@ -237,28 +238,28 @@ __global__ void __launch_bounds__(256) k_route_sims(const uint8_t* __restrict__ 
         qs[r * dim + j] = q0 + r < nq ? (double)q[(size_t)(q0 + r) * dpad + j] : 0.0;
     }
     __syncthreads();
-    // Thread: centroids cq + 16 b (b < 4), queries rp and rp + 16.  A warp
+    // Thread: centroids cq + 16 b and queries rp + 16 a (a, b < 4).  A warp
     // reads 16 centroid rows 129 doubles apart (every bank once) and
     // broadcasts two query rows.
     const int cq = threadIdx.x & 15, rp = threadIdx.x >> 4;
-    double acc[2][4];
+    double acc[4][4];
 #pragma unroll
-    for (int a = 0; a < 2; a++)
+    for (int a = 0; a < 4; a++)
 #pragma unroll
         for (int b = 0; b < 4; b++) acc[a][b] = 0.0;
     for (int j = 0; j < dim; j++) {
-        double qv[2], cv[4];
+        double qv[4], cv[4];
 #pragma unroll
-        for (int a = 0; a < 2; a++) qv[a] = qs[(rp + 16 * a) * dim + j];
+        for (int a = 0; a < 4; a++) qv[a] = qs[(rp + 16 * a) * dim + j];
 #pragma unroll
         for (int b = 0; b < 4; b++) cv[b] = cs[(cq + 16 * b) * cstride + j];
 #pragma unroll
-        for (int a = 0; a < 2; a++)
+        for (int a = 0; a < 4; a++)
 #pragma unroll
             for (int b = 0; b < 4; b++) acc[a][b] = __fma_rn(qv[a], cv[b], acc[a][b]);
     }
 #pragma unroll
-    for (int a = 0; a < 2; a++)
+    for (int a = 0; a < 4; a++)
 #pragma unroll
         for (int b = 0; b < 4; b++) {
             const int qi = q0 + rp + 16 * a, c = c0 + cq + 16 * b;

@@ -66,7 +66,7 @@ using namespace tc;
 
 constexpr int BM = 128;           // queries per query tile (TMEM lanes)
 constexpr int BK = 128;           // bytes per row (K)
-constexpr int BOX_ROWS = 128;     // corpus rows per TMA box (BN / BOX_ROWS boxes per stage)
+constexpr int BOX_ROWS = 256;     // corpus rows per TMA box (BN / BOX_ROWS boxes per stage; 256 is the box limit)
 constexpr int TMEM_COLS = 512;
 constexpr int EPI_WARPS = 16;     // 4 per TMEM lane quarter
 constexpr int COLS_PER_WARP = 64; // two 32-column chunks
@@ -90,14 +90,17 @@ struct TcCfg {
     static constexpr uint32_t B_BYTES = BN * BK;
     static constexpr uint32_t IDESC = idesc_u8(BM, BN);
     // Shared memory map (offsets from a 1024-byte aligned base).
+    // Two query-tile slots: the producer loads the next unit's queries while
+    // the current unit's MMAs still read the other slot.
+    static constexpr int A_SLOTS = 2;
     static constexpr uint32_t OFF_A = 0;
-    static constexpr uint32_t OFF_B = OFF_A + A_BYTES;
+    static constexpr uint32_t OFF_B = OFF_A + A_SLOTS * A_BYTES;
     static constexpr uint32_t OFF_BUF = OFF_B + STAGES * B_BYTES;
     static constexpr uint32_t OFF_BAR = OFF_BUF + BUFN * EPI_THREADS * 8;
     static constexpr uint32_t BAR_FULL = 0, BAR_EMPTY = STAGES, BAR_ACC_FULL = 2 * STAGES,
                               BAR_ACC_EMPTY = 2 * STAGES + ACC_STAGES, BAR_A_FULL = 2 * STAGES + 2 * ACC_STAGES,
-                              BAR_A_EMPTY = BAR_A_FULL + 1, BAR_DRAIN = BAR_A_FULL + 2,
-                              BAR_UNIT_FULL = BAR_A_FULL + 3, BAR_UNIT_EMPTY = BAR_UNIT_FULL + 2,
+                              BAR_A_EMPTY = BAR_A_FULL + A_SLOTS, BAR_DRAIN = BAR_A_EMPTY + A_SLOTS,
+                              BAR_UNIT_FULL = BAR_DRAIN + 1, BAR_UNIT_EMPTY = BAR_UNIT_FULL + 2,
                               NUM_BARS = BAR_UNIT_EMPTY + 2;
     static constexpr uint32_t OFF_USLOT = OFF_BAR + NUM_BARS * 8;  // two unit indices handed out at run time
     static constexpr uint32_t OFF_TMEM_SLOT = OFF_USLOT + 8;
@@ -384,8 +387,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(bars + 8 * (C::BAR_ACC_FULL + s), 1);
             mbar_init(bars + 8 * (C::BAR_ACC_EMPTY + s), EPI_WARPS);
         }
-        mbar_init(bars + 8 * C::BAR_A_FULL, 1);
-        mbar_init(bars + 8 * C::BAR_A_EMPTY, 1);
+        for (int s = 0; s < C::A_SLOTS; s++) {
+            mbar_init(bars + 8 * (C::BAR_A_FULL + s), 1);
+            mbar_init(bars + 8 * (C::BAR_A_EMPTY + s), 1);
+        }
         mbar_init(bars + 8 * C::BAR_DRAIN, 1);
         for (int s = 0; s < 2; s++) {
             mbar_init(bars + 8 * (C::BAR_UNIT_FULL + s), 1);
@@ -416,7 +421,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             int stage = 0;
             uint32_t phase = 0, a_iter = 0;
             uint32_t issued_mask = 0, last_parity = 0;
-            bool a_issued = false;
             bool ok = true;
             for (long long u = blockIdx.x;; u += gridDim.x) {
                 if (!ok) break;
@@ -429,14 +433,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 const UnitView uv = unit_view<C, UNITS>(sched, units, u, n_rows, nq);
                 const int t0 = uv.t0, t1 = uv.t1;
-                ok = mbar_wait<false>(bars + 8 * C::BAR_A_EMPTY, (a_iter & 1) ^ 1, abort_flag, status);
+                // Query slot a_iter % 2, its (a_iter / 2)-th use.
+                const int as = (int)(a_iter & 1);
+                ok = mbar_wait<false>(bars + 8 * (C::BAR_A_EMPTY + as), ((a_iter >> 1) & 1) ^ 1, abort_flag, status);
                 if (!ok) break;
-                mbar_expect_tx(bars + 8 * C::BAR_A_FULL, C::A_BYTES);
+                mbar_expect_tx(bars + 8 * (C::BAR_A_FULL + as), C::A_BYTES);
 #pragma unroll
                 for (int qt = 0; qt < QT; qt++)
-                    tma_load_2d(sbase + C::OFF_A + qt * A_TILE_BYTES, &tmap_q, bars + 8 * C::BAR_A_FULL, 0,
-                                uv.q_row + qt * BM);
-                a_issued = true;
+                    tma_load_2d(sbase + C::OFF_A + as * C::A_BYTES + qt * A_TILE_BYTES, &tmap_q,
+                                bars + 8 * (C::BAR_A_FULL + as), 0, uv.q_row + qt * BM);
                 a_iter++;
                 for (int t = t0; t < t1; t++) {
                     ok = mbar_wait<false>(bars + 8 * (C::BAR_EMPTY + stage), phase ^ 1, abort_flag, status);
@@ -459,7 +464,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int s = 0; s < STAGES; s++)
                     if (issued_mask & (1u << s))
                         mbar_drain_wait<false>(bars + 8 * (C::BAR_FULL + s), (last_parity >> s) & 1);
-                if (a_issued) mbar_drain_wait<false>(bars + 8 * C::BAR_A_FULL, (a_iter - 1) & 1);
+                // The last load of each query slot (use a_iter - 1 and a_iter - 2).
+                for (uint32_t i = a_iter > 2 ? a_iter - 2 : 0; i < a_iter; i++)
+                    mbar_drain_wait<false>(bars + 8 * (C::BAR_A_FULL + (i & 1)), (i >> 1) & 1);
             }
         }
     } else if (warp == MMA_WARP) {
@@ -484,7 +491,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 const UnitView uv = unit_view<C, UNITS>(sched, units, u, n_rows, nq);
                 const int t0 = uv.t0, t1 = uv.t1;
-                ok = mbar_wait<false>(bars + 8 * C::BAR_A_FULL, a_iter & 1, abort_flag, status);
+                const int as = (int)(a_iter & 1);
+                ok = mbar_wait<false>(bars + 8 * (C::BAR_A_FULL + as), (a_iter >> 1) & 1, abort_flag, status);
                 if (!ok) break;
                 a_iter++;
                 tc_fence_after();
@@ -507,7 +515,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint64_t bdesc = sw128_desc(sbase + C::OFF_B + stage * C::B_BYTES);
 #pragma unroll
                     for (int qt = 0; qt < QT; qt++) {
-                        const uint64_t adesc = sw128_desc(sbase + C::OFF_A + qt * A_TILE_BYTES);
+                        const uint64_t adesc = sw128_desc(sbase + C::OFF_A + as * C::A_BYTES + qt * A_TILE_BYTES);
                         const uint32_t d = tmem_base + (uint32_t)(acc * C::ACC_COLS + qt * BN);
 #pragma unroll
                         for (int kk = 0; kk < BK / 32; kk++) {
@@ -529,7 +537,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     acc_phase = nacc_phase;
                 }
                 if (!ok) break;
-                umma_commit(bars + 8 * C::BAR_A_EMPTY);
+                umma_commit(bars + 8 * (C::BAR_A_EMPTY + as));
             }
             if (!ok && issued) {
                 umma_commit(bars + 8 * C::BAR_DRAIN);
