@@ -123,6 +123,64 @@ def test_audit_two_shards_agree(gmm):
     assert L.mdh_index_destroy(h1) == 0 and L.mdh_index_destroy(h2) == 0
 
 
+def test_audit_cosine_index_matches_oracle():
+    """A u8 index ranked by MadhavaL2's cosine score, float queries
+    (mdh_audit_f32): the threshold is the k-th score, `within` counts the rows
+    scoring at least that, and the records are the next rows by (score
+    descending, id) -- all from the oracle's full ranking."""
+    import oracle
+
+    L = capi()
+    rng = np.random.default_rng(107)
+    C = rng.integers(0, 256, (4_000, 64), dtype=np.uint8)
+    Q = (rng.random((3, 64)) * 200).astype(np.float32)
+    h = ctypes.c_void_p()
+    assert L.mdh_index_create_u8(ptr(C), len(C), 64, 0, None, 0, 0, ctypes.byref(h)) == 0, L.mdh_last_error()
+    k, m = 10, 25
+    ids = np.empty((3, k), np.int32)
+    val = np.empty((3, k), np.float32)
+    rid = np.empty((3, m), np.int32)
+    rval = np.empty((3, m), np.float32)
+    aud = (Audit * 3)()
+    st = L.mdh_audit_f32(h, ptr(Q), 3, k, m, ptr(ids), ptr(val), ptr(rid), ptr(rval), aud, None)
+    assert st == 0, L.mdh_last_error()
+    all_ids, all_sc = oracle.cosine_exact_u8(C, Q, len(C))
+    for i in range(3):
+        T = all_sc[i, k - 1]
+        np.testing.assert_array_equal(ids[i], all_ids[i, :k])
+        np.testing.assert_array_equal(val[i], all_sc[i, :k])
+        within = int((all_sc[i] >= T).sum())
+        assert aud[i].threshold == T and aud[i].within == within and aud[i].excluded == len(C) - within
+        assert aud[i].excluded_by_bound == -1 and aud[i].violations == 0
+        assert aud[i].n_records == m
+        np.testing.assert_array_equal(rid[i], all_ids[i, within:within + m])
+        np.testing.assert_array_equal(rval[i], all_sc[i, within:within + m])
+    assert L.mdh_index_destroy(h) == 0
+
+
+def test_audit_edges():
+    """k at least n (every row returned, none excluded), no queries, and no
+    records requested."""
+    L = capi()
+    rng = np.random.default_rng(109)
+    C = rng.integers(0, 256, (100, 128), dtype=np.uint8)
+    q = rng.integers(0, 256, (2, 128), dtype=np.uint8)
+    h = _index(L, C)
+    ids, dist, rid, rdist, aud, _ = _audit_u8(L, h, q, 150, 5)
+    for i in range(2):
+        top, topd, T, within, _, _ = _oracle_audit(C, q[i], 150, 0)
+        np.testing.assert_array_equal(ids[i, :100], top)
+        assert (ids[i, 100:] == -1).all()
+        assert aud[i].within == 100 and aud[i].excluded == 0 and aud[i].n_records == 0 and aud[i].threshold == T
+    ids, dist, rid, rdist, aud, _ = _audit_u8(L, h, q, 10, 0)
+    top, topd, T, within, _, _ = _oracle_audit(C, q[0], 10, 0)
+    np.testing.assert_array_equal(ids[0], top)
+    assert aud[0].n_records == 0 and aud[0].excluded == 100 - within
+    st = Stats()
+    assert L.mdh_audit_u8(h, ptr(q), 0, 10, 5, None, None, None, None, None, ctypes.byref(st)) == 0
+    assert L.mdh_index_destroy(h) == 0
+
+
 def test_audit_rejects_bad_arguments(gmm):
     L = capi()
     C, Q = gmm

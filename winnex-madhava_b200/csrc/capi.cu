@@ -213,7 +213,7 @@ float bf16_cos_eps(int dim) {
 
 int run_filter(mdh_index* ix, Shard& sh, const Level& lv, const QueryPlan& qp, const uint8_t* q_u8,
                const int32_t* qn, const float* q_f32, int nq, const uint32_t* tk, const int32_t* ti, int cap,
-               bool dense, const uint16_t* q_bf16 = nullptr, bool exact_only = false) {
+               bool dense, const uint16_t* q_bf16 = nullptr, bool exact_only = false, int k_dense = 0) {
     Workspace& w = sh.ws;
     unsigned long long* bstats = reinterpret_cast<unsigned long long*>(w.status + kStatusBlockStats);
     const int d = dense ? 1 : 0;
@@ -226,6 +226,16 @@ int run_filter(mdh_index* ix, Shard& sh, const Level& lv, const QueryPlan& qp, c
         launch_filter_tc_bf16_cos(lv, ix->dim, q_bf16, nq, tk, w.counts, w.cand, cap, d, bf16_cos_eps(ix->dim),
                                   w.status, sh.stream);
         if (dense) launch_fill_u32(w.counts, nq, (uint32_t)lv.n, sh.stream);
+        if (dense && k_dense > 0 && lv.n > k_dense) {
+            // A dense list holds every row: rescore only the band of bf16
+            // scores that can hold the exact top k.  The k-th bf16 key goes
+            // through the thresholds, which are then reset, so the level's
+            // exact selection starts from infinity again.
+            launch_select(w.counts, w.cand, cap, lv.ids, nq, k_dense, 0, w.thr_key, w.thr_id, w.out_key, w.out_id,
+                          w.flags, w.status + 1, nullptr, nullptr, sh.stream);
+            launch_compact_bf16_band(w.counts, w.cand, cap, w.thr_key, 2.0f * bf16_cos_eps(ix->dim), nq, sh.stream);
+            launch_fill_threshold(w.thr_key, w.thr_id, nq, kKeyInf, kIdInf, sh.stream);
+        }
         MDH_CUDA(cudaEventRecord(w.ev_rescore, sh.stream));
         launch_rescore_speed_cos(w.counts, w.cand, cap, lv.rows_f32, ix->dim, q_f32, nq, sh.stream);
         return 4;
@@ -346,9 +356,9 @@ ShardResult search_shard(mdh_index* ix, Shard& sh, const QueryPlan& qp, int nq, 
         }
         const bool dense = s.dense && s.cap >= lv.n;
         const int used = run_filter(ix, sh, lv, qp, w.q_u8, w.qn, w.q_f32, nq, w.thr_key, w.thr_id, s.cap, dense,
-                                    w.q_bf16);
+                                    w.q_bf16, false, dense ? k : 0);
         count_tc(lv, used, nq);
-        res.launches += (dense ? 2 : 1) + (used == 4 ? 1 : 0);
+        res.launches += (dense ? 2 : 1) + (used == 4 ? 1 : 0) + (used == 4 && dense && lv.n > k ? 3 : 0);
         if (last_level) {
             MDH_CUDA(cudaEventRecord(w.ev1, st));
             res.scan_pairs = lv.n * (int64_t)nq;

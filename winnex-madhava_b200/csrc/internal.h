@@ -227,6 +227,10 @@ void launch_filter_tc2_u8_l2(const Level& lv, int dpad, const uint8_t* q, const 
 bool tc_bf16_supported(const mdh_index* ix, const Level& lv);
 void ensure_bf16_rows(mdh_index* ix, Shard& sh);
 void launch_convert_bf16(const float* src, int64_t count, uint16_t* dst, cudaStream_t st);
+// Dense bf16 lists: keep only rows within two_eps of each list's k-th bf16
+// score (thr_key), the only rows that can be in the exact top k.
+void launch_compact_bf16_band(uint32_t* counts, uint2* cand, int cap, const uint32_t* thr_key, float two_eps, int nq,
+                              cudaStream_t st);
 void launch_filter_tc_bf16_cos(const Level& lv, int dim, const uint16_t* q_bf16, int nq, const uint32_t* thr_key,
                                uint32_t* counts, uint2* cand, int cap, int dense, float eps, int32_t* status,
                                cudaStream_t st);

@@ -374,6 +374,51 @@ __global__ void __launch_bounds__(RESCORE_WARPS * 32) k_rescore_speed_cos(const 
 
 }  // namespace
 
+// A dense level's lists hold every row with its bf16 score.  Only rows whose
+// bf16 score is within 2 eps of the list's k-th bf16 score s' can be in its
+// exact top k: k rows score >= s' in bf16, so >= s' - eps exactly, so the
+// exact k-th score is >= s' - eps and every row of the exact top k has a
+// bf16 score >= s' - 2 eps.  thr_key holds s' (k-th key, from a selection);
+// each list is compacted in place, in order, to those rows (one block per
+// query, chunk by chunk: a chunk is read before any of its slots is
+// written).  A list with fewer than k rows (infinite threshold) is kept.
+__global__ void __launch_bounds__(256) k_compact_bf16_band(uint32_t* __restrict__ counts, uint2* __restrict__ cand,
+                                                           int cap, const uint32_t* __restrict__ thr_key,
+                                                           float two_eps) {
+    __shared__ uint32_t warp_n[8];
+    __shared__ uint32_t base_s;
+    const int qi = blockIdx.x;
+    const uint32_t tk = thr_key[qi];
+    if (tk == kKeyInf) return;
+    const uint32_t c_all = counts[qi];
+    const int c = (int)(c_all < (uint32_t)cap ? c_all : (uint32_t)cap);
+    uint2* lst = cand + (size_t)qi * cap;
+    const float lo = __fsub_rd(key_to_float_asc(~tk), two_eps);
+    const uint32_t bound = ordered_key_desc(lo);  // key <= bound  <=>  bf16 score >= lo
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) base_s = 0;
+    __syncthreads();
+    for (int i0 = 0; i0 < c; i0 += blockDim.x) {
+        const int i = i0 + threadIdx.x;
+        const uint2 e = i < c ? lst[i] : make_uint2(0xffffffffu, 0u);
+        const bool keep = i < c && e.x <= bound;
+        const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+        if (lane == 0) warp_n[warp] = __popc(bal);
+        __syncthreads();  // every entry of this chunk is read
+        uint32_t before = base_s;
+        for (int w = 0; w < warp; w++) before += warp_n[w];
+        if (keep) lst[before + __popc(bal & ((1u << lane) - 1u))] = e;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            uint32_t t = base_s;
+            for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += warp_n[w];
+            base_s = t;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) counts[qi] = base_s;
+}
+
 bool tc_bf16_supported(const mdh_index* ix, const Level& lv) {
     return ix && ix->dim % 8 == 0 && ix->dim <= KB * MAX_KBLOCKS && lv.rows_f32 && lv.n_pad % BN == 0 &&
            lv.n_pad < (int64_t(1) << 31);
@@ -472,6 +517,13 @@ void launch_normalize_speed_cos(float* q, int nq, int dim, int batch_guard, uint
     if (nq <= 0) return;
     k_normalize_speed_cos<<<(nq + 7) / 8, 256, 0, st>>>(q, nq, dim, batch_guard,
                                                         reinterpret_cast<__nv_bfloat16*>(q_bf16));
+    MDH_CUDA(cudaGetLastError());
+}
+
+void launch_compact_bf16_band(uint32_t* counts, uint2* cand, int cap, const uint32_t* thr_key, float two_eps, int nq,
+                              cudaStream_t st) {
+    if (nq <= 0) return;
+    k_compact_bf16_band<<<nq, 256, 0, st>>>(counts, cand, cap, thr_key, two_eps);
     MDH_CUDA(cudaGetLastError());
 }
 
