@@ -154,8 +154,9 @@ void encode_tmap_2d_sw128(CUtensorMap* map, int bf16, const void* base, uint64_t
                          uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows);
 // TMA map over u8 rows [rows][dpad], 128-byte swizzle, boxes of box_rows rows.
 void encode_u8_rows_tmap(CUtensorMap* map, const void* base, int64_t rows, int dpad, int box_rows);
-// Corpus chunks per query group so that groups x chunks spreads evenly over workers.
-int choose_scan_chunks(int groups, int n_tiles, int workers);
+// Corpus chunks per query group for a schedule of groups x chunks units on
+// `workers` CTAs; every unit keeps at least min_unit_tiles tiles.
+int choose_scan_chunks(int groups, int n_tiles, int workers, int min_unit_tiles);
 bool tc_supported(const mdh_index* ix, const Level& lv);
 void make_tmap_rows(Level& lv, int dpad);
 // One CTA runs the scans' bounded mbarrier wait on a barrier that never

@@ -893,10 +893,15 @@ void encode_u8_rows_tmap(CUtensorMap* map, const void* base, int64_t rows, int d
     MDH_REQUIRE(r == CUDA_SUCCESS, MDH_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
 }
 
-int choose_scan_chunks(int groups, int n_tiles, int workers) {
-    // Smallest chunk count that makes the unit count (groups x chunks) a
-    // multiple of the worker count (no tail round), scaled up while chunks
-    // keep >= 64 tiles.
+int choose_scan_chunks(int groups, int n_tiles, int workers, int min_unit_tiles) {
+    // A unit has a fixed cost of a few microseconds (its query tile, the
+    // per-query thresholds, the final candidate flush), so every unit keeps
+    // at least min_unit_tiles tiles.  Within that: the smallest chunk count
+    // that makes the unit count (groups x chunks) a multiple of the worker
+    // count (no tail round), scaled up while chunks keep >= 64 tiles.  A
+    // level too small for that (the sample levels) takes the most chunks
+    // that keep units long, and lives with a partial last round.
+    const int max_chunks = std::max(1, n_tiles / std::max(1, min_unit_tiles));
     int a = groups, b = workers;
     while (b) {
         int t = a % b;
@@ -904,7 +909,7 @@ int choose_scan_chunks(int groups, int n_tiles, int workers) {
         b = t;
     }
     const int base = workers / a;
-    if (base > n_tiles) return n_tiles;
+    if (base > max_chunks) return max_chunks;
     int mult = 1;
     while ((long long)base * (mult + 1) * 64 <= n_tiles && mult < 8) mult++;
     return base * mult;
@@ -932,7 +937,7 @@ void launch_tc(const Level& lv, const CUtensorMap& tq, const int32_t* qn, int nq
     s.n_groups = (nq + C::QGROUP - 1) / C::QGROUP;
     s.n_tiles = (int)(lv.n_pad / C::BN);
     int ctas = sms;
-    s.n_chunks = choose_scan_chunks(s.n_groups, s.n_tiles, ctas);
+    s.n_chunks = choose_scan_chunks(s.n_groups, s.n_tiles, ctas, 64);
     s.n_units = (long long)s.n_groups * s.n_chunks;
     if (s.n_units < ctas) ctas = (int)s.n_units;
     // A function attribute belongs to the current device: set it on every launch.

@@ -365,7 +365,7 @@ void launch_filter_tc2_u8_l2(const Level& lv, int dpad, const uint8_t* q, const 
     s.n_groups = (nq + QGROUP - 1) / QGROUP;
     s.n_tiles = (int)(lv.n_pad / BN);
     int pairs = max_pairs;
-    s.n_chunks = choose_scan_chunks(s.n_groups, s.n_tiles, pairs);
+    s.n_chunks = choose_scan_chunks(s.n_groups, s.n_tiles, pairs, 64);
     s.n_units = (long long)s.n_groups * s.n_chunks;
     if (s.n_units < pairs) pairs = (int)s.n_units;
     cfg.gridDim = dim3(2 * pairs, 1, 1);

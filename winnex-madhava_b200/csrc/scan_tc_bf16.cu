@@ -470,7 +470,7 @@ void launch_filter_tc_bf16_cos(const Level& lv, int dim, const uint16_t* q_bf16,
     s.n_tiles = (int)(lv.n_pad / BN);
     s.nkb = (dim + KB - 1) / KB;
     int ctas = sms;
-    s.n_chunks = choose_scan_chunks(s.n_groups, s.n_tiles, ctas);
+    s.n_chunks = choose_scan_chunks(s.n_groups, s.n_tiles, ctas, 16);  // a tile streams 12 dimension blocks
     s.n_units = (long long)s.n_groups * s.n_chunks;
     if (s.n_units < ctas) ctas = (int)s.n_units;
     MDH_CUDA(cudaFuncSetAttribute(k_filter_tc_bf16_cos, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
