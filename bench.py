@@ -37,7 +37,7 @@ SEED = 20261201
 CHUNK = 3_125_000
 L2_BYTES = 126 << 20        # B200 L2
 L2_FLUSH_BYTES = 512 << 20
-TRAFFIC_BYTES_PER_ROW = (1.288509e9 + 34.518272e6) / 10_000_000
+TRAFFIC_BYTES_PER_ROW = (1.288255e9 + 35.171072e6) / 10_000_000
 METRIC = "queries/sec, 100M×128 u8 exact top-10, 10K-query batch at 1/2/4/8 B200; % roofline"
 
 
@@ -870,7 +870,7 @@ def main():
         achieved = 2.0 * pairs * DIM / (ms_scan / 1e3) / 1e12 if ms_scan > 0 else None
         # DRAM traffic of the scan: ncu capture of the same kernel on a
         # 10M-row case (dram__bytes_read.sum + dram__bytes_write.sum =
-        # 1.3230e9 B per launch for 10,000 queries); the corpus and norms cross
+        # 1.3234e9 B per launch for 10,000 queries); the corpus and norms cross
         # HBM once per launch, so traffic scales with the rows scanned.
         traffic = TRAFFIC_BYTES_PER_ROW * rows_scanned if pairs else None
         roofline = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",
