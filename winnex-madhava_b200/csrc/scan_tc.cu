@@ -894,14 +894,10 @@ void encode_u8_rows_tmap(CUtensorMap* map, const void* base, int64_t rows, int d
 }
 
 int choose_scan_chunks(int groups, int n_tiles, int workers, int min_unit_tiles) {
-    // A unit has a fixed cost of a few microseconds (its query tile, the
-    // per-query thresholds, the final candidate flush), so every unit keeps
-    // at least min_unit_tiles tiles.  Within that: the smallest chunk count
-    // that makes the unit count (groups x chunks) a multiple of the worker
-    // count (no tail round), scaled up while chunks keep >= 64 tiles.  A
-    // level too small for that (the sample levels) takes the most chunks
-    // that keep units long, and lives with a partial last round.
-    const int max_chunks = std::max(1, n_tiles / std::max(1, min_unit_tiles));
+    // A large level: the smallest chunk count that makes the unit count
+    // (groups x chunks) a multiple of the worker count (no tail round),
+    // scaled up while chunks keep >= 64 tiles (neighbouring units share
+    // chunks through L2), as long as units keep at least min_unit_tiles.
     int a = groups, b = workers;
     while (b) {
         int t = a % b;
@@ -909,10 +905,29 @@ int choose_scan_chunks(int groups, int n_tiles, int workers, int min_unit_tiles)
         b = t;
     }
     const int base = workers / a;
-    if (base > max_chunks) return max_chunks;
-    int mult = 1;
-    while ((long long)base * (mult + 1) * 64 <= n_tiles && mult < 8) mult++;
-    return base * mult;
+    if (base <= std::max(1, n_tiles / std::max(1, min_unit_tiles))) {
+        int mult = 1;
+        while ((long long)base * (mult + 1) * 64 <= n_tiles && mult < 8) mult++;
+        return base * mult;
+    }
+    // A small level (the sample levels): the chunk count with the shortest
+    // last-finishing worker, rounds x (tiles per unit + a unit's fixed cost
+    // of ~4 tiles), over units of at least 4 tiles.  Their tiles carry more
+    // epilogue work than the full level's, so filling the SMs pays more than
+    // long units.
+    constexpr double kUnitCostTiles = 4.0;
+    int best = 1;
+    double best_cost = 1e300;
+    for (int c = 1; c <= std::max(1, n_tiles / 4); c++) {
+        const long long units = (long long)groups * c;
+        const long long rounds = (units + workers - 1) / workers;
+        const double cost = (double)rounds * ((double)n_tiles / c + kUnitCostTiles);
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best = c;
+        }
+    }
+    return best;
 }
 
 bool tc_supported(const mdh_index* ix, const Level& lv) {
