@@ -170,12 +170,28 @@ __device__ __forceinline__ UnitView unit_view(const Sched& s, const ScanUnit* un
 // a tie, its id) and keep only rows at or under (tkey, tid), so every rerun's
 // list holds rows under its threshold alone and the next threshold is
 // strictly tighter.
-template <bool EXACT>
+template <bool EXACT, bool DENSE>
 __device__ __forceinline__ void chunk_emit(const uint32_t (&v)[32], int32_t need, int32_t row0, int row_end, int qi,
-                                           int dense, uint32_t tkey, int32_t tid, int32_t qnv,
+                                           uint32_t tkey, int32_t tid, int32_t qnv,
                                            const int32_t* __restrict__ norms, const int32_t* __restrict__ ids,
                                            CandBuf<EPI_THREADS, BUFN>& buf, uint32_t* __restrict__ counts,
                                            uint2* __restrict__ cand, int cap) {
+    if constexpr (DENSE) {
+        // Every row of a dense level is a candidate at slot r: the chunk's
+        // 32 entries are one 256-byte run of the list (rows start at
+        // multiples of 32, the capacity is even), stored two at a time.
+        const int32_t valid = row_end - row0;  // pad rows trail the level
+        uint2* run = cand + (size_t)qi * cap + row0;
+        uint4* run4 = reinterpret_cast<uint4*>(run);
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+            if (j + 1 < valid)
+                run4[j >> 1] = make_uint4(v[j], (uint32_t)(row0 + j), v[j + 1], (uint32_t)(row0 + j + 1));
+            else if (j < valid)
+                run[j] = make_uint2(v[j], (uint32_t)(row0 + j));
+        }
+        return;
+    }
     if (2 * max32(v) < need) return;
     uint32_t mask = pass_mask32(v, need);
     const int32_t valid = row_end - row0;  // pad rows trail the level
@@ -184,9 +200,7 @@ __device__ __forceinline__ void chunk_emit(const uint32_t (&v)[32], int32_t need
         const int j = __ffs(mask) - 1;
         mask &= mask - 1;
         const uint32_t x = pick32(v, j), r = (uint32_t)(row0 + j);
-        if (dense) {
-            cand[(size_t)qi * cap + r] = make_uint2(x, r);
-        } else if (EXACT) {
+        if (EXACT) {
             const uint32_t key = (uint32_t)(qnv + __ldg(norms + r) - 2 * (int32_t)x);
             if (key < tkey || (key == tkey && __ldg(ids + r) <= tid)) buf.push(key, r, counts, cand, cap, qi);
         } else {
@@ -355,7 +369,7 @@ __device__ __forceinline__ int feed_take(bool whole_warp, volatile int32_t* slot
 // and k_rekey_chunks forms the keys after the scan.  The schedule form walks
 // the columns any lane keeps, warp-uniformly, with the norms already in
 // registers.
-template <class C, bool UNITS, bool EXACT>
+template <class C, bool UNITS, bool EXACT, bool DENSE = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_filter_tc_u8_l2(const __grid_constant__ CUtensorMap tmap_rows, const __grid_constant__ CUtensorMap tmap_q,
                       const int32_t* __restrict__ norms, const int32_t* __restrict__ ids, int32_t n_rows,
@@ -622,9 +636,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         stat_add(stats + 1, 1u);
                         stat_add(stats + 2, (uint32_t)min(max(row_end - row0, 0), COLS_PER_WARP));
                     }
-                    chunk_emit<EXACT>(v[0], need, row0, row_end, qi, dense, tkey, tid, qnv, norms, ids, buf,
+                    chunk_emit<EXACT, DENSE>(v[0], need, row0, row_end, qi, tkey, tid, qnv, norms, ids, buf,
                                       counts, cand, cap);
-                    chunk_emit<EXACT>(v[1], need, row0 + 32, row_end, qi, dense, tkey, tid, qnv, norms, ids, buf,
+                    chunk_emit<EXACT, DENSE>(v[1], need, row0 + 32, row_end, qi, tkey, tid, qnv, norms, ids, buf,
                                       counts, cand, cap);
                 }
                 buf.warp_flush_at(BUF_FLUSH_AT, counts, cand, cap, qi);
@@ -956,7 +970,11 @@ void launch_tc(const Level& lv, const CUtensorMap& tq, const int32_t* qn, int nq
     s.n_units = (long long)s.n_groups * s.n_chunks;
     if (s.n_units < ctas) ctas = (int)s.n_units;
     // A function attribute belongs to the current device: set it on every launch.
-    auto kern = exact ? k_filter_tc_u8_l2<C, false, true> : k_filter_tc_u8_l2<C, false, false>;
+    // Dense levels (the first, with infinite thresholds) have their own
+    // instantiation, so the others carry no dense store path.
+    auto kern = dense   ? k_filter_tc_u8_l2<C, false, false, true>
+                : exact ? k_filter_tc_u8_l2<C, false, true>
+                        : k_filter_tc_u8_l2<C, false, false>;
     MDH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM_BYTES));
     kern<<<ctas, NUM_THREADS, C::SMEM_BYTES, st>>>(lv.tmap_rows, tq, lv.norms, lv.ids, (int32_t)lv.n, qn, nq, thr_key,
                                                    thr_id, counts, cand, cap, dense, s, status, nullptr, nullptr,
@@ -970,6 +988,7 @@ void launch_filter_tc_u8_l2(const Level& lv, int dpad, const uint8_t* q, const i
     if (nq <= 0 || lv.n == 0) return;
     MDH_REQUIRE(dpad == BK && lv.has_tmap, MDH_ERR_INTERNAL, "tensor-core scan needs 128-byte rows and a TMA map");
     MDH_REQUIRE(!dense || cap >= lv.n, MDH_ERR_INTERNAL, "dense scan needs cap >= rows");
+    MDH_REQUIRE(!dense || !exact, MDH_ERR_INTERNAL, "a dense scan forms no keys");
     CUtensorMap tq;
     encode_u8_rows_tmap(&tq, q, nq, dpad, BM);
     launch_tc<CfgNarrow>(lv, tq, qn, nq, thr_key, thr_id, counts, cand, cap, dense, status, block_stats, exact, st);
