@@ -315,6 +315,22 @@ mdh_status mdh_ivf_search_u8(mdh_ivf* index, const uint8_t* host_queries, int32_
 mdh_status mdh_ivf_info(const mdh_ivf* index, int64_t* n, int32_t* dim, int32_t* nlist, int64_t* cell_rows);
 mdh_status mdh_ivf_destroy(mdh_ivf* index);
 
+/* Clustered search over a float32 corpus: replaces MadHybrid's float path
+ * (python/winnex_madhava/__init__.py:547-654: routing `centroids @ q` at
+ * :631-632, per-cell float64 scores `vecs @ q` at :526, merge by score at
+ * :650).  Every row of the probed cells is scored, so the result is the
+ * exact top k of their union by (float64 inner product descending, row id
+ * ascending); routing and scores are fp64 with one fused multiply-add per
+ * dimension in dimension order.  labels[i] in [0, nlist) is row i's cell;
+ * dim <= 4096; k in [1, 16] (MDH_ERR_UNSUPPORTED above); out_scores may be
+ * null.  Rows past the probed cells' total come back as id -1. */
+typedef struct mdh_ivf_f32 mdh_ivf_f32;
+mdh_status mdh_ivf_create_f32(const float* host_rows, int64_t n, int32_t dim, const float* centroids, int32_t nlist,
+                              const int32_t* labels, int32_t device, mdh_ivf_f32** out);
+mdh_status mdh_ivf_search_f32(mdh_ivf_f32* index, const float* host_queries, int32_t nq, int32_t k, int32_t nprobe,
+                              int32_t* out_ids, double* out_scores, mdh_stats* stats);
+mdh_status mdh_ivf_destroy_f32(mdh_ivf_f32* index);
+
 /* Options (process-wide): force the scan path for testing and measurement.
  * path: 0 = automatic, 1 = CUDA-core scan only, 2 = tensor-core scan on
  * single SMs, 3 = tensor-core scan on SM pairs (each whenever the shape

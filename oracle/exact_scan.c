@@ -434,6 +434,80 @@ void oracle_score_ids(int kind, int is_cosine, const uint8_t* corpus_u8, const f
  * summation order is unspecified; this restatement fixes it: fp64
  * multiply-adds in dimension order from 0.0, ties to the lower cell id.
  * out_cells: [nq][nprobe], best first. */
+/* Float-query routing and the exact inner-product ranking of float32 IVF
+ * cells (MadHybrid over a float corpus, python/winnex_madhava/__init__.py:
+ * routing `centroids @ q` at :631-632; each cell scores its rows by
+ * `vecs @ q` in float64 at :526 and the merge orders by score at :650).
+ * Here every row of the probed cells is scored (the exact top-k over their
+ * union): s = sum_j fma(row[j], q[j]) in float64 in dimension order, ranked
+ * by (s descending, row id ascending).  Routing as oracle_ivf_route. */
+void oracle_ivf_route_f32(const float* centroids, int nlist, int d, const float* queries, int nq, int nprobe,
+                          int32_t* out_cells) {
+#pragma omp parallel
+    {
+        double* sims = (double*)malloc(sizeof(double) * (size_t)nlist);
+#pragma omp for schedule(dynamic, 4)
+        for (int qi = 0; qi < nq; qi++) {
+            const float* q = queries + (size_t)qi * d;
+            for (int c = 0; c < nlist; c++) {
+                const float* cr = centroids + (size_t)c * d;
+                double acc = 0.0;
+                for (int j = 0; j < d; j++) acc = fma((double)q[j], (double)cr[j], acc);
+                sims[c] = acc;
+            }
+            for (int p = 0; p < nprobe; p++) {
+                int bi = -1;
+                for (int c = 0; c < nlist; c++)
+                    if (bi < 0 || sims[c] > sims[bi]) bi = c;
+                out_cells[(size_t)qi * nprobe + p] = bi;
+                sims[bi] = -INFINITY;
+            }
+        }
+        free(sims);
+    }
+}
+
+void oracle_ivf_ip_f32(const float* rows, int64_t n, int d, const int32_t* labels, const int32_t* cells, int nprobe,
+                       const float* queries, int nq, int k, int32_t* out_ids, double* out_scores) {
+#pragma omp parallel
+    {
+        double* ts = (double*)malloc(sizeof(double) * (size_t)k);
+        int32_t* ti = (int32_t*)malloc(sizeof(int32_t) * (size_t)k);
+#pragma omp for schedule(dynamic, 1)
+        for (int qi = 0; qi < nq; qi++) {
+            const float* q = queries + (size_t)qi * d;
+            const int32_t* cq = cells + (size_t)qi * nprobe;
+            int cnt = 0;
+            for (int64_t r = 0; r < n; r++) {
+                int hit = 0;
+                for (int p = 0; p < nprobe; p++) hit |= labels[r] == cq[p];
+                if (!hit) continue;
+                const float* v = rows + (size_t)r * d;
+                double s = 0.0;
+                for (int j = 0; j < d; j++) s = fma((double)v[j], (double)q[j], s);
+                /* insert (s, r) into the descending list (ties: lower id first) */
+                int pos = cnt < k ? cnt : k;
+                while (pos > 0 && (ts[pos - 1] < s)) pos--;
+                if (pos >= k) continue;
+                int last = cnt < k ? cnt : k - 1;
+                for (int m = last; m > pos; m--) {
+                    ts[m] = ts[m - 1];
+                    ti[m] = ti[m - 1];
+                }
+                ts[pos] = s;
+                ti[pos] = (int32_t)r;
+                if (cnt < k) cnt++;
+            }
+            for (int m = 0; m < k; m++) {
+                out_ids[(size_t)qi * k + m] = m < cnt ? ti[m] : -1;
+                out_scores[(size_t)qi * k + m] = m < cnt ? ts[m] : -INFINITY;
+            }
+        }
+        free(ts);
+        free(ti);
+    }
+}
+
 void oracle_ivf_route(const float* centroids, int nlist, int d, const uint8_t* queries, int nq, int nprobe,
                       int32_t* out_cells) {
 #pragma omp parallel

@@ -64,6 +64,8 @@ def lib() -> ctypes.CDLL:
         L.oracle_num_threads.restype = i32
         L.oracle_score_ids.argtypes = [i32, i32, P, P, P, i32, P, P, i32, P]
         L.oracle_ivf_route.argtypes = [P, i32, i32, P, i32, i32, P]
+        L.oracle_ivf_route_f32.argtypes = [P, i32, i32, P, i32, i32, P]
+        L.oracle_ivf_ip_f32.argtypes = [P, i64, i32, P, P, i32, P, i32, i32, P, P]
         L.oracle_score_ids.restype = None
         for fn in ("oracle_l2_exact_u8", "oracle_l2_exact_u8_int", "oracle_l2_topk_u8_update", "oracle_cosine_exact_u8",
                    "oracle_speed_exact", "oracle_speed_prepare_u8", "oracle_speed_prepare_f32"):
@@ -265,6 +267,37 @@ def ivf_exact(corpus, labels, centroids, queries_u8, k, nprobe, metric="l2"):
         ids[i, :len(order)] = rows[order]
         dist[i, :len(order)] = d[order]
     return ids, dist
+
+
+def ivf_route_f32(centroids, queries, nprobe):
+    """[nq, nprobe] cells per float query, best first (fp64 in dimension
+    order, as ivf_route)."""
+    Cn = np.ascontiguousarray(centroids, dtype=np.float32)
+    Q = np.ascontiguousarray(queries, dtype=np.float32)
+    if Q.ndim == 1:
+        Q = Q[None, :]
+    out = np.empty((Q.shape[0], nprobe), np.int32)
+    lib().oracle_ivf_route_f32(_p(Cn), Cn.shape[0], Cn.shape[1], _p(Q), Q.shape[0], nprobe, _p(out))
+    return out
+
+
+def ivf_ip_f32(rows, labels, centroids, queries, k, nprobe):
+    """(ids int32, scores float64) [nq, k]: the exact top-k by float64 inner
+    product (descending, then row id) over the union of each float query's
+    probed cells -- MadHybrid over a float corpus with every probed row
+    scored (python/winnex_madhava/__init__.py:526, :650); -1 / -inf past
+    the rows available."""
+    X = np.ascontiguousarray(rows, dtype=np.float32)
+    Q = np.ascontiguousarray(queries, dtype=np.float32)
+    if Q.ndim == 1:
+        Q = Q[None, :]
+    lab = np.ascontiguousarray(labels, dtype=np.int32)
+    cells = ivf_route_f32(centroids, Q, nprobe)
+    ids = np.empty((Q.shape[0], k), np.int32)
+    sc = np.empty((Q.shape[0], k), np.float64)
+    lib().oracle_ivf_ip_f32(_p(X), X.shape[0], X.shape[1], _p(lab), _p(cells), nprobe, _p(Q), Q.shape[0], k,
+                            _p(ids), _p(sc))
+    return ids, sc
 
 
 def num_threads() -> int:

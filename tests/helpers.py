@@ -66,6 +66,9 @@ def capi():
     L.mdh_ivf_search_u8.argtypes = [P, P, i32, i32, i32, P, P, ctypes.POINTER(Stats)]
     L.mdh_ivf_info.argtypes = [P, P, P, P, P]
     L.mdh_ivf_destroy.argtypes = [P]
+    L.mdh_ivf_create_f32.argtypes = [P, i64, i32, P, i32, P, i32, ctypes.POINTER(P)]
+    L.mdh_ivf_search_f32.argtypes = [P, P, i32, i32, i32, P, P, ctypes.POINTER(Stats)]
+    L.mdh_ivf_destroy_f32.argtypes = [P]
     L.mdh_index_save.argtypes = [P, ctypes.c_char_p]
     L.mdh_index_load.argtypes = [ctypes.c_char_p, P, i32, ctypes.POINTER(P)]
     L.mdh_index_file_info.argtypes = [ctypes.c_char_p, P, P, P, P, P]

@@ -42,6 +42,10 @@ def test_argument_validation_before_device_use():
     assert L.mdh_search_f32(None, None, 1, 10, 0, None, None, None) == 1
     assert L.mdh_audit_u8(None, None, 1, 10, 5, None, None, None, None, None, None) == 1
     assert L.mdh_audit_f32(None, None, 1, 0, 5, None, None, None, None, None, None) == 1
+    assert L.mdh_ivf_create_f32(None, 10, 8, None, 2, None, -1, None) == 1
+    h = ctypes.c_void_p()
+    assert L.mdh_ivf_create_f32(None, 10, 8, None, 2, None, -1, ctypes.byref(h)) == 1 and not h.value
+    assert L.mdh_ivf_search_f32(None, None, 1, 10, 2, None, None, None) == 1
 
 
 def test_no_cpu_fallback_without_gpu():

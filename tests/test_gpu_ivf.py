@@ -226,3 +226,89 @@ def test_hybrid_facade_default_metric_on_gpu():
     np.testing.assert_array_equal(got, want)
     assert eng.search(Q[3].astype(np.float32), k=10).indices == [int(v) for v in want[3] if v >= 0]
     assert not eng._cells  # no per-cell engines were built
+
+
+# ---------------------------------------------------------------- float32 corpora
+def _ivf_f32(L, X, cen, labels):
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    cen = np.ascontiguousarray(cen, dtype=np.float32)
+    labels = np.ascontiguousarray(labels, dtype=np.int32)
+    h = ctypes.c_void_p()
+    st = L.mdh_ivf_create_f32(ptr(X), X.shape[0], X.shape[1], ptr(cen), cen.shape[0], ptr(labels), -1,
+                              ctypes.byref(h))
+    assert st == 0, L.mdh_last_error()
+    return h
+
+
+def _search_f32(L, h, Q, k, nprobe):
+    Q = np.ascontiguousarray(Q, dtype=np.float32)
+    ids = np.empty((len(Q), k), np.int32)
+    sc = np.empty((len(Q), k), np.float64)
+    s = Stats()
+    st = L.mdh_ivf_search_f32(h, ptr(Q), len(Q), k, nprobe, ptr(ids), ptr(sc), ctypes.byref(s))
+    assert st == 0, L.mdh_last_error()
+    return ids, sc, s
+
+
+def test_ivf_f32_matches_oracle():
+    """Float32 cells (the reference's float hybrid path): the exact top-k by
+    float64 inner product over the union of the probed cells, ids and scores
+    bit for bit (fp64, one fused multiply-add per dimension in order)."""
+    L = capi()
+    X, _ = _structured(n=20_000, d=64, n_clusters=16, seed=7)
+    rng = np.random.default_rng(121)
+    nlist = 24
+    cen = X[rng.choice(len(X), nlist, replace=False)].astype(np.float32)
+    labels = np.argmax(X @ cen.T, axis=1).astype(np.int32)
+    Q = (X[rng.choice(len(X), 40, replace=False)] + 0.05 * rng.standard_normal((40, 64))).astype(np.float32)
+    h = _ivf_f32(L, X, cen, labels)
+    for k, nprobe in ((1, 1), (10, 3), (16, 5), (10, nlist)):
+        ids, sc, s = _search_f32(L, h, Q, k, nprobe)
+        want_ids, want_sc = oracle.ivf_ip_f32(X, labels, cen, Q, k, nprobe)
+        np.testing.assert_array_equal(ids, want_ids)
+        np.testing.assert_array_equal(sc[want_ids >= 0], want_sc[want_ids >= 0])
+        cells = oracle.ivf_route_f32(cen, Q, nprobe)
+        rows = np.bincount(labels, minlength=nlist)
+        assert s.pairs_scored == int(rows[cells].sum())
+    assert L.mdh_ivf_destroy_f32(h) == 0
+
+
+def test_ivf_f32_edges():
+    """Empty cells, cells holding fewer than k rows (-1 padding), k above 16
+    refused, and a query batch of one."""
+    L = capi()
+    rng = np.random.default_rng(123)
+    X = rng.standard_normal((300, 40)).astype(np.float32)
+    cen = rng.standard_normal((6, 40)).astype(np.float32)
+    labels = np.where(np.arange(300) < 5, 0, 1 + np.arange(300) % 2).astype(np.int32)  # cells 3..5 empty
+    h = _ivf_f32(L, X, cen, labels)
+    Q = rng.standard_normal((7, 40)).astype(np.float32)
+    for k, nprobe in ((16, 1), (8, 2), (16, 6)):
+        ids, sc, _ = _search_f32(L, h, Q, k, nprobe)
+        want_ids, want_sc = oracle.ivf_ip_f32(X, labels, cen, Q, k, nprobe)
+        np.testing.assert_array_equal(ids, want_ids)
+        np.testing.assert_array_equal(sc[want_ids >= 0], want_sc[want_ids >= 0])
+    ids, _, _ = _search_f32(L, h, Q[:1], 10, 6)
+    np.testing.assert_array_equal(ids, oracle.ivf_ip_f32(X, labels, cen, Q[:1], 10, 6)[0])
+    out = np.empty((1, 17), np.int32)
+    assert L.mdh_ivf_search_f32(h, ptr(Q[:1]), 1, 17, 2, ptr(out), None, None) != 0
+    assert b"k must be" in L.mdh_last_error()
+    assert L.mdh_ivf_destroy_f32(h) == 0
+
+
+def test_hybrid_facade_float32_on_gpu():
+    """build_engine(X_float, hybrid=True): one batched GPU call per search,
+    equal to the oracle's exact top-k over the union of the probed cells of
+    the engine's own k-means cells (default metric, and L2: the float cells
+    rank by inner product either way)."""
+    import winnex_madhava as wm
+
+    X, _ = _structured(n=12_000, d=48, n_clusters=12, seed=9)
+    for metric in ("cosine", "l2"):
+        eng = wm.build_engine(X, dim=48, k=10, hybrid=True, nlist=16, nprobe=4, metric=metric)
+        assert eng._ivf_f32 is not None
+        Q = X[:25] + 0.01
+        want, _ = oracle.ivf_ip_f32(X, eng._labels, eng._centroids, Q, 10, 4)
+        got = np.asarray(eng.search_batch(Q, k=10).indices).reshape(25, 10)
+        np.testing.assert_array_equal(got, want)
+        assert list(eng.search(Q[3], k=10).indices) == [int(i) for i in want[3] if i >= 0]

@@ -23,7 +23,7 @@ LIB = os.path.join(PKG, "libwinnex_madhava_b200.so")
 EXT = os.path.join(PKG, "_winnex_madhava" + sysconfig.get_config_var("EXT_SUFFIX"))
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
-CU_SOURCES = ["capi.cu", "index.cu", "scan_simt.cu", "select.cu", "scan_tc.cu", "scan_tc2.cu", "scan_stream.cu", "scan_tc_bf16.cu", "ivf.cu", "noalloc.cu", "persist.cu"]
+CU_SOURCES = ["capi.cu", "index.cu", "scan_simt.cu", "select.cu", "scan_tc.cu", "scan_tc2.cu", "scan_stream.cu", "scan_tc_bf16.cu", "ivf.cu", "ivf_f32.cu", "noalloc.cu", "persist.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I" + INCLUDE, "-I" + CSRC,
                      "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]

@@ -384,6 +384,65 @@ private:
     int dim_ = 0, nlist_ = 0;
 };
 
+// The float32 clustered index (mdh_ivf_*_f32): MadHybrid over a float
+// corpus, every probed row scored in float64.
+class IvfIndexF32 {
+public:
+    IvfIndexF32(const F32Array& corpus, const F32Array& centroids,
+                py::array_t<int32_t, py::array::c_style | py::array::forcecast> labels, int device) {
+        auto ic = corpus.request(), ie = centroids.request(), il = labels.request();
+        if (ic.ndim != 2) throw std::runtime_error("corpus must be a 2-D float32 array");
+        if (ie.ndim != 2 || ie.shape[1] != ic.shape[1]) throw std::runtime_error("centroids must be [nlist][dim]");
+        if (il.size != ic.shape[0]) throw std::runtime_error("labels must hold one cell per row");
+        n_ = (int64_t)ic.shape[0];
+        dim_ = (int)ic.shape[1];
+        nlist_ = (int)ie.shape[0];
+        mdh_ivf_f32* p = nullptr;
+        mdh_status s;
+        {
+            py::gil_scoped_release nogil;
+            s = mdh_ivf_create_f32((const float*)ic.ptr, n_, dim_, (const float*)ie.ptr, nlist_,
+                                   (const int32_t*)il.ptr, device, &p);
+        }
+        check(s);
+        ix_ = p;
+    }
+    ~IvfIndexF32() {
+        if (ix_) mdh_ivf_destroy_f32(ix_);
+    }
+    IvfIndexF32(const IvfIndexF32&) = delete;
+    IvfIndexF32& operator=(const IvfIndexF32&) = delete;
+
+    // queries [nq][dim] float32 -> (ids, scores float64) [nq][k] and stats
+    py::tuple search(const F32Array& q, int k, int nprobe) const {
+        auto info = q.request();
+        const int nq = info.ndim == 1 ? 1 : (int)info.shape[0];
+        if ((size_t)info.size != (size_t)nq * dim_) throw std::runtime_error("queries must be float32 [nq][dim]");
+        py::array_t<int32_t> ids({nq, k});
+        py::array_t<double> sc({nq, k});
+        mdh_stats st{};
+        mdh_status s;
+        {
+            py::gil_scoped_release nogil;
+            s = mdh_ivf_search_f32(ix_, (const float*)info.ptr, nq, k, nprobe, ids.mutable_data(), sc.mutable_data(),
+                                   &st);
+        }
+        check(s);
+        py::dict d;
+        d["latency_ms"] = st.latency_ms;
+        d["pairs_scored"] = (long long)st.pairs_scored;
+        d["kernel_launches"] = (long long)st.kernel_launches;
+        return py::make_tuple(ids, sc, d);
+    }
+    int64_t num_vectors() const { return n_; }
+    int nlist() const { return nlist_; }
+
+private:
+    mdh_ivf_f32* ix_ = nullptr;
+    int64_t n_ = 0;
+    int dim_ = 0, nlist_ = 0;
+};
+
 // ---------------------------------------------------------------------------
 class SpeedEngine {
 public:
@@ -764,6 +823,14 @@ PYBIND11_MODULE(_winnex_madhava, m) {
         .def("route", &IvfIndex::route, py::arg("queries"), py::arg("nprobe"))
         .def("num_vectors", &IvfIndex::num_vectors)
         .def("nlist", &IvfIndex::nlist);
+
+    py::class_<IvfIndexF32>(m, "IvfIndexF32")
+        .def(py::init<const F32Array&, const F32Array&, py::array_t<int32_t, py::array::c_style | py::array::forcecast>,
+                      int>(),
+             py::arg("corpus"), py::arg("centroids"), py::arg("labels"), py::arg("device") = -1)
+        .def("search", &IvfIndexF32::search, py::arg("queries"), py::arg("k"), py::arg("nprobe"))
+        .def("num_vectors", &IvfIndexF32::num_vectors)
+        .def("nlist", &IvfIndexF32::nlist);
 
     py::class_<SpeedEngine>(m, "SpeedEngine")
         .def(py::init([](py::array_t<float, py::array::c_style> arr, int dim, int metric, int n_anchors, int nprobe,

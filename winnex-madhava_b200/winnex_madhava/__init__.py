@@ -337,8 +337,12 @@ class MadHybrid:
     fp64, ties to the lower cell id): under L2 ranked by (squared distance,
     row id), under the default metric "cosine" by (inner product, row id) --
     the reference merges a u8 corpus by ``corpus[ids] @ q`` (:640-646), exact
-    in integers here.  Float corpora and non-integral queries use one exact
-    GPU engine per cell.
+    in integers here.  A float32 corpus runs on the GPU index ``IvfIndexF32``,
+    also in one batched call: the reference's float cells score their rows by
+    the float64 inner product ``vecs @ q`` and the merge orders by that score
+    (:526, :650), so the result is the top-k of the probed cells' union by
+    (float64 inner product, row id), for k <= 16.  Larger k and non-integral
+    queries on a uint8 corpus use one exact GPU engine per cell.
     """
 
     def __init__(self, corpus, *, nlist: int = 64, nprobe: int = 5, dtype: str | None = None,
@@ -369,7 +373,18 @@ class MadHybrid:
         self._cells = {}
         self._devices = devices
         self._ivf = None
+        self._ivf_f32 = None
         t0 = time.time()
+        if self._dtype != "uint8":
+            dev = int(devices[0]) if devices else -1
+            self._ivf_f32 = _native.IvfIndexF32(np.ascontiguousarray(E, dtype=np.float32), self._centroids,
+                                                np.ascontiguousarray(labels, dtype=np.int32), dev)
+            for cid in range(self._nlist):
+                idxs = np.where(labels == cid)[0]
+                if len(idxs):
+                    self._members[cid] = idxs
+            self._build_time = time.time() - t0
+            return
         if self._dtype == "uint8" and self._dim <= 128:
             # metric "cosine" merges by the raw inner product corpus @ q
             # (python/winnex_madhava/__init__.py:640-646): the index's
@@ -422,6 +437,9 @@ class MadHybrid:
         if self._ivf is not None and np.all((q >= 0) & (q <= 255) & (q == np.round(q))):
             ids, _, st = self._ivf.search(q.astype(np.uint8)[None, :], kk, np_)
             return self._ivf_result([int(i) for i in ids[0] if i >= 0], st)
+        if self._ivf_f32 is not None and kk <= 16:
+            ids, _, st = self._ivf_f32.search(q[None, :], kk, np_)
+            return self._ivf_result([int(i) for i in ids[0] if i >= 0], st)
         if not self._cells:
             self._build_cells()
         cands = []
@@ -459,6 +477,9 @@ class MadHybrid:
         Q = np.ascontiguousarray(queries, dtype=np.float32).reshape(-1, self._dim)
         if self._ivf is not None and np.all((Q >= 0) & (Q <= 255) & (Q == np.round(Q))):
             ids, _, st = self._ivf.search(Q.astype(np.uint8), kk, np_)
+            return self._ivf_result([int(i) for i in ids.reshape(-1)], st)
+        if self._ivf_f32 is not None and kk <= 16:
+            ids, _, st = self._ivf_f32.search(Q, kk, np_)
             return self._ivf_result([int(i) for i in ids.reshape(-1)], st)
         out = []
         for q in Q:
