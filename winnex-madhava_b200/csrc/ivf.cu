@@ -229,13 +229,17 @@ __global__ void __launch_bounds__(256) k_route_sims(const uint8_t* __restrict__ 
     double* cs = route_smem + kRouteQ * kRouteDim;  // [kRouteC][dim + 1]
     const int q0 = blockIdx.y * kRouteQ, c0 = blockIdx.x * kRouteC;
     const int cstride = dim + 1;
-    for (int i = threadIdx.x; i < kRouteC * dim; i += blockDim.x) {
-        const int c = i / dim, j = i - c * dim;
-        cs[c * cstride + j] = c0 + c < nlist ? (double)centroids[(size_t)(c0 + c) * dim + j] : 0.0;
+    // A warp per row, lanes along the row (coalesced, no index division).
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    for (int c = warp; c < kRouteC; c += nwarps) {
+        const bool have = c0 + c < nlist;
+        const float* src = centroids + (size_t)(c0 + c) * dim;
+        for (int j = lane; j < dim; j += 32) cs[c * cstride + j] = have ? (double)__ldg(src + j) : 0.0;
     }
-    for (int i = threadIdx.x; i < kRouteQ * dim; i += blockDim.x) {
-        const int r = i / dim, j = i - r * dim;
-        qs[r * dim + j] = q0 + r < nq ? (double)q[(size_t)(q0 + r) * dpad + j] : 0.0;
+    for (int r = warp; r < kRouteQ; r += nwarps) {
+        const bool have = q0 + r < nq;
+        const uint8_t* src = q + (size_t)(q0 + r) * dpad;
+        for (int j = lane; j < dim; j += 32) qs[r * dim + j] = have ? (double)__ldg(src + j) : 0.0;
     }
     __syncthreads();
     // Thread: centroids cq + 16 b and queries rp + 16 a (a, b < 4).  A warp
