@@ -168,6 +168,25 @@ def test_speed_engine_counters_with_verification():
     assert one.verified_queries == 0 and one.pruned_by_bound >= 0
 
 
+@pytest.mark.parametrize("metric", ["l2", "cosine"])
+def test_speed_engine_anchors_scan_exactly(metric):
+    """speed_n_anchors / speed_nprobe are accepted and the scan stays exact,
+    as in the reference on a machine with a CUDA device: enable_gpu sets
+    use_gpu_ (src/speed_gpu.cu:136-160) and search / search_batch take the
+    brute-force GPU top-k (src/speed_cpu.cpp:426-448) without the anchor
+    cells."""
+    C = cases.gmm_u8(30_000, 128, 64, seed=113)
+    Q = cases.gmm_u8_queries(12, 128, 64, seed_means=113, seed_q=114).astype(np.float32)
+    plain = wm.build_engine(C, dim=128, k=10, metric=metric, speed=True)
+    anch = wm.build_engine(C, dim=128, k=10, metric=metric, speed=True, speed_n_anchors=16, speed_nprobe=2)
+    got = np.asarray(anch.search_batch(Q, k=10).indices).reshape(len(Q), 10)
+    np.testing.assert_array_equal(got, np.asarray(plain.search_batch(Q, k=10).indices).reshape(len(Q), 10))
+    want, _ = oracle.speed_exact(C, Q, 10, metric == "cosine")
+    np.testing.assert_array_equal(got, want)
+    for i in (0, 5):
+        assert list(anch.search(Q[i], k=10).indices) == list(want[i])
+
+
 def test_overflow_rerun_keeps_results_exact():
     """Tiny candidate lists force the overflow / tighter-threshold reruns."""
     C, Q = cases.case_dups()

@@ -13,7 +13,11 @@
 //     bound_violations is measured when verification is on (set_verify) and
 //     is 0 otherwise;
 //   * SpeedEngine always runs on the GPU (has_gpu() is True); n_anchors is
-//     accepted, and the scan stays exact;
+//     accepted, and the scan stays exact.  The reference does the same when
+//     a CUDA device is present: enable_gpu sets use_gpu_ (src/speed_gpu.cu:
+//     136-160) and search / search_batch then take the brute-force
+//     scores_gpu_topk (src/speed_cpu.cpp:426-448); only its CPU single-query
+//     path routes through the anchor cells (:295-328);
 //   * save_index / load_index write and read this library's index file (the
 //     norm-sorted corpus, norms and ids; no re-attached base is needed);
 //   * audit certificates and commitments (search_audited, audit_json,
