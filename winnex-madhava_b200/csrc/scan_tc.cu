@@ -227,15 +227,17 @@ __global__ void k_rekey_l2(const uint32_t* __restrict__ counts, uint2* __restric
     }
 }
 
-// Keys of a deferred unit scan's entries (see ChunkOut), one thread per
-// entry: the thread reads the entry's 32 dot products and the 32 row norms
-// (16-byte loads of 128-byte aligned runs; chunks start at multiples of 32
-// rows), marks each row with (key, id) <= the query's threshold -- the
-// epilogue's exact test -- and appends the marked rows with one atomic on the
-// query's count (a few rows per entry in the IVF passes; the values are read
-// again, from cache, for them).  The keys and ids are those of the EXACT
-// epilogue, so a list gets the same rows in another order.  Headers are
-// bounds-checked, and nothing runs after a scan that did not finish.
+// Keys of a deferred unit scan's entries (see ChunkOut), eight lanes per
+// entry: lane s of the group reads 16 bytes of the entry's dot products (rows
+// 4s .. 4s+3) and the same rows' norms, so each group's loads are two
+// coalesced 128-byte runs (entries and chunks start at multiples of 128
+// bytes).  A lane marks its rows with (key, id) <= the query's threshold --
+// the epilogue's exact test, ids read only on a key tie -- the group ORs the
+// lane masks, its first lane takes the list's slots with one atomic on the
+// query's count, and every lane writes its own rows.  The keys and ids are
+// those of the EXACT epilogue, so a list gets the same rows in another
+// order.  Headers are bounds-checked, and nothing runs after a scan that did
+// not finish.
 __global__ void __launch_bounds__(256) k_rekey_chunks(ChunkOut out, const int32_t* __restrict__ norms,
                                                       const int32_t* __restrict__ ids, int32_t n_rows_pad,
                                                       const int32_t* __restrict__ qn, int nq,
@@ -245,43 +247,42 @@ __global__ void __launch_bounds__(256) k_rekey_chunks(ChunkOut out, const int32_
                                                       const int32_t* __restrict__ status) {
     if (*reinterpret_cast<const volatile int32_t*>(status) != kDevOk) return;
     const uint32_t n = min(*out.counter, out.capacity);
-    const uint32_t stride = gridDim.x * blockDim.x;
-    const uint32_t* xs = reinterpret_cast<const uint32_t*>(out.x);
-    for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += stride) {
+    const int lane = threadIdx.x & 31, sub = lane & 7, lead = lane & 24;
+    const unsigned group = 0xffu << lead;  // the entry's eight lanes
+    const int r0 = 4 * sub;                 // this lane's first row in the chunk
+    const uint32_t stride = gridDim.x * (blockDim.x / 8);
+    for (uint32_t e = (blockIdx.x * blockDim.x + threadIdx.x) / 8; e < n; e += stride) {
         const int4 h = out.hdr[e];
         const int qi = h.x, row0 = h.y, valid = h.z;
         if (qi < 0 || qi >= nq || valid <= 0 || valid > 32 || row0 < 0 || row0 > n_rows_pad - 32 || (row0 & 31))
             continue;
         const int32_t qv = __ldg(qn + qi);
         const uint32_t tk = __ldg(thr_key + qi);
-        const uint4* xp = out.x + (size_t)e * 8;
-        const int4* np = reinterpret_cast<const int4*>(norms + row0);
-        uint32_t mask = 0;
+        const uint4 x = out.x[(size_t)e * 8 + sub];
+        const int4 nv = __ldg(reinterpret_cast<const int4*>(norms + row0) + sub);
+        const uint32_t key[4] = {(uint32_t)(qv + nv.x - 2 * (int32_t)x.x), (uint32_t)(qv + nv.y - 2 * (int32_t)x.y),
+                                 (uint32_t)(qv + nv.z - 2 * (int32_t)x.z), (uint32_t)(qv + nv.w - 2 * (int32_t)x.w)};
+        uint32_t mine = 0;
 #pragma unroll
-        for (int c8 = 0; c8 < 4; c8++) {
-            const uint4 xa = xp[2 * c8], xb = xp[2 * c8 + 1];
-            const int4 na = __ldg(np + 2 * c8), nb = __ldg(np + 2 * c8 + 1);
-            const uint32_t xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-            const int32_t nv[8] = {na.x, na.y, na.z, na.w, nb.x, nb.y, nb.z, nb.w};
+        for (int j = 0; j < 4; j++) {
+            // Rows tied with the threshold key stay only up to its id.
+            const bool keep = r0 + j < valid &&
+                              (key[j] < tk || (key[j] == tk && __ldg(ids + row0 + r0 + j) <= __ldg(thr_id + qi)));
+            mine |= (uint32_t)keep << j;
+        }
+        uint32_t mask = mine << r0;
+        mask |= __shfl_xor_sync(group, mask, 1);
+        mask |= __shfl_xor_sync(group, mask, 2);
+        mask |= __shfl_xor_sync(group, mask, 4);
+        if (mask == 0u) continue;
+        uint32_t at = 0;
+        if (sub == 0) at = atomicAdd(counts + qi, (uint32_t)__popc(mask));
+        at = __shfl_sync(group, at, lead) + (uint32_t)__popc(mask & ((1u << r0) - 1u));
 #pragma unroll
-            for (int j = 0; j < 8; j++)
-                if ((uint32_t)(qv + nv[j] - 2 * (int32_t)xv[j]) <= tk) mask |= 1u << (8 * c8 + j);
-        }
-        mask &= valid == 32 ? 0xffffffffu : (1u << valid) - 1u;
-        if (mask == 0u) continue;
-        // Rows tied with the threshold key stay only up to its id.
-        for (uint32_t m = mask; m; m &= m - 1u) {
-            const int j = __ffs(m) - 1;
-            const uint32_t key = (uint32_t)(qv + __ldg(norms + row0 + j) - 2 * (int32_t)xs[(size_t)e * 32 + j]);
-            if (key == tk && __ldg(ids + row0 + j) > __ldg(thr_id + qi)) mask &= ~(1u << j);
-        }
-        if (mask == 0u) continue;
-        uint32_t at = atomicAdd(counts + qi, (uint32_t)__popc(mask));
-        for (; mask; mask &= mask - 1u, at++) {
-            const int j = __ffs(mask) - 1;
-            if (at >= (uint32_t)cap) break;
-            const uint32_t key = (uint32_t)(qv + __ldg(norms + row0 + j) - 2 * (int32_t)xs[(size_t)e * 32 + j]);
-            cand[(size_t)qi * cap + at] = make_uint2(key, (uint32_t)(row0 + j));
+        for (int j = 0; j < 4; j++) {
+            if (!(mine >> j & 1u)) continue;
+            if (at < (uint32_t)cap) cand[(size_t)qi * cap + at] = make_uint2(key[j], (uint32_t)(row0 + r0 + j));
+            at++;
         }
     }
 }
