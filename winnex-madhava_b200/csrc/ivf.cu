@@ -215,18 +215,22 @@ __global__ void k_ivf_fill(int32_t* __restrict__ p, int64_t n, int32_t v) {
 
 // Routing, step 1: sims[q][c] = sum_j q[j] * centroid[c][j] in fp64, one
 // fused multiply-add per j in dimension order from 0.0 (deterministic, so the
-// cell order is reproducible).  Block tile: 64 queries x 64 centroids, both
-// converted to fp64 once in shared memory; each thread forms 4 x 4 of the
-// 4096 dot products, so a step of j is 8 shared loads for 16 multiply-adds
-// (one shared-memory wavefront per fp64 pipe slot of the SM).
+// cell order is reproducible).  Block tile: 64 queries x 64 centroids in
+// shared memory, the queries converted to fp64 once and the centroids kept in
+// fp32 and widened as they are read (exact either way).  The fp32 centroid
+// tile halves its size, so two blocks share an SM (16 warps): the kernel is
+// bound by the latency of its shared loads, and with one block per SM (fp64
+// tiles) it ran 1.65x longer.  Each thread forms 4 x 4 of the 4096 dot
+// products, so a step of j is 8 shared loads for 16 multiply-adds.
 constexpr int kRouteQ = 64, kRouteC = 64, kRouteDim = 128;
-constexpr size_t kRouteSmem = (size_t)(kRouteQ * kRouteDim + kRouteC * (kRouteDim + 1)) * sizeof(double);
+constexpr size_t kRouteSmem = (size_t)kRouteQ * kRouteDim * sizeof(double) +
+                              (size_t)kRouteC * (kRouteDim + 1) * sizeof(float);
 __global__ void __launch_bounds__(256) k_route_sims(const uint8_t* __restrict__ q, int nq, int dpad, int dim,
                                                     const float* __restrict__ centroids, int nlist,
                                                     double* __restrict__ sims) {
     extern __shared__ double route_smem[];
-    double* qs = route_smem;                       // [kRouteQ][dim]
-    double* cs = route_smem + kRouteQ * kRouteDim;  // [kRouteC][dim + 1]
+    double* qs = route_smem;                                            // [kRouteQ][dim]
+    float* cs = reinterpret_cast<float*>(route_smem + kRouteQ * kRouteDim);  // [kRouteC][dim + 1]
     const int q0 = blockIdx.y * kRouteQ, c0 = blockIdx.x * kRouteC;
     const int cstride = dim + 1;
     // A warp per row, lanes along the row (coalesced, no index division).
@@ -234,7 +238,7 @@ __global__ void __launch_bounds__(256) k_route_sims(const uint8_t* __restrict__ 
     for (int c = warp; c < kRouteC; c += nwarps) {
         const bool have = c0 + c < nlist;
         const float* src = centroids + (size_t)(c0 + c) * dim;
-        for (int j = lane; j < dim; j += 32) cs[c * cstride + j] = have ? (double)__ldg(src + j) : 0.0;
+        for (int j = lane; j < dim; j += 32) cs[c * cstride + j] = have ? __ldg(src + j) : 0.0f;
     }
     for (int r = warp; r < kRouteQ; r += nwarps) {
         const bool have = q0 + r < nq;
@@ -243,7 +247,7 @@ __global__ void __launch_bounds__(256) k_route_sims(const uint8_t* __restrict__ 
     }
     __syncthreads();
     // Thread: centroids cq + 16 b and queries rp + 16 a (a, b < 4).  A warp
-    // reads 16 centroid rows 129 doubles apart (every bank once) and
+    // reads 16 centroid rows 129 floats apart (every bank once) and
     // broadcasts two query rows.
     const int cq = threadIdx.x & 15, rp = threadIdx.x >> 4;
     double acc[4][4];
@@ -256,7 +260,7 @@ __global__ void __launch_bounds__(256) k_route_sims(const uint8_t* __restrict__ 
 #pragma unroll
         for (int a = 0; a < 4; a++) qv[a] = qs[(rp + 16 * a) * dim + j];
 #pragma unroll
-        for (int b = 0; b < 4; b++) cv[b] = cs[(cq + 16 * b) * cstride + j];
+        for (int b = 0; b < 4; b++) cv[b] = (double)cs[(cq + 16 * b) * cstride + j];
 #pragma unroll
         for (int a = 0; a < 4; a++)
 #pragma unroll
