@@ -67,6 +67,30 @@ def test_ivf_matches_oracle_on_reference_cells():
     assert L.mdh_ivf_destroy(h) == 0
 
 
+def test_ivf_route_ties_and_one_lane_holding_the_best():
+    """Routing order on ties and when one lane's cells are all the best:
+    centroids repeated every 10 cells (each similarity appears 20 times, so
+    the lower id decides), then cells 3, 35, 67, ... (one lane of the
+    selecting warp) made the 7 best, and every cell probed."""
+    L = capi()
+    rng = np.random.default_rng(77)
+    nlist = 200
+    C = rng.integers(0, 256, (2_000, 128), dtype=np.uint8)
+    labels = rng.integers(0, nlist, len(C)).astype(np.int32)
+    Q = rng.integers(0, 256, (50, 128), dtype=np.uint8)
+    base = rng.uniform(0, 1, (10, 128)).astype(np.float32)
+    tied = np.ascontiguousarray(np.tile(base, (nlist // 10, 1)))
+    one_lane = rng.uniform(0, 1, (nlist, 128)).astype(np.float32)
+    one_lane[3::32] *= 10
+    for cen, probes in ((tied, (1, 16, 45)), (one_lane, (12, nlist))):
+        h = _ivf(L, C, cen, labels)
+        for nprobe in probes:
+            cells = np.empty((len(Q), nprobe), np.int32)
+            assert L.mdh_ivf_route_u8(h, ptr(Q), len(Q), nprobe, ptr(cells)) == 0, L.mdh_last_error()
+            np.testing.assert_array_equal(cells, oracle.ivf_route(cen, Q, nprobe), err_msg=f"nprobe {nprobe}")
+        assert L.mdh_ivf_destroy(h) == 0
+
+
 def test_ivf_edge_cells_and_batches():
     """Empty cells, cells smaller than k, a cell larger than a unit's 64 tiles,
     one query and a 700-query batch."""

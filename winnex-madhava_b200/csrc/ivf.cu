@@ -308,9 +308,48 @@ __global__ void __launch_bounds__(256) k_route_select(double* __restrict__ sims,
     }
 }
 
+// (x, c) ranks before (y, d): larger similarity, then the lower cell id.
+__device__ __forceinline__ bool route_before(double x, int c, double y, int d) { return x > y || (x == y && c < d); }
+
+// Lane l's kRouteList best cells (of l, l + 32, ...) ranked after (av, ac),
+// best first; empty slots hold (-inf, INT_MAX).  Each cell is inserted by
+// the full (similarity, id) order: an entry it displaces can tie with a later
+// one of higher id and must still move ahead of it.
+constexpr int kRouteList = 4;
+template <int PER>
+__device__ __forceinline__ void route_lane_list(const double (&v)[PER], int lane, int nlist, double av, int ac,
+                                                double (&hv)[kRouteList], int (&hc)[kRouteList]) {
+#pragma unroll
+    for (int s = 0; s < kRouteList; s++) {
+        hv[s] = -INFINITY;
+        hc[s] = 0x7fffffff;
+    }
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const int c = lane + 32 * i;
+        if (c >= nlist || !route_before(av, ac, v[i], c)) continue;
+        double tv = v[i];
+        int tc = c;
+#pragma unroll
+        for (int s = 0; s < kRouteList; s++) {
+            if (route_before(tv, tc, hv[s], hc[s])) {
+                const double xv = hv[s];
+                const int xc = hc[s];
+                hv[s] = tv;
+                hc[s] = tc;
+                tv = xv;
+                tc = xc;
+            }
+        }
+    }
+}
+
 // The same selection with the row held in registers (nlist <= 32 * PER):
-// lane l holds cells l, l + 32, ...; each round takes the warp's best
-// (largest similarity, lower id on ties) and retires it.
+// lane l holds cells l, l + 32, ..., and keeps a sorted list of its best
+// kRouteList.  Each round the warp takes the best of the lists' heads
+// (largest similarity, lower id on ties) and its lane pops it; a lane whose
+// list runs out rebuilds it from the cells ranked after its last pop.  A
+// round is one warp argmax, not a pass over every lane's PER values.
 template <int PER>
 __global__ void __launch_bounds__(256) k_route_select_reg(const double* __restrict__ sims, int nq, int nlist,
                                                           int nprobe, int32_t* __restrict__ probe) {
@@ -324,30 +363,33 @@ __global__ void __launch_bounds__(256) k_route_select_reg(const double* __restri
         const int c = lane + 32 * i;
         v[i] = c < nlist ? row[c] : -INFINITY;
     }
+    double hv[kRouteList];
+    int hc[kRouteList];
+    route_lane_list(v, lane, nlist, INFINITY, -1, hv, hc);
     for (int p = 0; p < nprobe; p++) {
-        double bv = -INFINITY;
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int i = 0; i < PER; i++) {
-            const int c = lane + 32 * i;  // ascending, so '>' keeps the lower id on ties
-            if (c < nlist && v[i] > bv) {
-                bv = v[i];
-                bi = c;
-            }
-        }
+        double bv = hv[0];
+        int bi = hc[0];
 #pragma unroll
         for (int m = 16; m >= 1; m >>= 1) {
             const double ov = __shfl_xor_sync(0xffffffffu, bv, m);
             const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
-            if (ov > bv || (ov == bv && oi < bi)) {
+            if (route_before(ov, oi, bv, bi)) {
                 bv = ov;
                 bi = oi;
             }
         }
         if (lane == 0) probe[(size_t)qi * nprobe + p] = bi;
+        if (bi == hc[0] && bi < nlist) {  // this lane's head was taken
+            const double lv = hv[0];
 #pragma unroll
-        for (int i = 0; i < PER; i++)
-            if (lane + 32 * i == bi) v[i] = -INFINITY;  // taken
+            for (int s = 0; s + 1 < kRouteList; s++) {
+                hv[s] = hv[s + 1];
+                hc[s] = hc[s + 1];
+            }
+            hv[kRouteList - 1] = -INFINITY;
+            hc[kRouteList - 1] = 0x7fffffff;
+            if (hc[0] == 0x7fffffff) route_lane_list(v, lane, nlist, lv, bi, hv, hc);
+        }
     }
 }
 
